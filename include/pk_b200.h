@@ -1,0 +1,204 @@
+/*
+ * pk_b200.h -- C ABI of libpk_b200.so, the B200 (sm_100a) engine for the
+ * FastConformer encoder hot path of parakeet.wgsl.
+ *
+ * Every entry point returns a pk_status (0 = OK, negative = error) and records
+ * a per-thread message readable with pk_last_error().  All pointers named
+ * "device" are CUDA device pointers owned by the caller; streams are
+ * cudaStream_t passed as void* (NULL = the legacy default stream).  Handles are
+ * opaque.  No entry point takes or returns a framework type.
+ *
+ * Each declaration cites the reference interface it replaces
+ * (narcotic-sh/parakeet.wgsl v1.0.1, path:line).
+ */
+#ifndef PK_B200_H
+#define PK_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  The reference throws synchronous Error / RangeError from
+ * createDispatch/encode (src/webgpu/kernels/gemm.ts:971-1161, :434-436); these
+ * are their C equivalents. */
+typedef enum pk_status {
+  PK_OK = 0,
+  PK_E_INVALID = -1,   /* null handle / argument out of range            */
+  PK_E_SHAPE = -2,     /* RangeError: unsupported shape                  */
+  PK_E_LAYOUT = -3,    /* Error: invalid packed palette / tensor layout  */
+  PK_E_SIGNATURE = -4, /* Error: not a fixed production GEMM signature   */
+  PK_E_CUDA = -5,      /* CUDA runtime error                             */
+  PK_E_OOM = -6,       /* device allocation failed                       */
+  PK_E_TIMEOUT = -7,   /* a bounded device wait expired                  */
+  PK_E_DESTROYED = -8, /* handle used after destroy                      */
+  PK_E_NOT_FOUND = -9  /* model tensor missing (ParakeetGpuPackage.tensor) */
+} pk_status;
+
+/* Execution precision: the reference's FP16 / FP32 packages
+ * (src/webgpu/capabilities.ts, ParakeetExecutionProfile.precision). */
+enum { PK_FP16 = 0, PK_FP32 = 1 };
+/* GemmActivation (src/webgpu/kernels/gemm.ts:148). */
+enum { PK_ACT_NONE = 0, PK_ACT_SILU = 1, PK_ACT_RELU = 2 };
+/* Expanded palette target layouts (src/model/runtime-plan.ts:26-33):
+ * k-by-output-row-major-{f16,f32} and n{256,128}-k32-tile-major-{f16,f32}. */
+enum { PK_LAYOUT_ROW_MAJOR = 0, PK_LAYOUT_TILE_MAJOR = 1 };
+/* Tensor element types (ParakeetTensorRecord.dtype). */
+enum { PK_DTYPE_F16 = 0, PK_DTYPE_F32 = 1, PK_DTYPE_U32 = 2 };
+
+typedef struct pk_device pk_device;
+typedef struct pk_weights pk_weights;
+typedef struct pk_encoder pk_encoder;
+typedef void* pk_stream;
+
+/* Copies the calling thread's last error message (NUL-terminated). */
+int pk_last_error(char* buffer, size_t length);
+int pk_version(void);
+
+/* Opens CUDA device `ordinal`.  Replaces the WebGPU adapter/device request in
+ * createRawWebGpuParakeetEngine (src/runtime/webgpu-engine.ts:1062-1120). */
+int pk_device_open(int ordinal, pk_device** out);
+int pk_device_close(pk_device* device);
+/* Reads and clears the device status word (bit 0..4: a bounded wait inside a
+ * kernel expired).  Replaces the uncapturederror listener / throwGpuError
+ * (src/runtime/webgpu-engine.ts:274, :959).  Synchronizes the device. */
+int pk_device_status(pk_device* device, uint32_t* status_bits);
+
+/* ---------------------------------------------------------------- operators
+ * Palette expansion, bit-exact with paletteDequantWgslForScalar
+ * (src/model/palette-expander.ts:478-587) and the index map
+ * runtimeGemmTileMajorScalarIndex (src/model/runtime-plan.ts:454-490).
+ * Replaces PaletteWeightExpander.createPooledDispatch + encode
+ * (src/model/palette-expander.ts:234-309). */
+typedef struct pk_palette_desc {
+  int precision;             /* PK_FP16 (f16 palette/target) or PK_FP32 */
+  int bits;                  /* 5 or 6 */
+  int64_t inner;             /* K */
+  int64_t columns;           /* N */
+  int palette_groups;        /* G: palette is [G, 2^bits] */
+  int64_t palette_group_columns; /* N / G */
+  int layout;                /* PK_LAYOUT_ROW_MAJOR or PK_LAYOUT_TILE_MAJOR */
+  const uint32_t* codes;     /* device [K*N/codes_per_group, words_per_group] */
+  const void* palette;       /* device [G, 2^bits] f16 or f32 */
+  void* target;              /* device [K*N] f16 or f32 */
+} pk_palette_desc;
+int pk_palette_expand(pk_device* device, const pk_palette_desc* desc, pk_stream stream);
+
+/* Fused palette-dequantizing GEMM: C = epilogue(A . W), W decoded from its
+ * packed codes on chip (never written to HBM).  Mirrors GemmDescriptor
+ * (src/webgpu/kernels/gemm.ts:358-373) and the epilogues
+ * specializedBias/Activation/Residual (:2006-2044, :2847-2869); replaces
+ * F16GemmKernel/F32GemmKernel.createDispatch + GemmDispatch.encode
+ * (:483-855, :2974-3340, :400-470).  Bias and residual are exclusive. */
+typedef struct pk_gemm_desc {
+  int precision;             /* PK_FP16: A/C/residual f16, LUT f16; PK_FP32: all f32 */
+  int64_t rows;              /* M (active rows) */
+  int64_t inner;             /* K */
+  int64_t columns;           /* N */
+  int bits;                  /* 5 or 6 */
+  int palette_groups;        /* G */
+  int64_t palette_group_columns; /* N / G */
+  int activation;            /* PK_ACT_* */
+  int has_residual;          /* residual = residual + scale * value */
+  float residual_scale;
+  const float* bias;         /* device f32 [N] or NULL */
+  const void* residual;      /* device [M, N] or NULL */
+  const void* a;             /* device [M, K] */
+  const uint32_t* codes;     /* device packed k-by-output-row-major codes */
+  const void* palette;       /* device [G, 2^bits] */
+  void* c;                   /* device [M, N] */
+} pk_gemm_desc;
+int pk_palette_gemm(pk_device* device, const pk_gemm_desc* desc, pk_stream stream);
+
+/* LayerNorm over `channels` per row (src/webgpu/kernels/layernorm.ts:309-389);
+ * replaces LayerNormKernel.createDispatch + encode (:73-240). */
+int pk_layernorm(pk_device* device, int precision, int64_t rows, int64_t channels, const void* x,
+                 const float* gamma, const float* beta, float epsilon, void* y, pk_stream stream);
+
+/* Fused relative-position MHSA, 8 heads x 128 (src/webgpu/kernels/attention.ts:
+ * 418-728); replaces RelativeAttentionKernel.createDispatch + encode
+ * (:105-321).  qkv [B*T, 3072]; positions head-vector-position-vec4
+ * [8][32][2T-1][4]; bias_u/v f32 [8,128]; valid_lengths u32 [B] (device);
+ * context [B*T, 1024].  Requires 1 <= T <= 192. */
+int pk_rel_attention(pk_device* device, int precision, int batch, int frames, const void* qkv,
+                     const void* positions, const float* bias_u, const float* bias_v,
+                     const uint32_t* valid_lengths, void* context, pk_stream stream);
+
+/* Fused GLU + depthwise k9 + folded BN + SiLU (src/webgpu/kernels/
+ * conformer-conv.ts:471-575); replaces FusedConformerConvKernel
+ * (:174-351).  pointwise [B*T, 2048]; dw [9, 1024]; scale/shift f32 [1024];
+ * out [B*T, 1024]. */
+int pk_conformer_conv(pk_device* device, int precision, int batch, int frames, const void* pointwise,
+                      const void* dw_weights, const float* bn_scale, const float* bn_shift,
+                      const uint32_t* valid_lengths, void* out, pk_stream stream);
+
+/* Subsampling kernels (src/webgpu/kernels/subsampling.ts): fused conv0 +
+ * depthwise2 (:1092-1268; FusedSubsamplingConv0Depthwise2Kernel :620),
+ * depthwise (:1270-1372; DepthwiseSubsamplingKernel :438) and time mask
+ * (:1374-1425; SubsamplingTimeMaskKernel :250).  feature_lengths are the raw
+ * feature-frame lengths (device u32 [B]). */
+int pk_subsampling_conv0_dw2(pk_device* device, int precision, int batch, const float* features,
+                             const void* conv0_w, const float* conv0_b, const void* dw_w,
+                             const float* dw_b, const uint32_t* feature_lengths, void* out,
+                             pk_stream stream);
+int pk_subsampling_depthwise(pk_device* device, int precision, int batch, int in_height, int in_width,
+                             int channels, const void* input, const void* weights, const float* bias,
+                             const uint32_t* feature_lengths, int steps, void* out, pk_stream stream);
+int pk_subsampling_time_mask(pk_device* device, int precision, int batch, int height, int width,
+                             int channels, void* values, const uint32_t* feature_lengths, int steps,
+                             pk_stream stream);
+
+/* ------------------------------------------------------------ model + graph
+ * One named tensor of a weight package (ParakeetTensorRecord,
+ * src/model/manifest.ts; runtime layouts src/model/runtime-plan.ts:26-37). */
+typedef struct pk_tensor_desc {
+  const char* name;          /* e.g. "encoder.layers.0.self_attn.qkv.weight" */
+  int dtype;                 /* PK_DTYPE_* */
+  int ndim;
+  int64_t shape[4];          /* logical shape */
+  const char* layout;        /* e.g. "k-by-output-row-major-palette5-lsb-u32" */
+  const void* data;          /* host pointer */
+  size_t bytes;
+} pk_tensor_desc;
+/* Uploads a package to the device.  Replaces ParakeetGpuPackage
+ * (src/model/package.ts:45-52) plus the runtime plan (runtime-plan.ts:144-340). */
+int pk_weights_upload(pk_device* device, const pk_tensor_desc* tensors, int count, pk_weights** out);
+int pk_weights_release(pk_weights* weights);
+
+/* Builds the fixed-shape 24-layer encoder graph for up to batch_capacity 15 s
+ * windows (<= 40).  Replaces ParakeetEncoderGraph.create
+ * (src/webgpu/encoder.ts:1299-1535). */
+int pk_encoder_create(pk_device* device, pk_weights* weights, int precision, int batch_capacity,
+                      pk_encoder** out);
+/* Runs subsampling, 24 Conformer layers and the projector for `batch`
+ * windows.  features: f32 [batch, 128, 1501] feature-major; feature_lengths:
+ * host u32 [batch] in [1, 1501]; projected_out: [batch*188, 640] in the
+ * profile scalar; encoded_lengths (host, optional): u32 [batch].
+ * features_on_device / out_on_device select device or host buffers (host
+ * buffers are copied inside the call).  Replaces encodeSubmissionChunks +
+ * decoderInput (src/webgpu/encoder.ts:1711-1743, :1821). */
+int pk_encoder_forward(pk_encoder* encoder, const float* features, int features_on_device,
+                       const uint32_t* feature_lengths, int batch, void* projected_out, int out_on_device,
+                       uint32_t* encoded_lengths, pk_stream stream);
+/* Diagnostic per-layer capture, the analogue of encodeDiagnosticB1Checkpoints
+ * (src/webgpu/encoder.ts:1751-1819, plan :621-688): after
+ * pk_encoder_set_checkpoints(encoder, 1) every forward also keeps the
+ * subsampling output and each layer's output; pk_encoder_checkpoint copies
+ * the [capacity*188, 1024] buffer of `layer` (-1 = subsampling) into `out`
+ * (device). */
+int pk_encoder_set_checkpoints(pk_encoder* encoder, int enable);
+int pk_encoder_checkpoint(pk_encoder* encoder, int layer, void* out, pk_stream stream);
+int pk_encoder_destroy(pk_encoder* encoder);
+
+/* Test hook (no reference counterpart): selects the GEMM kernel for later
+ * pk_palette_gemm / encoder launches in this process.  0 = automatic
+ * (tensor cores where the shape tiles, else CUDA cores), 1 = CUDA-core
+ * kernel only, 2 = tensor-core kernel only (unsupported shapes fail). */
+int pk_debug_set_gemm_route(int route);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PK_B200_H */

@@ -1,0 +1,416 @@
+// gemm_tc.cu -- fused palette-dequantizing GEMM on the sm_100a tensor cores.
+//
+// Computes C[M, N] = epilogue(A[M, K] . W[K, N]) for the FP16 package, where W
+// arrives as the reference's bit-packed 5/6-bit palette codes
+// (k-by-output-row-major-palette{5,6}-lsb-u32, src/model/runtime-plan.ts:352-368)
+// plus a [G, 2^bits] f16 lookup table, and is decoded on chip: the dequantized
+// weights never go to HBM (the reference expands them to a scratch buffer
+// first, src/model/palette-expander.ts:478-587, then runs
+// f16SubgroupGemmWgsl, src/webgpu/kernels/gemm.ts:1362-1716).
+//
+// Formulation (swapped): D^T = W^T . A^T, so the 128 MMA rows are output
+// features and the MMA N dimension is BN tokens.
+//   * MMA-A = decoded weights, [128 features x 64 k] per stage, MN-major with
+//     128-byte swizzle, written to shared memory by 4 decoder warps from the
+//     packed-code tile (TMA, no swizzle) through the LUT held in shared memory;
+//   * MMA-B = activations, [BN tokens x 64 k] per stage, K-major, loaded by TMA
+//     with 128-byte swizzle (rows past M are zero-filled by TMA);
+//   * D = fp32 accumulators in TMEM, double buffered (2 x BN columns) so the
+//     epilogue of one tile overlaps the main loop of the next.
+// Persistent CTAs (one per SM) walk the tile list; warp roles:
+//   warp 0 TMA producer, warp 1 MMA issuer (+TMEM owner), warps 2-5 decoders,
+//   warps 6-9 epilogue (bias / SiLU / ReLU / residual, f16 store).
+// Accumulation is fp32 (the reference accumulates in f16, gemm.ts:1445-1453),
+// so results agree with the reference algorithm within the FP16 package
+// tolerance and with the oracle's wide-accumulation mode to f16 rounding.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+
+#include "pk_common.cuh"
+#include "pk_internal.h"
+
+namespace pk {
+
+constexpr int TC_BM = 128;        // output features per tile (MMA M)
+constexpr int TC_BK = 64;         // k per stage: one 128-byte swizzle row of f16
+constexpr int TC_STAGES = 4;
+constexpr int TC_THREADS = 320;   // 10 warps
+constexpr int TC_DECODE_THREADS = 128;
+constexpr int TC_EPI_THREADS = 128;
+
+struct TcGemmParams {
+  CUtensorMap tmap_a;       // activations [M, K] f16, box {64, BN}, 128B swizzle
+  CUtensorMap tmap_codes;   // packed codes [K, N*bits/32] u32, box {128*bits/32, 64}
+  const uint16_t* palette;  // f16 bits [G, 2^bits]
+  const float* bias;
+  const __half* residual;
+  __half* out;
+  unsigned int* status;
+  int rows, inner, columns;
+  int groups, group_cols;
+  int act, has_residual;
+  float res_scale;
+  int m_tiles, n_tiles;
+};
+
+template <int BN, int BITS>
+struct TcLayout {
+  static constexpr int CPG = BITS == 5 ? 32 : 16;         // codes per packed group
+  static constexpr int WPG = BITS == 5 ? 5 : 3;           // u32 words per packed group
+  static constexpr int WORDS_PER_ROW = TC_BM * BITS / 32; // 20 or 24 words per k row of a tile
+  static constexpr int A_BYTES = BN * TC_BK * 2;
+  static constexpr int W_BYTES = TC_BM * TC_BK * 2;
+  static constexpr int CODE_BYTES = TC_BK * WORDS_PER_ROW * 4;
+  static constexpr int OFF_A = 0;
+  static constexpr int OFF_W = OFF_A + TC_STAGES * A_BYTES;
+  static constexpr int OFF_C = OFF_W + TC_STAGES * W_BYTES;
+  static constexpr int OFF_LUT = OFF_C + TC_STAGES * CODE_BYTES;
+  static constexpr int LUT_BYTES = 3 * 64 * 2;
+  static constexpr int OFF_BAR = (OFF_LUT + LUT_BYTES + 7) / 8 * 8;
+  static constexpr int NUM_BARS = 3 * TC_STAGES + 2 + 2 + 1;
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+  static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
+  static constexpr uint32_t IDESC = umma_idesc_f16(TC_BM, BN, /*A MN-major*/ 1, /*B K-major*/ 0);
+  static_assert(A_BYTES % 1024 == 0 && W_BYTES % 1024 == 0, "stage buffers must keep 1024B alignment");
+  static_assert(CODE_BYTES % 128 == 0, "code stage must keep 128B alignment");
+};
+
+// Extract code i of a packed group held in registers (LSB-first bit stream).
+template <int BITS, int I>
+__device__ __forceinline__ uint32_t code_of(const uint32_t (&w)[BITS == 5 ? 5 : 3]) {
+  constexpr int bit = I * BITS, word = bit >> 5, sh = bit & 31;
+  if constexpr (sh + BITS <= 32) {
+    return (w[word] >> sh) & ((1u << BITS) - 1u);
+  } else {
+    return __funnelshift_r(w[word], w[word + 1], sh) & ((1u << BITS) - 1u);
+  }
+}
+
+template <int BITS, int I, int N>
+struct DecodePairs {
+  // Decode codes [I, N) of a group into packed f16 pairs.
+  static __device__ __forceinline__ void run(const uint32_t (&w)[BITS == 5 ? 5 : 3], const uint16_t* lut,
+                                             uint32_t* out) {
+    if constexpr (I < N) {
+      const uint32_t lo = lut[code_of<BITS, I>(w)];
+      const uint32_t hi = lut[code_of<BITS, I + 1>(w)];
+      out[I / 2] = lo | (hi << 16);
+      DecodePairs<BITS, I + 2, N>::run(w, lut, out);
+    }
+  }
+};
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+
+// Decode one packed group (fixed k, CPG consecutive features starting at
+// feature-in-tile `f0`) into the MN-major SW128 weight tile.
+// Tile layout: atom(n_block, k_group) at n_block * 8192 + k_group * 1024;
+// row (k % 8) at 128 B; 16-byte chunk c (features 8c..8c+7 of the 64-wide
+// block) at physical chunk c ^ (k % 8).
+template <int BITS>
+__device__ __forceinline__ void decode_group(const uint32_t* src, const uint16_t* lut, uint32_t w_stage, int k,
+                                             int f0) {
+  constexpr int WPG = BITS == 5 ? 5 : 3, CPG = BITS == 5 ? 32 : 16;
+  uint32_t words[WPG];
+#pragma unroll
+  for (int j = 0; j < WPG; ++j) words[j] = src[j];
+  uint32_t packed[CPG / 2];
+  DecodePairs<BITS, 0, CPG>::run(words, lut, packed);
+  const int r = k & 7;
+  const uint32_t row = w_stage + (uint32_t)((f0 >> 6) * 8192 + (k >> 3) * 1024 + r * 128);
+  const int c0 = (f0 & 63) >> 3;
+#pragma unroll
+  for (int q = 0; q < CPG / 8; ++q) {
+    const uint32_t chunk = (uint32_t)((c0 + q) ^ r);
+    st_shared_v4(row + chunk * 16, packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+  }
+}
+
+template <int BN, int BITS>
+__global__ void __launch_bounds__(TC_THREADS, 1) tc_palette_gemm_kernel(const __grid_constant__ TcGemmParams p) {
+  using L = TcLayout<BN, BITS>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem + L::OFF_A;
+  uint8_t* sW = smem + L::OFF_W;
+  uint32_t* sCodes = reinterpret_cast<uint32_t*>(smem + L::OFF_C);
+  uint16_t* sLut = reinterpret_cast<uint16_t*>(smem + L::OFF_LUT);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* full_tma = bars;
+  uint64_t* full_dec = bars + TC_STAGES;
+  uint64_t* empty = bars + 2 * TC_STAGES;
+  uint64_t* tm_full = bars + 3 * TC_STAGES;
+  uint64_t* tm_empty = tm_full + 2;
+  uint64_t* drain = tm_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int lut_entries = p.groups << BITS;
+  for (int i = threadIdx.x; i < lut_entries; i += blockDim.x) sLut[i] = p.palette[i];
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < TC_STAGES; ++s) {
+      mbar_init(&full_tma[s], 1);
+      mbar_init(&full_dec[s], TC_DECODE_THREADS);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tm_full[a], 1);
+      mbar_init(&tm_empty[a], TC_EPI_THREADS);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&p.tmap_a);
+    tma_prefetch_desc(&p.tmap_codes);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 2 * BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int kb_count = p.inner / TC_BK;
+  const int num_tiles = p.m_tiles * p.n_tiles;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int last_round[TC_STAGES];
+#pragma unroll
+      for (int s = 0; s < TC_STAGES; ++s) last_round[s] = -1;
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int n_tile = tile % p.n_tiles, m_tile = tile / p.n_tiles;
+        for (int kb = 0; kb < kb_count; ++kb, ++it) {
+          const int s = it % TC_STAGES;
+          const uint32_t round = it / TC_STAGES;
+          if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1, abort_flag, p.status, PK_STATUS_TIMEOUT_TMA)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full_tma[s], L::A_BYTES + L::CODE_BYTES);
+          tma_load_2d(sA + s * L::A_BYTES, &p.tmap_a, &full_tma[s], kb * TC_BK, m_tile * BN);
+          tma_load_2d(sCodes + s * (L::CODE_BYTES / 4), &p.tmap_codes, &full_tma[s], n_tile * L::WORDS_PER_ROW,
+                      kb * TC_BK);
+          last_round[s] = (int)round;
+        }
+      }
+      // Unwind: every load this thread issued must have landed before exit.
+      for (int s = 0; s < TC_STAGES; ++s)
+        if (last_round[s] >= 0) mbar_wait_drain(&full_tma[s], (uint32_t)last_round[s] & 1, p.status);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      uint32_t it = 0;
+      int tile_iter = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++tile_iter) {
+        const int acc = tile_iter & 1;
+        const uint32_t acc_round = (uint32_t)tile_iter >> 1;
+        if (acc_round > 0 &&
+            !mbar_wait(&tm_empty[acc], (acc_round - 1) & 1, abort_flag, p.status, PK_STATUS_TIMEOUT_MMA)) {
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < kb_count; ++kb, ++it) {
+          const int s = it % TC_STAGES;
+          const uint32_t round = it / TC_STAGES;
+          if (!mbar_wait(&full_tma[s], round & 1, abort_flag, p.status, PK_STATUS_TIMEOUT_MMA) ||
+              !mbar_wait(&full_dec[s], round & 1, abort_flag, p.status, PK_STATUS_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t w_addr = smem_addr(sW + s * L::W_BYTES);
+          const uint32_t a_addr = smem_addr(sA + s * L::A_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < TC_BK / 16; ++kk) {
+            // A (weights, MN-major): two 8-row k groups per K=16 step, SBO = 1024 B
+            // between k groups, LBO = 8192 B between 64-feature blocks.
+            const uint64_t a_desc = umma_smem_desc(w_addr + kk * 2048, 8192, 1024, 2);
+            // B (activations, K-major): advance 32 B (16 f16) inside the swizzle row.
+            const uint64_t b_desc = umma_smem_desc(a_addr + kk * 32, 16, 1024, 2);
+            tc_mma_f16(d_tmem, a_desc, b_desc, L::IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(&empty[s]);
+        }
+        if (!ok) break;
+        tc_commit(&tm_full[acc]);
+      }
+      // Unwind: wait until every MMA issued by this thread has completed.
+      tc_commit(drain);
+      mbar_wait_drain(drain, 0, p.status);
+    }
+  } else if (warp < 6) {
+    // ------------------------------------------------------------ decoders
+    const int dw = warp - 2;  // 0..3, 16 k rows each per stage
+    uint32_t it = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      const int n_tile = tile % p.n_tiles;
+      const int f_base = n_tile * TC_BM;
+      // Palette group of each group this lane decodes (constant over k).
+      constexpr int GROUPS_PER_LANE = BITS == 5 ? 1 : 2;
+      const uint16_t* lut_g[GROUPS_PER_LANE];
+      int f0[GROUPS_PER_LANE];
+#pragma unroll
+      for (int j = 0; j < GROUPS_PER_LANE; ++j) {
+        const int ng = (lane >> 3) + 4 * j;
+        f0[j] = ng * L::CPG;
+        const int pg = min((f_base + f0[j]) / p.group_cols, p.groups - 1);
+        lut_g[j] = sLut + (pg << BITS);
+      }
+      bool ok = true;
+      for (int kb = 0; kb < kb_count; ++kb, ++it) {
+        const int s = it % TC_STAGES;
+        const uint32_t round = it / TC_STAGES;
+        if (!mbar_wait(&full_tma[s], round & 1, abort_flag, p.status, PK_STATUS_TIMEOUT_DECODE)) {
+          ok = false;
+          break;
+        }
+        const uint32_t* codes = sCodes + s * (L::CODE_BYTES / 4);
+        const uint32_t w_stage = smem_addr(sW + s * L::W_BYTES);
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const int k = dw * 16 + i * 8 + (lane & 7);
+#pragma unroll
+          for (int j = 0; j < GROUPS_PER_LANE; ++j) {
+            const int ng = (lane >> 3) + 4 * j;
+            decode_group<BITS>(codes + k * L::WORDS_PER_ROW + ng * L::WPG, lut_g[j], w_stage, k, f0[j]);
+          }
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&full_dec[s]);
+      }
+      if (!ok) break;
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int tile_iter = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++tile_iter) {
+      const int acc = tile_iter & 1;
+      const uint32_t acc_round = (uint32_t)tile_iter >> 1;
+      if (!mbar_wait(&tm_full[acc], acc_round & 1, abort_flag, p.status, PK_STATUS_TIMEOUT_EPILOGUE)) break;
+      tc_fence_after();
+      const int n_tile = tile % p.n_tiles, m_tile = tile / p.n_tiles;
+      const int n = n_tile * TC_BM + q * 32 + lane;
+      const int m0 = m_tile * BN;
+      const float bias_v = p.bias ? p.bias[n] : 0.0f;
+      const uint32_t t_base = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tc_ld_32x32b_x32(t_base + (uint32_t)c, r);
+        tc_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int t = m0 + c + j;
+          if (t < p.rows) {
+            float v = __uint_as_float(r[j]) + bias_v;
+            if (p.act == PK_ACT_SILU) v = silu_ref(v);
+            else if (p.act == PK_ACT_RELU) v = fmaxf(v, 0.0f);
+            const size_t idx = (size_t)t * p.columns + n;
+            if (p.has_residual) v = __half2float(p.residual[idx]) + p.res_scale * v;
+            p.out[idx] = __float2half_rn(v);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tm_empty[acc]);
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+// ------------------------------------------------------------------ host
+static bool encode_2d(const DeviceCtx& dev, CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
+                      uint64_t inner, uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+                      CUtensorMapSwizzle swizzle) {
+  auto fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(dev.encode_tiled);
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+bool gemm_tc_supported(const GemmArgs& g) {
+  return g.precision == PK_FP16 && g.columns % TC_BM == 0 && g.inner % TC_BK == 0 && g.rows > 0 &&
+         g.rows <= (int64_t)1 << 30 && (g.bits == 5 || g.bits == 6) &&
+         (reinterpret_cast<uintptr_t>(g.a) & 15) == 0 && (reinterpret_cast<uintptr_t>(g.codes) & 15) == 0;
+}
+
+template <int BN, int BITS>
+static int launch_tc(const DeviceCtx& dev, const GemmArgs& g, cudaStream_t stream) {
+  using L = TcLayout<BN, BITS>;
+  TcGemmParams p;
+  if (!encode_2d(dev, &p.tmap_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, g.a, (uint64_t)g.inner, (uint64_t)g.rows,
+                 (uint64_t)g.inner * 2, TC_BK, BN, CU_TENSOR_MAP_SWIZZLE_128B))
+    return set_error(PK_E_CUDA, "cuTensorMapEncodeTiled failed for the activation operand");
+  const uint64_t words_per_k = (uint64_t)g.columns * BITS / 32;
+  if (!encode_2d(dev, &p.tmap_codes, CU_TENSOR_MAP_DATA_TYPE_UINT32, g.codes, words_per_k, (uint64_t)g.inner,
+                 words_per_k * 4, L::WORDS_PER_ROW, TC_BK, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return set_error(PK_E_CUDA, "cuTensorMapEncodeTiled failed for the packed codes");
+  p.palette = static_cast<const uint16_t*>(g.palette);
+  p.bias = g.bias;
+  p.residual = static_cast<const __half*>(g.residual);
+  p.out = static_cast<__half*>(g.c);
+  p.status = dev.status;
+  p.rows = (int)g.rows;
+  p.inner = (int)g.inner;
+  p.columns = (int)g.columns;
+  p.groups = g.groups;
+  p.group_cols = (int)g.group_cols;
+  p.act = g.act;
+  p.has_residual = g.has_residual;
+  p.res_scale = g.residual_scale;
+  p.m_tiles = (int)((g.rows + BN - 1) / BN);
+  p.n_tiles = (int)(g.columns / TC_BM);
+  const int tiles = p.m_tiles * p.n_tiles;
+  const int grid = std::min(tiles, dev.sm_count);
+  // Opt-in shared memory is a per-device function attribute; set it once per
+  // device (a racing duplicate set is harmless).
+  static int configured[32][8] = {};
+  const int slot = (BN == 256 ? 0 : BN == 128 ? 2 : 4) + (BITS == 6);
+  if (dev.ordinal < 0 || dev.ordinal >= 32 || !configured[dev.ordinal][slot]) {
+    cudaError_t e = cudaFuncSetAttribute(tc_palette_gemm_kernel<BN, BITS>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM_BYTES);
+    if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(tc_palette_gemm)");
+    if (dev.ordinal >= 0 && dev.ordinal < 32) configured[dev.ordinal][slot] = 1;
+  }
+  tc_palette_gemm_kernel<BN, BITS><<<grid, TC_THREADS, L::SMEM_BYTES, stream>>>(p);
+  return cuda_error(cudaGetLastError(), "tc_palette_gemm launch");
+}
+
+int launch_gemm_tc(const DeviceCtx& dev, const GemmArgs& g, cudaStream_t stream, int forced_bn) {
+  if (!gemm_tc_supported(g)) return set_error(PK_E_SHAPE, "shape not supported by the tensor-core GEMM");
+  // Token tile: 256 when there are enough rows to fill it, else 128.
+  int bn = forced_bn ? forced_bn : (g.rows > 128 ? 256 : 128);
+  if (bn == 256) return g.bits == 5 ? launch_tc<256, 5>(dev, g, stream) : launch_tc<256, 6>(dev, g, stream);
+  return g.bits == 5 ? launch_tc<128, 5>(dev, g, stream) : launch_tc<128, 6>(dev, g, stream);
+}
+
+}  // namespace pk

@@ -1,0 +1,77 @@
+// pk_internal.h -- host-side declarations shared by the libpk_b200 sources.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <string>
+
+#include "../../include/pk_b200.h"
+
+namespace pk {
+
+// Per-device context (the pk_device handle's payload).
+struct DeviceCtx {
+  int ordinal = 0;
+  int sm_count = 148;
+  int max_smem_optin = 0;
+  unsigned int* status = nullptr;  // device word; kernels OR PK_STATUS_* bits into it
+  void* encode_tiled = nullptr;    // cuTensorMapEncodeTiled
+};
+
+// Thread-local error reporting.
+int set_error(int code, const char* fmt, ...);
+int cuda_error(cudaError_t err, const char* what);
+
+struct GemmArgs {
+  int precision = PK_FP16;
+  int64_t rows = 0, inner = 0, columns = 0;
+  int bits = 5;
+  int groups = 1;
+  int64_t group_cols = 0;
+  int act = PK_ACT_NONE;
+  int has_residual = 0;
+  float residual_scale = 1.0f;
+  const float* bias = nullptr;
+  const void* residual = nullptr;
+  const void* a = nullptr;
+  const uint32_t* codes = nullptr;
+  const void* palette = nullptr;
+  void* c = nullptr;
+};
+
+// Validation shared by every GEMM entry point (returns pk_status).
+int validate_gemm(const GemmArgs& g);
+
+// Kernel launchers (return pk_status; errors recorded with set_error).
+int launch_gemm_tc(const DeviceCtx& dev, const GemmArgs& g, cudaStream_t stream, int forced_bn = 0);
+int launch_gemm_simt(const DeviceCtx& dev, const GemmArgs& g, cudaStream_t stream);
+bool gemm_tc_supported(const GemmArgs& g);
+int launch_palette_expand(const pk_palette_desc& d, cudaStream_t stream);
+int launch_layernorm(int precision, int64_t rows, int64_t channels, const void* x, const float* gamma,
+                     const float* beta, float eps, void* y, cudaStream_t stream);
+int launch_rel_attention(const DeviceCtx& dev, int precision, int batch, int frames, const void* qkv,
+                         const void* positions, const float* bias_u, const float* bias_v,
+                         const uint32_t* valid_lengths, void* context, cudaStream_t stream);
+int launch_conformer_conv(int precision, int batch, int frames, const void* pointwise, const void* dw,
+                          const float* scale, const float* shift, const uint32_t* valid_lengths, void* out,
+                          cudaStream_t stream);
+int launch_subsampling_conv0_dw2(int precision, int batch, const float* features, const void* conv0_w,
+                                 const float* conv0_b, const void* dw_w, const float* dw_b,
+                                 const uint32_t* feature_lengths, void* out, cudaStream_t stream);
+int launch_subsampling_depthwise(int precision, int batch, int ih, int iw, int channels, const void* input,
+                                 const void* w, const float* b, const uint32_t* feature_lengths, int steps,
+                                 void* out, cudaStream_t stream);
+int launch_subsampling_time_mask(int precision, int batch, int height, int width, int channels, void* values,
+                                 const uint32_t* feature_lengths, int steps, cudaStream_t stream);
+
+// Debug / test knob: 0 = automatic kernel choice, 1 = force the SIMT GEMM,
+// 2 = force the tensor-core GEMM (fails if the shape is unsupported).
+extern int g_gemm_route;
+
+}  // namespace pk
+
+// Payload of the opaque pk_device handle.
+struct pk_device {
+  pk::DeviceCtx ctx;
+  bool closed = false;
+};
