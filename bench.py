@@ -333,6 +333,81 @@ def run_ours(args):
     return 0
 
 
+def run_kernel(args):
+    """Profiling target: launch one operator `--steps` times at the C3 shapes
+    (no JSON line).  `--kernel gemm --shape M,K,N,BITS` picks the GEMM shape."""
+    import ctypes
+
+    import torch
+
+    import __graft_entry__
+
+    pk = __graft_entry__.load()
+    L = pk._lib
+    device = pk.kernels.Device(0)
+    rng = np.random.default_rng(0)
+    keep = []
+
+    def dev(a):
+        t = torch.from_numpy(np.ascontiguousarray(a).view(np.int32) if a.dtype == np.dtype("<u4") else a).cuda()
+        keep.append(t)
+        return ctypes.c_void_p(t.data_ptr())
+
+    if args.kernel == "gemm":
+        m, k, n, bits = (int(x) for x in args.shape.split(","))
+        codes, lut = pk.synthetic.palette_matrix(rng, k, n, bits, 1, "fp16")
+        a = torch.randn((m, k), dtype=torch.float16, device="cuda")
+        c = torch.empty((m, n), dtype=torch.float16, device="cuda")
+        desc = L.GemmDesc(L.FP16, m, k, n, bits, 1, n, L.ACT[args.act], 0, 1.0, None, None, a.data_ptr(),
+                          dev(codes["data"]).value, dev(lut["data"]).value, c.data_ptr())
+        launch = lambda: L.call("pk_palette_gemm", device.handle, ctypes.byref(desc), None)  # noqa: E731
+    elif args.kernel == "attention":
+        b = int(args.shape or BATCH)
+        qkv = torch.randn((b * FRAMES, 3072), dtype=torch.float16, device="cuda")
+        ctx = torch.empty((b * FRAMES, 1024), dtype=torch.float16, device="cuda")
+        pos = dev((0.5 * rng.standard_normal((8, 32, 375, 4))).astype(np.float16))
+        u = dev((0.02 * rng.standard_normal((8, 128))).astype(np.float32))
+        v = dev((0.02 * rng.standard_normal((8, 128))).astype(np.float32))
+        lens = dev(np.full(b, FRAMES, np.uint32))
+        launch = lambda: L.call("pk_rel_attention", device.handle, L.FP16, b, FRAMES,  # noqa: E731
+                                ctypes.c_void_p(qkv.data_ptr()), pos, u, v, lens, ctypes.c_void_p(ctx.data_ptr()),
+                                None)
+    elif args.kernel == "layernorm":
+        rows = int(args.shape or BATCH * FRAMES)
+        x = torch.randn((rows, 1024), dtype=torch.float16, device="cuda")
+        y = torch.empty_like(x)
+        g = dev(np.ones(1024, np.float32))
+        bb = dev(np.zeros(1024, np.float32))
+        launch = lambda: L.call("pk_layernorm", device.handle, L.FP16, rows, 1024,  # noqa: E731
+                                ctypes.c_void_p(x.data_ptr()), g, bb, 1e-5, ctypes.c_void_p(y.data_ptr()), None)
+    elif args.kernel == "conv":
+        b = int(args.shape or BATCH)
+        gin = torch.randn((b * FRAMES, 2048), dtype=torch.float16, device="cuda")
+        out = torch.empty((b * FRAMES, 1024), dtype=torch.float16, device="cuda")
+        dw = dev((0.1 * rng.standard_normal((9, 1024))).astype(np.float16))
+        sc = dev(np.ones(1024, np.float32))
+        sh = dev(np.zeros(1024, np.float32))
+        lens = dev(np.full(b, FRAMES, np.uint32))
+        launch = lambda: L.call("pk_conformer_conv", device.handle, L.FP16, b, FRAMES,  # noqa: E731
+                                ctypes.c_void_p(gin.data_ptr()), dw, sc, sh, lens, ctypes.c_void_p(out.data_ptr()),
+                                None)
+    else:
+        raise SystemExit(f"unknown kernel {args.kernel}")
+    for _ in range(args.steps):
+        launch()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        launch()
+    end.record()
+    end.synchronize()
+    print(f"{args.kernel} {args.shape}: {start.elapsed_time(end) / args.steps * 1e3:.1f} us/launch, "
+          f"status {device.status()}")
+    device.close()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -340,7 +415,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel", choices=["gemm", "attention", "layernorm", "conv"],
+                    help="profiling target: launch one operator only")
+    ap.add_argument("--shape", default="", help="gemm: M,K,N,BITS; attention/conv: batch; layernorm: rows")
+    ap.add_argument("--act", default="none", choices=["none", "silu", "relu"])
     args = ap.parse_args()
+    if args.kernel:
+        return run_kernel(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

@@ -197,6 +197,9 @@ int pk_encoder_destroy(pk_encoder* encoder);
  * (tensor cores where the shape tiles, else CUDA cores), 1 = CUDA-core
  * kernel only, 2 = tensor-core kernel only (unsupported shapes fail). */
 int pk_debug_set_gemm_route(int route);
+/* Test hook (no reference counterpart): 0 = automatic (tensor-core attention
+ * for the FP16 package), 1 = CUDA-core attention kernel. */
+int pk_debug_set_attention_route(int route);
 
 #ifdef __cplusplus
 }

@@ -21,6 +21,7 @@ namespace pk {
 
 static thread_local std::string t_last_error;
 int g_gemm_route = 0;
+int g_attention_route = 0;
 
 int set_error(int code, const char* fmt, ...) {
   char buf[1024];
@@ -190,6 +191,12 @@ int pk_palette_gemm(pk_device* device, const pk_gemm_desc* d, pk_stream stream) 
 int pk_debug_set_gemm_route(int route) {
   if (route < 0 || route > 2) return set_error(PK_E_INVALID, "route must be 0, 1 or 2");
   g_gemm_route = route;
+  return PK_OK;
+}
+
+int pk_debug_set_attention_route(int route) {
+  if (route < 0 || route > 1) return set_error(PK_E_INVALID, "route must be 0 or 1");
+  g_attention_route = route;
   return PK_OK;
 }
 

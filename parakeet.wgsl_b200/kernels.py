@@ -524,3 +524,8 @@ class SubsamplingTimeMaskKernel:
 def set_gemm_route(route: str) -> None:
     """Test hook: "auto", "simt" (CUDA cores) or "tensor" (tcgen05)."""
     _lib.call("pk_debug_set_gemm_route", {"auto": 0, "simt": 1, "tensor": 2}[route])
+
+
+def set_attention_route(route: str) -> None:
+    """Test hook: "auto" (tensor cores for FP16) or "simt"."""
+    _lib.call("pk_debug_set_attention_route", {"auto": 0, "simt": 1}[route])

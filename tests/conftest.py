@@ -40,3 +40,12 @@ def device(pk):
     dev = pk.kernels.Device(0)
     yield dev
     dev.close()
+
+
+@pytest.fixture(autouse=True)
+def _release_device_temporaries(request):
+    yield
+    if request.node.get_closest_marker("gpu") is not None:
+        import gpu_util
+
+        gpu_util.release()

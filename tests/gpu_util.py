@@ -7,13 +7,30 @@ import ctypes
 import numpy as np
 
 
+# Device copies made by cuda() stay referenced until release(): a raw pointer
+# handed to the C ABI does not keep a torch tensor alive, and the caching
+# allocator would otherwise hand the same block to the next temporary.
+_KEEP: list = []
+
+
 def cuda(arr):
     import torch
 
     arr = np.ascontiguousarray(arr)
     if arr.dtype == np.dtype("<u4"):
-        return torch.from_numpy(arr.view(np.int32)).cuda()
-    return torch.from_numpy(arr).cuda()
+        t = torch.from_numpy(arr.view(np.int32)).cuda()
+    else:
+        t = torch.from_numpy(arr).cuda()
+    _KEEP.append(t)
+    return t
+
+
+def release():
+    import torch
+
+    if _KEEP:
+        torch.cuda.synchronize()
+        _KEEP.clear()
 
 
 def host(t, dtype=None):

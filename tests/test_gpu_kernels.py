@@ -264,6 +264,34 @@ def test_rel_attention(pk, oracle, device, precision, lengths):
         assert np.all(got.reshape(batch, frames, 1024)[b, L:] == 0)
 
 
+def test_rel_attention_simt_route_matches_tensor_core(pk, oracle, device):
+    """FP16: the CUDA-core kernel (f32 math throughout, like the shader) and the
+    tensor-core kernel agree with the oracle and with each other."""
+    import torch
+
+    batch, frames = 2, 188
+    rng = np.random.default_rng(77)
+    qkv = rng.standard_normal((batch * frames, 3072)).astype(np.float16)
+    pos = (0.5 * rng.standard_normal((8, 32, 375, 4))).astype(np.float16)
+    u = (0.02 * rng.standard_normal((8, 128))).astype(np.float32)
+    v = (0.02 * rng.standard_normal((8, 128))).astype(np.float32)
+    lens = np.array([188, 61], np.uint32)
+    outs = []
+    for route in ("simt", "auto"):
+        ctx = torch.full((batch * frames, 1024), float("nan"), dtype=torch.float16, device="cuda")
+        pk.kernels.set_attention_route(route)
+        try:
+            pk._lib.call("pk_rel_attention", device.handle, pk._lib.FP16, batch, frames, vp(cuda(qkv)),
+                         vp(cuda(pos)), vp(cuda(u)), vp(cuda(v)), vp(cuda(lens)), vp(ctx), None)
+        finally:
+            pk.kernels.set_attention_route("auto")
+        outs.append(host(ctx))
+    ref = oracle.rel_attention(qkv, pos, u, v, lens, batch, frames)
+    assert rel(outs[0], ref) < 1e-3
+    assert rel(outs[1], ref) < 5e-3
+    assert rel(outs[0], outs[1]) < 5e-3
+
+
 def test_rel_attention_rejects_long_windows(pk, device):
     x = cuda(np.zeros(8, np.float32))
     with pytest.raises(pk.PkError, match="PK_E_SHAPE"):
