@@ -54,19 +54,20 @@ def env_rank():
 
 
 def gemm_shapes(batch: int):
-    """(rows, inner, columns, bits, launches per step) of every palette GEMM of one step."""
+    """(rows, inner, columns, bits, groups, activation, epilogue, launches per step) of every
+    palette GEMM of one step, with the epilogue each one runs in the encoder."""
     rows = batch * FRAMES
     return [
-        (batch * 376 * 32, 256, 256, 5, 1),   # subsampling pointwise 3
-        (batch * 188 * 16, 256, 256, 5, 1),   # subsampling pointwise 6
-        (rows, 4096, 1024, 5, 1),             # flatten projection
-        (rows, 1024, 4096, 5, 48),            # ff1/ff2 linear1
-        (rows, 4096, 1024, 5, 48),            # ff1/ff2 linear2
-        (rows, 1024, 3072, 5, 24),            # qkv
-        (rows, 1024, 1024, 6, 24),            # o_proj (6-bit)
-        (rows, 1024, 2048, 5, 24),            # pointwise conv 1
-        (rows, 1024, 1024, 5, 24),            # pointwise conv 2
-        (rows, 1024, 640, 5, 1),              # projector
+        (batch * 376 * 32, 256, 256, 5, 1, "relu", "bias", 1),   # subsampling pointwise 3
+        (batch * 188 * 16, 256, 256, 5, 1, "relu", "bias", 1),   # subsampling pointwise 6
+        (rows, 4096, 1024, 5, 1, "none", "bias", 1),             # flatten projection
+        (rows, 1024, 4096, 5, 1, "silu", "plain", 48),           # ff1/ff2 linear1
+        (rows, 4096, 1024, 5, 1, "none", "residual", 48),        # ff1/ff2 linear2 (+0.5 residual)
+        (rows, 1024, 3072, 5, 3, "none", "plain", 24),           # qkv (3 palette groups)
+        (rows, 1024, 1024, 6, 1, "none", "residual", 24),        # o_proj (6-bit, + residual)
+        (rows, 1024, 2048, 5, 1, "none", "plain", 24),           # pointwise conv 1
+        (rows, 1024, 1024, 5, 1, "none", "residual", 24),        # pointwise conv 2 (+ residual)
+        (rows, 1024, 640, 5, 1, "none", "bias", 1),              # projector
     ]
 
 
@@ -140,14 +141,18 @@ def time_gemms(pk, device, batch, stream, reps=5):
     rng = np.random.default_rng(0)
     total_flops = total_ms = 0.0
     detail = []
-    for rows, inner, columns, bits, launches in gemm_shapes(batch):
-        codes, lut = pk.synthetic.palette_matrix(rng, inner, columns, bits, 1, "fp16")
+    for rows, inner, columns, bits, groups, act, epi, launches in gemm_shapes(batch):
+        codes, lut = pk.synthetic.palette_matrix(rng, inner, columns, bits, groups, "fp16")
         a = torch.randn((rows, inner), dtype=torch.float16, device="cuda")
         c = torch.empty((rows, columns), dtype=torch.float16, device="cuda")
+        res = torch.randn((rows, columns), dtype=torch.float16, device="cuda") if epi == "residual" else None
+        bias = torch.randn(columns, dtype=torch.float32, device="cuda") if epi == "bias" else None
         tc = torch.from_numpy(codes["data"].view(np.int32)).cuda()
         tl = torch.from_numpy(lut["data"]).cuda()
-        desc = L.GemmDesc(L.FP16, rows, inner, columns, bits, 1, columns, 0, 0, 1.0, None, None,
-                          a.data_ptr(), tc.data_ptr(), tl.data_ptr(), c.data_ptr())
+        desc = L.GemmDesc(L.FP16, rows, inner, columns, bits, groups, columns // groups, L.ACT[act],
+                          int(res is not None), 0.5, None if bias is None else bias.data_ptr(),
+                          None if res is None else res.data_ptr(), a.data_ptr(), tc.data_ptr(), tl.data_ptr(),
+                          c.data_ptr())
         h = ctypes.c_void_p(stream.cuda_stream)
         for _ in range(2):
             L.call("pk_palette_gemm", device.handle, ctypes.byref(desc), h)
@@ -162,7 +167,8 @@ def time_gemms(pk, device, batch, stream, reps=5):
         flops = 2.0 * rows * inner * columns
         total_flops += flops * launches
         total_ms += ms * launches
-        detail.append({"m": rows, "k": inner, "n": columns, "bits": bits, "launches": launches,
+        detail.append({"m": rows, "k": inner, "n": columns, "bits": bits, "epilogue": f"{epi}+{act}",
+                       "launches": launches,
                        "us": round(ms * 1e3, 2), "tflops": round(flops / (ms * 1e-3) / 1e12, 1)})
     return total_flops, total_ms, detail
 

@@ -13,7 +13,10 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
+#include <set>
 #include <string>
+#include <utility>
 
 #include "pk_internal.h"
 
@@ -38,6 +41,20 @@ int cuda_error(cudaError_t err, const char* what) {
   if (err == cudaErrorMemoryAllocation)
     return set_error(PK_E_OOM, "%s: %s", what, cudaGetErrorString(err));
   return set_error(PK_E_CUDA, "%s: %s", what, cudaGetErrorString(err));
+}
+
+int set_max_dynamic_smem(const void* kernel, int bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_error(e, "cudaGetDevice");
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({kernel, dev})) return PK_OK;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(max dynamic shared memory)");
+  done.insert({kernel, dev});
+  return PK_OK;
 }
 
 int validate_gemm(const GemmArgs& g) {

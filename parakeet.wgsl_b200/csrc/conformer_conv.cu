@@ -6,9 +6,10 @@
 //   s[t, c]    = fma chain over k = 0..8 of glu[t + k - 4, c] * w[k, c];
 //   a          = s * scale[c] + shift[c]   (BN folded, model/convert.py:1705-1735);
 //   y[t, c]    = a * sigmoid(a), for every frame t < T.
-// Each thread owns one 16-byte channel vector of one window and walks a frame
-// range with a 9-frame register window, so every input row is read once per
-// frame range (HBM-bound: read 2048 + write 1024 values per frame).
+// One CTA = (window, 32 frames, 128 channels): the 40-frame GLU halo tile is
+// computed once into shared memory from 128-bit loads of the pointwise output,
+// then every output vector is a 9-tap register FMA chain.  Each input element
+// is read from HBM once (plus the 8-frame halo, from L2); HBM-bound.
 #include "pk_common.cuh"
 #include "pk_internal.h"
 
@@ -16,7 +17,15 @@ namespace pk {
 
 constexpr int CONV_C = 1024;
 constexpr int CONV_K = 9;
-constexpr int CONV_FRAME_CHUNK = 16;  // frames per thread (halo of 8 re-read from L2)
+constexpr int CONV_TF = 32;                  // frames per CTA
+constexpr int CONV_TC = 128;                 // channels per CTA
+constexpr int CONV_ROWS = CONV_TF + CONV_K - 1;
+constexpr int CONV_THREADS = 256;
+
+__device__ __forceinline__ float fast_sigmoid(float v) {
+  const float b = fminf(fmaxf(v, -20.0f), 20.0f);
+  return __fdividef(1.0f, 1.0f + __expf(-b));
+}
 
 template <typename T>
 __device__ __forceinline__ void load_vec(const T* p, float* v);
@@ -55,80 +64,92 @@ __device__ __forceinline__ void store_vec<float>(float* p, const float* v) {
 }
 
 template <typename T>
-__global__ void __launch_bounds__(128) conformer_conv_kernel(const T* __restrict__ g, const T* __restrict__ dw,
-                                                             const float* __restrict__ scale,
-                                                             const float* __restrict__ shift,
-                                                             const uint32_t* __restrict__ valid_lengths,
-                                                             T* __restrict__ out, int batch, int frames) {
-  constexpr int VEC = 16 / sizeof(T);
-  constexpr int CV = CONV_C / VEC;  // channel vectors per frame
-  const int cv = blockIdx.x * blockDim.x + threadIdx.x;
-  const int b = blockIdx.z;
-  if (cv >= CV || b >= batch) return;
-  const int t0 = blockIdx.y * CONV_FRAME_CHUNK;
-  const int t1 = min(frames, t0 + CONV_FRAME_CHUNK);
-  if (t0 >= t1) return;
+__global__ void __launch_bounds__(CONV_THREADS) conformer_conv_kernel(
+    const T* __restrict__ g, const T* __restrict__ dw, const float* __restrict__ scale,
+    const float* __restrict__ shift, const uint32_t* __restrict__ valid_lengths, T* __restrict__ out, int frames) {
+  constexpr int VEC = 16 / sizeof(T);          // channels per 16-byte vector
+  constexpr int NV = CONV_TC / VEC;            // vectors per tile row
+  constexpr int GROUPS = CONV_THREADS / NV;    // frame groups
+  constexpr int FPT = CONV_TF / GROUPS;        // frames per thread
+  __shared__ __align__(16) float glu[CONV_ROWS][CONV_TC];
+  const int c0 = blockIdx.x * CONV_TC, t0 = blockIdx.y * CONV_TF, b = blockIdx.z;
+  const int tid = threadIdx.x;
   const int valid = min((int)valid_lengths[b], frames);
-  const int c0 = cv * VEC;
-  float w[CONV_K][VEC];
+  // ---- GLU halo tile
+  for (int i = tid; i < CONV_ROWS * NV; i += CONV_THREADS) {
+    const int r = i / NV, v = i % NV;
+    const int t = t0 - CONV_K / 2 + r;
+    float val[VEC];
+    if (t >= 0 && t < valid) {
+      const T* row = g + ((size_t)b * frames + t) * (2 * CONV_C) + c0 + v * VEC;
+      float gate[VEC];
+      load_vec<T>(row, val);
+      load_vec<T>(row + CONV_C, gate);
 #pragma unroll
-  for (int k = 0; k < CONV_K; ++k) load_vec<T>(dw + k * CONV_C + c0, w[k]);
-  float sc[VEC], sh[VEC];
-#pragma unroll
-  for (int j = 0; j < VEC; ++j) {
-    sc[j] = __ldg(scale + c0 + j);
-    sh[j] = __ldg(shift + c0 + j);
-  }
-  float win[CONV_K][VEC];  // GLU values of frames t-4 .. t+4
-  auto glu_at = [&](int tt, float* dst) {
-    if (tt >= 0 && tt < frames && tt < valid) {
-      const T* row = g + ((size_t)b * frames + tt) * (2 * CONV_C);
-      float v[VEC], gt[VEC];
-      load_vec<T>(row + c0, v);
-      load_vec<T>(row + CONV_C + c0, gt);
-#pragma unroll
-      for (int j = 0; j < VEC; ++j) dst[j] = v[j] * sigmoid_ref(gt[j]);
+      for (int j = 0; j < VEC; ++j) val[j] *= fast_sigmoid(gate[j]);
     } else {
 #pragma unroll
-      for (int j = 0; j < VEC; ++j) dst[j] = 0.0f;
+      for (int j = 0; j < VEC; ++j) val[j] = 0.0f;
     }
-  };
 #pragma unroll
-  for (int k = 0; k < CONV_K - 1; ++k) glu_at(t0 - 4 + k, win[k + 1]);
-  for (int t = t0; t < t1; ++t) {
+    for (int j = 0; j < VEC; j += 4)
+      *reinterpret_cast<float4*>(&glu[r][v * VEC + j]) = make_float4(val[j], val[j + 1], val[j + 2], val[j + 3]);
+  }
+  // ---- this thread's channel vector: taps, scale, shift in registers
+  const int v = tid % NV, grp = tid / NV;
+  const int c = c0 + v * VEC;
+  float w[CONV_K][VEC];
 #pragma unroll
-    for (int k = 0; k < CONV_K - 1; ++k)
+  for (int k = 0; k < CONV_K; ++k) load_vec<T>(dw + k * CONV_C + c, w[k]);
+  float sc[VEC], sh[VEC];
 #pragma unroll
-      for (int j = 0; j < VEC; ++j) win[k][j] = win[k + 1][j];
-    glu_at(t + 4, win[CONV_K - 1]);
+  for (int j = 0; j < VEC; j += 4) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(scale + c + j));
+    const float4 s = __ldg(reinterpret_cast<const float4*>(shift + c + j));
+    sc[j] = a.x, sc[j + 1] = a.y, sc[j + 2] = a.z, sc[j + 3] = a.w;
+    sh[j] = s.x, sh[j + 1] = s.y, sh[j + 2] = s.z, sh[j + 3] = s.w;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int f = 0; f < FPT; ++f) {
+    const int tl = grp + f * GROUPS;  // frame within the tile
+    const int t = t0 + tl;
+    if (t >= frames) break;
     float y[VEC];
 #pragma unroll
-    for (int j = 0; j < VEC; ++j) {
-      float s = 0.0f;
+    for (int j = 0; j < VEC; ++j) y[j] = 0.0f;
 #pragma unroll
-      for (int k = 0; k < CONV_K; ++k) s = fmaf(win[k][j], w[k][j], s);
-      const float a = fmaf(s, sc[j], sh[j]);
-      y[j] = a * sigmoid_ref(a);
+    for (int k = 0; k < CONV_K; ++k) {
+      float x[VEC];
+#pragma unroll
+      for (int j = 0; j < VEC; j += 4) {
+        const float4 q = *reinterpret_cast<const float4*>(&glu[tl + k][v * VEC + j]);
+        x[j] = q.x, x[j + 1] = q.y, x[j + 2] = q.z, x[j + 3] = q.w;
+      }
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) y[j] = fmaf(x[j], w[k][j], y[j]);
     }
-    store_vec<T>(out + ((size_t)b * frames + t) * CONV_C + c0, y);
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      const float a = fmaf(y[j], sc[j], sh[j]);
+      y[j] = a * fast_sigmoid(a);
+    }
+    store_vec<T>(out + ((size_t)b * frames + t) * CONV_C + c, y);
   }
 }
 
 int launch_conformer_conv(int precision, int batch, int frames, const void* pointwise, const void* dw,
                           const float* scale, const float* shift, const uint32_t* valid_lengths, void* out,
                           cudaStream_t stream) {
-  const int vec = precision == PK_FP16 ? 8 : 4;
-  const int cvs = CONV_C / vec;
-  const dim3 block(128);
-  const dim3 grid((cvs + 127) / 128, (frames + CONV_FRAME_CHUNK - 1) / CONV_FRAME_CHUNK, batch);
+  const dim3 grid(CONV_C / CONV_TC, (frames + CONV_TF - 1) / CONV_TF, batch);
   if (precision == PK_FP16)
-    conformer_conv_kernel<__half><<<grid, block, 0, stream>>>(
+    conformer_conv_kernel<__half><<<grid, CONV_THREADS, 0, stream>>>(
         static_cast<const __half*>(pointwise), static_cast<const __half*>(dw), scale, shift, valid_lengths,
-        static_cast<__half*>(out), batch, frames);
+        static_cast<__half*>(out), frames);
   else
-    conformer_conv_kernel<float><<<grid, block, 0, stream>>>(
+    conformer_conv_kernel<float><<<grid, CONV_THREADS, 0, stream>>>(
         static_cast<const float*>(pointwise), static_cast<const float*>(dw), scale, shift, valid_lengths,
-        static_cast<float*>(out), batch, frames);
+        static_cast<float*>(out), frames);
   return cuda_error(cudaGetLastError(), "conformer_conv launch");
 }
 

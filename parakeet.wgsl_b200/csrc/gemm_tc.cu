@@ -11,15 +11,17 @@
 // Formulation (swapped): D^T = W^T . A^T, so the 128 MMA rows are output
 // features and the MMA N dimension is BN tokens.
 //   * MMA-A = decoded weights, [128 features x 64 k] per stage, MN-major with
-//     128-byte swizzle, written to shared memory by 4 decoder warps from the
+//     128-byte swizzle, written to shared memory by 8 decoder warps from the
 //     packed-code tile (TMA, no swizzle) through the LUT held in shared memory;
 //   * MMA-B = activations, [BN tokens x 64 k] per stage, K-major, loaded by TMA
 //     with 128-byte swizzle (rows past M are zero-filled by TMA);
 //   * D = fp32 accumulators in TMEM, double buffered (2 x BN columns) so the
 //     epilogue of one tile overlaps the main loop of the next.
 // Persistent CTAs (one per SM) walk the tile list; warp roles:
-//   warp 0 TMA producer, warp 1 MMA issuer (+TMEM owner), warps 2-5 decoders,
-//   warps 6-9 epilogue (bias / SiLU / ReLU / residual, f16 store).
+//   warp 0 TMA producer, warp 1 MMA issuer (+TMEM owner), warps 2-9 decoders,
+//   warps 10-13 epilogue.  The epilogue (bias / SiLU / ReLU / scaled residual,
+//   f16 store) is a compile-time specialization, so no dead activation or
+//   residual code is issued.
 // Accumulation is fp32 (the reference accumulates in f16, gemm.ts:1445-1453),
 // so results agree with the reference algorithm within the FP16 package
 // tolerance and with the oracle's wide-accumulation mode to f16 rounding.
@@ -33,12 +35,16 @@
 
 namespace pk {
 
-constexpr int TC_BM = 128;        // output features per tile (MMA M)
-constexpr int TC_BK = 64;         // k per stage: one 128-byte swizzle row of f16
+constexpr int TC_BM = 128;         // output features per tile (MMA M)
+constexpr int TC_BK = 64;          // k per stage: one 128-byte swizzle row of f16
 constexpr int TC_STAGES = 4;
-constexpr int TC_THREADS = 320;   // 10 warps
-constexpr int TC_DECODE_THREADS = 128;
+constexpr int TC_DECODE_WARPS = 8;
+constexpr int TC_FIRST_EPI_WARP = 2 + TC_DECODE_WARPS;  // 10: warps 10..13 cover TMEM lane quarters 2,3,0,1
+constexpr int TC_THREADS = (TC_FIRST_EPI_WARP + 4) * 32;  // 448
+constexpr int TC_DECODE_THREADS = TC_DECODE_WARPS * 32;
 constexpr int TC_EPI_THREADS = 128;
+
+enum { EPI_PLAIN = 0, EPI_BIAS = 1, EPI_RESIDUAL = 2 };
 
 struct TcGemmParams {
   CUtensorMap tmap_a;       // activations [M, K] f16, box {64, BN}, 128B swizzle
@@ -50,7 +56,6 @@ struct TcGemmParams {
   unsigned int* status;
   int rows, inner, columns;
   int groups, group_cols;
-  int act, has_residual;
   float res_scale;
   int m_tiles, n_tiles;
 };
@@ -66,9 +71,7 @@ struct TcLayout {
   static constexpr int OFF_A = 0;
   static constexpr int OFF_W = OFF_A + TC_STAGES * A_BYTES;
   static constexpr int OFF_C = OFF_W + TC_STAGES * W_BYTES;
-  static constexpr int OFF_LUT = OFF_C + TC_STAGES * CODE_BYTES;
-  static constexpr int LUT_BYTES = 3 * 64 * 2;
-  static constexpr int OFF_BAR = (OFF_LUT + LUT_BYTES + 7) / 8 * 8;
+  static constexpr int OFF_BAR = OFF_C + TC_STAGES * CODE_BYTES;
   static constexpr int NUM_BARS = 3 * TC_STAGES + 2 + 2 + 1;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
@@ -77,27 +80,34 @@ struct TcLayout {
   static_assert(CODE_BYTES % 128 == 0, "code stage must keep 128B alignment");
 };
 
-// Extract code i of a packed group held in registers (LSB-first bit stream).
+// Byte offset of code I's LUT entry (code * 2) ORed with the palette group's
+// byte offset `goff` (a multiple of 2^(BITS+1), so the OR is an add): one
+// shift and one 3-input logic op per code.
 template <int BITS, int I>
-__device__ __forceinline__ uint32_t code_of(const uint32_t (&w)[BITS == 5 ? 5 : 3]) {
+__device__ __forceinline__ uint32_t lut_offset(const uint32_t (&w)[BITS == 5 ? 5 : 3], uint32_t goff) {
   constexpr int bit = I * BITS, word = bit >> 5, sh = bit & 31;
-  if constexpr (sh + BITS <= 32) {
-    return (w[word] >> sh) & ((1u << BITS) - 1u);
+  constexpr uint32_t mask2 = ((1u << BITS) - 1u) << 1;
+  uint32_t x;
+  if constexpr (sh + BITS > 32) {
+    x = __funnelshift_r(w[word], w[word + 1], sh - 1);
+  } else if constexpr (sh == 0) {
+    x = w[word] << 1;
   } else {
-    return __funnelshift_r(w[word], w[word + 1], sh) & ((1u << BITS) - 1u);
+    x = w[word] >> (sh - 1);
   }
+  return (x & mask2) | goff;
 }
 
 template <int BITS, int I, int N>
 struct DecodePairs {
   // Decode codes [I, N) of a group into packed f16 pairs.
-  static __device__ __forceinline__ void run(const uint32_t (&w)[BITS == 5 ? 5 : 3], const uint16_t* lut,
-                                             uint32_t* out) {
+  static __device__ __forceinline__ void run(const uint32_t (&w)[BITS == 5 ? 5 : 3], const uint8_t* lut,
+                                             uint32_t goff, uint32_t* out) {
     if constexpr (I < N) {
-      const uint32_t lo = lut[code_of<BITS, I>(w)];
-      const uint32_t hi = lut[code_of<BITS, I + 1>(w)];
-      out[I / 2] = lo | (hi << 16);
-      DecodePairs<BITS, I + 2, N>::run(w, lut, out);
+      const uint32_t lo = *reinterpret_cast<const uint16_t*>(lut + lut_offset<BITS, I>(w, goff));
+      const uint32_t hi = *reinterpret_cast<const uint16_t*>(lut + lut_offset<BITS, I + 1>(w, goff));
+      out[I / 2] = __byte_perm(lo, hi, 0x5410);
+      DecodePairs<BITS, I + 2, N>::run(w, lut, goff, out);
     }
   }
 };
@@ -113,14 +123,14 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
 // row (k % 8) at 128 B; 16-byte chunk c (features 8c..8c+7 of the 64-wide
 // block) at physical chunk c ^ (k % 8).
 template <int BITS>
-__device__ __forceinline__ void decode_group(const uint32_t* src, const uint16_t* lut, uint32_t w_stage, int k,
-                                             int f0) {
+__device__ __forceinline__ void decode_group(const uint32_t* src, const uint8_t* lut, uint32_t goff,
+                                             uint32_t w_stage, int k, int f0) {
   constexpr int WPG = BITS == 5 ? 5 : 3, CPG = BITS == 5 ? 32 : 16;
   uint32_t words[WPG];
 #pragma unroll
   for (int j = 0; j < WPG; ++j) words[j] = src[j];
   uint32_t packed[CPG / 2];
-  DecodePairs<BITS, 0, CPG>::run(words, lut, packed);
+  DecodePairs<BITS, 0, CPG>::run(words, lut, goff, packed);
   const int r = k & 7;
   const uint32_t row = w_stage + (uint32_t)((f0 >> 6) * 8192 + (k >> 3) * 1024 + r * 128);
   const int c0 = (f0 & 63) >> 3;
@@ -131,15 +141,54 @@ __device__ __forceinline__ void decode_group(const uint32_t* src, const uint16_t
   }
 }
 
-template <int BN, int BITS>
+template <int ACT>
+__device__ __forceinline__ float activate(float v) {
+  if constexpr (ACT == PK_ACT_SILU) {
+    // v / (1 + exp(-clamp(v, -20, 20))) (gemm.ts:2018-2032), fast intrinsics:
+    // the result is rounded to f16, far coarser than their error.
+    const float b = fminf(fmaxf(v, -20.0f), 20.0f);
+    return __fdividef(v, 1.0f + __expf(-b));
+  } else if constexpr (ACT == PK_ACT_RELU) {
+    return fmaxf(v, 0.0f);
+  } else {
+    return v;
+  }
+}
+
+// Epilogue of `count` consecutive tokens of one output feature (one TMEM lane).
+// Residual values are all loaded before the first store so their latencies
+// overlap (the output never aliases the residual: the encoder ping-pongs
+// between two slots).
+template <int EPI, int ACT, int COUNT>
+__device__ __forceinline__ void epilogue_run(const uint32_t (&r)[32], float bias_v, const __half* __restrict__ res,
+                                             __half* __restrict__ out, int ld, float res_scale, int count) {
+  __half rv[EPI == EPI_RESIDUAL ? 32 : 1];
+  if constexpr (EPI == EPI_RESIDUAL) {
+#pragma unroll
+    for (int j = 0; j < COUNT; ++j)
+      if (COUNT == 32 || j < count) rv[j] = __ldg(res + (size_t)j * ld);
+  }
+#pragma unroll
+  for (int j = 0; j < COUNT; ++j) {
+    if (COUNT == 32 || j < count) {
+      float v = __uint_as_float(r[j]);
+      if constexpr (EPI == EPI_BIAS) v += bias_v;
+      v = activate<ACT>(v);
+      if constexpr (EPI == EPI_RESIDUAL) v = __half2float(rv[j]) + res_scale * v;
+      out[(size_t)j * ld] = __float2half_rn(v);
+    }
+  }
+}
+
+template <int BN, int BITS, int EPI, int ACT>
 __global__ void __launch_bounds__(TC_THREADS, 1) tc_palette_gemm_kernel(const __grid_constant__ TcGemmParams p) {
   using L = TcLayout<BN, BITS>;
+  __shared__ __align__(16) uint16_t s_lut[3 * 64];
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem + L::OFF_A;
   uint8_t* sW = smem + L::OFF_W;
   uint32_t* sCodes = reinterpret_cast<uint32_t*>(smem + L::OFF_C);
-  uint16_t* sLut = reinterpret_cast<uint16_t*>(smem + L::OFF_LUT);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
   uint64_t* full_tma = bars;
   uint64_t* full_dec = bars + TC_STAGES;
@@ -152,7 +201,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_palette_gemm_kernel(const __
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int lut_entries = p.groups << BITS;
-  for (int i = threadIdx.x; i < lut_entries; i += blockDim.x) sLut[i] = p.palette[i];
+  for (int i = threadIdx.x; i < lut_entries; i += blockDim.x) s_lut[i] = p.palette[i];
   if (threadIdx.x == 0) {
     for (int s = 0; s < TC_STAGES; ++s) {
       mbar_init(&full_tma[s], 1);
@@ -255,23 +304,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_palette_gemm_kernel(const __
       tc_commit(drain);
       mbar_wait_drain(drain, 0, p.status);
     }
-  } else if (warp < 6) {
+  } else if (warp < TC_FIRST_EPI_WARP) {
     // ------------------------------------------------------------ decoders
-    const int dw = warp - 2;  // 0..3, 16 k rows each per stage
+    // Warp dw owns k rows dw*8 .. dw*8+7 of each stage; lane = (k % 8) + 8 * g,
+    // g picking the packed group(s) along the 128 features (conflict-free
+    // word reads and 16-byte swizzled stores).
+    const int dw = warp - 2;
+    const int k = dw * 8 + (lane & 7);
+    constexpr int GROUPS_PER_LANE = BITS == 5 ? 1 : 2;
+    const uint8_t* lut = reinterpret_cast<const uint8_t*>(s_lut);
     uint32_t it = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      const int n_tile = tile % p.n_tiles;
-      const int f_base = n_tile * TC_BM;
-      // Palette group of each group this lane decodes (constant over k).
-      constexpr int GROUPS_PER_LANE = BITS == 5 ? 1 : 2;
-      const uint16_t* lut_g[GROUPS_PER_LANE];
+      const int f_base = (tile % p.n_tiles) * TC_BM;
+      uint32_t goff[GROUPS_PER_LANE];
       int f0[GROUPS_PER_LANE];
 #pragma unroll
       for (int j = 0; j < GROUPS_PER_LANE; ++j) {
-        const int ng = (lane >> 3) + 4 * j;
-        f0[j] = ng * L::CPG;
+        f0[j] = ((lane >> 3) + 4 * j) * L::CPG;
         const int pg = min((f_base + f0[j]) / p.group_cols, p.groups - 1);
-        lut_g[j] = sLut + (pg << BITS);
+        goff[j] = (uint32_t)pg << (BITS + 1);
       }
       bool ok = true;
       for (int kb = 0; kb < kb_count; ++kb, ++it) {
@@ -281,17 +332,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_palette_gemm_kernel(const __
           ok = false;
           break;
         }
-        const uint32_t* codes = sCodes + s * (L::CODE_BYTES / 4);
+        const uint32_t* codes = sCodes + s * (L::CODE_BYTES / 4) + k * L::WORDS_PER_ROW;
         const uint32_t w_stage = smem_addr(sW + s * L::W_BYTES);
 #pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          const int k = dw * 16 + i * 8 + (lane & 7);
-#pragma unroll
-          for (int j = 0; j < GROUPS_PER_LANE; ++j) {
-            const int ng = (lane >> 3) + 4 * j;
-            decode_group<BITS>(codes + k * L::WORDS_PER_ROW + ng * L::WPG, lut_g[j], w_stage, k, f0[j]);
-          }
-        }
+        for (int j = 0; j < GROUPS_PER_LANE; ++j)
+          decode_group<BITS>(codes + (f0[j] / L::CPG) * L::WPG, lut, goff[j], w_stage, k, f0[j]);
         fence_proxy_async_smem();
         mbar_arrive(&full_dec[s]);
       }
@@ -309,25 +354,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_palette_gemm_kernel(const __
       const int n_tile = tile % p.n_tiles, m_tile = tile / p.n_tiles;
       const int n = n_tile * TC_BM + q * 32 + lane;
       const int m0 = m_tile * BN;
-      const float bias_v = p.bias ? p.bias[n] : 0.0f;
+      const float bias_v = EPI == EPI_BIAS ? __ldg(p.bias + n) : 0.0f;
       const uint32_t t_base = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      const int ld = p.columns;
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
+        const int left = p.rows - (m0 + c);
+        if (left <= 0) break;
         uint32_t r[32];
         tc_ld_32x32b_x32(t_base + (uint32_t)c, r);
         tc_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int t = m0 + c + j;
-          if (t < p.rows) {
-            float v = __uint_as_float(r[j]) + bias_v;
-            if (p.act == PK_ACT_SILU) v = silu_ref(v);
-            else if (p.act == PK_ACT_RELU) v = fmaxf(v, 0.0f);
-            const size_t idx = (size_t)t * p.columns + n;
-            if (p.has_residual) v = __half2float(p.residual[idx]) + p.res_scale * v;
-            p.out[idx] = __float2half_rn(v);
-          }
-        }
+        const size_t base = (size_t)(m0 + c) * ld + n;
+        const __half* res = EPI == EPI_RESIDUAL ? p.residual + base : nullptr;
+        if (left >= 32)
+          epilogue_run<EPI, ACT, 32>(r, bias_v, res, p.out + base, ld, p.res_scale, 32);
+        else
+          epilogue_run<EPI, ACT, 31>(r, bias_v, res, p.out + base, ld, p.res_scale, left);
       }
       tc_fence_before();
       mbar_arrive(&tm_empty[acc]);
@@ -359,8 +401,25 @@ static bool encode_2d(const DeviceCtx& dev, CUtensorMap* map, CUtensorMapDataTyp
 
 bool gemm_tc_supported(const GemmArgs& g) {
   return g.precision == PK_FP16 && g.columns % TC_BM == 0 && g.inner % TC_BK == 0 && g.rows > 0 &&
-         g.rows <= (int64_t)1 << 30 && (g.bits == 5 || g.bits == 6) &&
+         g.rows <= (int64_t)1 << 30 && (g.bits == 5 || g.bits == 6) && (g.groups << g.bits) <= 192 &&
          (reinterpret_cast<uintptr_t>(g.a) & 15) == 0 && (reinterpret_cast<uintptr_t>(g.codes) & 15) == 0;
+}
+
+template <int BN, int BITS, int EPI, int ACT>
+static int launch_tc_spec(const DeviceCtx& dev, const TcGemmParams& p, cudaStream_t stream) {
+  using L = TcLayout<BN, BITS>;
+  auto kernel = tc_palette_gemm_kernel<BN, BITS, EPI, ACT>;
+  // Opt-in shared memory is a per-device function attribute; set it once per
+  // device (a racing duplicate set is harmless).
+  static bool configured[32] = {};
+  if (dev.ordinal < 0 || dev.ordinal >= 32 || !configured[dev.ordinal]) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM_BYTES);
+    if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(tc_palette_gemm)");
+    if (dev.ordinal >= 0 && dev.ordinal < 32) configured[dev.ordinal] = true;
+  }
+  const int tiles = p.m_tiles * p.n_tiles;
+  kernel<<<std::min(tiles, dev.sm_count), TC_THREADS, L::SMEM_BYTES, stream>>>(p);
+  return cuda_error(cudaGetLastError(), "tc_palette_gemm launch");
 }
 
 template <int BN, int BITS>
@@ -384,31 +443,29 @@ static int launch_tc(const DeviceCtx& dev, const GemmArgs& g, cudaStream_t strea
   p.columns = (int)g.columns;
   p.groups = g.groups;
   p.group_cols = (int)g.group_cols;
-  p.act = g.act;
-  p.has_residual = g.has_residual;
   p.res_scale = g.residual_scale;
   p.m_tiles = (int)((g.rows + BN - 1) / BN);
   p.n_tiles = (int)(g.columns / TC_BM);
-  const int tiles = p.m_tiles * p.n_tiles;
-  const int grid = std::min(tiles, dev.sm_count);
-  // Opt-in shared memory is a per-device function attribute; set it once per
-  // device (a racing duplicate set is harmless).
-  static int configured[32][8] = {};
-  const int slot = (BN == 256 ? 0 : BN == 128 ? 2 : 4) + (BITS == 6);
-  if (dev.ordinal < 0 || dev.ordinal >= 32 || !configured[dev.ordinal][slot]) {
-    cudaError_t e = cudaFuncSetAttribute(tc_palette_gemm_kernel<BN, BITS>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM_BYTES);
-    if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(tc_palette_gemm)");
-    if (dev.ordinal >= 0 && dev.ordinal < 32) configured[dev.ordinal][slot] = 1;
+  const int epi = g.has_residual ? EPI_RESIDUAL : (g.bias ? EPI_BIAS : EPI_PLAIN);
+  // The epilogues the encoder uses (gemm.ts:204-356): SiLU plain, plain,
+  // residual, bias, bias + ReLU; the rest of the 3 x 3 grid for general callers.
+  switch (epi * 3 + g.act) {
+    case EPI_PLAIN * 3 + PK_ACT_NONE: return launch_tc_spec<BN, BITS, EPI_PLAIN, PK_ACT_NONE>(dev, p, stream);
+    case EPI_PLAIN * 3 + PK_ACT_SILU: return launch_tc_spec<BN, BITS, EPI_PLAIN, PK_ACT_SILU>(dev, p, stream);
+    case EPI_PLAIN * 3 + PK_ACT_RELU: return launch_tc_spec<BN, BITS, EPI_PLAIN, PK_ACT_RELU>(dev, p, stream);
+    case EPI_BIAS * 3 + PK_ACT_NONE: return launch_tc_spec<BN, BITS, EPI_BIAS, PK_ACT_NONE>(dev, p, stream);
+    case EPI_BIAS * 3 + PK_ACT_SILU: return launch_tc_spec<BN, BITS, EPI_BIAS, PK_ACT_SILU>(dev, p, stream);
+    case EPI_BIAS * 3 + PK_ACT_RELU: return launch_tc_spec<BN, BITS, EPI_BIAS, PK_ACT_RELU>(dev, p, stream);
+    case EPI_RESIDUAL * 3 + PK_ACT_NONE: return launch_tc_spec<BN, BITS, EPI_RESIDUAL, PK_ACT_NONE>(dev, p, stream);
+    case EPI_RESIDUAL * 3 + PK_ACT_SILU: return launch_tc_spec<BN, BITS, EPI_RESIDUAL, PK_ACT_SILU>(dev, p, stream);
+    default: return launch_tc_spec<BN, BITS, EPI_RESIDUAL, PK_ACT_RELU>(dev, p, stream);
   }
-  tc_palette_gemm_kernel<BN, BITS><<<grid, TC_THREADS, L::SMEM_BYTES, stream>>>(p);
-  return cuda_error(cudaGetLastError(), "tc_palette_gemm launch");
 }
 
 int launch_gemm_tc(const DeviceCtx& dev, const GemmArgs& g, cudaStream_t stream, int forced_bn) {
   if (!gemm_tc_supported(g)) return set_error(PK_E_SHAPE, "shape not supported by the tensor-core GEMM");
   // Token tile: 256 when there are enough rows to fill it, else 128.
-  int bn = forced_bn ? forced_bn : (g.rows > 128 ? 256 : 128);
+  const int bn = forced_bn ? forced_bn : (g.rows > 128 ? 256 : 128);
   if (bn == 256) return g.bits == 5 ? launch_tc<256, 5>(dev, g, stream) : launch_tc<256, 6>(dev, g, stream);
   return g.bits == 5 ? launch_tc<128, 5>(dev, g, stream) : launch_tc<128, 6>(dev, g, stream);
 }

@@ -11,69 +11,103 @@
 
 namespace pk {
 
-// Fast path: channels == 1024.  f16 rows: 4 x 16-byte loads per lane;
-// f32 rows: 8 x 16-byte loads per lane.
+// Fast path: channels == 1024.  Each warp owns LN_ROWS consecutive rows: it
+// loads gamma/beta for its lane's channels once (128-bit loads), issues every
+// row's 128-bit loads before reducing (f16: 4 per lane per row, f32: 8), then
+// normalizes and stores.  One HBM read and one write of each row.
+// Rows per warp: 4 for f16 rows, 2 for f32 rows (register budget).
+template <typename T>
+constexpr int ln_rows() { return sizeof(T) == 2 ? 4 : 2; }
+
+template <typename T>
+__device__ __forceinline__ void unpack16(const uint4& raw, float* v) {
+  if constexpr (sizeof(T) == 2) {
+    const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __half22float2(h[j]);
+      v[2 * j] = f.x;
+      v[2 * j + 1] = f.y;
+    }
+  } else {
+    const float* f = reinterpret_cast<const float*>(&raw);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = f[j];
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(256) layernorm1024_kernel(const T* __restrict__ x, const float* __restrict__ gamma,
                                                             const float* __restrict__ beta, float eps,
                                                             T* __restrict__ y, int64_t rows) {
   constexpr int VEC = 16 / sizeof(T);        // elements per 16-byte load
-  constexpr int LOADS = 1024 / (32 * VEC);   // loads per lane
-  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  constexpr int LOADS = 1024 / (32 * VEC);   // loads per lane per row
   const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
-  const uint4* src = reinterpret_cast<const uint4*>(x + row * 1024);
-  float v[LOADS][VEC];
-  float sum = 0.0f, sq = 0.0f;
+  constexpr int LN_ROWS = ln_rows<T>();
+  const int64_t row0 = ((int64_t)blockIdx.x * 8 + (threadIdx.x >> 5)) * LN_ROWS;
+  if (row0 >= rows) return;
+  uint4 raw[LN_ROWS][LOADS];
 #pragma unroll
-  for (int i = 0; i < LOADS; ++i) {
-    const uint4 raw = __ldg(src + i * 32 + lane);
-    if constexpr (sizeof(T) == 2) {
-      const __half2* h = reinterpret_cast<const __half2*>(&raw);
+  for (int r = 0; r < LN_ROWS; ++r) {
+    if (row0 + r < rows) {
+      const uint4* src = reinterpret_cast<const uint4*>(x + (row0 + r) * 1024);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = __half22float2(h[j]);
-        v[i][2 * j] = f.x;
-        v[i][2 * j + 1] = f.y;
-      }
-    } else {
-      const float* f = reinterpret_cast<const float*>(&raw);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) v[i][j] = f[j];
-    }
-#pragma unroll
-    for (int j = 0; j < VEC; ++j) {
-      sum += v[i][j];
-      sq = fmaf(v[i][j], v[i][j], sq);
+      for (int i = 0; i < LOADS; ++i) raw[r][i] = __ldg(src + i * 32 + lane);
     }
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    sq += __shfl_xor_sync(0xffffffffu, sq, o);
-  }
-  const float inv = 1.0f / 1024.0f;
-  const float mean = sum * inv;
-  const float var = fmaxf(sq * inv - mean * mean, 0.0f);
-  const float rstd = 1.0f / sqrtf(var + eps);
-  uint4* dst = reinterpret_cast<uint4*>(y + row * 1024);
+  float g[LOADS][VEC], b[LOADS][VEC];
 #pragma unroll
   for (int i = 0; i < LOADS; ++i) {
     const int c0 = (i * 32 + lane) * VEC;
-    float o[VEC];
 #pragma unroll
-    for (int j = 0; j < VEC; ++j) o[j] = fmaf((v[i][j] - mean) * rstd, __ldg(gamma + c0 + j), __ldg(beta + c0 + j));
-    uint4 raw;
-    if constexpr (sizeof(T) == 2) {
-      __half2* h = reinterpret_cast<__half2*>(&raw);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) h[j] = __floats2half2_rn(o[2 * j], o[2 * j + 1]);
-    } else {
-      float* f = reinterpret_cast<float*>(&raw);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) f[j] = o[j];
+    for (int j = 0; j < VEC; j += 4) {
+      const float4 gg = __ldg(reinterpret_cast<const float4*>(gamma + c0 + j));
+      const float4 bb = __ldg(reinterpret_cast<const float4*>(beta + c0 + j));
+      g[i][j] = gg.x, g[i][j + 1] = gg.y, g[i][j + 2] = gg.z, g[i][j + 3] = gg.w;
+      b[i][j] = bb.x, b[i][j + 1] = bb.y, b[i][j + 2] = bb.z, b[i][j + 3] = bb.w;
     }
-    dst[i * 32 + lane] = raw;
+  }
+#pragma unroll
+  for (int r = 0; r < LN_ROWS; ++r) {
+    if (row0 + r >= rows) break;
+    float v[LOADS][VEC];
+    float sum = 0.0f, sq = 0.0f;
+#pragma unroll
+    for (int i = 0; i < LOADS; ++i) {
+      unpack16<T>(raw[r][i], v[i]);
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        sum += v[i][j];
+        sq = fmaf(v[i][j], v[i][j], sq);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    }
+    const float inv = 1.0f / 1024.0f;
+    const float mean = sum * inv;
+    const float var = fmaxf(sq * inv - mean * mean, 0.0f);
+    const float rstd = 1.0f / sqrtf(var + eps);
+    uint4* dst = reinterpret_cast<uint4*>(y + (row0 + r) * 1024);
+#pragma unroll
+    for (int i = 0; i < LOADS; ++i) {
+      float o[VEC];
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) o[j] = fmaf((v[i][j] - mean) * rstd, g[i][j], b[i][j]);
+      uint4 out;
+      if constexpr (sizeof(T) == 2) {
+        __half2* h = reinterpret_cast<__half2*>(&out);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) h[j] = __floats2half2_rn(o[2 * j], o[2 * j + 1]);
+      } else {
+        float* f = reinterpret_cast<float*>(&out);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) f[j] = o[j];
+      }
+      dst[i * 32 + lane] = out;
+    }
   }
 }
 
@@ -120,8 +154,10 @@ __global__ void __launch_bounds__(256) layernorm_generic_kernel(const T* __restr
 int launch_layernorm(int precision, int64_t rows, int64_t channels, const void* x, const float* gamma,
                      const float* beta, float eps, void* y, cudaStream_t stream) {
   const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0;
-  if (channels == 1024 && aligned) {
-    const unsigned blocks = (unsigned)((rows + 7) / 8);
+  const bool params_aligned = ((reinterpret_cast<uintptr_t>(gamma) | reinterpret_cast<uintptr_t>(beta)) & 15) == 0;
+  if (channels == 1024 && aligned && params_aligned) {
+    const int per_block = 8 * (precision == PK_FP16 ? ln_rows<__half>() : ln_rows<float>());
+    const unsigned blocks = (unsigned)((rows + per_block - 1) / per_block);
     if (precision == PK_FP16)
       layernorm1024_kernel<__half><<<blocks, 256, 0, stream>>>(static_cast<const __half*>(x), gamma, beta, eps,
                                                               static_cast<__half*>(y), rows);

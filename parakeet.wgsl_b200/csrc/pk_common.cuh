@@ -61,6 +61,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the
+// phase completes or `hint_ns` elapses, instead of spinning on issue slots.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for the phase with the given parity to complete.  Returns false (and
 // raises *abort and the status bit) when the wait exceeds PK_WAIT_NS or when
 // another role of this CTA has already aborted.
@@ -68,16 +82,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
                                           unsigned int* status, unsigned int bit) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = global_timer_ns();
-  uint32_t spins = 0;
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
     if (*abort) return false;
-    if ((++spins & 255u) == 0u) {
-      if (global_timer_ns() - start > PK_WAIT_NS) {
-        *abort = 1;
-        if (status) atomicOr(status, bit);
-        return false;
-      }
+    if (global_timer_ns() - start > PK_WAIT_NS) {
+      *abort = 1;
+      if (status) atomicOr(status, bit);
+      return false;
     }
   }
 }

@@ -39,6 +39,10 @@ struct GemmArgs {
   void* c = nullptr;
 };
 
+// Raises a kernel's dynamic shared-memory limit on the current device, once
+// per (kernel, device) (returns pk_status).
+int set_max_dynamic_smem(const void* kernel, int bytes);
+
 // Validation shared by every GEMM entry point (returns pk_status).
 int validate_gemm(const GemmArgs& g);
 

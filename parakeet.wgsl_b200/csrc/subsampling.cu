@@ -14,127 +14,197 @@
 //     src/webgpu/encoder.ts:2370-2377).
 // The pointwise 1x1 convolutions and the flatten projection run through the
 // palette GEMM.  Arithmetic order (fma chains from the bias, ky outer, kx
-// inner, skipped taps outside the valid area) follows the shaders.
+// inner, skipped taps outside the valid area) follows the shaders.  Each
+// thread owns 8 channels so taps live in registers and every shared-memory
+// read feeds 8 FMAs.
 #include "pk_common.cuh"
 #include "pk_internal.h"
 
 namespace pk {
 
 constexpr int SUB_IH = 1501, SUB_IW = 128, SUB_CH = 751, SUB_CW = 64, SUB_OH = 376, SUB_OW = 32, SUB_C = 256;
+constexpr int C0_CG = 32;        // channels per CTA
+constexpr int C0_ROWS = 5;       // conv0 rows per CTA (two depthwise output rows)
+constexpr int C0_IN_ROWS = 11;   // input time samples per CTA
+constexpr int C0_PITCH = C0_CG + 4;  // padded channel pitch of the conv0 tile (conflict-free 16-byte access)
+// The input tile is padded to a multiple of 4 floats so the conv0 tile that
+// follows it starts on a 16-byte boundary (it is accessed with float4).
+constexpr int C0_IN_FLOATS = (C0_IN_ROWS * (SUB_IW + 1) + 3) / 4 * 4;
+constexpr int C0_SMEM = (C0_IN_FLOATS + C0_ROWS * SUB_CW * C0_PITCH) * 4;
+static_assert(C0_IN_FLOATS % 4 == 0 && C0_PITCH % 4 == 0, "conv0 tile must stay 16-byte aligned");
 
 __device__ __forceinline__ int sub_len(int raw, int steps) {
   for (int s = 0; s < steps; ++s) raw = (raw + 1) >> 1;
   return raw;
 }
 
+// 8 consecutive profile scalars <-> floats.
 template <typename T>
-__device__ __forceinline__ float ldf(const T* p) {
-  return (float)*p;
+__device__ __forceinline__ void load8(const T* p, float* v);
+template <>
+__device__ __forceinline__ void load8<__half>(const __half* p, float* v) {
+  const uint4 raw = __ldg(reinterpret_cast<const uint4*>(p));
+  const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 f = __half22float2(h[j]);
+    v[2 * j] = f.x;
+    v[2 * j + 1] = f.y;
+  }
+}
+template <>
+__device__ __forceinline__ void load8<float>(const float* p, float* v) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(p + 4));
+  v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+}
+template <typename T>
+__device__ __forceinline__ void store8(T* p, const float* v);
+template <>
+__device__ __forceinline__ void store8<__half>(__half* p, const float* v) {
+  uint4 raw;
+  __half2* h = reinterpret_cast<__half2*>(&raw);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) h[j] = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+  *reinterpret_cast<uint4*>(p) = raw;
+}
+template <>
+__device__ __forceinline__ void store8<float>(float* p, const float* v) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
 }
 
-// One CTA: window b, two output rows (2*blockIdx.y, +1), 16 channels
-// (blockIdx.x).  conv0 rows 4y-1 .. 4y+3 are computed once into shared memory
-// (as the rounded profile scalar, held in f32) and reused by the depthwise.
+// One CTA: window b, depthwise output rows 2*blockIdx.y and +1, 32 channels.
+// conv0 rows 4y-1 .. 4y+3 are computed once into shared memory (rounded to
+// the profile scalar, held as f32) and reused by the depthwise.
 template <typename T>
 __global__ void __launch_bounds__(256) conv0_dw2_kernel(const float* __restrict__ fbank, const T* __restrict__ w0,
                                                         const float* __restrict__ b0, const T* __restrict__ wd,
                                                         const float* __restrict__ bd,
                                                         const uint32_t* __restrict__ feature_lengths,
                                                         T* __restrict__ out) {
-  constexpr int CG = 16;        // channels per CTA
-  constexpr int ROWS0 = 5;      // conv0 rows per CTA
-  constexpr int IN_ROWS = 11;   // input time samples per CTA
-  __shared__ float in_tile[IN_ROWS][SUB_IW + 1];
-  __shared__ float c0_tile[ROWS0][SUB_CW][CG + 1];
-  __shared__ float w0s[9][CG], wds[9][CG], b0s[CG], bds[CG];
+  extern __shared__ __align__(16) float sub_smem[];
+  float* in_tile = sub_smem;                                  // [11][129]
+  float* c0_tile = sub_smem + C0_IN_FLOATS;                   // [5][64][C0_PITCH], 16-byte aligned
   const int b = blockIdx.z;
   const int oy0 = blockIdx.y * 2;
-  const int cbase = blockIdx.x * CG;
+  const int cbase = blockIdx.x * C0_CG;
+  const int tid = threadIdx.x;
   const int raw = (int)feature_lengths[b];
   const int vin = sub_len(raw, 1), vout = sub_len(raw, 2);
-  const int y0_first = 2 * oy0 - 1;      // first conv0 row
-  const int iy_first = 2 * y0_first - 1; // first input time sample
-  for (int i = threadIdx.x; i < 9 * CG; i += 256) {
-    w0s[i / CG][i % CG] = ldf(w0 + (i / CG) * SUB_C + cbase + i % CG);
-    wds[i / CG][i % CG] = ldf(wd + (i / CG) * SUB_C + cbase + i % CG);
-  }
-  if (threadIdx.x < CG) {
-    b0s[threadIdx.x] = b0[cbase + threadIdx.x];
-    bds[threadIdx.x] = bd[cbase + threadIdx.x];
-  }
-  for (int i = threadIdx.x; i < IN_ROWS * SUB_IW; i += 256) {
-    const int r = i % IN_ROWS, x = i / IN_ROWS;  // consecutive threads walk time (contiguous)
+  const int y0_first = 2 * oy0 - 1;       // first conv0 row
+  const int iy_first = 2 * y0_first - 1;  // first input time sample
+  for (int i = tid; i < C0_IN_ROWS * SUB_IW; i += 256) {
+    const int r = i % C0_IN_ROWS, x = i / C0_IN_ROWS;  // consecutive threads walk time (contiguous)
     const int iy = iy_first + r;
-    in_tile[r][x] = (iy >= 0 && iy < SUB_IH) ? fbank[((size_t)b * SUB_IW + x) * SUB_IH + iy] : 0.0f;
+    in_tile[r * (SUB_IW + 1) + x] = (iy >= 0 && iy < SUB_IH) ? fbank[((size_t)b * SUB_IW + x) * SUB_IH + iy] : 0.0f;
   }
+  const int cg = tid >> 6;           // 8-channel group within the CTA
+  const int c = cbase + cg * 8;
+  float w[9][8], bias[8];
+#pragma unroll
+  for (int k = 0; k < 9; ++k) load8<T>(w0 + k * SUB_C + c, w[k]);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) bias[j] = __ldg(b0 + c + j);
   __syncthreads();
-  for (int i = threadIdx.x; i < ROWS0 * SUB_CW * CG; i += 256) {
-    const int c = i % CG, x = (i / CG) % SUB_CW, r = i / (CG * SUB_CW);
-    const int y = y0_first + r;
-    float v = 0.0f;
-    if (y >= 0 && y < SUB_CH && y < vin) {
-      float sum = b0s[c];
+  {  // conv0: thread = (channel group, x), 5 rows
+    const int x = tid & 63;
+#pragma unroll 1
+    for (int r = 0; r < C0_ROWS; ++r) {
+      const int y = y0_first + r;
+      float acc[8];
+      if (y >= 0 && y < SUB_CH && y < vin) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = bias[j];
+#pragma unroll
+        for (int ky = 0; ky < 3; ++ky) {
+          const int iy = y * 2 + ky - 1;
+          if (iy < 0 || iy >= SUB_IH) continue;
+#pragma unroll
+          for (int kx = 0; kx < 3; ++kx) {
+            const int ix = x * 2 + kx - 1;
+            if (ix < 0 || ix >= SUB_IW) continue;
+            const float v = in_tile[(iy - iy_first) * (SUB_IW + 1) + ix];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[j] = fmaf(w[ky * 3 + kx][j], v, acc[j]);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = (float)(T)fmaxf(acc[j], 0.0f);  // rounded to the profile scalar
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+      }
+      float* dst = c0_tile + (r * SUB_CW + x) * C0_PITCH + cg * 8;
+      *reinterpret_cast<float4*>(dst) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      *reinterpret_cast<float4*>(dst + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 9; ++k) load8<T>(wd + k * SUB_C + c, w[k]);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) bias[j] = __ldg(bd + c + j);
+  __syncthreads();
+  {  // depthwise: thread = (channel group, output x, output row)
+    const int ox = tid & 31, ry = (tid >> 5) & 1;
+    const int oy = oy0 + ry;
+    float acc[8];
+    if (oy >= vout) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = bias[j];
 #pragma unroll
       for (int ky = 0; ky < 3; ++ky) {
-        const int iy = y * 2 + ky - 1;
-        if (iy < 0 || iy >= SUB_IH) continue;
+        const int iy = oy * 2 + ky - 1;
+        if (iy < 0 || iy >= SUB_CH || iy >= vin) continue;
 #pragma unroll
         for (int kx = 0; kx < 3; ++kx) {
-          const int ix = x * 2 + kx - 1;
-          if (ix < 0 || ix >= SUB_IW) continue;
-          sum = fmaf(w0s[ky * 3 + kx][c], in_tile[iy - iy_first][ix], sum);
+          const int ix = ox * 2 + kx - 1;
+          if (ix < 0 || ix >= SUB_CW) continue;
+          const float* src = c0_tile + ((iy - y0_first) * SUB_CW + ix) * C0_PITCH + cg * 8;
+          const float4 lo = *reinterpret_cast<const float4*>(src);
+          const float4 hi = *reinterpret_cast<const float4*>(src + 4);
+          const float v[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[j] = fmaf(v[j], w[ky * 3 + kx][j], acc[j]);
         }
       }
-      v = (float)(T)fmaxf(sum, 0.0f);  // rounded to the profile scalar
     }
-    c0_tile[r][x][c] = v;
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < 2 * SUB_OW * CG; i += 256) {
-    const int c = i % CG, ox = (i / CG) % SUB_OW, ry = i / (CG * SUB_OW);
-    const int oy = oy0 + ry;
-    const size_t oi = (((size_t)b * SUB_OH + oy) * SUB_OW + ox) * SUB_C + cbase + c;
-    if (oy >= vout) {
-      out[oi] = (T)0.0f;
-      continue;
-    }
-    float sum = bds[c];
-#pragma unroll
-    for (int ky = 0; ky < 3; ++ky) {
-      const int iy = oy * 2 + ky - 1;
-      if (iy < 0 || iy >= SUB_CH || iy >= vin) continue;
-#pragma unroll
-      for (int kx = 0; kx < 3; ++kx) {
-        const int ix = ox * 2 + kx - 1;
-        if (ix < 0 || ix >= SUB_CW) continue;
-        sum = fmaf(c0_tile[iy - y0_first][ix][c], wds[ky * 3 + kx][c], sum);
-      }
-    }
-    out[oi] = (T)sum;
+    store8<T>(out + (((size_t)b * SUB_OH + oy) * SUB_OW + ox) * SUB_C + c, acc);
   }
 }
 
 // Depthwise 3x3 stride 2 pad 1 + bias, channel-last; one thread per output
-// element.
+// pixel and 8 channels.
 template <typename T>
-__global__ void depthwise_kernel(const T* __restrict__ in, const T* __restrict__ w, const float* __restrict__ bias,
-                                 const uint32_t* __restrict__ feature_lengths, T* __restrict__ out, int batch, int ih,
-                                 int iw, int channels, int steps) {
+__global__ void __launch_bounds__(256) depthwise_kernel(const T* __restrict__ in, const T* __restrict__ w,
+                                                        const float* __restrict__ bias,
+                                                        const uint32_t* __restrict__ feature_lengths,
+                                                        T* __restrict__ out, int batch, int ih, int iw,
+                                                        int channels, int steps) {
   const int oh = (ih - 1) / 2 + 1, ow = (iw - 1) / 2 + 1;
-  const int64_t total = (int64_t)batch * oh * ow * channels;
+  const int cv = channels / 8;
+  const int64_t total = (int64_t)batch * oh * ow * cv;
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= total) return;
-  const int c = (int)(i % channels);
-  const int ox = (int)((i / channels) % ow);
-  const int oy = (int)((i / ((int64_t)channels * ow)) % oh);
-  const int b = (int)(i / ((int64_t)channels * ow * oh));
+  const int c = (int)(i % cv) * 8;
+  const int ox = (int)((i / cv) % ow);
+  const int oy = (int)((i / ((int64_t)cv * ow)) % oh);
+  const int b = (int)(i / ((int64_t)cv * ow * oh));
   const int raw = (int)feature_lengths[b];
   const int vin = sub_len(raw, steps - 1), vout = sub_len(raw, steps);
+  T* dst = out + (((int64_t)b * oh + oy) * ow + ox) * channels + c;
+  float acc[8];
   if (oy >= vout) {
-    out[i] = (T)0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+    store8<T>(dst, acc);
     return;
   }
-  float sum = bias[c];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = __ldg(bias + c + j);
 #pragma unroll
   for (int ky = 0; ky < 3; ++ky) {
     const int iy = oy * 2 + ky - 1;
@@ -143,11 +213,14 @@ __global__ void depthwise_kernel(const T* __restrict__ in, const T* __restrict__
     for (int kx = 0; kx < 3; ++kx) {
       const int ix = ox * 2 + kx - 1;
       if (ix < 0 || ix >= iw) continue;
-      sum = fmaf(ldf(in + (((int64_t)b * ih + iy) * iw + ix) * channels + c), ldf(w + (ky * 3 + kx) * channels + c),
-                 sum);
+      float v[8], wk[8];
+      load8<T>(in + (((int64_t)b * ih + iy) * iw + ix) * channels + c, v);
+      load8<T>(w + (ky * 3 + kx) * channels + c, wk);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = fmaf(v[j], wk[j], acc[j]);
     }
   }
-  out[i] = (T)sum;
+  store8<T>(dst, acc);
 }
 
 template <typename T>
@@ -162,23 +235,29 @@ __global__ void time_mask_kernel(T* __restrict__ values, const uint32_t* __restr
 int launch_subsampling_conv0_dw2(int precision, int batch, const float* features, const void* conv0_w,
                                  const float* conv0_b, const void* dw_w, const float* dw_b,
                                  const uint32_t* feature_lengths, void* out, cudaStream_t stream) {
-  const dim3 grid(SUB_C / 16, SUB_OH / 2, batch);
-  if (precision == PK_FP16)
-    conv0_dw2_kernel<__half><<<grid, 256, 0, stream>>>(features, static_cast<const __half*>(conv0_w), conv0_b,
-                                                       static_cast<const __half*>(dw_w), dw_b, feature_lengths,
-                                                       static_cast<__half*>(out));
-  else
-    conv0_dw2_kernel<float><<<grid, 256, 0, stream>>>(features, static_cast<const float*>(conv0_w), conv0_b,
-                                                      static_cast<const float*>(dw_w), dw_b, feature_lengths,
-                                                      static_cast<float*>(out));
+  const dim3 grid(SUB_C / C0_CG, SUB_OH / 2, batch);
+  if (precision == PK_FP16) {
+    int st = set_max_dynamic_smem(reinterpret_cast<const void*>(conv0_dw2_kernel<__half>), C0_SMEM);
+    if (st != PK_OK) return st;
+    conv0_dw2_kernel<__half><<<grid, 256, C0_SMEM, stream>>>(features, static_cast<const __half*>(conv0_w), conv0_b,
+                                                             static_cast<const __half*>(dw_w), dw_b, feature_lengths,
+                                                             static_cast<__half*>(out));
+  } else {
+    int st = set_max_dynamic_smem(reinterpret_cast<const void*>(conv0_dw2_kernel<float>), C0_SMEM);
+    if (st != PK_OK) return st;
+    conv0_dw2_kernel<float><<<grid, 256, C0_SMEM, stream>>>(features, static_cast<const float*>(conv0_w), conv0_b,
+                                                            static_cast<const float*>(dw_w), dw_b, feature_lengths,
+                                                            static_cast<float*>(out));
+  }
   return cuda_error(cudaGetLastError(), "subsampling conv0+dw2 launch");
 }
 
 int launch_subsampling_depthwise(int precision, int batch, int ih, int iw, int channels, const void* input,
                                  const void* w, const float* b, const uint32_t* feature_lengths, int steps,
                                  void* out, cudaStream_t stream) {
+  if (channels % 8 != 0) return set_error(PK_E_SHAPE, "depthwise subsampling needs channels %% 8 == 0");
   const int oh = (ih - 1) / 2 + 1, ow = (iw - 1) / 2 + 1;
-  const int64_t total = (int64_t)batch * oh * ow * channels;
+  const int64_t total = (int64_t)batch * oh * ow * (channels / 8);
   const unsigned blocks = (unsigned)((total + 255) / 256);
   if (precision == PK_FP16)
     depthwise_kernel<__half><<<blocks, 256, 0, stream>>>(static_cast<const __half*>(input),
