@@ -48,6 +48,25 @@ __device__ __forceinline__ void load_vec<float>(const float* p, float* v) {
   v[2] = f.z;
   v[3] = f.w;
 }
+// 16 bytes already in registers -> floats.
+template <typename T>
+__device__ __forceinline__ void unpack_vec(const uint4& raw, float* v) {
+  if constexpr (sizeof(T) == 2) {
+    const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __half22float2(h[j]);
+      v[2 * j] = f.x;
+      v[2 * j + 1] = f.y;
+    }
+  } else {
+    v[0] = __uint_as_float(raw.x);
+    v[1] = __uint_as_float(raw.y);
+    v[2] = __uint_as_float(raw.z);
+    v[3] = __uint_as_float(raw.w);
+  }
+}
+
 template <typename T>
 __device__ __forceinline__ void store_vec(T* p, const float* v);
 template <>
@@ -64,7 +83,7 @@ __device__ __forceinline__ void store_vec<float>(float* p, const float* v) {
 }
 
 template <typename T>
-__global__ void __launch_bounds__(CONV_THREADS) conformer_conv_kernel(
+__global__ void __launch_bounds__(CONV_THREADS, 2) conformer_conv_kernel(
     const T* __restrict__ g, const T* __restrict__ dw, const float* __restrict__ scale,
     const float* __restrict__ shift, const uint32_t* __restrict__ valid_lengths, T* __restrict__ out, int frames) {
   constexpr int VEC = 16 / sizeof(T);          // channels per 16-byte vector
@@ -75,22 +94,32 @@ __global__ void __launch_bounds__(CONV_THREADS) conformer_conv_kernel(
   const int c0 = blockIdx.x * CONV_TC, t0 = blockIdx.y * CONV_TF, b = blockIdx.z;
   const int tid = threadIdx.x;
   const int valid = min((int)valid_lengths[b], frames);
-  // ---- GLU halo tile
-  for (int i = tid; i < CONV_ROWS * NV; i += CONV_THREADS) {
+  // ---- GLU halo tile: all of this thread's 128-bit loads are issued before
+  // any GLU math so their latencies overlap.
+  constexpr int ITEMS = (CONV_ROWS * NV + CONV_THREADS - 1) / CONV_THREADS;
+  uint4 vraw[ITEMS], graw[ITEMS];
+#pragma unroll
+  for (int it = 0; it < ITEMS; ++it) {
+    const int i = tid + it * CONV_THREADS;
     const int r = i / NV, v = i % NV;
     const int t = t0 - CONV_K / 2 + r;
-    float val[VEC];
-    if (t >= 0 && t < valid) {
+    vraw[it] = graw[it] = make_uint4(0, 0, 0, 0);
+    if (i < CONV_ROWS * NV && t >= 0 && t < valid) {
       const T* row = g + ((size_t)b * frames + t) * (2 * CONV_C) + c0 + v * VEC;
-      float gate[VEC];
-      load_vec<T>(row, val);
-      load_vec<T>(row + CONV_C, gate);
-#pragma unroll
-      for (int j = 0; j < VEC; ++j) val[j] *= fast_sigmoid(gate[j]);
-    } else {
-#pragma unroll
-      for (int j = 0; j < VEC; ++j) val[j] = 0.0f;
+      vraw[it] = __ldg(reinterpret_cast<const uint4*>(row));
+      graw[it] = __ldg(reinterpret_cast<const uint4*>(row + CONV_C));
     }
+  }
+#pragma unroll
+  for (int it = 0; it < ITEMS; ++it) {
+    const int i = tid + it * CONV_THREADS;
+    if (i >= CONV_ROWS * NV) break;
+    const int r = i / NV, v = i % NV;
+    float val[VEC], gate[VEC];
+    unpack_vec<T>(vraw[it], val);
+    unpack_vec<T>(graw[it], gate);
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) val[j] *= fast_sigmoid(gate[j]);  // zero rows stay zero
 #pragma unroll
     for (int j = 0; j < VEC; j += 4)
       *reinterpret_cast<float4*>(&glu[r][v * VEC + j]) = make_float4(val[j], val[j + 1], val[j + 2], val[j + 3]);

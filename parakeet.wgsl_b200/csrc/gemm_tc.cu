@@ -76,6 +76,8 @@ struct TcLayout {
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
   static constexpr uint32_t IDESC = umma_idesc_f16(TC_BM, BN, /*A MN-major*/ 1, /*B K-major*/ 0);
+  // Two accumulators of BN fp32 columns; TMEM allocations are powers of two.
+  static constexpr uint32_t TMEM_COLS = 2 * BN <= 256 ? 256 : 512;
   static_assert(A_BYTES % 1024 == 0 && W_BYTES % 1024 == 0, "stage buffers must keep 1024B alignment");
   static_assert(CODE_BYTES % 128 == 0, "code stage must keep 128B alignment");
 };
@@ -221,7 +223,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_palette_gemm_kernel(const __
     tma_prefetch_desc(&p.tmap_codes);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 2 * BN);
+    tmem_alloc(tmem_slot, L::TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -379,7 +381,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_palette_gemm_kernel(const __
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 2 * BN);
+    tmem_dealloc(tmem_base, L::TMEM_COLS);
   }
 }
 
@@ -462,11 +464,29 @@ static int launch_tc(const DeviceCtx& dev, const GemmArgs& g, cudaStream_t strea
   }
 }
 
+// Token-tile choice: minimise (waves of persistent CTAs) x (per-tile cost),
+// with a per-stage cost model of the shared-memory traffic that bounds this
+// kernel: decode (~424 wavefronts) + weight-tile reads (128) + activation
+// tile TMA write and MMA read (BN each) + code tile (40).
+static int choose_bn(const DeviceCtx& dev, const GemmArgs& g) {
+  if (g.rows <= 128) return 128;
+  const int n_tiles = (int)(g.columns / TC_BM);
+  int best = 256;
+  double best_cost = 1e30;
+  for (int bn : {256, 192, 128}) {
+    const int64_t tiles = (g.rows + bn - 1) / bn * n_tiles;
+    const int64_t waves = (tiles + dev.sm_count - 1) / dev.sm_count;
+    const double cost = (double)waves * (592.0 + 2.0 * bn);
+    if (cost < best_cost - 1e-9) best_cost = cost, best = bn;
+  }
+  return best;
+}
+
 int launch_gemm_tc(const DeviceCtx& dev, const GemmArgs& g, cudaStream_t stream, int forced_bn) {
   if (!gemm_tc_supported(g)) return set_error(PK_E_SHAPE, "shape not supported by the tensor-core GEMM");
-  // Token tile: 256 when there are enough rows to fill it, else 128.
-  const int bn = forced_bn ? forced_bn : (g.rows > 128 ? 256 : 128);
+  const int bn = forced_bn ? forced_bn : choose_bn(dev, g);
   if (bn == 256) return g.bits == 5 ? launch_tc<256, 5>(dev, g, stream) : launch_tc<256, 6>(dev, g, stream);
+  if (bn == 192) return g.bits == 5 ? launch_tc<192, 5>(dev, g, stream) : launch_tc<192, 6>(dev, g, stream);
   return g.bits == 5 ? launch_tc<128, 5>(dev, g, stream) : launch_tc<128, 6>(dev, g, stream);
 }
 

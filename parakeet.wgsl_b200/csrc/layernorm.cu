@@ -11,13 +11,13 @@
 
 namespace pk {
 
-// Fast path: channels == 1024.  Each warp owns LN_ROWS consecutive rows: it
-// loads gamma/beta for its lane's channels once (128-bit loads), issues every
-// row's 128-bit loads before reducing (f16: 4 per lane per row, f32: 8), then
-// normalizes and stores.  One HBM read and one write of each row.
-// Rows per warp: 4 for f16 rows, 2 for f32 rows (register budget).
+// Fast path: channels == 1024.  One warp per row, all of the row's 128-bit
+// loads issued before reducing (f16: 4 per lane, f32: 8); gamma/beta are
+// 128-bit L1-resident loads.  A small register footprint keeps every row of
+// a batch-32 launch resident at once (one wave), so HBM latency overlaps
+// across the whole launch.  One HBM read and one write of each row.
 template <typename T>
-constexpr int ln_rows() { return sizeof(T) == 2 ? 4 : 2; }
+constexpr int ln_rows() { return sizeof(T) == 2 ? 2 : 1; }
 
 template <typename T>
 __device__ __forceinline__ void unpack16(const uint4& raw, float* v) {
@@ -55,18 +55,6 @@ __global__ void __launch_bounds__(256) layernorm1024_kernel(const T* __restrict_
       for (int i = 0; i < LOADS; ++i) raw[r][i] = __ldg(src + i * 32 + lane);
     }
   }
-  float g[LOADS][VEC], b[LOADS][VEC];
-#pragma unroll
-  for (int i = 0; i < LOADS; ++i) {
-    const int c0 = (i * 32 + lane) * VEC;
-#pragma unroll
-    for (int j = 0; j < VEC; j += 4) {
-      const float4 gg = __ldg(reinterpret_cast<const float4*>(gamma + c0 + j));
-      const float4 bb = __ldg(reinterpret_cast<const float4*>(beta + c0 + j));
-      g[i][j] = gg.x, g[i][j + 1] = gg.y, g[i][j + 2] = gg.z, g[i][j + 3] = gg.w;
-      b[i][j] = bb.x, b[i][j + 1] = bb.y, b[i][j + 2] = bb.z, b[i][j + 3] = bb.w;
-    }
-  }
 #pragma unroll
   for (int r = 0; r < LN_ROWS; ++r) {
     if (row0 + r >= rows) break;
@@ -93,9 +81,17 @@ __global__ void __launch_bounds__(256) layernorm1024_kernel(const T* __restrict_
     uint4* dst = reinterpret_cast<uint4*>(y + (row0 + r) * 1024);
 #pragma unroll
     for (int i = 0; i < LOADS; ++i) {
+      const int c0 = (i * 32 + lane) * VEC;
       float o[VEC];
 #pragma unroll
-      for (int j = 0; j < VEC; ++j) o[j] = fmaf((v[i][j] - mean) * rstd, g[i][j], b[i][j]);
+      for (int j = 0; j < VEC; j += 4) {
+        const float4 gg = __ldg(reinterpret_cast<const float4*>(gamma + c0 + j));
+        const float4 bb = __ldg(reinterpret_cast<const float4*>(beta + c0 + j));
+        o[j] = fmaf((v[i][j] - mean) * rstd, gg.x, bb.x);
+        o[j + 1] = fmaf((v[i][j + 1] - mean) * rstd, gg.y, bb.y);
+        o[j + 2] = fmaf((v[i][j + 2] - mean) * rstd, gg.z, bb.z);
+        o[j + 3] = fmaf((v[i][j + 3] - mean) * rstd, gg.w, bb.w);
+      }
       uint4 out;
       if constexpr (sizeof(T) == 2) {
         __half2* h = reinterpret_cast<__half2*>(&out);

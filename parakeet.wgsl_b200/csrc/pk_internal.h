@@ -56,6 +56,8 @@ int launch_layernorm(int precision, int64_t rows, int64_t channels, const void* 
 int launch_rel_attention(const DeviceCtx& dev, int precision, int batch, int frames, const void* qkv,
                          const void* positions, const float* bias_u, const float* bias_v,
                          const uint32_t* valid_lengths, void* context, cudaStream_t stream);
+int launch_rel_attention_tc(int batch, int frames, const void* qkv, const void* positions, const float* bias_u,
+                            const float* bias_v, const uint32_t* valid_lengths, void* context, cudaStream_t stream);
 int launch_conformer_conv(int precision, int batch, int frames, const void* pointwise, const void* dw,
                           const float* scale, const float* shift, const uint32_t* valid_lengths, void* out,
                           cudaStream_t stream);

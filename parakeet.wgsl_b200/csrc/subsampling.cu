@@ -24,14 +24,18 @@ namespace pk {
 
 constexpr int SUB_IH = 1501, SUB_IW = 128, SUB_CH = 751, SUB_CW = 64, SUB_OH = 376, SUB_OW = 32, SUB_C = 256;
 constexpr int C0_CG = 32;        // channels per CTA
-constexpr int C0_ROWS = 5;       // conv0 rows per CTA (two depthwise output rows)
-constexpr int C0_IN_ROWS = 11;   // input time samples per CTA
-constexpr int C0_PITCH = C0_CG + 4;  // padded channel pitch of the conv0 tile (conflict-free 16-byte access)
-// The input tile is padded to a multiple of 4 floats so the conv0 tile that
-// follows it starts on a 16-byte boundary (it is accessed with float4).
-constexpr int C0_IN_FLOATS = (C0_IN_ROWS * (SUB_IW + 1) + 3) / 4 * 4;
-constexpr int C0_SMEM = (C0_IN_FLOATS + C0_ROWS * SUB_CW * C0_PITCH) * 4;
-static_assert(C0_IN_FLOATS % 4 == 0 && C0_PITCH % 4 == 0, "conv0 tile must stay 16-byte aligned");
+constexpr int C0_SR = 24;        // depthwise output rows per CTA (a strip)
+constexpr int C0_STRIPS = (SUB_OH + C0_SR - 1) / C0_SR;
+constexpr int C0_IN_ROWS = 4 * C0_SR + 3;  // input time samples a strip needs
+constexpr int C0_IN_PITCH = SUB_IW + 1;
+constexpr int C0_PITCH = C0_CG + 4;  // padded channel pitch of the conv0 ring (conflict-free 16-byte access)
+// The input strip is padded to a multiple of 4 floats so the conv0 ring and
+// the depthwise taps that follow it start on 16-byte boundaries (float4).
+constexpr int C0_IN_FLOATS = (C0_IN_ROWS * C0_IN_PITCH + 3) / 4 * 4;
+constexpr int C0_RING_FLOATS = 3 * SUB_CW * C0_PITCH;
+constexpr int C0_SMEM = (C0_IN_FLOATS + C0_RING_FLOATS + 9 * C0_CG + C0_CG) * 4;
+static_assert(C0_IN_FLOATS % 4 == 0 && C0_PITCH % 4 == 0 && C0_RING_FLOATS % 4 == 0,
+              "conv0 ring must stay 16-byte aligned");
 
 __device__ __forceinline__ int sub_len(int raw, int steps) {
   for (int s = 0; s < steps; ++s) raw = (raw + 1) >> 1;
@@ -74,105 +78,117 @@ __device__ __forceinline__ void store8<float>(float* p, const float* v) {
   *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
 }
 
-// One CTA: window b, depthwise output rows 2*blockIdx.y and +1, 32 channels.
-// conv0 rows 4y-1 .. 4y+3 are computed once into shared memory (rounded to
-// the profile scalar, held as f32) and reused by the depthwise.
+// One CTA: window b, a strip of C0_SR depthwise output rows, 32 channels.
+// The strip's input time samples (4*SR+3 of them, all 128 mel bins) are
+// staged once with coalesced loads; conv0 rows are produced in order into a
+// 3-row ring (rounded to the profile scalar, held as f32): each depthwise row
+// oy needs conv0 rows 2oy-1 .. 2oy+1, and consecutive rows share one.
 template <typename T>
-__global__ void __launch_bounds__(256) conv0_dw2_kernel(const float* __restrict__ fbank, const T* __restrict__ w0,
-                                                        const float* __restrict__ b0, const T* __restrict__ wd,
-                                                        const float* __restrict__ bd,
-                                                        const uint32_t* __restrict__ feature_lengths,
-                                                        T* __restrict__ out) {
+__global__ void __launch_bounds__(256, 2) conv0_dw2_kernel(const float* __restrict__ fbank,
+                                                           const T* __restrict__ w0, const float* __restrict__ b0,
+                                                           const T* __restrict__ wd, const float* __restrict__ bd,
+                                                           const uint32_t* __restrict__ feature_lengths,
+                                                           T* __restrict__ out) {
   extern __shared__ __align__(16) float sub_smem[];
-  float* in_tile = sub_smem;                                  // [11][129]
-  float* c0_tile = sub_smem + C0_IN_FLOATS;                   // [5][64][C0_PITCH], 16-byte aligned
+  float* in_s = sub_smem;                                 // [C0_IN_ROWS][129]
+  float* ring = sub_smem + C0_IN_FLOATS;                  // [3][64][C0_PITCH], 16-byte aligned
+  float* wd_s = ring + C0_RING_FLOATS;                    // [9][32] depthwise taps
+  float* bd_s = wd_s + 9 * C0_CG;                         // [32] depthwise bias
   const int b = blockIdx.z;
-  const int oy0 = blockIdx.y * 2;
+  const int oy0 = blockIdx.y * C0_SR;
+  const int oy_end = min(oy0 + C0_SR, SUB_OH);
   const int cbase = blockIdx.x * C0_CG;
   const int tid = threadIdx.x;
   const int raw = (int)feature_lengths[b];
   const int vin = sub_len(raw, 1), vout = sub_len(raw, 2);
-  const int y0_first = 2 * oy0 - 1;       // first conv0 row
-  const int iy_first = 2 * y0_first - 1;  // first input time sample
+  const int y_first = 2 * oy0 - 1;       // first conv0 row of the strip
+  const int iy_first = 2 * y_first - 1;  // first input time sample
   for (int i = tid; i < C0_IN_ROWS * SUB_IW; i += 256) {
     const int r = i % C0_IN_ROWS, x = i / C0_IN_ROWS;  // consecutive threads walk time (contiguous)
     const int iy = iy_first + r;
-    in_tile[r * (SUB_IW + 1) + x] = (iy >= 0 && iy < SUB_IH) ? fbank[((size_t)b * SUB_IW + x) * SUB_IH + iy] : 0.0f;
+    in_s[r * C0_IN_PITCH + x] = (iy >= 0 && iy < SUB_IH) ? fbank[((size_t)b * SUB_IW + x) * SUB_IH + iy] : 0.0f;
   }
-  const int cg = tid >> 6;           // 8-channel group within the CTA
+  for (int i = tid; i < 9 * C0_CG; i += 256) wd_s[i] = (float)wd[(i / C0_CG) * SUB_C + cbase + i % C0_CG];
+  if (tid < C0_CG) bd_s[tid] = bd[cbase + tid];
+  const int cg = tid >> 6;  // 8-channel group of this thread's conv0 outputs
   const int c = cbase + cg * 8;
+  const int x = tid & 63;
   float w[9][8], bias[8];
 #pragma unroll
   for (int k = 0; k < 9; ++k) load8<T>(w0 + k * SUB_C + c, w[k]);
 #pragma unroll
   for (int j = 0; j < 8; ++j) bias[j] = __ldg(b0 + c + j);
   __syncthreads();
-  {  // conv0: thread = (channel group, x), 5 rows
-    const int x = tid & 63;
-#pragma unroll 1
-    for (int r = 0; r < C0_ROWS; ++r) {
-      const int y = y0_first + r;
-      float acc[8];
-      if (y >= 0 && y < SUB_CH && y < vin) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[j] = bias[j];
-#pragma unroll
-        for (int ky = 0; ky < 3; ++ky) {
-          const int iy = y * 2 + ky - 1;
-          if (iy < 0 || iy >= SUB_IH) continue;
-#pragma unroll
-          for (int kx = 0; kx < 3; ++kx) {
-            const int ix = x * 2 + kx - 1;
-            if (ix < 0 || ix >= SUB_IW) continue;
-            const float v = in_tile[(iy - iy_first) * (SUB_IW + 1) + ix];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) acc[j] = fmaf(w[ky * 3 + kx][j], v, acc[j]);
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[j] = (float)(T)fmaxf(acc[j], 0.0f);  // rounded to the profile scalar
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
-      }
-      float* dst = c0_tile + (r * SUB_CW + x) * C0_PITCH + cg * 8;
-      *reinterpret_cast<float4*>(dst) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-      *reinterpret_cast<float4*>(dst + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
-    }
-  }
-#pragma unroll
-  for (int k = 0; k < 9; ++k) load8<T>(wd + k * SUB_C + c, w[k]);
-#pragma unroll
-  for (int j = 0; j < 8; ++j) bias[j] = __ldg(bd + c + j);
-  __syncthreads();
-  {  // depthwise: thread = (channel group, output x, output row)
-    const int ox = tid & 31, ry = (tid >> 5) & 1;
-    const int oy = oy0 + ry;
+
+  // conv0 row y (3x3 stride 2 over the staged input) -> ring slot (y + 3) % 3.
+  auto conv0_row = [&](int y) {
     float acc[8];
-    if (oy >= vout) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
-    } else {
+    if (y >= 0 && y < SUB_CH && y < vin) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) acc[j] = bias[j];
 #pragma unroll
       for (int ky = 0; ky < 3; ++ky) {
-        const int iy = oy * 2 + ky - 1;
-        if (iy < 0 || iy >= SUB_CH || iy >= vin) continue;
+        const int iy = y * 2 + ky - 1;
+        if (iy < 0 || iy >= SUB_IH) continue;
 #pragma unroll
         for (int kx = 0; kx < 3; ++kx) {
-          const int ix = ox * 2 + kx - 1;
-          if (ix < 0 || ix >= SUB_CW) continue;
-          const float* src = c0_tile + ((iy - y0_first) * SUB_CW + ix) * C0_PITCH + cg * 8;
-          const float4 lo = *reinterpret_cast<const float4*>(src);
-          const float4 hi = *reinterpret_cast<const float4*>(src + 4);
-          const float v[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+          const int ix = x * 2 + kx - 1;
+          if (ix < 0 || ix >= SUB_IW) continue;
+          const float v = in_s[(iy - iy_first) * C0_IN_PITCH + ix];
 #pragma unroll
-          for (int j = 0; j < 8; ++j) acc[j] = fmaf(v[j], w[ky * 3 + kx][j], acc[j]);
+          for (int j = 0; j < 8; ++j) acc[j] = fmaf(w[ky * 3 + kx][j], v, acc[j]);
         }
       }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = (float)(T)fmaxf(acc[j], 0.0f);  // rounded to the profile scalar
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
     }
-    store8<T>(out + (((size_t)b * SUB_OH + oy) * SUB_OW + ox) * SUB_C + c, acc);
+    float* dst = ring + (((y + 3) % 3) * SUB_CW + x) * C0_PITCH + cg * 8;
+    *reinterpret_cast<float4*>(dst) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    *reinterpret_cast<float4*>(dst + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+  };
+
+  conv0_row(y_first);
+#pragma unroll 1
+  for (int oy = oy0; oy < oy_end; ++oy) {
+    conv0_row(2 * oy);
+    conv0_row(2 * oy + 1);
+    __syncthreads();
+    if (tid < 128) {  // depthwise: thread = (channel group, output x)
+      const int dcg = tid >> 5, ox = tid & 31;
+      float acc[8];
+      if (oy >= vout) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = bd_s[dcg * 8 + j];
+#pragma unroll
+        for (int ky = 0; ky < 3; ++ky) {
+          const int iy = oy * 2 + ky - 1;
+          if (iy < 0 || iy >= SUB_CH || iy >= vin) continue;
+#pragma unroll
+          for (int kx = 0; kx < 3; ++kx) {
+            const int ix = ox * 2 + kx - 1;
+            if (ix < 0 || ix >= SUB_CW) continue;
+            const float* src = ring + (((iy + 3) % 3) * SUB_CW + ix) * C0_PITCH + dcg * 8;
+            const float4 lo = *reinterpret_cast<const float4*>(src);
+            const float4 hi = *reinterpret_cast<const float4*>(src + 4);
+            const float* wk = wd_s + (ky * 3 + kx) * C0_CG + dcg * 8;
+            const float4 wl = *reinterpret_cast<const float4*>(wk);
+            const float4 wh = *reinterpret_cast<const float4*>(wk + 4);
+            const float v[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+            const float ww[8] = {wl.x, wl.y, wl.z, wl.w, wh.x, wh.y, wh.z, wh.w};
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[j] = fmaf(v[j], ww[j], acc[j]);
+          }
+        }
+      }
+      store8<T>(out + (((size_t)b * SUB_OH + oy) * SUB_OW + ox) * SUB_C + cbase + dcg * 8, acc);
+    }
+    __syncthreads();  // the next iteration overwrites the slot of row 2oy-1
   }
 }
 
@@ -235,7 +251,7 @@ __global__ void time_mask_kernel(T* __restrict__ values, const uint32_t* __restr
 int launch_subsampling_conv0_dw2(int precision, int batch, const float* features, const void* conv0_w,
                                  const float* conv0_b, const void* dw_w, const float* dw_b,
                                  const uint32_t* feature_lengths, void* out, cudaStream_t stream) {
-  const dim3 grid(SUB_C / C0_CG, SUB_OH / 2, batch);
+  const dim3 grid(SUB_C / C0_CG, C0_STRIPS, batch);
   if (precision == PK_FP16) {
     int st = set_max_dynamic_smem(reinterpret_cast<const void*>(conv0_dw2_kernel<__half>), C0_SMEM);
     if (st != PK_OK) return st;
