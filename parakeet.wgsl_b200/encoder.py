@@ -98,10 +98,16 @@ class ParakeetEncoderGraph:
         """model: a package dict (name -> record) or an uploaded ModelWeights."""
         if not 0 < capacity <= BATCH_CAPACITY:
             raise RangeError(f"Encoder batch capacity must be in [1, {BATCH_CAPACITY}]")
-        weights = model if isinstance(model, ModelWeights) else ModelWeights(device, model)
+        owned = not isinstance(model, ModelWeights)
+        weights = ModelWeights(device, model) if owned else model
         handle = ctypes.c_void_p()
-        _lib.call("pk_encoder_create", device.handle, weights.handle, _precision(profile), capacity,
-                  ctypes.byref(handle))
+        try:
+            _lib.call("pk_encoder_create", device.handle, weights.handle, _precision(profile), capacity,
+                      ctypes.byref(handle))
+        except Exception:
+            if owned:
+                weights.release()
+            raise
         return ParakeetEncoderGraph(device, weights, profile, capacity, handle)
 
     def _alive(self):

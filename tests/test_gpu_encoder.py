@@ -100,6 +100,40 @@ def test_encoder_rejects_bad_inputs(pk, graph):
         graph.encode(np.zeros((33, 128, 1501), np.float32), [1500] * 33)
 
 
+def test_fp32_package_encoder(pk, oracle, device):
+    """FP32 package (f32 activations and LUTs, fp32-accumulating GEMMs): the
+    north-star tolerance is 1e-4 relative Frobenius against the reference
+    algorithm (whose FP32 GEMM is the same fp32 fma chain)."""
+    package = pk.synthetic.make_package("fp32", layers=24, seed=7)
+    g = pk.encoder.ParakeetEncoderGraph.create(device, package, "fp32", capacity=2)
+    try:
+        fb = pk.synthetic.make_features(2, seed=8)
+        lengths = [1500, 900]
+        out, enc = g.encode(fb, lengths)
+        ref, ref_len = oracle.encoder(package, fb, lengths, np.float32, acc_mode=0)
+        err = rel(out.cpu().numpy(), ref)
+        print(f"fp32 encoder vs oracle rel-Frobenius {err:.3e}")
+        assert list(enc) == list(ref_len)
+        assert err < 1e-4
+    finally:
+        g.destroy()
+        g.weights.release()
+
+
+def test_all_six_bit_package(pk, oracle, device):
+    """All matrices 6-bit (BASELINE config 5's bit-policy variant)."""
+    package = pk.synthetic.make_package("fp16", layers=24, bits_policy="all6", seed=9)
+    g = pk.encoder.ParakeetEncoderGraph.create(device, package, "fp16", capacity=1)
+    try:
+        fb = pk.synthetic.make_features(1, seed=10)
+        out, _ = g.encode(fb, [1500])
+        ref, _ = oracle.encoder(package, fb, [1500], np.float16, acc_mode=1)
+        assert rel(out.cpu().numpy(), ref) < 2e-2
+    finally:
+        g.destroy()
+        g.weights.release()
+
+
 def test_missing_tensor_is_reported(pk, device, package):
     broken = dict(package)
     broken.pop("encoder.layers.7.conv.norm.shift")
