@@ -195,8 +195,15 @@ int pk_encoder_destroy(pk_encoder* encoder);
 /* Test hook (no reference counterpart): selects the GEMM kernel for later
  * pk_palette_gemm / encoder launches in this process.  0 = automatic
  * (tensor cores where the shape tiles, else CUDA cores), 1 = CUDA-core
- * kernel only, 2 = tensor-core kernel only (unsupported shapes fail). */
+ * kernel only, 2 = tensor-core kernel only (unsupported shapes fail),
+ * 3 = as 2 but single-CTA tiles only, 4 = as 2 but CTA-pair tiles
+ * (cta_group::2) wherever N is a multiple of 256. */
 int pk_debug_set_gemm_route(int route);
+/* Test hook (no reference counterpart): forces the tensor-core GEMM token
+ * tile for later launches in this process.  0 = automatic (cost model),
+ * 128 / 192 / 256 = single-CTA tile, -256 / -384 / -512 = CTA-pair tile
+ * (used where N is a multiple of 256, else the 256-token single-CTA tile). */
+int pk_debug_set_gemm_tile(int tile);
 /* Test hook (no reference counterpart): 0 = automatic (tensor-core attention
  * for the FP16 package), 1 = CUDA-core attention kernel. */
 int pk_debug_set_attention_route(int route);

@@ -29,7 +29,7 @@ EXPORTED = (
     "pk_subsampling_conv0_dw2", "pk_subsampling_depthwise", "pk_subsampling_time_mask",
     "pk_weights_upload", "pk_weights_release", "pk_encoder_create", "pk_encoder_forward",
     "pk_encoder_set_checkpoints", "pk_encoder_checkpoint", "pk_encoder_destroy", "pk_debug_set_gemm_route",
-    "pk_debug_set_attention_route",
+    "pk_debug_set_gemm_tile", "pk_debug_set_attention_route",
 )
 
 
@@ -105,6 +105,7 @@ def load() -> ctypes.CDLL:
             "pk_encoder_checkpoint": [vp, i32, vp, vp],
             "pk_encoder_destroy": [vp],
             "pk_debug_set_gemm_route": [i32],
+            "pk_debug_set_gemm_tile": [i32],
             "pk_debug_set_attention_route": [i32],
         }
         for name, args in sig.items():

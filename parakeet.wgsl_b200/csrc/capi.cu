@@ -24,6 +24,7 @@ namespace pk {
 
 static thread_local std::string t_last_error;
 int g_gemm_route = 0;
+int g_gemm_tile = 0;
 int g_attention_route = 0;
 
 int set_error(int code, const char* fmt, ...) {
@@ -199,16 +200,30 @@ int pk_palette_gemm(pk_device* device, const pk_gemm_desc* d, pk_stream stream) 
   if (st != PK_OK) return st;
   cudaSetDevice(device->ctx.ordinal);
   const bool tc = gemm_tc_supported(g);
-  if (g_gemm_route == 2 && !tc) return set_error(PK_E_SHAPE, "tensor-core GEMM forced but shape unsupported");
+  if (g_gemm_route >= 2 && !tc) return set_error(PK_E_SHAPE, "tensor-core GEMM forced but shape unsupported");
   if (tc && g_gemm_route != 1) return launch_gemm_tc(device->ctx, g, as_stream(stream));
   return launch_gemm_simt(device->ctx, g, as_stream(stream));
 }
 
-// Test hook: 0 automatic, 1 SIMT only, 2 tensor cores only.
+// Test hook: 0 automatic, 1 SIMT only, 2 tensor cores only, 3 tensor cores
+// with single-CTA tiles only, 4 tensor cores with CTA-pair tiles wherever N
+// is a multiple of 256.
 int pk_debug_set_gemm_route(int route) {
-  if (route < 0 || route > 2) return set_error(PK_E_INVALID, "route must be 0, 1 or 2");
+  if (route < 0 || route > 4) return set_error(PK_E_INVALID, "route must be 0..4");
   g_gemm_route = route;
   return PK_OK;
+}
+
+// Test hook: 0 automatic; 128/192/256 a single-CTA token tile; -256/-384/-512
+// a CTA-pair token tile (pairs only where N is a multiple of 256).
+int pk_debug_set_gemm_tile(int tile) {
+  switch (tile) {
+    case 0: case 128: case 192: case 256: case -256: case -384: case -512:
+      g_gemm_tile = tile;
+      return PK_OK;
+    default:
+      return set_error(PK_E_INVALID, "tile must be 0, 128, 192, 256, -256, -384 or -512");
+  }
 }
 
 int pk_debug_set_attention_route(int route) {

@@ -41,7 +41,6 @@ constexpr int TC_STAGES = 4;
 constexpr int TC_DECODE_WARPS = 8;
 constexpr int TC_FIRST_EPI_WARP = 2 + TC_DECODE_WARPS;  // 10: warps 10..13 cover TMEM lane quarters 2,3,0,1
 constexpr int TC_THREADS = (TC_FIRST_EPI_WARP + 4) * 32;  // 448
-constexpr int TC_DECODE_THREADS = TC_DECODE_WARPS * 32;
 constexpr int TC_EPI_THREADS = 128;
 
 enum { EPI_PLAIN = 0, EPI_BIAS = 1, EPI_RESIDUAL = 2 };
@@ -207,12 +206,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_palette_gemm_kernel(const __
   if (threadIdx.x == 0) {
     for (int s = 0; s < TC_STAGES; ++s) {
       mbar_init(&full_tma[s], 1);
-      mbar_init(&full_dec[s], TC_DECODE_THREADS);
+      mbar_init(&full_dec[s], TC_DECODE_WARPS);
       mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tm_full[a], 1);
-      mbar_init(&tm_empty[a], TC_EPI_THREADS);
+      mbar_init(&tm_empty[a], TC_EPI_THREADS / 32);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -330,7 +329,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_palette_gemm_kernel(const __
       for (int kb = 0; kb < kb_count; ++kb, ++it) {
         const int s = it % TC_STAGES;
         const uint32_t round = it / TC_STAGES;
-        if (!mbar_wait(&full_tma[s], round & 1, abort_flag, p.status, PK_STATUS_TIMEOUT_DECODE)) {
+        // Warp-uniform outcome: the arrive below is one lane's, after __syncwarp.
+        if (!__all_sync(0xffffffffu, mbar_wait(&full_tma[s], round & 1, abort_flag, p.status,
+                                               PK_STATUS_TIMEOUT_DECODE))) {
           ok = false;
           break;
         }
@@ -339,8 +340,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_palette_gemm_kernel(const __
 #pragma unroll
         for (int j = 0; j < GROUPS_PER_LANE; ++j)
           decode_group<BITS>(codes + (f0[j] / L::CPG) * L::WPG, lut, goff[j], w_stage, k, f0[j]);
+        // Each lane makes its generic-proxy stores visible to the tensor core
+        // (async proxy); the warp's lanes are ordered by __syncwarp, and one
+        // lane's release-arrive covers the warp.
         fence_proxy_async_smem();
-        mbar_arrive(&full_dec[s]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full_dec[s]);
       }
       if (!ok) break;
     }
@@ -351,7 +356,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_palette_gemm_kernel(const __
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++tile_iter) {
       const int acc = tile_iter & 1;
       const uint32_t acc_round = (uint32_t)tile_iter >> 1;
-      if (!mbar_wait(&tm_full[acc], acc_round & 1, abort_flag, p.status, PK_STATUS_TIMEOUT_EPILOGUE)) break;
+      if (!__all_sync(0xffffffffu,
+                      mbar_wait(&tm_full[acc], acc_round & 1, abort_flag, p.status, PK_STATUS_TIMEOUT_EPILOGUE)))
+        break;
       tc_fence_after();
       const int n_tile = tile % p.n_tiles, m_tile = tile / p.n_tiles;
       const int n = n_tile * TC_BM + q * 32 + lane;
@@ -374,7 +381,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_palette_gemm_kernel(const __
           epilogue_run<EPI, ACT, 31>(r, bias_v, res, p.out + base, ld, p.res_scale, left);
       }
       tc_fence_before();
-      mbar_arrive(&tm_empty[acc]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tm_empty[acc]);
     }
   }
 
@@ -382,6 +390,336 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_palette_gemm_kernel(const __
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, L::TMEM_COLS);
+  }
+}
+
+// ===========================================================================
+// CTA-pair variant (cluster of 2, tcgen05 cta_group::2, MMA M = 256).
+// A pair owns 256 output features x T tokens, T = NSUB x BN_MMA.  Each CTA
+// decodes its own 128 features (MMA-A rows 128*rank ..) and TMA-loads a
+// contiguous half of the token tile, T/2 rows; per stage the leader issues
+// NSUB MMAs of N = BN_MMA against the same decoded weights, MMA j taking rows
+// [j*BN_MMA/2, (j+1)*BN_MMA/2) of each CTA's half.  Decoding a weight stage
+// once for up to 512 tokens halves the decode work per FLOP of the
+// single-CTA kernel (whose MMA N, and so its token tile, stops at 256).
+// D rows of each CTA land in its own TMEM, so both CTAs run their own
+// epilogue; accumulators are double buffered when 2T columns fit in TMEM,
+// single buffered otherwise.
+// Barriers: the leader's full_b[s] collects both halves' TMA bytes,
+// full_dec[s] both CTAs' decoders, tm_empty[a] both epilogues; each CTA's
+// own full_c[s] (its code tile), empty[s] and tm_full[a] are signalled by the
+// leader's MMA commits (one commit addressed to each CTA).  The peer signals
+// the leader with 16-byte shared-to-shared bulk copies that complete as
+// transaction bytes on the leader's barrier (bulk_signal_cluster): a
+// release.cluster arrive would make every signalling warp wait on a memory
+// barrier, which measured 1.6x slower than the single-CTA kernel.
+// ===========================================================================
+template <int BN_MMA, int NSUB, int BITS>
+struct Tc2Layout {
+  static constexpr int T = BN_MMA * NSUB;                  // tokens per pair tile
+  static constexpr int CPG = BITS == 5 ? 32 : 16;
+  static constexpr int WPG = BITS == 5 ? 5 : 3;
+  static constexpr int WORDS_PER_ROW = TC_BM * BITS / 32;
+  static constexpr int HALF_ROWS = T / 2;                  // tokens this CTA loads
+  static constexpr int SUB_ROWS = BN_MMA / 2;              // rows of one MMA's B half
+  static constexpr int A_BYTES = HALF_ROWS * TC_BK * 2;
+  static constexpr int W_BYTES = TC_BM * TC_BK * 2;
+  static constexpr int CODE_BYTES = TC_BK * WORDS_PER_ROW * 4;
+  static constexpr int STAGE_BYTES = A_BYTES + W_BYTES + CODE_BYTES;
+  static constexpr int STAGES = (227 * 1024 - 2048) / STAGE_BYTES > 6 ? 6 : (227 * 1024 - 2048) / STAGE_BYTES;
+  static constexpr int OFF_A = 0;
+  static constexpr int OFF_W = OFF_A + STAGES * A_BYTES;
+  static constexpr int OFF_C = OFF_W + STAGES * W_BYTES;
+  static constexpr int OFF_BAR = OFF_C + STAGES * CODE_BYTES;
+  static constexpr int NUM_BARS = 5 * STAGES + 2 + 2 + 1;
+  // misc: TMEM slot, abort flag, then the 16-byte signal payload, which a
+  // bulk copy reads and writes and so must be 16-byte aligned.
+  static constexpr int OFF_MISC = (OFF_BAR + NUM_BARS * 8 + 15) / 16 * 16;
+  static constexpr int SMEM_BYTES = OFF_MISC + 32 + 1024;
+  static constexpr int ACC_BUFS = 2 * T <= 512 ? 2 : 1;
+  static constexpr uint32_t IDESC = umma_idesc_f16(2 * TC_BM, BN_MMA, /*A MN-major*/ 1, /*B K-major*/ 0);
+  static constexpr uint32_t TMEM_COLS = ACC_BUFS * T <= 256 ? 256 : 512;
+  static_assert(STAGES >= 3, "pipeline too shallow");
+  static_assert(OFF_MISC % 16 == 0 && OFF_C % 128 == 0 && CODE_BYTES % 128 == 0, "TMA / bulk-copy alignment");
+  static_assert(SUB_ROWS % 32 == 0, "an epilogue chunk of 32 columns must not straddle the CTA halves");
+  static_assert(A_BYTES % 1024 == 0 && W_BYTES % 1024 == 0, "stage buffers must keep 1024B alignment");
+  static_assert(ACC_BUFS * T <= 512, "TMEM holds 512 columns");
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+};
+
+template <int BN_MMA, int NSUB, int BITS, int EPI, int ACT>
+__global__ void __launch_bounds__(TC_THREADS, 1) tc2_palette_gemm_kernel(const __grid_constant__ TcGemmParams p) {
+  using L = Tc2Layout<BN_MMA, NSUB, BITS>;
+  constexpr int S = L::STAGES;
+  constexpr int T = L::T;
+  __shared__ __align__(16) uint16_t s_lut[3 * 64];
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem + L::OFF_A;
+  uint8_t* sW = smem + L::OFF_W;
+  uint32_t* sCodes = reinterpret_cast<uint32_t*>(smem + L::OFF_C);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* full_b = bars;              // leader: both B halves landed
+  uint64_t* full_c = bars + S;          // own code tile landed
+  uint64_t* full_dec = bars + 2 * S;    // leader: both CTAs decoded
+  uint64_t* empty = bars + 3 * S;       // own: stage consumed by the pair MMA
+  uint64_t* dec_local = bars + 4 * S;   // peer: own decoders done (relayed to full_dec)
+  uint64_t* tm_full = bars + 5 * S;     // own: accumulator ready
+  uint64_t* tm_empty = tm_full + 2;     // leader: both epilogues drained
+  uint64_t* drain = tm_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
+  const uint32_t signal_payload = smem_addr(smem + L::OFF_MISC + 16);  // 16 bytes, contents unused
+  constexpr uint32_t SIGNAL_BYTES = 16;
+
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int lut_entries = p.groups << BITS;
+  for (int i = threadIdx.x; i < lut_entries; i += blockDim.x) s_lut[i] = p.palette[i];
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full_b[s], 1);
+      mbar_init(&full_c[s], 1);
+      mbar_init(&full_dec[s], TC_DECODE_WARPS);  // + SIGNAL_BYTES from the peer's relay
+      mbar_init(&empty[s], 1);
+      mbar_init(&dec_local[s], TC_DECODE_WARPS);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tm_full[a], 1);
+      mbar_init(&tm_empty[a], TC_EPI_THREADS / 32);  // + SIGNAL_BYTES per peer epilogue warp
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&p.tmap_a);
+    tma_prefetch_desc(&p.tmap_codes);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, L::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // barriers of both CTAs initialised before any remote signal
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int kb_count = p.inner / TC_BK;
+  const int pair_n_tiles = p.n_tiles / 2;  // 256-feature tiles
+  const int num_tiles = p.m_tiles * pair_n_tiles;
+  const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    if (lane == 0) {
+      int last_round[S];
+#pragma unroll
+      for (int s = 0; s < S; ++s) last_round[s] = -1;
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
+        const int np = tile % pair_n_tiles, m_tile = tile / pair_n_tiles;
+        const int n_tile = np * 2 + (int)rank;  // this CTA's 128-feature tile
+        for (int kb = 0; kb < kb_count; ++kb, ++it) {
+          const int s = it % S;
+          const uint32_t round = it / S;
+          if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1, abort_flag, p.status, PK_STATUS_TIMEOUT_TMA)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full_c[s], L::CODE_BYTES);
+          tma_load_2d(sCodes + s * (L::CODE_BYTES / 4), &p.tmap_codes, &full_c[s], n_tile * L::WORDS_PER_ROW,
+                      kb * TC_BK);
+          if (leader) mbar_arrive_expect_tx(&full_b[s], 2 * L::A_BYTES);
+          tma_load_2d_pair(sA + s * L::A_BYTES, &p.tmap_a, mapa_shared(smem_addr(&full_b[s]), 0), kb * TC_BK,
+                           m_tile * T + (int)rank * L::HALF_ROWS);
+          last_round[s] = (int)round;
+        }
+      }
+      // Unwind: this CTA's code tiles must have landed (the B halves are
+      // tracked by the leader's barriers, which its MMA thread drains).
+      for (int s = 0; s < S; ++s)
+        if (last_round[s] >= 0) mbar_wait_drain(&full_c[s], (uint32_t)last_round[s] & 1, p.status);
+      if (leader)
+        for (int s = 0; s < S; ++s)
+          if (last_round[s] >= 0) mbar_wait_drain(&full_b[s], (uint32_t)last_round[s] & 1, p.status);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---------------------------------------------------------- MMA issuer (leader)
+      const uint32_t peer_base = mapa_shared(smem_addr(bars), 1);
+      auto peer = [&](uint64_t* b) { return peer_base + (uint32_t)((b - bars) * 8); };
+      uint32_t it = 0;
+      int tile_iter = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += num_pairs, ++tile_iter) {
+        const int acc = tile_iter % L::ACC_BUFS;
+        const uint32_t acc_round = (uint32_t)(tile_iter / L::ACC_BUFS);
+        if (acc_round > 0 &&
+            !mbar_wait(&tm_empty[acc], (acc_round - 1) & 1, abort_flag, p.status, PK_STATUS_TIMEOUT_MMA)) {
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * T);
+        for (int kb = 0; kb < kb_count; ++kb, ++it) {
+          const int s = it % S;
+          const uint32_t round = it / S;
+          if (!mbar_wait(&full_b[s], round & 1, abort_flag, p.status, PK_STATUS_TIMEOUT_MMA) ||
+              !mbar_wait(&full_dec[s], round & 1, abort_flag, p.status, PK_STATUS_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t w_addr = smem_addr(sW + s * L::W_BYTES);
+          const uint32_t a_addr = smem_addr(sA + s * L::A_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < TC_BK / 16; ++kk) {
+            const uint64_t a_desc = umma_smem_desc(w_addr + kk * 2048, 8192, 1024, 2);
+#pragma unroll
+            for (int j = 0; j < NSUB; ++j) {
+              const uint64_t b_desc = umma_smem_desc(a_addr + j * L::SUB_ROWS * 128 + kk * 32, 16, 1024, 2);
+              tc_mma_f16_pair(d_tmem + (uint32_t)(j * BN_MMA), a_desc, b_desc, L::IDESC,
+                              (kb > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
+          tc_commit_pair(smem_addr(&empty[s]));
+          tc_commit_pair(peer(&empty[s]));
+        }
+        if (!ok) break;
+        tc_commit_pair(smem_addr(&tm_full[acc]));
+        tc_commit_pair(peer(&tm_full[acc]));
+      }
+      // The last epilogue signals of each accumulator: the peer's bulk-copy
+      // signals must land before this CTA's shared memory is released.
+      for (int a = 0; a < L::ACC_BUFS && tile_iter > a; ++a)
+        mbar_wait_drain(&tm_empty[a], (uint32_t)((tile_iter - 1 - a) / L::ACC_BUFS) & 1, p.status);
+      tc_commit_pair(smem_addr(drain));
+      mbar_wait_drain(drain, 0, p.status);
+    } else if (lane == 0) {
+      // ---------------------------------------------------------- peer relay
+      // Once this CTA's decoder warps have arrived on dec_local[s], signal the
+      // leader's full_dec[s].
+      const uint32_t full_dec_leader = mapa_shared(smem_addr(full_dec), 0);
+      const uint32_t payload_leader = mapa_shared(signal_payload, 0);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
+        for (int kb = 0; kb < kb_count; ++kb, ++it) {
+          const int s = it % S;
+          const uint32_t round = it / S;
+          if (!mbar_wait(&dec_local[s], round & 1, abort_flag, p.status, PK_STATUS_TIMEOUT_DECODE)) {
+            ok = false;
+            break;
+          }
+          bulk_signal_cluster(payload_leader, signal_payload, SIGNAL_BYTES, full_dec_leader + (uint32_t)(s * 8));
+        }
+      }
+    }
+  } else if (warp < TC_FIRST_EPI_WARP) {
+    // ------------------------------------------------------------ decoders (both CTAs)
+    const int dw = warp - 2;
+    const int k = dw * 8 + (lane & 7);
+    constexpr int GROUPS_PER_LANE = BITS == 5 ? 1 : 2;
+    const uint8_t* lut = reinterpret_cast<const uint8_t*>(s_lut);
+    uint32_t it = 0;
+    for (int tile = pair; tile < num_tiles; tile += num_pairs) {
+      const int f_base = ((tile % pair_n_tiles) * 2 + (int)rank) * TC_BM;
+      uint32_t goff[GROUPS_PER_LANE];
+      int f0[GROUPS_PER_LANE];
+#pragma unroll
+      for (int j = 0; j < GROUPS_PER_LANE; ++j) {
+        f0[j] = ((lane >> 3) + 4 * j) * L::CPG;
+        const int pg = min((f_base + f0[j]) / p.group_cols, p.groups - 1);
+        goff[j] = (uint32_t)pg << (BITS + 1);
+      }
+      bool ok = true;
+      for (int kb = 0; kb < kb_count; ++kb, ++it) {
+        const int s = it % S;
+        const uint32_t round = it / S;
+        if (!__all_sync(0xffffffffu, mbar_wait(&full_c[s], round & 1, abort_flag, p.status,
+                                               PK_STATUS_TIMEOUT_DECODE))) {
+          ok = false;
+          break;
+        }
+        const uint32_t* codes = sCodes + s * (L::CODE_BYTES / 4) + k * L::WORDS_PER_ROW;
+        const uint32_t w_stage = smem_addr(sW + s * L::W_BYTES);
+#pragma unroll
+        for (int j = 0; j < GROUPS_PER_LANE; ++j)
+          decode_group<BITS>(codes + (f0[j] / L::CPG) * L::WPG, lut, goff[j], w_stage, k, f0[j]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (!leader)
+            mbar_arrive(&dec_local[s]);
+          else if (dw == 0)
+            mbar_arrive_expect_tx(&full_dec[s], SIGNAL_BYTES);
+          else
+            mbar_arrive(&full_dec[s]);
+        }
+      }
+      if (!ok) break;
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int q = warp & 3;
+    const uint32_t tm_empty_leader = mapa_shared(smem_addr(tm_empty), 0);
+    const uint32_t payload_leader = mapa_shared(signal_payload, 0);
+    int tile_iter = 0;
+    for (int tile = pair; tile < num_tiles; tile += num_pairs, ++tile_iter) {
+      const int acc = tile_iter % L::ACC_BUFS;
+      const uint32_t acc_round = (uint32_t)(tile_iter / L::ACC_BUFS);
+      if (!__all_sync(0xffffffffu,
+                      mbar_wait(&tm_full[acc], acc_round & 1, abort_flag, p.status, PK_STATUS_TIMEOUT_EPILOGUE)))
+        break;
+      tc_fence_after();
+      const int np = tile % pair_n_tiles, m_tile = tile / pair_n_tiles;
+      const int n = (np * 2 + (int)rank) * TC_BM + q * 32 + lane;
+      const int m0 = m_tile * T;
+      const float bias_v = EPI == EPI_BIAS ? __ldg(p.bias + n) : 0.0f;
+      const uint32_t t_base = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * T);
+      const int ld = p.columns;
+      // Column c of MMA j's accumulator is B row c of that MMA: row
+      // j*SUB_ROWS + c of CTA 0's half (c < SUB_ROWS), else row
+      // j*SUB_ROWS + c - SUB_ROWS of CTA 1's half (tokens from m0 + T/2).
+#pragma unroll 1
+      for (int col = 0; col < T; col += 32) {
+        const int j = col / BN_MMA, c = col % BN_MMA;
+        const int token0 =
+            m0 + (c < L::SUB_ROWS ? j * L::SUB_ROWS + c : L::HALF_ROWS + j * L::SUB_ROWS + c - L::SUB_ROWS);
+        const int left = p.rows - token0;
+        if (left <= 0) continue;
+        uint32_t r[32];
+        tc_ld_32x32b_x32(t_base + (uint32_t)col, r);
+        tc_wait_ld();
+        const size_t base = (size_t)token0 * ld + n;
+        const __half* res = EPI == EPI_RESIDUAL ? p.residual + base : nullptr;
+        if (left >= 32)
+          epilogue_run<EPI, ACT, 32>(r, bias_v, res, p.out + base, ld, p.res_scale, 32);
+        else
+          epilogue_run<EPI, ACT, 31>(r, bias_v, res, p.out + base, ld, p.res_scale, left);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (!leader)
+          bulk_signal_cluster(payload_leader, signal_payload, SIGNAL_BYTES, tm_empty_leader + (uint32_t)(acc * 8));
+        else if (q == 0)
+          mbar_arrive_expect_tx(&tm_empty[acc], (TC_EPI_THREADS / 32) * SIGNAL_BYTES);
+        else
+          mbar_arrive(&tm_empty[acc]);
+      }
+    }
+  }
+
+  __syncthreads();
+  tc_fence_before();
+  cluster_sync();  // the leader's MMAs are drained and both epilogues are done with TMEM
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, L::TMEM_COLS);
   }
 }
 
@@ -464,30 +802,135 @@ static int launch_tc(const DeviceCtx& dev, const GemmArgs& g, cudaStream_t strea
   }
 }
 
-// Token-tile choice: minimise (waves of persistent CTAs) x (per-tile cost),
-// with a per-stage cost model of the shared-memory traffic that bounds this
-// kernel: decode (~424 wavefronts) + weight-tile reads (128) + activation
-// tile TMA write and MMA read (BN each) + code tile (40).
-static int choose_bn(const DeviceCtx& dev, const GemmArgs& g) {
-  if (g.rows <= 128) return 128;
-  const int n_tiles = (int)(g.columns / TC_BM);
-  int best = 256;
-  double best_cost = 1e30;
-  for (int bn : {256, 192, 128}) {
-    const int64_t tiles = (g.rows + bn - 1) / bn * n_tiles;
-    const int64_t waves = (tiles + dev.sm_count - 1) / dev.sm_count;
-    const double cost = (double)waves * (592.0 + 2.0 * bn);
-    if (cost < best_cost - 1e-9) best_cost = cost, best = bn;
+template <int BN_MMA, int NSUB, int BITS, int EPI, int ACT>
+static int launch_tc2_spec(const DeviceCtx& dev, const TcGemmParams& p, cudaStream_t stream) {
+  using L = Tc2Layout<BN_MMA, NSUB, BITS>;
+  auto kernel = tc2_palette_gemm_kernel<BN_MMA, NSUB, BITS, EPI, ACT>;
+  // Per device: opt-in shared memory, then how many CTA pairs can be resident
+  // at once (a pair needs two SMs of one GPC, so this can be below
+  // sm_count / 2).
+  static int max_pairs[32] = {};
+  if (dev.ordinal < 0 || dev.ordinal >= 32) return set_error(PK_E_INVALID, "device ordinal out of range");
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(TC_THREADS);
+  cfg.dynamicSmemBytes = L::SMEM_BYTES;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (!max_pairs[dev.ordinal]) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM_BYTES);
+    if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(tc2_palette_gemm)");
+    cfg.gridDim = dim3(2 * (dev.sm_count / 2));
+    int clusters = 0;
+    e = cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg);
+    if (e != cudaSuccess) return cuda_error(e, "cudaOccupancyMaxActiveClusters(tc2_palette_gemm)");
+    if (clusters <= 0) return set_error(PK_E_CUDA, "no CTA pair of the palette GEMM fits on this device");
+    max_pairs[dev.ordinal] = std::min(clusters, dev.sm_count / 2);
   }
+  const int pair_tiles = p.m_tiles * (p.n_tiles / 2);
+  cfg.gridDim = dim3(2 * std::min(pair_tiles, max_pairs[dev.ordinal]));
+  return cuda_error(cudaLaunchKernelEx(&cfg, kernel, p), "tc2_palette_gemm launch");
+}
+
+template <int BN_MMA, int NSUB, int BITS>
+static int launch_tc2(const DeviceCtx& dev, const GemmArgs& g, cudaStream_t stream) {
+  using L = Tc2Layout<BN_MMA, NSUB, BITS>;
+  TcGemmParams p;
+  if (!encode_2d(dev, &p.tmap_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, g.a, (uint64_t)g.inner, (uint64_t)g.rows,
+                 (uint64_t)g.inner * 2, TC_BK, L::HALF_ROWS, CU_TENSOR_MAP_SWIZZLE_128B))
+    return set_error(PK_E_CUDA, "cuTensorMapEncodeTiled failed for the activation operand");
+  const uint64_t words_per_k = (uint64_t)g.columns * BITS / 32;
+  if (!encode_2d(dev, &p.tmap_codes, CU_TENSOR_MAP_DATA_TYPE_UINT32, g.codes, words_per_k, (uint64_t)g.inner,
+                 words_per_k * 4, L::WORDS_PER_ROW, TC_BK, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return set_error(PK_E_CUDA, "cuTensorMapEncodeTiled failed for the packed codes");
+  p.palette = static_cast<const uint16_t*>(g.palette);
+  p.bias = g.bias;
+  p.residual = static_cast<const __half*>(g.residual);
+  p.out = static_cast<__half*>(g.c);
+  p.status = dev.status;
+  p.rows = (int)g.rows;
+  p.inner = (int)g.inner;
+  p.columns = (int)g.columns;
+  p.groups = g.groups;
+  p.group_cols = (int)g.group_cols;
+  p.res_scale = g.residual_scale;
+  p.m_tiles = (int)((g.rows + L::T - 1) / L::T);
+  p.n_tiles = (int)(g.columns / TC_BM);
+  const int epi = g.has_residual ? EPI_RESIDUAL : (g.bias ? EPI_BIAS : EPI_PLAIN);
+#define PK_TC2(E, A) launch_tc2_spec<BN_MMA, NSUB, BITS, E, A>(dev, p, stream)
+  switch (epi * 3 + g.act) {
+    case EPI_PLAIN * 3 + PK_ACT_NONE: return PK_TC2(EPI_PLAIN, PK_ACT_NONE);
+    case EPI_PLAIN * 3 + PK_ACT_SILU: return PK_TC2(EPI_PLAIN, PK_ACT_SILU);
+    case EPI_PLAIN * 3 + PK_ACT_RELU: return PK_TC2(EPI_PLAIN, PK_ACT_RELU);
+    case EPI_BIAS * 3 + PK_ACT_NONE: return PK_TC2(EPI_BIAS, PK_ACT_NONE);
+    case EPI_BIAS * 3 + PK_ACT_SILU: return PK_TC2(EPI_BIAS, PK_ACT_SILU);
+    case EPI_BIAS * 3 + PK_ACT_RELU: return PK_TC2(EPI_BIAS, PK_ACT_RELU);
+    case EPI_RESIDUAL * 3 + PK_ACT_NONE: return PK_TC2(EPI_RESIDUAL, PK_ACT_NONE);
+    case EPI_RESIDUAL * 3 + PK_ACT_SILU: return PK_TC2(EPI_RESIDUAL, PK_ACT_SILU);
+    default: return PK_TC2(EPI_RESIDUAL, PK_ACT_RELU);
+  }
+#undef PK_TC2
+}
+
+// Tile choice: minimise (waves of persistent CTAs or CTA pairs) x (time per
+// k-stage).  The stage time model is per SM: a fixed decode cost for the
+// 128 x 64 weight tile plus a cost per token of the tile held by the SM
+// (activation TMA write, tensor-core reads), floored by the tensor-core time
+// (2 cycles per token for 128 features x 64 k).  Single-CTA tiles hold BN
+// tokens per SM; a CTA pair's T-token tile puts T/2 on each SM and decodes
+// once for all T.
+// Returns the token tile, negated for the CTA-pair kernel.
+constexpr double kStageDecode = 1100.0, kStagePerToken = 2.4;
+static double stage_cost(int tokens_per_sm, int mma_tokens) {
+  return std::max(kStageDecode + kStagePerToken * tokens_per_sm, 2.0 * mma_tokens);
+}
+
+static int choose_tile(const DeviceCtx& dev, const GemmArgs& g, bool allow_single, bool allow_pair) {
+  if (g.rows <= 128 && allow_single) return 128;
+  const int n_tiles = (int)(g.columns / TC_BM);
+  int best = allow_single ? 256 : -256;
+  double best_cost = 1e30;
+  if (allow_single)
+    for (int bn : {256, 192, 128}) {
+      const int64_t tiles = (g.rows + bn - 1) / bn * n_tiles;
+      const int64_t waves = (tiles + dev.sm_count - 1) / dev.sm_count;
+      const double cost = (double)waves * stage_cost(bn, bn);
+      if (cost < best_cost - 1e-9) best_cost = cost, best = bn;
+    }
+  if (allow_pair)
+    for (int t : {512, 384, 256}) {
+      const int64_t tiles = (g.rows + t - 1) / t * (n_tiles / 2);
+      const int64_t waves = (tiles + dev.sm_count / 2 - 1) / (dev.sm_count / 2);
+      const double cost = (double)waves * stage_cost(t / 2, t);
+      if (cost < best_cost - 1e-9) best_cost = cost, best = -t;
+    }
   return best;
 }
 
 int launch_gemm_tc(const DeviceCtx& dev, const GemmArgs& g, cudaStream_t stream, int forced_bn) {
   if (!gemm_tc_supported(g)) return set_error(PK_E_SHAPE, "shape not supported by the tensor-core GEMM");
-  const int bn = forced_bn ? forced_bn : choose_bn(dev, g);
-  if (bn == 256) return g.bits == 5 ? launch_tc<256, 5>(dev, g, stream) : launch_tc<256, 6>(dev, g, stream);
-  if (bn == 192) return g.bits == 5 ? launch_tc<192, 5>(dev, g, stream) : launch_tc<192, 6>(dev, g, stream);
-  return g.bits == 5 ? launch_tc<128, 5>(dev, g, stream) : launch_tc<128, 6>(dev, g, stream);
+  // Route 3 keeps to single-CTA tiles, route 4 to CTA pairs (where N tiles
+  // by 256); otherwise the cost model picks.  A tile forced through
+  // pk_debug_set_gemm_tile overrides both.
+  const bool allow_pair = g_gemm_route != 3 && g.columns % (2 * TC_BM) == 0;
+  const bool allow_single = g_gemm_route != 4 || !allow_pair;
+  int bn = forced_bn ? forced_bn : g_gemm_tile ? g_gemm_tile : choose_tile(dev, g, allow_single, allow_pair);
+  if (bn < 0 && !allow_pair) bn = 256;
+  const bool b5 = g.bits == 5;
+  switch (bn) {
+    case -512: return b5 ? launch_tc2<256, 2, 5>(dev, g, stream) : launch_tc2<256, 2, 6>(dev, g, stream);
+    case -384: return b5 ? launch_tc2<192, 2, 5>(dev, g, stream) : launch_tc2<192, 2, 6>(dev, g, stream);
+    case -256: return b5 ? launch_tc2<256, 1, 5>(dev, g, stream) : launch_tc2<256, 1, 6>(dev, g, stream);
+    case 256: return b5 ? launch_tc<256, 5>(dev, g, stream) : launch_tc<256, 6>(dev, g, stream);
+    case 192: return b5 ? launch_tc<192, 5>(dev, g, stream) : launch_tc<192, 6>(dev, g, stream);
+    case 128: return b5 ? launch_tc<128, 5>(dev, g, stream) : launch_tc<128, 6>(dev, g, stream);
+    default: return set_error(PK_E_INVALID, "unknown GEMM tile");
+  }
 }
 
 }  // namespace pk

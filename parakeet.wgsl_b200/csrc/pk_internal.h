@@ -73,6 +73,7 @@ int launch_subsampling_time_mask(int precision, int batch, int height, int width
 // Debug / test knob: 0 = automatic kernel choice, 1 = force the SIMT GEMM,
 // 2 = force the tensor-core GEMM (fails if the shape is unsupported).
 extern int g_gemm_route;
+extern int g_gemm_tile;
 // Debug / test knob: 0 = automatic (tensor cores for FP16), 1 = CUDA-core attention.
 extern int g_attention_route;
 

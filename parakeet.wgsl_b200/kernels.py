@@ -522,8 +522,17 @@ class SubsamplingTimeMaskKernel:
 
 
 def set_gemm_route(route: str) -> None:
-    """Test hook: "auto", "simt" (CUDA cores) or "tensor" (tcgen05)."""
-    _lib.call("pk_debug_set_gemm_route", {"auto": 0, "simt": 1, "tensor": 2}[route])
+    """Test hook: "auto", "simt" (CUDA cores), "tensor" (tcgen05),
+    "tensor-single" (tcgen05, single-CTA tiles only) or "tensor-pair"
+    (tcgen05 CTA pairs wherever N is a multiple of 256)."""
+    routes = {"auto": 0, "simt": 1, "tensor": 2, "tensor-single": 3, "tensor-pair": 4}
+    _lib.call("pk_debug_set_gemm_route", routes[route])
+
+
+def set_gemm_tile(tile: int) -> None:
+    """Test hook: force the tensor-core GEMM token tile (0 = automatic;
+    128/192/256 single-CTA; -256/-384/-512 CTA pair)."""
+    _lib.call("pk_debug_set_gemm_tile", int(tile))
 
 
 def set_attention_route(route: str) -> None:

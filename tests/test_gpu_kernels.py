@@ -109,6 +109,39 @@ def test_fp16_tensor_core_gemm(pk, oracle, device, case):
     assert rel(out, ref) < FP16_TOL
 
 
+PAIR_CASES = [c for c in GEMM_CASES if c[2] % 256 == 0] + [
+    (6016, 1024, 1024, 5, 1, "none", False, 1.0),  # C3 o_proj shape, 47 row tiles of 128
+    (3000, 4096, 1024, 6, 1, "none", True, None),  # 6-bit, bias, K = 4096, ragged rows
+]
+
+
+@pytest.mark.parametrize("tile", [-256, -384, -512])
+@pytest.mark.parametrize("case", PAIR_CASES)
+def test_fp16_cta_pair_gemm(pk, oracle, device, case, tile):
+    """The cta_group::2 kernel (256 features per CTA pair, half of a 256-,
+    384- or 512-token tile per CTA, one or two MMAs per decoded weight stage)
+    against the oracle's wide mode and the single-CTA kernel."""
+    rows, inner, columns, bits, groups, act, bias, rs = case
+    a, codes, lut, b, r = _gemm_inputs(pk, case, "fp16", 5 * rows + columns)
+    kw = dict(bias=b, residual=r, residual_scale=rs or 1.0, activation=act)
+    try:
+        pk.kernels.set_gemm_tile(tile)
+        pair = gemm(pk, device, a, codes, lut, bits, columns, **kw)
+        pair2 = gemm(pk, device, a, codes, lut, bits, columns, **kw)
+        pk.kernels.set_gemm_tile(0)
+        pk.kernels.set_gemm_route("tensor-single")
+        single = gemm(pk, device, a, codes, lut, bits, columns, **kw)
+    finally:
+        pk.kernels.set_gemm_tile(0)
+        pk.kernels.set_gemm_route("auto")
+    assert device.status() == 0
+    np.testing.assert_array_equal(pair.view(np.uint16), pair2.view(np.uint16))  # deterministic
+    assert rel(pair, single) < 1e-3
+    if rows <= 1024:
+        wide = oracle.palette_gemm(a, codes, lut, bits, columns, acc_mode=1, **kw)
+        assert rel(pair, wide) < WIDE_TOL
+
+
 @pytest.mark.parametrize("case", GEMM_CASES[:6])
 def test_fp16_simt_gemm_matches_oracle_wide(pk, oracle, device, case):
     rows, inner, columns, bits, groups, act, bias, rs = case
