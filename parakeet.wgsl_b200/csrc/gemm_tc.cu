@@ -29,6 +29,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cmath>
 
 #include "pk_common.cuh"
 #include "pk_internal.h"
@@ -43,7 +44,11 @@ constexpr int TC_FIRST_EPI_WARP = 2 + TC_DECODE_WARPS;  // 10: warps 10..13 cove
 constexpr int TC_THREADS = (TC_FIRST_EPI_WARP + 4) * 32;  // 448
 constexpr int TC_EPI_THREADS = 128;
 
-enum { EPI_PLAIN = 0, EPI_BIAS = 1, EPI_RESIDUAL = 2 };
+// EPI_RESIDUAL adds res_scale * acc to a residual loaded in the epilogue;
+// EPI_RESADD folds the residual into the accumulator instead (residual
+// k-steps, see the kernels) and only scales: used whenever 1/res_scale is a
+// power of two and no activation follows, so both kernels round alike.
+enum { EPI_PLAIN = 0, EPI_BIAS = 1, EPI_RESIDUAL = 2, EPI_RESADD = 3 };
 
 struct TcGemmParams {
   CUtensorMap tmap_a;       // activations [M, K] f16, box {64, BN}, 128B swizzle
@@ -57,6 +62,8 @@ struct TcGemmParams {
   int groups, group_cols;
   float res_scale;
   int m_tiles, n_tiles;
+  CUtensorMap tmap_res;     // CTA-pair kernel: residual [M, N] f16, box {64, T/2}, 128B swizzle
+  uint32_t res_inv_h;       // CTA-pair kernel: f16 bits of 1 / res_scale (a power of two)
 };
 
 template <int BN, int BITS>
@@ -118,20 +125,13 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
                : "memory");
 }
 
-// Decode one packed group (fixed k, CPG consecutive features starting at
-// feature-in-tile `f0`) into the MN-major SW128 weight tile.
+// Store CPG weights (fixed k, consecutive features from feature-in-tile `f0`,
+// f16 pairs) into the MN-major SW128 weight tile.
 // Tile layout: atom(n_block, k_group) at n_block * 8192 + k_group * 1024;
 // row (k % 8) at 128 B; 16-byte chunk c (features 8c..8c+7 of the 64-wide
 // block) at physical chunk c ^ (k % 8).
-template <int BITS>
-__device__ __forceinline__ void decode_group(const uint32_t* src, const uint8_t* lut, uint32_t goff,
-                                             uint32_t w_stage, int k, int f0) {
-  constexpr int WPG = BITS == 5 ? 5 : 3, CPG = BITS == 5 ? 32 : 16;
-  uint32_t words[WPG];
-#pragma unroll
-  for (int j = 0; j < WPG; ++j) words[j] = src[j];
-  uint32_t packed[CPG / 2];
-  DecodePairs<BITS, 0, CPG>::run(words, lut, goff, packed);
+template <int CPG>
+__device__ __forceinline__ void store_group(const uint32_t (&packed)[CPG / 2], uint32_t w_stage, int k, int f0) {
   const int r = k & 7;
   const uint32_t row = w_stage + (uint32_t)((f0 >> 6) * 8192 + (k >> 3) * 1024 + r * 128);
   const int c0 = (f0 & 63) >> 3;
@@ -142,13 +142,43 @@ __device__ __forceinline__ void decode_group(const uint32_t* src, const uint8_t*
   }
 }
 
+// Decode one packed group (fixed k, CPG consecutive features starting at
+// feature-in-tile `f0`) into the weight tile.
+template <int BITS>
+__device__ __forceinline__ void decode_group(const uint32_t* src, const uint8_t* lut, uint32_t goff,
+                                             uint32_t w_stage, int k, int f0) {
+  constexpr int WPG = BITS == 5 ? 5 : 3, CPG = BITS == 5 ? 32 : 16;
+  uint32_t words[WPG];
+#pragma unroll
+  for (int j = 0; j < WPG; ++j) words[j] = src[j];
+  uint32_t packed[CPG / 2];
+  DecodePairs<BITS, 0, CPG>::run(words, lut, goff, packed);
+  store_group<CPG>(packed, w_stage, k, f0);
+}
+
+// Identity block of the residual k-steps (CTA-pair kernel): weight (k, f) of
+// this group is `inv` where f == fsel, else zero.
+template <int CPG>
+__device__ __forceinline__ void identity_group(uint32_t inv, int fsel, uint32_t w_stage, int k, int f0) {
+  uint32_t packed[CPG / 2];
+#pragma unroll
+  for (int i = 0; i < CPG / 2; ++i)
+    packed[i] = (f0 + 2 * i == fsel ? inv : 0u) | (f0 + 2 * i + 1 == fsel ? inv << 16 : 0u);
+  store_group<CPG>(packed, w_stage, k, f0);
+}
+
 template <int ACT>
 __device__ __forceinline__ float activate(float v) {
   if constexpr (ACT == PK_ACT_SILU) {
-    // v / (1 + exp(-clamp(v, -20, 20))) (gemm.ts:2018-2032), fast intrinsics:
-    // the result is rounded to f16, far coarser than their error.
-    const float b = fminf(fmaxf(v, -20.0f), 20.0f);
-    return __fdividef(v, 1.0f + __expf(-b));
+    // SiLU v * sigmoid(v) (gemm.ts:2018-2032 writes v / (1 + exp(-v)) with v
+    // clamped inside exp) through sigmoid(v) = (1 + tanh(v/2)) / 2:
+    // h + h * tanh(h), h = v/2, one special-function op per element (the
+    // hardware tanh approximation, absolute error below 2^-10) where
+    // exp + divide take two.  The special-function unit bounds this epilogue.
+    const float h = 0.5f * v;
+    float t;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(h));
+    return fmaf(h, t, h);
   } else if constexpr (ACT == PK_ACT_RELU) {
     return fmaxf(v, 0.0f);
   } else {
@@ -176,6 +206,27 @@ __device__ __forceinline__ void epilogue_run(const uint32_t (&r)[32], float bias
       if constexpr (EPI == EPI_BIAS) v += bias_v;
       v = activate<ACT>(v);
       if constexpr (EPI == EPI_RESIDUAL) v = __half2float(rv[j]) + res_scale * v;
+      if constexpr (EPI == EPI_RESADD) v *= res_scale;
+      out[(size_t)j * ld] = __float2half_rn(v);
+    }
+  }
+}
+
+// CTA-pair epilogue of `left` consecutive tokens of one output feature (all
+// 32 when FULL, with no per-element predicate).  The CTA-pair kernel only
+// takes the folded residual (EPI_RESADD), which scales.
+template <int EPI, int ACT, bool FULL>
+__device__ __forceinline__ void epilogue_store(const uint32_t (&r)[32], float bias_v, __half* __restrict__ out,
+                                               float res_scale, int ld, int left) {
+  static_assert(EPI != EPI_RESIDUAL, "the CTA-pair kernel folds the residual");
+  static_assert(EPI != EPI_RESADD || ACT == PK_ACT_NONE, "the folded residual admits no activation");
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if (FULL || j < left) {
+      float v = __uint_as_float(r[j]);
+      if constexpr (EPI == EPI_BIAS) v += bias_v;
+      if constexpr (EPI == EPI_RESADD) v *= res_scale;
+      v = activate<ACT>(v);
       out[(size_t)j * ld] = __float2half_rn(v);
     }
   }
@@ -230,7 +281,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_palette_gemm_kernel(const __
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int kb_count = p.inner / TC_BK;
+  // EPI_RESADD: KR extra k-steps first with B = the residual tile (the
+  // tile's 128 output features as K) and A = 1/res_scale times the identity,
+  // so the accumulator starts at residual / res_scale.
+  constexpr int KR = EPI == EPI_RESADD ? TC_BM / TC_BK : 0;
+  const int kb_count = p.inner / TC_BK + KR;
   const int num_tiles = p.m_tiles * p.n_tiles;
 
   if (warp == 0) {
@@ -250,10 +305,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_palette_gemm_kernel(const __
             ok = false;
             break;
           }
+          if (kb < KR) {
+            mbar_arrive_expect_tx(&full_tma[s], L::A_BYTES);
+            tma_load_2d(sA + s * L::A_BYTES, &p.tmap_res, &full_tma[s], n_tile * TC_BM + kb * TC_BK, m_tile * BN);
+            last_round[s] = (int)round;
+            continue;
+          }
           mbar_arrive_expect_tx(&full_tma[s], L::A_BYTES + L::CODE_BYTES);
-          tma_load_2d(sA + s * L::A_BYTES, &p.tmap_a, &full_tma[s], kb * TC_BK, m_tile * BN);
+          tma_load_2d(sA + s * L::A_BYTES, &p.tmap_a, &full_tma[s], (kb - KR) * TC_BK, m_tile * BN);
           tma_load_2d(sCodes + s * (L::CODE_BYTES / 4), &p.tmap_codes, &full_tma[s], n_tile * L::WORDS_PER_ROW,
-                      kb * TC_BK);
+                      (kb - KR) * TC_BK);
           last_round[s] = (int)round;
         }
       }
@@ -335,11 +396,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_palette_gemm_kernel(const __
           ok = false;
           break;
         }
-        const uint32_t* codes = sCodes + s * (L::CODE_BYTES / 4) + k * L::WORDS_PER_ROW;
         const uint32_t w_stage = smem_addr(sW + s * L::W_BYTES);
+        if (kb < KR) {
+          // Residual feature kb*64 + k of the tile carries weight 1/res_scale.
 #pragma unroll
-        for (int j = 0; j < GROUPS_PER_LANE; ++j)
-          decode_group<BITS>(codes + (f0[j] / L::CPG) * L::WPG, lut, goff[j], w_stage, k, f0[j]);
+          for (int j = 0; j < GROUPS_PER_LANE; ++j)
+            identity_group<L::CPG>(p.res_inv_h, kb * TC_BK + k, w_stage, k, f0[j]);
+        } else {
+          const uint32_t* codes = sCodes + s * (L::CODE_BYTES / 4) + k * L::WORDS_PER_ROW;
+#pragma unroll
+          for (int j = 0; j < GROUPS_PER_LANE; ++j)
+            decode_group<BITS>(codes + (f0[j] / L::CPG) * L::WPG, lut, goff[j], w_stage, k, f0[j]);
+        }
         // Each lane makes its generic-proxy stores visible to the tensor core
         // (async proxy); the warp's lanes are ordered by __syncwarp, and one
         // lane's release-arrive covers the warp.
@@ -507,7 +575,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc2_palette_gemm_kernel(const _
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int kb_count = p.inner / TC_BK;
+  // Residual GEMMs run KR extra k-steps first: B = the residual tile (the
+  // pair's 256 output features as K), A = 1/res_scale times the identity
+  // block of this CTA's features, so the accumulator starts at
+  // residual / res_scale and the epilogue's res_scale * acc is
+  // residual + res_scale * (A . W), exactly for a power-of-two scale.
+  constexpr int KR = EPI == EPI_RESADD ? 2 * TC_BM / TC_BK : 0;
+  const int kb_count = p.inner / TC_BK + KR;
   const int pair_n_tiles = p.n_tiles / 2;  // 256-feature tiles
   const int num_tiles = p.m_tiles * pair_n_tiles;
   const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
@@ -530,12 +604,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc2_palette_gemm_kernel(const _
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full_c[s], L::CODE_BYTES);
-          tma_load_2d(sCodes + s * (L::CODE_BYTES / 4), &p.tmap_codes, &full_c[s], n_tile * L::WORDS_PER_ROW,
-                      kb * TC_BK);
           if (leader) mbar_arrive_expect_tx(&full_b[s], 2 * L::A_BYTES);
-          tma_load_2d_pair(sA + s * L::A_BYTES, &p.tmap_a, mapa_shared(smem_addr(&full_b[s]), 0), kb * TC_BK,
-                           m_tile * T + (int)rank * L::HALF_ROWS);
+          const uint32_t full_b_leader = mapa_shared(smem_addr(&full_b[s]), 0);
+          const int y = m_tile * T + (int)rank * L::HALF_ROWS;
+          if (kb < KR) {
+            mbar_arrive(&full_c[s]);  // no code tile: the decoders write an identity block
+            tma_load_2d_pair(sA + s * L::A_BYTES, &p.tmap_res, full_b_leader, np * 2 * TC_BM + kb * TC_BK, y);
+          } else {
+            mbar_arrive_expect_tx(&full_c[s], L::CODE_BYTES);
+            tma_load_2d(sCodes + s * (L::CODE_BYTES / 4), &p.tmap_codes, &full_c[s], n_tile * L::WORDS_PER_ROW,
+                        (kb - KR) * TC_BK);
+            tma_load_2d_pair(sA + s * L::A_BYTES, &p.tmap_a, full_b_leader, (kb - KR) * TC_BK, y);
+          }
           last_round[s] = (int)round;
         }
       }
@@ -644,11 +724,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc2_palette_gemm_kernel(const _
           ok = false;
           break;
         }
-        const uint32_t* codes = sCodes + s * (L::CODE_BYTES / 4) + k * L::WORDS_PER_ROW;
         const uint32_t w_stage = smem_addr(sW + s * L::W_BYTES);
+        if (kb < KR) {
+          // Residual feature kb*64 + k of the pair is this CTA's feature
+          // kb*64 + k - 128*rank.
+          const int fsel = kb * TC_BK + k - (int)rank * TC_BM;
 #pragma unroll
-        for (int j = 0; j < GROUPS_PER_LANE; ++j)
-          decode_group<BITS>(codes + (f0[j] / L::CPG) * L::WPG, lut, goff[j], w_stage, k, f0[j]);
+          for (int j = 0; j < GROUPS_PER_LANE; ++j) identity_group<L::CPG>(p.res_inv_h, fsel, w_stage, k, f0[j]);
+        } else {
+          const uint32_t* codes = sCodes + s * (L::CODE_BYTES / 4) + k * L::WORDS_PER_ROW;
+#pragma unroll
+          for (int j = 0; j < GROUPS_PER_LANE; ++j)
+            decode_group<BITS>(codes + (f0[j] / L::CPG) * L::WPG, lut, goff[j], w_stage, k, f0[j]);
+        }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
@@ -667,39 +755,41 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc2_palette_gemm_kernel(const _
     const int q = warp & 3;
     const uint32_t tm_empty_leader = mapa_shared(smem_addr(tm_empty), 0);
     const uint32_t payload_leader = mapa_shared(signal_payload, 0);
+    constexpr int NCH = T / 32;
     int tile_iter = 0;
     for (int tile = pair; tile < num_tiles; tile += num_pairs, ++tile_iter) {
       const int acc = tile_iter % L::ACC_BUFS;
       const uint32_t acc_round = (uint32_t)(tile_iter / L::ACC_BUFS);
+      const int np = tile % pair_n_tiles, m_tile = tile / pair_n_tiles;
+      const int n0 = (np * 2 + (int)rank) * TC_BM + q * 32;
+      const int m0 = m_tile * T;
+      const int ld = p.columns;
       if (!__all_sync(0xffffffffu,
                       mbar_wait(&tm_full[acc], acc_round & 1, abort_flag, p.status, PK_STATUS_TIMEOUT_EPILOGUE)))
         break;
       tc_fence_after();
-      const int np = tile % pair_n_tiles, m_tile = tile / pair_n_tiles;
-      const int n = (np * 2 + (int)rank) * TC_BM + q * 32 + lane;
-      const int m0 = m_tile * T;
+      const int n = n0 + lane;
       const float bias_v = EPI == EPI_BIAS ? __ldg(p.bias + n) : 0.0f;
       const uint32_t t_base = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * T);
-      const int ld = p.columns;
       // Column c of MMA j's accumulator is B row c of that MMA: row
       // j*SUB_ROWS + c of CTA 0's half (c < SUB_ROWS), else row
       // j*SUB_ROWS + c - SUB_ROWS of CTA 1's half (tokens from m0 + T/2).
-#pragma unroll 1
-      for (int col = 0; col < T; col += 32) {
-        const int j = col / BN_MMA, c = col % BN_MMA;
-        const int token0 =
-            m0 + (c < L::SUB_ROWS ? j * L::SUB_ROWS + c : L::HALF_ROWS + j * L::SUB_ROWS + c - L::SUB_ROWS);
-        const int left = p.rows - token0;
-        if (left <= 0) continue;
+      auto chunk_token = [&](int ci) {
+        const int col = ci * 32, j = col / BN_MMA, c = col % BN_MMA;
+        return m0 + (c < L::SUB_ROWS ? j * L::SUB_ROWS + c : L::HALF_ROWS + j * L::SUB_ROWS + c - L::SUB_ROWS);
+      };
+#pragma unroll 2
+      for (int ci = 0; ci < NCH; ++ci) {
+        const int token0 = chunk_token(ci);
         uint32_t r[32];
-        tc_ld_32x32b_x32(t_base + (uint32_t)col, r);
+        tc_ld_32x32b_x32(t_base + (uint32_t)(ci * 32), r);
         tc_wait_ld();
-        const size_t base = (size_t)token0 * ld + n;
-        const __half* res = EPI == EPI_RESIDUAL ? p.residual + base : nullptr;
+        const int left = p.rows - token0;
+        __half* out = p.out + (size_t)token0 * ld + n;
         if (left >= 32)
-          epilogue_run<EPI, ACT, 32>(r, bias_v, res, p.out + base, ld, p.res_scale, 32);
-        else
-          epilogue_run<EPI, ACT, 31>(r, bias_v, res, p.out + base, ld, p.res_scale, left);
+          epilogue_store<EPI, ACT, true>(r, bias_v, out, p.res_scale, ld, 32);
+        else if (left > 0)
+          epilogue_store<EPI, ACT, false>(r, bias_v, out, p.res_scale, ld, left);
       }
       tc_fence_before();
       __syncwarp();
@@ -762,6 +852,24 @@ static int launch_tc_spec(const DeviceCtx& dev, const TcGemmParams& p, cudaStrea
   return cuda_error(cudaGetLastError(), "tc_palette_gemm launch");
 }
 
+// Whether the residual is folded into the accumulator as residual / scale
+// (EPI_RESADD): exact only when 1/scale is a power of two that f16 holds as a
+// normal number; no activation may follow the residual (the encoder's
+// residual GEMMs have none), and TMA needs a 16-byte aligned base.  The
+// CTA-pair kernel only takes residuals that fold.
+static bool residual_folds(const GemmArgs& g) {
+  if (!g.has_residual || g.act != PK_ACT_NONE || (reinterpret_cast<uintptr_t>(g.residual) & 15) != 0) return false;
+  int e = 0;
+  const float m = std::frexp(g.residual_scale, &e);  // scale = m * 2^e, m in [0.5, 1)
+  return m == 0.5f && e >= -13 && e <= 15;           // 1/scale = 2^(1-e) in [2^-14, 2^14]
+}
+
+static bool encode_residual(const DeviceCtx& dev, const GemmArgs& g, TcGemmParams& p, uint32_t box_rows) {
+  p.res_inv_h = __half_as_ushort(__float2half_rn(1.0f / g.residual_scale));
+  return encode_2d(dev, &p.tmap_res, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, g.residual, (uint64_t)g.columns,
+                   (uint64_t)g.rows, (uint64_t)g.columns * 2, TC_BK, box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
 template <int BN, int BITS>
 static int launch_tc(const DeviceCtx& dev, const GemmArgs& g, cudaStream_t stream) {
   using L = TcLayout<BN, BITS>;
@@ -786,9 +894,13 @@ static int launch_tc(const DeviceCtx& dev, const GemmArgs& g, cudaStream_t strea
   p.res_scale = g.residual_scale;
   p.m_tiles = (int)((g.rows + BN - 1) / BN);
   p.n_tiles = (int)(g.columns / TC_BM);
+  const bool fold = residual_folds(g);
+  if (fold && !encode_residual(dev, g, p, BN))
+    return set_error(PK_E_CUDA, "cuTensorMapEncodeTiled failed for the residual operand");
+  if (fold) return launch_tc_spec<BN, BITS, EPI_RESADD, PK_ACT_NONE>(dev, p, stream);
   const int epi = g.has_residual ? EPI_RESIDUAL : (g.bias ? EPI_BIAS : EPI_PLAIN);
   // The epilogues the encoder uses (gemm.ts:204-356): SiLU plain, plain,
-  // residual, bias, bias + ReLU; the rest of the 3 x 3 grid for general callers.
+  // folded residual, bias, bias + ReLU; the rest of the grid for general callers.
   switch (epi * 3 + g.act) {
     case EPI_PLAIN * 3 + PK_ACT_NONE: return launch_tc_spec<BN, BITS, EPI_PLAIN, PK_ACT_NONE>(dev, p, stream);
     case EPI_PLAIN * 3 + PK_ACT_SILU: return launch_tc_spec<BN, BITS, EPI_PLAIN, PK_ACT_SILU>(dev, p, stream);
@@ -861,7 +973,10 @@ static int launch_tc2(const DeviceCtx& dev, const GemmArgs& g, cudaStream_t stre
   p.res_scale = g.residual_scale;
   p.m_tiles = (int)((g.rows + L::T - 1) / L::T);
   p.n_tiles = (int)(g.columns / TC_BM);
-  const int epi = g.has_residual ? EPI_RESIDUAL : (g.bias ? EPI_BIAS : EPI_PLAIN);
+  if (g.has_residual && !residual_folds(g)) return set_error(PK_E_INVALID, "CTA-pair GEMM: residual must fold");
+  if (g.has_residual && !encode_residual(dev, g, p, L::HALF_ROWS))
+    return set_error(PK_E_CUDA, "cuTensorMapEncodeTiled failed for the residual operand");
+  const int epi = g.has_residual ? EPI_RESADD : (g.bias ? EPI_BIAS : EPI_PLAIN);
 #define PK_TC2(E, A) launch_tc2_spec<BN_MMA, NSUB, BITS, E, A>(dev, p, stream)
   switch (epi * 3 + g.act) {
     case EPI_PLAIN * 3 + PK_ACT_NONE: return PK_TC2(EPI_PLAIN, PK_ACT_NONE);
@@ -870,43 +985,44 @@ static int launch_tc2(const DeviceCtx& dev, const GemmArgs& g, cudaStream_t stre
     case EPI_BIAS * 3 + PK_ACT_NONE: return PK_TC2(EPI_BIAS, PK_ACT_NONE);
     case EPI_BIAS * 3 + PK_ACT_SILU: return PK_TC2(EPI_BIAS, PK_ACT_SILU);
     case EPI_BIAS * 3 + PK_ACT_RELU: return PK_TC2(EPI_BIAS, PK_ACT_RELU);
-    case EPI_RESIDUAL * 3 + PK_ACT_NONE: return PK_TC2(EPI_RESIDUAL, PK_ACT_NONE);
-    case EPI_RESIDUAL * 3 + PK_ACT_SILU: return PK_TC2(EPI_RESIDUAL, PK_ACT_SILU);
-    default: return PK_TC2(EPI_RESIDUAL, PK_ACT_RELU);
+    case EPI_RESADD * 3 + PK_ACT_NONE: return PK_TC2(EPI_RESADD, PK_ACT_NONE);
+    default: return set_error(PK_E_INVALID, "CTA-pair GEMM: residual with an activation");
   }
 #undef PK_TC2
 }
 
-// Tile choice: minimise (waves of persistent CTAs or CTA pairs) x (time per
-// k-stage).  The stage time model is per SM: a fixed decode cost for the
-// 128 x 64 weight tile plus a cost per token of the tile held by the SM
-// (activation TMA write, tensor-core reads), floored by the tensor-core time
-// (2 cycles per token for 128 features x 64 k).  Single-CTA tiles hold BN
-// tokens per SM; a CTA pair's T-token tile puts T/2 on each SM and decodes
-// once for all T.
-// Returns the token tile, negated for the CTA-pair kernel.
-constexpr double kStageDecode = 1100.0, kStagePerToken = 2.4;
-static double stage_cost(int tokens_per_sm, int mma_tokens) {
-  return std::max(kStageDecode + kStagePerToken * tokens_per_sm, 2.0 * mma_tokens);
-}
 
+// Tile choice: minimise (waves of persistent CTAs or CTA pairs) x (time per
+// tile), with the tile time fitted to B200 measurements of the encoder's
+// shapes (cycles): single-CTA tiles run k-stages of 900 + 2 * BN with their
+// epilogue hidden behind the next tile (double-buffered TMEM) but for ~1200;
+// CTA-pair tiles of T tokens decode each weight stage once for all T, so a
+// stage costs 1100 + 1.3 * T for twice the features, but their accumulator
+// fills TMEM, so the epilogue (~25 * T) is not hidden.  The 256-token pair
+// tile measured no faster than the single-CTA one and is left to the test
+// hook.  Residual k-steps (no decode) count half a stage.
+// Returns the token tile, negated for the CTA-pair kernel.
 static int choose_tile(const DeviceCtx& dev, const GemmArgs& g, bool allow_single, bool allow_pair) {
   if (g.rows <= 128 && allow_single) return 128;
   const int n_tiles = (int)(g.columns / TC_BM);
-  int best = allow_single ? 256 : -256;
+  const double kb = (double)(g.inner / TC_BK);
+  const bool fold = residual_folds(g);
+  int best = allow_single ? 256 : -384;
   double best_cost = 1e30;
   if (allow_single)
     for (int bn : {256, 192, 128}) {
       const int64_t tiles = (g.rows + bn - 1) / bn * n_tiles;
       const int64_t waves = (tiles + dev.sm_count - 1) / dev.sm_count;
-      const double cost = (double)waves * stage_cost(bn, bn);
+      const double stages = kb + (fold ? 0.5 * TC_BM / TC_BK : 0.0);
+      const double cost = (double)waves * (stages * (900.0 + 2.0 * bn) + 1200.0);
       if (cost < best_cost - 1e-9) best_cost = cost, best = bn;
     }
   if (allow_pair)
-    for (int t : {512, 384, 256}) {
+    for (int t : {512, 384}) {
       const int64_t tiles = (g.rows + t - 1) / t * (n_tiles / 2);
       const int64_t waves = (tiles + dev.sm_count / 2 - 1) / (dev.sm_count / 2);
-      const double cost = (double)waves * stage_cost(t / 2, t);
+      const double stages = kb + (fold ? 0.5 * 2 * TC_BM / TC_BK : 0.0);
+      const double cost = (double)waves * (stages * (1100.0 + 1.3 * t) + 25.0 * t);
       if (cost < best_cost - 1e-9) best_cost = cost, best = -t;
     }
   return best;
@@ -917,7 +1033,8 @@ int launch_gemm_tc(const DeviceCtx& dev, const GemmArgs& g, cudaStream_t stream,
   // Route 3 keeps to single-CTA tiles, route 4 to CTA pairs (where N tiles
   // by 256); otherwise the cost model picks.  A tile forced through
   // pk_debug_set_gemm_tile overrides both.
-  const bool allow_pair = g_gemm_route != 3 && g.columns % (2 * TC_BM) == 0;
+  const bool allow_pair =
+      g_gemm_route != 3 && g.columns % (2 * TC_BM) == 0 && (!g.has_residual || residual_folds(g));
   const bool allow_single = g_gemm_route != 4 || !allow_pair;
   int bn = forced_bn ? forced_bn : g_gemm_tile ? g_gemm_tile : choose_tile(dev, g, allow_single, allow_pair);
   if (bn < 0 && !allow_pair) bn = 256;

@@ -112,6 +112,8 @@ def test_fp16_tensor_core_gemm(pk, oracle, device, case):
 PAIR_CASES = [c for c in GEMM_CASES if c[2] % 256 == 0] + [
     (6016, 1024, 1024, 5, 1, "none", False, 1.0),  # C3 o_proj shape, 47 row tiles of 128
     (3000, 4096, 1024, 6, 1, "none", True, None),  # 6-bit, bias, K = 4096, ragged rows
+    (700, 1024, 1024, 5, 1, "none", False, 0.3),   # residual scale not a power of two: single-CTA path
+    (300, 1024, 2048, 5, 1, "silu", False, 0.5),   # activation before a residual: single-CTA path
 ]
 
 
