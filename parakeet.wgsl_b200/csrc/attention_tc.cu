@@ -33,8 +33,10 @@ constexpr int ABD = 80;       // BD columns per warp per chunk (16 + 63, padded)
 constexpr int ATHREADS = 128;
 constexpr int ASMEM = (2 * AKC + APR) * AS * 2 + 4 * 16 * ABD * 4;
 
+// Not volatile: no side effects, so the compiler may interleave independent
+// accumulator chains.
 __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
       "{%0, %1, %2, %3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -49,6 +51,15 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
 __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
                                                   uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+// Four 8x8 b16 matrices, row addresses from lanes 8m..8m+7 for matrix m:
+// thread (g, t) gets row g, columns 2t, 2t+1 of each -- the B fragment of
+// mma.m16n8k16 .col when the rows are keys (positions) and the columns dims.
+__device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                : "r"(addr));
 }
@@ -149,42 +160,60 @@ __global__ void __launch_bounds__(ATHREADS, 2) rel_attention_flash_kernel(
     if (!active) continue;
 
     // ---- BD for this warp's 16 queries x the chunk's 64 keys (+15 diagonal)
+    // Two passes of five independent 8-column tiles, k-steps outermost, so
+    // consecutive MMAs do not wait on one another's accumulators.
     const int wb = 48 - 16 * warp;  // this warp's first band row
-#pragma unroll 2
-    for (int nt = 0; nt < ABD / 8; ++nt) {
-      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      const __half* prow = Ps + (wb + nt * 8 + g) * AS + 2 * t;
 #pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(prow + ks * 16);
-        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(prow + ks * 16 + 8);
-        mma16816(acc, qv[ks], b0, b1);
+    for (int half = 0; half < 2; ++half) {
+      float acc[5][4];
+#pragma unroll
+      for (int u = 0; u < 5; ++u)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[u][e] = 0.0f;
+#pragma unroll
+      for (int ks = 0; ks < 8; ks += 2) {
+#pragma unroll
+        for (int u = 0; u < 5; ++u) {
+          uint32_t b0, b1, b2, b3;  // dims ks*16 + {0, 8, 16, 24} .. +7 of band rows (half*5+u)*8 ..
+          ldmatrix_x4(smem_addr(Ps + (wb + (half * 5 + u) * 8 + (lane & 7)) * AS + ks * 16 + (lane >> 3) * 8), b0,
+                      b1, b2, b3);
+          mma16816(acc[u], qv[ks], b0, b1);
+          mma16816(acc[u], qv[ks + 1], b2, b3);
+        }
       }
-      bd[g * ABD + nt * 8 + 2 * t] = acc[0];
-      bd[g * ABD + nt * 8 + 2 * t + 1] = acc[1];
-      bd[(g + 8) * ABD + nt * 8 + 2 * t] = acc[2];
-      bd[(g + 8) * ABD + nt * 8 + 2 * t + 1] = acc[3];
+#pragma unroll
+      for (int u = 0; u < 5; ++u) {
+        const int c = (half * 5 + u) * 8 + 2 * t;
+        *reinterpret_cast<float2*>(bd + g * ABD + c) = make_float2(acc[u][0], acc[u][1]);
+        *reinterpret_cast<float2*>(bd + (g + 8) * ABD + c) = make_float2(acc[u][2], acc[u][3]);
+      }
     }
     __syncwarp();
 
     // ---- AC + shifted BD, scale, mask; chunk max
     float s[AKC / 8][4];
+#pragma unroll
+    for (int nt = 0; nt < AKC / 8; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s[nt][e] = 0.0f;
+#pragma unroll
+    for (int ks = 0; ks < 8; ks += 2) {
+#pragma unroll
+      for (int nt = 0; nt < AKC / 8; ++nt) {
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4(smem_addr(Ks + (nt * 8 + (lane & 7)) * AS + ks * 16 + (lane >> 3) * 8), b0, b1, b2, b3);
+        mma16816(s[nt], qu[ks], b0, b1);
+        mma16816(s[nt], qu[ks + 1], b2, b3);
+      }
+    }
     float cm0 = -3.402823466e+38f, cm1 = -3.402823466e+38f;
 #pragma unroll
     for (int nt = 0; nt < AKC / 8; ++nt) {
-      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      const __half* krow = Ks + (nt * 8 + g) * AS + 2 * t;
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(krow + ks * 16);
-        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(krow + ks * 16 + 8);
-        mma16816(acc, qu[ks], b0, b1);
-      }
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int r = g + (e >> 1) * 8;          // row within the warp's 16 queries
         const int jl = nt * 8 + 2 * t + (e & 1); // key within the chunk
-        float v = (acc[e] + bd[r * ABD + jl + 15 - r]) * scale;
+        float v = (s[nt][e] + bd[r * ABD + jl + 15 - r]) * scale;
         if (j0 + jl >= valid) v = -3.402823466e+38f;
         s[nt][e] = v;
       }

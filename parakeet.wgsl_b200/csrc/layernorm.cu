@@ -11,14 +11,12 @@
 
 namespace pk {
 
-// Fast path: channels == 1024.  One warp per row, all of the row's 128-bit
-// loads issued before reducing (f16: 4 per lane, f32: 8); gamma/beta are
-// 128-bit L1-resident loads.  A small register footprint keeps every row of
-// a batch-32 launch resident at once (one wave), so HBM latency overlaps
-// across the whole launch.  One HBM read and one write of each row.
-template <typename T>
-constexpr int ln_rows() { return sizeof(T) == 2 ? 2 : 1; }
-
+// Fast path: channels == 1024.  One warp per row, the row's 128-bit loads
+// (f16: 4 per lane, f32: 8) all issued before reducing; gamma and beta are
+// staged once per CTA in shared memory (while the rows are in flight), so
+// the only global traffic is one read and one write of each row.  Small
+// CTAs and a small register footprint keep every row of a batch-32 launch
+// resident at once, so load latency overlaps across the whole launch.
 template <typename T>
 __device__ __forceinline__ void unpack16(const uint4& raw, float* v) {
   if constexpr (sizeof(T) == 2) {
@@ -36,74 +34,75 @@ __device__ __forceinline__ void unpack16(const uint4& raw, float* v) {
   }
 }
 
+constexpr int LN_WARPS = 8;
+
 template <typename T>
-__global__ void __launch_bounds__(256) layernorm1024_kernel(const T* __restrict__ x, const float* __restrict__ gamma,
-                                                            const float* __restrict__ beta, float eps,
-                                                            T* __restrict__ y, int64_t rows) {
+__global__ void __launch_bounds__(LN_WARPS * 32) layernorm1024_kernel(const T* __restrict__ x,
+                                                                    const float* __restrict__ gamma,
+                                                                    const float* __restrict__ beta, float eps,
+                                                                    T* __restrict__ y, int64_t rows) {
   constexpr int VEC = 16 / sizeof(T);        // elements per 16-byte load
   constexpr int LOADS = 1024 / (32 * VEC);   // loads per lane per row
+  __shared__ __align__(16) float s_gamma[1024], s_beta[1024];
   const int lane = threadIdx.x & 31;
-  constexpr int LN_ROWS = ln_rows<T>();
-  const int64_t row0 = ((int64_t)blockIdx.x * 8 + (threadIdx.x >> 5)) * LN_ROWS;
-  if (row0 >= rows) return;
-  uint4 raw[LN_ROWS][LOADS];
+  const int64_t row = (int64_t)blockIdx.x * LN_WARPS + (threadIdx.x >> 5);
+  uint4 raw[LOADS];
+  if (row < rows) {
+    const uint4* src = reinterpret_cast<const uint4*>(x + row * 1024);
 #pragma unroll
-  for (int r = 0; r < LN_ROWS; ++r) {
-    if (row0 + r < rows) {
-      const uint4* src = reinterpret_cast<const uint4*>(x + (row0 + r) * 1024);
+    for (int i = 0; i < LOADS; ++i) raw[i] = __ldg(src + i * 32 + lane);
+  }
+  for (int c = threadIdx.x * 4; c < 1024; c += LN_WARPS * 32 * 4) {
+    *reinterpret_cast<float4*>(s_gamma + c) = __ldg(reinterpret_cast<const float4*>(gamma + c));
+    *reinterpret_cast<float4*>(s_beta + c) = __ldg(reinterpret_cast<const float4*>(beta + c));
+  }
+  __syncthreads();
+  if (row >= rows) return;
+  float v[LOADS][VEC];
+  float sum = 0.0f, sq = 0.0f;
 #pragma unroll
-      for (int i = 0; i < LOADS; ++i) raw[r][i] = __ldg(src + i * 32 + lane);
+  for (int i = 0; i < LOADS; ++i) {
+    unpack16<T>(raw[i], v[i]);
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      sum += v[i][j];
+      sq = fmaf(v[i][j], v[i][j], sq);
     }
   }
 #pragma unroll
-  for (int r = 0; r < LN_ROWS; ++r) {
-    if (row0 + r >= rows) break;
-    float v[LOADS][VEC];
-    float sum = 0.0f, sq = 0.0f;
+  for (int o = 16; o > 0; o >>= 1) {
+    sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    sq += __shfl_xor_sync(0xffffffffu, sq, o);
+  }
+  const float inv = 1.0f / 1024.0f;
+  const float mean = sum * inv;
+  const float var = fmaxf(sq * inv - mean * mean, 0.0f);
+  const float rstd = 1.0f / sqrtf(var + eps);
+  uint4* dst = reinterpret_cast<uint4*>(y + row * 1024);
 #pragma unroll
-    for (int i = 0; i < LOADS; ++i) {
-      unpack16<T>(raw[r][i], v[i]);
+  for (int i = 0; i < LOADS; ++i) {
+    const int c0 = (i * 32 + lane) * VEC;
+    float o[VEC];
 #pragma unroll
-      for (int j = 0; j < VEC; ++j) {
-        sum += v[i][j];
-        sq = fmaf(v[i][j], v[i][j], sq);
-      }
+    for (int j = 0; j < VEC; j += 4) {
+      const float4 gg = *reinterpret_cast<const float4*>(s_gamma + c0 + j);
+      const float4 bb = *reinterpret_cast<const float4*>(s_beta + c0 + j);
+      o[j] = fmaf((v[i][j] - mean) * rstd, gg.x, bb.x);
+      o[j + 1] = fmaf((v[i][j + 1] - mean) * rstd, gg.y, bb.y);
+      o[j + 2] = fmaf((v[i][j + 2] - mean) * rstd, gg.z, bb.z);
+      o[j + 3] = fmaf((v[i][j + 3] - mean) * rstd, gg.w, bb.w);
     }
+    uint4 out;
+    if constexpr (sizeof(T) == 2) {
+      __half2* h = reinterpret_cast<__half2*>(&out);
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      sum += __shfl_xor_sync(0xffffffffu, sum, o);
-      sq += __shfl_xor_sync(0xffffffffu, sq, o);
+      for (int j = 0; j < 4; ++j) h[j] = __floats2half2_rn(o[2 * j], o[2 * j + 1]);
+    } else {
+      float* f = reinterpret_cast<float*>(&out);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) f[j] = o[j];
     }
-    const float inv = 1.0f / 1024.0f;
-    const float mean = sum * inv;
-    const float var = fmaxf(sq * inv - mean * mean, 0.0f);
-    const float rstd = 1.0f / sqrtf(var + eps);
-    uint4* dst = reinterpret_cast<uint4*>(y + (row0 + r) * 1024);
-#pragma unroll
-    for (int i = 0; i < LOADS; ++i) {
-      const int c0 = (i * 32 + lane) * VEC;
-      float o[VEC];
-#pragma unroll
-      for (int j = 0; j < VEC; j += 4) {
-        const float4 gg = __ldg(reinterpret_cast<const float4*>(gamma + c0 + j));
-        const float4 bb = __ldg(reinterpret_cast<const float4*>(beta + c0 + j));
-        o[j] = fmaf((v[i][j] - mean) * rstd, gg.x, bb.x);
-        o[j + 1] = fmaf((v[i][j + 1] - mean) * rstd, gg.y, bb.y);
-        o[j + 2] = fmaf((v[i][j + 2] - mean) * rstd, gg.z, bb.z);
-        o[j + 3] = fmaf((v[i][j + 3] - mean) * rstd, gg.w, bb.w);
-      }
-      uint4 out;
-      if constexpr (sizeof(T) == 2) {
-        __half2* h = reinterpret_cast<__half2*>(&out);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) h[j] = __floats2half2_rn(o[2 * j], o[2 * j + 1]);
-      } else {
-        float* f = reinterpret_cast<float*>(&out);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) f[j] = o[j];
-      }
-      dst[i * 32 + lane] = out;
-    }
+    dst[i * 32 + lane] = out;
   }
 }
 
@@ -152,14 +151,13 @@ int launch_layernorm(int precision, int64_t rows, int64_t channels, const void* 
   const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0;
   const bool params_aligned = ((reinterpret_cast<uintptr_t>(gamma) | reinterpret_cast<uintptr_t>(beta)) & 15) == 0;
   if (channels == 1024 && aligned && params_aligned) {
-    const int per_block = 8 * (precision == PK_FP16 ? ln_rows<__half>() : ln_rows<float>());
-    const unsigned blocks = (unsigned)((rows + per_block - 1) / per_block);
+    const unsigned blocks = (unsigned)((rows + LN_WARPS - 1) / LN_WARPS);
     if (precision == PK_FP16)
-      layernorm1024_kernel<__half><<<blocks, 256, 0, stream>>>(static_cast<const __half*>(x), gamma, beta, eps,
-                                                              static_cast<__half*>(y), rows);
+      layernorm1024_kernel<__half><<<blocks, LN_WARPS * 32, 0, stream>>>(
+          static_cast<const __half*>(x), gamma, beta, eps, static_cast<__half*>(y), rows);
     else
-      layernorm1024_kernel<float><<<blocks, 256, 0, stream>>>(static_cast<const float*>(x), gamma, beta, eps,
-                                                             static_cast<float*>(y), rows);
+      layernorm1024_kernel<float><<<blocks, LN_WARPS * 32, 0, stream>>>(
+          static_cast<const float*>(x), gamma, beta, eps, static_cast<float*>(y), rows);
   } else {
     if (precision == PK_FP16)
       layernorm_generic_kernel<__half><<<(unsigned)rows, 256, 0, stream>>>(
