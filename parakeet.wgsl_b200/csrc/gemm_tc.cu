@@ -212,23 +212,36 @@ __device__ __forceinline__ void epilogue_run(const uint32_t (&r)[32], float bias
   }
 }
 
-// CTA-pair epilogue of `left` consecutive tokens of one output feature (all
-// 32 when FULL, with no per-element predicate).  The CTA-pair kernel only
-// takes the folded residual (EPI_RESADD), which scales.
-template <int EPI, int ACT, bool FULL>
-__device__ __forceinline__ void epilogue_store(const uint32_t (&r)[32], float bias_v, __half* __restrict__ out,
-                                               float res_scale, int ld, int left) {
+// CTA-pair epilogue value of one accumulator element.  The CTA-pair kernel
+// only takes the folded residual (EPI_RESADD), which scales.
+template <int EPI, int ACT>
+__device__ __forceinline__ __half pair_epilogue_value(uint32_t r, float bias_v, float res_scale) {
   static_assert(EPI != EPI_RESIDUAL, "the CTA-pair kernel folds the residual");
   static_assert(EPI != EPI_RESADD || ACT == PK_ACT_NONE, "the folded residual admits no activation");
+  float v = __uint_as_float(r);
+  if constexpr (EPI == EPI_BIAS) v += bias_v;
+  if constexpr (EPI == EPI_RESADD) v *= res_scale;
+  return __float2half_rn(activate<ACT>(v));
+}
+
+// 32 accumulator columns of one output feature: columns e < split are tokens
+// tok_a + e, the rest tokens tok_b + e - split (a chunk crosses at most one
+// boundary between contiguous token runs); tokens >= rows are not stored.
+// The common case -- one run, all in range -- stores without predicates.
+template <int EPI, int ACT>
+__device__ __forceinline__ void pair_epilogue_chunk(const uint32_t (&r)[32], float bias_v, float res_scale,
+                                                    __half* __restrict__ col_out, int ld, int rows, int tok_a,
+                                                    int split, int tok_b) {
+  if (split == 32 && tok_a + 32 <= rows) {
+    __half* out = col_out + (size_t)tok_a * ld;
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    if (FULL || j < left) {
-      float v = __uint_as_float(r[j]);
-      if constexpr (EPI == EPI_BIAS) v += bias_v;
-      if constexpr (EPI == EPI_RESADD) v *= res_scale;
-      v = activate<ACT>(v);
-      out[(size_t)j * ld] = __float2half_rn(v);
-    }
+    for (int e = 0; e < 32; ++e) out[(size_t)e * ld] = pair_epilogue_value<EPI, ACT>(r[e], bias_v, res_scale);
+    return;
+  }
+#pragma unroll
+  for (int e = 0; e < 32; ++e) {
+    const int tok = e < split ? tok_a + e : tok_b + (e - split);
+    if (tok < rows) col_out[(size_t)tok * ld] = pair_epilogue_value<EPI, ACT>(r[e], bias_v, res_scale);
   }
 }
 
@@ -509,7 +522,8 @@ struct Tc2Layout {
   static constexpr uint32_t TMEM_COLS = ACC_BUFS * T <= 256 ? 256 : 512;
   static_assert(STAGES >= 3, "pipeline too shallow");
   static_assert(OFF_MISC % 16 == 0 && OFF_C % 128 == 0 && CODE_BYTES % 128 == 0, "TMA / bulk-copy alignment");
-  static_assert(SUB_ROWS % 32 == 0, "an epilogue chunk of 32 columns must not straddle the CTA halves");
+  static_assert(SUB_ROWS % 8 == 0 && SUB_ROWS >= 32, "MMA halves in whole 8-row swizzle atoms");
+  static_assert(T % 32 == 0, "epilogue chunks of 32 accumulator columns");
   static_assert(A_BYTES % 1024 == 0 && W_BYTES % 1024 == 0, "stage buffers must keep 1024B alignment");
   static_assert(ACC_BUFS * T <= 512, "TMEM holds 512 columns");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
@@ -773,23 +787,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc2_palette_gemm_kernel(const _
       const uint32_t t_base = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * T);
       // Column c of MMA j's accumulator is B row c of that MMA: row
       // j*SUB_ROWS + c of CTA 0's half (c < SUB_ROWS), else row
-      // j*SUB_ROWS + c - SUB_ROWS of CTA 1's half (tokens from m0 + T/2).
-      auto chunk_token = [&](int ci) {
-        const int col = ci * 32, j = col / BN_MMA, c = col % BN_MMA;
+      // j*SUB_ROWS + c - SUB_ROWS of CTA 1's half (tokens from m0 + T/2):
+      // runs of SUB_ROWS contiguous tokens, starting every SUB_ROWS columns.
+      auto col_token = [&](int col) {
+        const int j = col / BN_MMA, c = col - j * BN_MMA;
         return m0 + (c < L::SUB_ROWS ? j * L::SUB_ROWS + c : L::HALF_ROWS + j * L::SUB_ROWS + c - L::SUB_ROWS);
       };
 #pragma unroll 2
       for (int ci = 0; ci < NCH; ++ci) {
-        const int token0 = chunk_token(ci);
+        const int col0 = ci * 32;
+        const int split = min(32, (col0 / L::SUB_ROWS + 1) * L::SUB_ROWS - col0);
+        const int tok_a = col_token(col0);
+        const int tok_b = split < 32 ? col_token(col0 + split) : 0;
         uint32_t r[32];
-        tc_ld_32x32b_x32(t_base + (uint32_t)(ci * 32), r);
+        tc_ld_32x32b_x32(t_base + (uint32_t)col0, r);
         tc_wait_ld();
-        const int left = p.rows - token0;
-        __half* out = p.out + (size_t)token0 * ld + n;
-        if (left >= 32)
-          epilogue_store<EPI, ACT, true>(r, bias_v, out, p.res_scale, ld, 32);
-        else if (left > 0)
-          epilogue_store<EPI, ACT, false>(r, bias_v, out, p.res_scale, ld, left);
+        if (tok_a < p.rows || (split < 32 && tok_b < p.rows))
+          pair_epilogue_chunk<EPI, ACT>(r, bias_v, p.res_scale, p.out + n, ld, p.rows, tok_a, split, tok_b);
       }
       tc_fence_before();
       __syncwarp();
@@ -993,15 +1007,16 @@ static int launch_tc2(const DeviceCtx& dev, const GemmArgs& g, cudaStream_t stre
 
 
 // Tile choice: minimise (waves of persistent CTAs or CTA pairs) x (time per
-// tile), with the tile time fitted to B200 measurements of the encoder's
-// shapes (cycles): single-CTA tiles run k-stages of 900 + 2 * BN with their
-// epilogue hidden behind the next tile (double-buffered TMEM) but for ~1200;
-// CTA-pair tiles of T tokens decode each weight stage once for all T, so a
-// stage costs 1100 + 1.3 * T for twice the features, but their accumulator
-// fills TMEM, so the epilogue (~25 * T) is not hidden.  The 256-token pair
-// tile measured no faster than the single-CTA one and is left to the test
-// hook.  Residual k-steps (no decode) count half a stage.
-// Returns the token tile, negated for the CTA-pair kernel.
+// tile), with times fitted to B200 measurements of the encoder's shapes.  A
+// k-stage costs about the same whatever the token tile (the weight decode,
+// not the MMA, sets its pace): ~0.70 us for a single-CTA tile, ~0.78 us for a
+// CTA pair (twice the features, decoded in parallel), so larger token tiles
+// win per FLOP until wave quantization or the epilogue bites.  Single-CTA
+// tiles hide their epilogue behind the next tile (double-buffered TMEM,
+// ~0.6 us left); pair tiles of 384 / 512 tokens fill TMEM and expose it
+// (~5.1 / ~7.9 us).  Residual k-steps (no decode) count half a stage.  The
+// 256-token pair tile measured no faster than the single-CTA one and is left
+// to the test hook.  Returns the token tile, negated for the CTA-pair kernel.
 static int choose_tile(const DeviceCtx& dev, const GemmArgs& g, bool allow_single, bool allow_pair) {
   if (g.rows <= 128 && allow_single) return 128;
   const int n_tiles = (int)(g.columns / TC_BM);
@@ -1010,19 +1025,19 @@ static int choose_tile(const DeviceCtx& dev, const GemmArgs& g, bool allow_singl
   int best = allow_single ? 256 : -384;
   double best_cost = 1e30;
   if (allow_single)
-    for (int bn : {256, 192, 128}) {
+    for (int bn : {128, 192, 256}) {
       const int64_t tiles = (g.rows + bn - 1) / bn * n_tiles;
       const int64_t waves = (tiles + dev.sm_count - 1) / dev.sm_count;
       const double stages = kb + (fold ? 0.5 * TC_BM / TC_BK : 0.0);
-      const double cost = (double)waves * (stages * (900.0 + 2.0 * bn) + 1200.0);
+      const double cost = (double)waves * (stages * 0.70 + 0.6);
       if (cost < best_cost - 1e-9) best_cost = cost, best = bn;
     }
   if (allow_pair)
-    for (int t : {512, 384}) {
+    for (int t : {384, 512}) {
       const int64_t tiles = (g.rows + t - 1) / t * (n_tiles / 2);
       const int64_t waves = (tiles + dev.sm_count / 2 - 1) / (dev.sm_count / 2);
       const double stages = kb + (fold ? 0.5 * 2 * TC_BM / TC_BK : 0.0);
-      const double cost = (double)waves * (stages * (1100.0 + 1.3 * t) + 25.0 * t);
+      const double cost = (double)waves * (stages * 0.78 + (t == 384 ? 5.1 : 7.9));
       if (cost < best_cost - 1e-9) best_cost = cost, best = -t;
     }
   return best;
