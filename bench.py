@@ -47,6 +47,10 @@ UNIT = "audio-s/s"
 # Kernel launches of one encoder step: subsampling (conv0+dw2, pw3 GEMM, dw5,
 # pw6 GEMM, mask, flatten GEMM) + 24 x 15 layer dispatches + projector.
 LAUNCHES_PER_STEP = 6 + 24 * 15 + 1
+# DRAM bytes (read + write) of one step's palette-GEMM launches: per-launch bytes from one ncu
+# capture of each bench.gemm_shapes(32) shape run alone, times its launches per step (the
+# per-shape table and the command are kept with the other ncu summaries under profiles/).
+GEMM_DRAM_BYTES_PER_STEP = 6207566592
 
 
 def env_rank():
@@ -303,10 +307,7 @@ def run_ours(args):
         if world == 1 and not args.skip_cpu_baseline:
             os.environ.setdefault("OMP_NUM_THREADS", str(cores))
             cpu_value, cpu_dt = cpu_baseline(pk, package, 1)
-        traffic = None
-        prof = ROOT / "profiles" / "gemm_traffic.json"
-        if prof.exists():
-            traffic = json.loads(prof.read_text()).get("bytes_per_step")
+        traffic = GEMM_DRAM_BYTES_PER_STEP
         line = {
             "metric": METRIC, "value": round(audio / (ms * 1e-3), 1), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
@@ -319,7 +320,8 @@ def run_ours(args):
                     "h2d_bytes_per_step": int(features.nbytes), "d2h_bytes_per_step": int(host_out.numel() * 2)},
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": round(achieved / peak_tf, 4), "traffic": traffic,
-                         "kernel": "tc_palette_gemm (all palette GEMM launches of one step)",
+                         "kernel": "palette GEMMs (tc2_/tc_palette_gemm, all launches of one step)",
+                         "traffic_unit": "DRAM bytes per step (ncu, each shape captured alone)",
                          "peak_kind": f"bf16 dense burst, {peak_kind}",
                          "gemm_ms_per_step": round(gemm_ms, 3), "gemm_tflop_per_step": round(gemm_flops / 1e12, 3)},
             "gemm_shapes": gemm_detail,
