@@ -46,7 +46,7 @@ METRIC = "encoder audio-sec/sec (RTFx)"
 UNIT = "audio-s/s"
 # Kernel launches of one encoder step: subsampling (conv0+dw2, pw3 GEMM, dw5,
 # pw6 GEMM, mask, flatten GEMM) + 24 x 15 layer dispatches + projector.
-LAUNCHES_PER_STEP = 6 + 24 * 15 + 1
+LAUNCHES_PER_STEP = 6 + 24 * 14 + 1 + 1
 # DRAM bytes (read + write) of one step's palette-GEMM launches: per-launch bytes from one ncu
 # capture of each bench.gemm_shapes(32) shape run alone, times its launches per step (the
 # per-shape table and the command are kept with the other ncu summaries under profiles/).

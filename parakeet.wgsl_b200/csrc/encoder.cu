@@ -222,7 +222,9 @@ int record_forward(pk_encoder* e, int batch, cudaStream_t s) {
     void* x = e->slots[in_slot];
     void* y = e->slots[in_slot ^ 1];  // alternate == postFeedForward1 == output slot
     void* scratch = x;               // moduleScratch aliases the input slot
-    PK_TRY(launch_layernorm(prec, rows, kHidden, x, L.ln_ff1_w, L.ln_ff1_b, 1e-5f, y, s));
+    // norm_feed_forward1 of every layer after the first ran fused with the
+    // previous layer's norm_out (below).
+    if (l == 0) PK_TRY(launch_layernorm(prec, rows, kHidden, x, L.ln_ff1_w, L.ln_ff1_b, 1e-5f, y, s));
     PK_TRY(gemm(e, L.ff1_l1, rows, y, ff, PK_ACT_SILU, nullptr, nullptr, 1.0f, s));
     PK_TRY(gemm(e, L.ff1_l2, rows, ff, y, PK_ACT_NONE, nullptr, x, 0.5f, s));
     PK_TRY(launch_layernorm(prec, rows, kHidden, y, L.ln_att_w, L.ln_att_b, 1e-5f, scratch, s));
@@ -237,7 +239,16 @@ int record_forward(pk_encoder* e, int batch, cudaStream_t s) {
     PK_TRY(launch_layernorm(prec, rows, kHidden, y, L.ln_ff2_w, L.ln_ff2_b, 1e-5f, scratch, s));
     PK_TRY(gemm(e, L.ff2_l1, rows, scratch, ff, PK_ACT_SILU, nullptr, nullptr, 1.0f, s));
     PK_TRY(gemm(e, L.ff2_l2, rows, ff, scratch, PK_ACT_NONE, nullptr, y, 0.5f, s));
-    PK_TRY(launch_layernorm(prec, rows, kHidden, scratch, L.ln_out_w, L.ln_out_b, 1e-5f, y, s));
+    if (l + 1 < kLayers) {
+      // norm_out into y (the layer output), then the next layer's
+      // norm_feed_forward1 of it into the next layer's alternate slot, which
+      // is this layer's scratch slot (read by the same warp first).
+      const LayerRefs& N = e->layers[l + 1];
+      PK_TRY(launch_layernorm_dual(prec, rows, scratch, L.ln_out_w, L.ln_out_b, N.ln_ff1_w, N.ln_ff1_b, 1e-5f, y,
+                                   scratch, s));
+    } else {
+      PK_TRY(launch_layernorm(prec, rows, kHidden, scratch, L.ln_out_w, L.ln_out_b, 1e-5f, y, s));
+    }
     in_slot ^= 1;
     if (e->keep_checkpoints)
       PK_TRY(cuda_error(cudaMemcpyAsync(e->checkpoints[l + 1], y, rows * kHidden * e->scalar,

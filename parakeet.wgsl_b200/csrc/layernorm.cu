@@ -106,6 +106,106 @@ __global__ void __launch_bounds__(LN_WARPS * 32) layernorm1024_kernel(const T* _
   }
 }
 
+// Row statistics and normalization of one warp's 1024-wide row held as
+// v[LOADS][VEC] (lane's chunks i*32 + lane), gamma/beta from shared memory.
+template <int LOADS, int VEC>
+__device__ __forceinline__ void ln_row(float (&v)[LOADS][VEC], const float* s_gamma, const float* s_beta, float eps,
+                                       int lane) {
+  float sum = 0.0f, sq = 0.0f;
+#pragma unroll
+  for (int i = 0; i < LOADS; ++i)
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      sum += v[i][j];
+      sq = fmaf(v[i][j], v[i][j], sq);
+    }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    sq += __shfl_xor_sync(0xffffffffu, sq, o);
+  }
+  const float inv = 1.0f / 1024.0f;
+  const float mean = sum * inv;
+  const float var = fmaxf(sq * inv - mean * mean, 0.0f);
+  const float rstd = 1.0f / sqrtf(var + eps);
+#pragma unroll
+  for (int i = 0; i < LOADS; ++i) {
+    const int c0 = (i * 32 + lane) * VEC;
+#pragma unroll
+    for (int j = 0; j < VEC; j += 4) {
+      const float4 gg = *reinterpret_cast<const float4*>(s_gamma + c0 + j);
+      const float4 bb = *reinterpret_cast<const float4*>(s_beta + c0 + j);
+      v[i][j] = fmaf((v[i][j] - mean) * rstd, gg.x, bb.x);
+      v[i][j + 1] = fmaf((v[i][j + 1] - mean) * rstd, gg.y, bb.y);
+      v[i][j + 2] = fmaf((v[i][j + 2] - mean) * rstd, gg.z, bb.z);
+      v[i][j + 3] = fmaf((v[i][j + 3] - mean) * rstd, gg.w, bb.w);
+    }
+  }
+}
+
+// Pack VEC floats into 16 bytes of T; with ROUND, v is also replaced by the
+// values as stored (what a reader of the stored row sees).
+template <typename T, int VEC>
+__device__ __forceinline__ uint4 pack16(float (&v)[VEC]) {
+  uint4 out;
+  if constexpr (sizeof(T) == 2) {
+    __half2* h = reinterpret_cast<__half2*>(&out);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      h[j] = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+      const float2 f = __half22float2(h[j]);
+      v[2 * j] = f.x;
+      v[2 * j + 1] = f.y;
+    }
+  } else {
+    float* f = reinterpret_cast<float*>(&out);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) f[j] = v[j];
+  }
+  return out;
+}
+
+// Two LayerNorms in sequence on the same rows: y1 = LN(x; g1, b1) is stored
+// (rounded to T), then y2 = LN(y1 as stored; g2, b2).  The encoder ends
+// every layer with norm_out and starts the next with norm_feed_forward1 on
+// its output (encoder.ts:1869-2138), so this reads each row once instead of
+// twice.  y2 may alias x: a warp holds its whole row before storing.
+template <typename T>
+__global__ void __launch_bounds__(LN_WARPS * 32) layernorm1024_dual_kernel(
+    const T* x, const float* __restrict__ g1, const float* __restrict__ b1, const float* __restrict__ g2,
+    const float* __restrict__ b2, float eps, T* __restrict__ y1, T* y2, int64_t rows) {
+  constexpr int VEC = 16 / sizeof(T);
+  constexpr int LOADS = 1024 / (32 * VEC);
+  __shared__ __align__(16) float s_g1[1024], s_b1[1024], s_g2[1024], s_b2[1024];
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * LN_WARPS + (threadIdx.x >> 5);
+  uint4 raw[LOADS];
+  if (row < rows) {
+    const uint4* src = reinterpret_cast<const uint4*>(x + row * 1024);
+#pragma unroll
+    for (int i = 0; i < LOADS; ++i) raw[i] = src[i * 32 + lane];
+  }
+  for (int c = threadIdx.x * 4; c < 1024; c += LN_WARPS * 32 * 4) {
+    *reinterpret_cast<float4*>(s_g1 + c) = __ldg(reinterpret_cast<const float4*>(g1 + c));
+    *reinterpret_cast<float4*>(s_b1 + c) = __ldg(reinterpret_cast<const float4*>(b1 + c));
+    *reinterpret_cast<float4*>(s_g2 + c) = __ldg(reinterpret_cast<const float4*>(g2 + c));
+    *reinterpret_cast<float4*>(s_b2 + c) = __ldg(reinterpret_cast<const float4*>(b2 + c));
+  }
+  __syncthreads();
+  if (row >= rows) return;
+  float v[LOADS][VEC];
+#pragma unroll
+  for (int i = 0; i < LOADS; ++i) unpack16<T>(raw[i], v[i]);
+  ln_row<LOADS, VEC>(v, s_g1, s_b1, eps, lane);
+  uint4* d1 = reinterpret_cast<uint4*>(y1 + row * 1024);
+#pragma unroll
+  for (int i = 0; i < LOADS; ++i) d1[i * 32 + lane] = pack16<T, VEC>(v[i]);
+  ln_row<LOADS, VEC>(v, s_g2, s_b2, eps, lane);
+  uint4* d2 = reinterpret_cast<uint4*>(y2 + row * 1024);
+#pragma unroll
+  for (int i = 0; i < LOADS; ++i) d2[i * 32 + lane] = pack16<T, VEC>(v[i]);
+}
+
 // Generic path: any channel count, one 256-thread block per row.
 template <typename T>
 __global__ void __launch_bounds__(256) layernorm_generic_kernel(const T* __restrict__ x, const float* __restrict__ gamma,
@@ -167,6 +267,26 @@ int launch_layernorm(int precision, int64_t rows, int64_t channels, const void* 
           static_cast<const float*>(x), gamma, beta, eps, static_cast<float*>(y), channels);
   }
   return cuda_error(cudaGetLastError(), "layernorm launch");
+}
+
+int launch_layernorm_dual(int precision, int64_t rows, const void* x, const float* g1, const float* b1,
+                          const float* g2, const float* b2, float eps, void* y1, void* y2, cudaStream_t stream) {
+  const uintptr_t any = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y1) |
+                        reinterpret_cast<uintptr_t>(y2) | reinterpret_cast<uintptr_t>(g1) |
+                        reinterpret_cast<uintptr_t>(b1) | reinterpret_cast<uintptr_t>(g2) |
+                        reinterpret_cast<uintptr_t>(b2);
+  if ((any & 15) != 0) {  // unaligned: two single LayerNorms in stream order
+    int st = launch_layernorm(precision, rows, 1024, x, g1, b1, eps, y1, stream);
+    return st != PK_OK ? st : launch_layernorm(precision, rows, 1024, y1, g2, b2, eps, y2, stream);
+  }
+  const unsigned blocks = (unsigned)((rows + LN_WARPS - 1) / LN_WARPS);
+  if (precision == PK_FP16)
+    layernorm1024_dual_kernel<__half><<<blocks, LN_WARPS * 32, 0, stream>>>(
+        static_cast<const __half*>(x), g1, b1, g2, b2, eps, static_cast<__half*>(y1), static_cast<__half*>(y2), rows);
+  else
+    layernorm1024_dual_kernel<float><<<blocks, LN_WARPS * 32, 0, stream>>>(
+        static_cast<const float*>(x), g1, b1, g2, b2, eps, static_cast<float*>(y1), static_cast<float*>(y2), rows);
+  return cuda_error(cudaGetLastError(), "layernorm dual launch");
 }
 
 }  // namespace pk

@@ -53,6 +53,9 @@ bool gemm_tc_supported(const GemmArgs& g);
 int launch_palette_expand(const pk_palette_desc& d, cudaStream_t stream);
 int launch_layernorm(int precision, int64_t rows, int64_t channels, const void* x, const float* gamma,
                      const float* beta, float eps, void* y, cudaStream_t stream);
+// Two LayerNorms on 1024-wide rows: y1 = LN(x; g1, b1), y2 = LN(y1; g2, b2).
+int launch_layernorm_dual(int precision, int64_t rows, const void* x, const float* g1, const float* b1,
+                          const float* g2, const float* b2, float eps, void* y1, void* y2, cudaStream_t stream);
 int launch_rel_attention(const DeviceCtx& dev, int precision, int batch, int frames, const void* qkv,
                          const void* positions, const float* bias_u, const float* bias_v,
                          const uint32_t* valid_lengths, void* context, cudaStream_t stream);
