@@ -43,6 +43,14 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// 2^x (hardware approximation, relative error ~2^-22); softmax runs in base
+// 2 with log2(e) folded into the score scale.
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   const __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&h);
@@ -132,7 +140,7 @@ __global__ void __launch_bounds__(ATHREADS, 2) rel_attention_flash_kernel(
 #pragma unroll
     for (int e = 0; e < 4; ++e) o[dt][e] = 0.0f;
   float m0 = -3.402823466e+38f, m1 = -3.402823466e+38f, l0 = 0.0f, l1 = 0.0f;
-  const float scale = 0.08838834764831845f;  // 1 / sqrt(128)
+  const float scale = 0.08838834764831845f * 1.4426950408889634f;  // log2(e) / sqrt(128): base-2 softmax
   const int nchunks = min(ANC, (valid + AKC - 1) / AKC);  // chunks that hold a valid key
 
   for (int kc = 0; kc < nchunks; ++kc) {
@@ -226,7 +234,7 @@ __global__ void __launch_bounds__(ATHREADS, 2) rel_attention_flash_kernel(
     cm1 = fmaxf(cm1, __shfl_xor_sync(0xffffffffu, cm1, 1));
     cm1 = fmaxf(cm1, __shfl_xor_sync(0xffffffffu, cm1, 2));
     const float nm0 = fmaxf(m0, cm0), nm1 = fmaxf(m1, cm1);
-    const float a0 = expf(m0 - nm0), a1 = expf(m1 - nm1);
+    const float a0 = ex2(m0 - nm0), a1 = ex2(m1 - nm1);
     m0 = nm0;
     m1 = nm1;
     float sum0 = 0.0f, sum1 = 0.0f;
@@ -237,7 +245,7 @@ __global__ void __launch_bounds__(ATHREADS, 2) rel_attention_flash_kernel(
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int jl = nt * 8 + 2 * t + (e & 1);
-        p[e] = j0 + jl < valid ? expf(s[nt][e] - (e < 2 ? m0 : m1)) : 0.0f;
+        p[e] = j0 + jl < valid ? ex2(s[nt][e] - (e < 2 ? m0 : m1)) : 0.0f;
       }
       sum0 += p[0] + p[1];
       sum1 += p[2] + p[3];

@@ -78,6 +78,17 @@ __device__ __forceinline__ void store8<float>(float* p, const float* v) {
   *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
 }
 
+// D (+)= A . B on tensor cores, mma.m16n8k16 with f16 A/B and f32 D.
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_h2(__half lo, __half hi) {
+  return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
+}
+
 // One CTA: window b, a strip of C0_SR depthwise output rows, 32 channels.
 // The strip's input time samples (4*SR+3 of them, all 128 mel bins) are
 // staged once with coalesced loads; conv0 rows are produced in order into a
@@ -113,12 +124,96 @@ __global__ void __launch_bounds__(256, 2) conv0_dw2_kernel(const float* __restri
   const int cg = tid >> 6;  // 8-channel group of this thread's conv0 outputs
   const int c = cbase + cg * 8;
   const int x = tid & 63;
-  float w[9][8], bias[8];
+  constexpr bool kMma = sizeof(T) == 2;
+  float w[9][8], bias[8];  // FP32 profile (the FP16 path keeps its weights as MMA fragments)
+  if constexpr (!kMma) {
 #pragma unroll
-  for (int k = 0; k < 9; ++k) load8<T>(w0 + k * SUB_C + c, w[k]);
+    for (int k = 0; k < 9; ++k) load8<T>(w0 + k * SUB_C + c, w[k]);
 #pragma unroll
-  for (int j = 0; j < 8; ++j) bias[j] = __ldg(b0 + c + j);
+    for (int j = 0; j < 8; ++j) bias[j] = __ldg(b0 + c + j);
+  }
+  // FP16 profile: conv0 as a tensor-core GEMM, rows = 16 output positions of
+  // one conv0 row, k = the 9 taps (padded to 16), n = 8 channels.  The f32
+  // features are split into f16 hi + lo parts (two MMAs into the same f32
+  // accumulator), so the products keep f32-level precision; the weights are
+  // f16 in this profile.  Lane (g, t) holds weights of taps 2t, 2t+1, 2t+8,
+  // 2t+9 for channel cbase + 8 nt + g, and bias of channels 8 nt + 2t, +1.
+  const int lane = tid & 31, warp = tid >> 5, mg = lane >> 2, mt = lane & 3;
+  uint32_t bw[4][2];
+  float bb[4][2];
+  if constexpr (kMma) {
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      const int ch = cbase + nt * 8 + mg;
+      auto wv = [&](int k) { return k < 9 ? reinterpret_cast<const __half*>(w0)[k * SUB_C + ch] : __float2half(0.0f); };
+      bw[nt][0] = pack_h2(wv(2 * mt), wv(2 * mt + 1));
+      bw[nt][1] = pack_h2(wv(2 * mt + 8), wv(2 * mt + 9));
+      bb[nt][0] = __ldg(b0 + cbase + nt * 8 + 2 * mt);
+      bb[nt][1] = __ldg(b0 + cbase + nt * 8 + 2 * mt + 1);
+    }
+  }
   __syncthreads();
+
+  // conv0 row y, output positions x0 .. x0+15, all 32 channels, by one warp.
+  auto conv0_mma = [&](int y, int x0) {
+    float acc[4][4];
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      acc[nt][0] = acc[nt][2] = bb[nt][0];
+      acc[nt][1] = acc[nt][3] = bb[nt][1];
+    }
+    const bool live = y >= 0 && y < SUB_CH && y < vin;
+    if (live) {
+      const int xa = x0 + mg, xb = xa + 8;
+      float va[4], vb[4];  // taps 2t, 2t+1, 2t+8, 2t+9 at positions xa, xb
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int k = q < 2 ? 2 * mt + q : 2 * mt + 6 + q;
+        va[q] = vb[q] = 0.0f;
+        if (k < 9) {
+          const int ky = k / 3, kx = k % 3;
+          const float* rowp = in_s + (2 * y + ky - 1 - iy_first) * C0_IN_PITCH;
+          const int ia = 2 * xa + kx - 1, ib = 2 * xb + kx - 1;
+          if (ia >= 0) va[q] = rowp[ia];
+          vb[q] = rowp[ib];  // ib >= 15
+        }
+      }
+      uint32_t ahi[4], alo[4];
+      __half ha[4], hb[4], la[4], lb[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        ha[q] = __float2half_rn(va[q]);
+        hb[q] = __float2half_rn(vb[q]);
+        la[q] = __float2half_rn(va[q] - __half2float(ha[q]));
+        lb[q] = __float2half_rn(vb[q] - __half2float(hb[q]));
+      }
+      ahi[0] = pack_h2(ha[0], ha[1]), ahi[1] = pack_h2(hb[0], hb[1]);
+      ahi[2] = pack_h2(ha[2], ha[3]), ahi[3] = pack_h2(hb[2], hb[3]);
+      alo[0] = pack_h2(la[0], la[1]), alo[1] = pack_h2(lb[0], lb[1]);
+      alo[2] = pack_h2(la[2], la[3]), alo[3] = pack_h2(lb[2], lb[3]);
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        mma_16816(acc[nt], ahi, bw[nt][0], bw[nt][1]);
+        mma_16816(acc[nt], alo, bw[nt][0], bw[nt][1]);
+      }
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[nt][e] = __half2float(__float2half_rn(fmaxf(acc[nt][e], 0.0f)));
+    } else {
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[nt][e] = 0.0f;
+    }
+    float* slot = ring + ((y + 3) % 3) * SUB_CW * C0_PITCH;
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      *reinterpret_cast<float2*>(slot + (x0 + mg) * C0_PITCH + nt * 8 + 2 * mt) = make_float2(acc[nt][0], acc[nt][1]);
+      *reinterpret_cast<float2*>(slot + (x0 + mg + 8) * C0_PITCH + nt * 8 + 2 * mt) =
+          make_float2(acc[nt][2], acc[nt][3]);
+    }
+  };
 
   // conv0 row y (3x3 stride 2 over the staged input) -> ring slot (y + 3) % 3.
   auto conv0_row = [&](int y) {
@@ -150,11 +245,19 @@ __global__ void __launch_bounds__(256, 2) conv0_dw2_kernel(const float* __restri
     *reinterpret_cast<float4*>(dst + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
   };
 
-  conv0_row(y_first);
+  if constexpr (kMma) {
+    if (warp < 4) conv0_mma(y_first, warp * 16);
+  } else {
+    conv0_row(y_first);
+  }
 #pragma unroll 1
   for (int oy = oy0; oy < oy_end; ++oy) {
-    conv0_row(2 * oy);
-    conv0_row(2 * oy + 1);
+    if constexpr (kMma) {
+      conv0_mma(2 * oy + (warp >> 2), (warp & 3) * 16);  // 8 warps: 2 rows x 4 position tiles
+    } else {
+      conv0_row(2 * oy);
+      conv0_row(2 * oy + 1);
+    }
     __syncthreads();
     if (tid < 128) {  // depthwise: thread = (channel group, output x)
       const int dcg = tid >> 5, ox = tid & 31;
