@@ -47,6 +47,7 @@ __global__ void __launch_bounds__(ATT_THREADS) rel_attention_simt_kernel(
     const T* __restrict__ qkv, const T* __restrict__ positions, const float* __restrict__ bias_u,
     const float* __restrict__ bias_v, const uint32_t* __restrict__ valid_lengths, T* __restrict__ context,
     int frames) {
+  pdl_entry();
   __shared__ float qu[ATT_QB][128], qv[ATT_QB][128];
   __shared__ float probs[ATT_QB][ATT_MAXT];
   const int q0 = blockIdx.x * ATT_QB, h = blockIdx.y, b = blockIdx.z;
@@ -145,11 +146,11 @@ int launch_rel_attention(const DeviceCtx& dev, int precision, int batch, int fra
     return launch_rel_attention_tc(batch, frames, qkv, positions, bias_u, bias_v, valid_lengths, context, stream);
   const dim3 grid((frames + ATT_QB - 1) / ATT_QB, 8, batch);
   if (precision == PK_FP16)
-    rel_attention_simt_kernel<__half><<<grid, ATT_THREADS, 0, stream>>>(
+    launch_kernel(rel_attention_simt_kernel<__half>, grid, ATT_THREADS, 0, stream, 
         static_cast<const __half*>(qkv), static_cast<const __half*>(positions), bias_u, bias_v, valid_lengths,
         static_cast<__half*>(context), frames);
   else
-    rel_attention_simt_kernel<float><<<grid, ATT_THREADS, 0, stream>>>(
+    launch_kernel(rel_attention_simt_kernel<float>, grid, ATT_THREADS, 0, stream, 
         static_cast<const float*>(qkv), static_cast<const float*>(positions), bias_u, bias_v, valid_lengths,
         static_cast<float*>(context), frames);
   return cuda_error(cudaGetLastError(), "rel_attention launch");

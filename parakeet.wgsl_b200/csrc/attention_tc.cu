@@ -108,6 +108,7 @@ __global__ void __launch_bounds__(ATHREADS, 2) rel_attention_flash_kernel(
     const __half* __restrict__ qkv, const __half* __restrict__ positions, const float* __restrict__ bias_u,
     const float* __restrict__ bias_v, const uint32_t* __restrict__ valid_lengths, __half* __restrict__ context,
     int frames) {
+  pdl_entry();
   extern __shared__ __align__(16) uint8_t fa_smem[];
   __half* Ks = reinterpret_cast<__half*>(fa_smem);   // [64][AS]
   __half* Vs = Ks + AKC * AS;                         // [64][AS]
@@ -310,7 +311,7 @@ int launch_rel_attention_tc(int batch, int frames, const void* qkv, const void* 
   const int st = set_max_dynamic_smem(reinterpret_cast<const void*>(rel_attention_flash_kernel), ASMEM);
   if (st != PK_OK) return st;
   const dim3 grid((frames + AQ - 1) / AQ, 8, batch);
-  rel_attention_flash_kernel<<<grid, ATHREADS, ASMEM, stream>>>(
+  launch_kernel(rel_attention_flash_kernel, grid, ATHREADS, ASMEM, stream, 
       static_cast<const __half*>(qkv), static_cast<const __half*>(positions), bias_u, bias_v, valid_lengths,
       static_cast<__half*>(context), frames);
   return cuda_error(cudaGetLastError(), "rel_attention_flash launch");

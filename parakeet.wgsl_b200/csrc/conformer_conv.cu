@@ -89,6 +89,7 @@ template <typename T>
 __global__ void __launch_bounds__(CONV_THREADS, 2) conformer_conv_kernel(
     const T* __restrict__ g, const T* __restrict__ dw, const float* __restrict__ scale,
     const float* __restrict__ shift, const uint32_t* __restrict__ valid_lengths, T* __restrict__ out, int frames) {
+  pdl_entry();
   constexpr int VEC = 16 / sizeof(T);          // channels per 16-byte global vector
   constexpr int NV = CONV_TC / VEC;            // vectors per tile row
   constexpr int ITEMS = (CONV_ROWS * NV + CONV_THREADS - 1) / CONV_THREADS;
@@ -175,11 +176,11 @@ int launch_conformer_conv(int precision, int batch, int frames, const void* poin
                           cudaStream_t stream) {
   const dim3 grid(CONV_C / CONV_TC, (frames + CONV_TF - 1) / CONV_TF, batch);
   if (precision == PK_FP16)
-    conformer_conv_kernel<__half><<<grid, CONV_THREADS, CONV_SMEM, stream>>>(
+    launch_kernel(conformer_conv_kernel<__half>, grid, CONV_THREADS, CONV_SMEM, stream, 
         static_cast<const __half*>(pointwise), static_cast<const __half*>(dw), scale, shift, valid_lengths,
         static_cast<__half*>(out), frames);
   else
-    conformer_conv_kernel<float><<<grid, CONV_THREADS, CONV_SMEM, stream>>>(
+    launch_kernel(conformer_conv_kernel<float>, grid, CONV_THREADS, CONV_SMEM, stream, 
         static_cast<const float*>(pointwise), static_cast<const float*>(dw), scale, shift, valid_lengths,
         static_cast<float*>(out), frames);
   return cuda_error(cudaGetLastError(), "conformer_conv launch");

@@ -37,6 +37,7 @@ __global__ void __launch_bounds__(SG_THREADS) simt_palette_gemm_kernel(
     const T* __restrict__ a, const uint32_t* __restrict__ codes, const T* __restrict__ palette,
     const float* __restrict__ bias, const T* __restrict__ residual, T* __restrict__ out, int rows, int inner,
     int columns, int groups, int group_cols, int act, int has_residual, float res_scale) {
+  pdl_entry();
   constexpr int CPG = BITS == 5 ? 32 : 16, WPG = BITS == 5 ? 5 : 3, E = 1 << BITS;
   __shared__ float As[SG_BK][SG_BM + 4];
   __shared__ float Ws[SG_BK][SG_BN + 4];
@@ -127,11 +128,11 @@ int launch_gemm_simt(const DeviceCtx& dev, const GemmArgs& g, cudaStream_t strea
     auto* res = static_cast<const float*>(g.residual);
     auto* c = static_cast<float*>(g.c);
     if (g.bits == 5)
-      simt_palette_gemm_kernel<float, 5><<<grid, SG_THREADS, 0, stream>>>(
+      launch_kernel(simt_palette_gemm_kernel<float, 5>, grid, SG_THREADS, 0, stream, 
           a, g.codes, pal, g.bias, res, c, rows, inner, columns, g.groups, gc, g.act, g.has_residual,
           g.residual_scale);
     else
-      simt_palette_gemm_kernel<float, 6><<<grid, SG_THREADS, 0, stream>>>(
+      launch_kernel(simt_palette_gemm_kernel<float, 6>, grid, SG_THREADS, 0, stream, 
           a, g.codes, pal, g.bias, res, c, rows, inner, columns, g.groups, gc, g.act, g.has_residual,
           g.residual_scale);
   } else {
@@ -140,11 +141,11 @@ int launch_gemm_simt(const DeviceCtx& dev, const GemmArgs& g, cudaStream_t strea
     auto* res = static_cast<const __half*>(g.residual);
     auto* c = static_cast<__half*>(g.c);
     if (g.bits == 5)
-      simt_palette_gemm_kernel<__half, 5><<<grid, SG_THREADS, 0, stream>>>(
+      launch_kernel(simt_palette_gemm_kernel<__half, 5>, grid, SG_THREADS, 0, stream, 
           a, g.codes, pal, g.bias, res, c, rows, inner, columns, g.groups, gc, g.act, g.has_residual,
           g.residual_scale);
     else
-      simt_palette_gemm_kernel<__half, 6><<<grid, SG_THREADS, 0, stream>>>(
+      launch_kernel(simt_palette_gemm_kernel<__half, 6>, grid, SG_THREADS, 0, stream, 
           a, g.codes, pal, g.bias, res, c, rows, inner, columns, g.groups, gc, g.act, g.has_residual,
           g.residual_scale);
   }

@@ -293,6 +293,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_palette_gemm_kernel(const __
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_entry();  // activations / residual / output are touched only after this
 
   // EPI_RESADD: KR extra k-steps first with B = the residual tile (the
   // tile's 128 output features as K) and A = 1/res_scale times the identity,
@@ -588,6 +589,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc2_palette_gemm_kernel(const _
   cluster_sync();  // barriers of both CTAs initialised before any remote signal
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_entry();  // activations / residual / output are touched only after this
 
   // Residual GEMMs run KR extra k-steps first: B = the residual tile (the
   // pair's 256 output features as K), A = 1/res_scale times the identity
@@ -862,8 +864,8 @@ static int launch_tc_spec(const DeviceCtx& dev, const TcGemmParams& p, cudaStrea
     if (dev.ordinal >= 0 && dev.ordinal < 32) configured[dev.ordinal] = true;
   }
   const int tiles = p.m_tiles * p.n_tiles;
-  kernel<<<std::min(tiles, dev.sm_count), TC_THREADS, L::SMEM_BYTES, stream>>>(p);
-  return cuda_error(cudaGetLastError(), "tc_palette_gemm launch");
+  return cuda_error(launch_kernel(kernel, dim3(std::min(tiles, dev.sm_count)), dim3(TC_THREADS), L::SMEM_BYTES, stream, p),
+                    "tc_palette_gemm launch");
 }
 
 // Whether the residual is folded into the accumulator as residual / scale
@@ -938,16 +940,18 @@ static int launch_tc2_spec(const DeviceCtx& dev, const TcGemmParams& p, cudaStre
   static int max_pairs[32] = {};
   if (dev.ordinal < 0 || dev.ordinal >= 32) return set_error(PK_E_INVALID, "device ordinal out of range");
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see launch_kernel
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.blockDim = dim3(TC_THREADS);
   cfg.dynamicSmemBytes = L::SMEM_BYTES;
   cfg.stream = stream;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 1;  // occupancy query with the cluster shape only
   if (!max_pairs[dev.ordinal]) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM_BYTES);
     if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(tc2_palette_gemm)");
@@ -960,6 +964,7 @@ static int launch_tc2_spec(const DeviceCtx& dev, const TcGemmParams& p, cudaStre
   }
   const int pair_tiles = p.m_tiles * (p.n_tiles / 2);
   cfg.gridDim = dim3(2 * std::min(pair_tiles, max_pairs[dev.ordinal]));
+  cfg.numAttrs = 2;
   return cuda_error(cudaLaunchKernelEx(&cfg, kernel, p), "tc2_palette_gemm launch");
 }
 

@@ -41,6 +41,7 @@ __global__ void __launch_bounds__(LN_WARPS * 32) layernorm1024_kernel(const T* _
                                                                     const float* __restrict__ gamma,
                                                                     const float* __restrict__ beta, float eps,
                                                                     T* __restrict__ y, int64_t rows) {
+  pdl_entry();
   constexpr int VEC = 16 / sizeof(T);        // elements per 16-byte load
   constexpr int LOADS = 1024 / (32 * VEC);   // loads per lane per row
   __shared__ __align__(16) float s_gamma[1024], s_beta[1024];
@@ -174,6 +175,7 @@ template <typename T>
 __global__ void __launch_bounds__(LN_WARPS * 32) layernorm1024_dual_kernel(
     const T* x, const float* __restrict__ g1, const float* __restrict__ b1, const float* __restrict__ g2,
     const float* __restrict__ b2, float eps, T* __restrict__ y1, T* y2, int64_t rows) {
+  pdl_entry();
   constexpr int VEC = 16 / sizeof(T);
   constexpr int LOADS = 1024 / (32 * VEC);
   __shared__ __align__(16) float s_g1[1024], s_b1[1024], s_g2[1024], s_b2[1024];
@@ -211,6 +213,7 @@ template <typename T>
 __global__ void __launch_bounds__(256) layernorm_generic_kernel(const T* __restrict__ x, const float* __restrict__ gamma,
                                                                 const float* __restrict__ beta, float eps,
                                                                 T* __restrict__ y, int64_t channels) {
+  pdl_entry();
   __shared__ float red[2][8];
   const int64_t row = blockIdx.x;
   float sum = 0.0f, sq = 0.0f;
@@ -253,17 +256,17 @@ int launch_layernorm(int precision, int64_t rows, int64_t channels, const void* 
   if (channels == 1024 && aligned && params_aligned) {
     const unsigned blocks = (unsigned)((rows + LN_WARPS - 1) / LN_WARPS);
     if (precision == PK_FP16)
-      layernorm1024_kernel<__half><<<blocks, LN_WARPS * 32, 0, stream>>>(
+      launch_kernel(layernorm1024_kernel<__half>, blocks, LN_WARPS * 32, 0, stream, 
           static_cast<const __half*>(x), gamma, beta, eps, static_cast<__half*>(y), rows);
     else
-      layernorm1024_kernel<float><<<blocks, LN_WARPS * 32, 0, stream>>>(
+      launch_kernel(layernorm1024_kernel<float>, blocks, LN_WARPS * 32, 0, stream, 
           static_cast<const float*>(x), gamma, beta, eps, static_cast<float*>(y), rows);
   } else {
     if (precision == PK_FP16)
-      layernorm_generic_kernel<__half><<<(unsigned)rows, 256, 0, stream>>>(
+      launch_kernel(layernorm_generic_kernel<__half>, (unsigned)rows, 256, 0, stream, 
           static_cast<const __half*>(x), gamma, beta, eps, static_cast<__half*>(y), channels);
     else
-      layernorm_generic_kernel<float><<<(unsigned)rows, 256, 0, stream>>>(
+      launch_kernel(layernorm_generic_kernel<float>, (unsigned)rows, 256, 0, stream, 
           static_cast<const float*>(x), gamma, beta, eps, static_cast<float*>(y), channels);
   }
   return cuda_error(cudaGetLastError(), "layernorm launch");
@@ -281,10 +284,10 @@ int launch_layernorm_dual(int precision, int64_t rows, const void* x, const floa
   }
   const unsigned blocks = (unsigned)((rows + LN_WARPS - 1) / LN_WARPS);
   if (precision == PK_FP16)
-    layernorm1024_dual_kernel<__half><<<blocks, LN_WARPS * 32, 0, stream>>>(
+    launch_kernel(layernorm1024_dual_kernel<__half>, blocks, LN_WARPS * 32, 0, stream, 
         static_cast<const __half*>(x), g1, b1, g2, b2, eps, static_cast<__half*>(y1), static_cast<__half*>(y2), rows);
   else
-    layernorm1024_dual_kernel<float><<<blocks, LN_WARPS * 32, 0, stream>>>(
+    launch_kernel(layernorm1024_dual_kernel<float>, blocks, LN_WARPS * 32, 0, stream, 
         static_cast<const float*>(x), g1, b1, g2, b2, eps, static_cast<float*>(y1), static_cast<float*>(y2), rows);
   return cuda_error(cudaGetLastError(), "layernorm dual launch");
 }

@@ -17,6 +17,7 @@ template <typename T, int BITS, bool TILE>
 __global__ void palette_expand_kernel(const uint32_t* __restrict__ codes, const T* __restrict__ palette,
                                       T* __restrict__ target, int64_t inner, int64_t columns, int groups,
                                       int64_t group_cols) {
+  pdl_entry();
   constexpr int CPG = BITS == 5 ? 32 : 16, WPG = BITS == 5 ? 5 : 3, E = 1 << BITS;
   constexpr int64_t TILE_COLS = sizeof(T) == 2 ? 256 : 128;
   const int64_t group = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -56,17 +57,17 @@ static void dispatch_expand(const pk_palette_desc& d, cudaStream_t s) {
   const bool tile = d.layout == PK_LAYOUT_TILE_MAJOR;
   if (d.bits == 5) {
     if (tile)
-      palette_expand_kernel<T, 5, true><<<blocks, threads, 0, s>>>(codes, pal, tgt, d.inner, d.columns,
+      launch_kernel(palette_expand_kernel<T, 5, true>, blocks, threads, 0, s, codes, pal, tgt, d.inner, d.columns,
                                                                  d.palette_groups, d.palette_group_columns);
     else
-      palette_expand_kernel<T, 5, false><<<blocks, threads, 0, s>>>(codes, pal, tgt, d.inner, d.columns,
+      launch_kernel(palette_expand_kernel<T, 5, false>, blocks, threads, 0, s, codes, pal, tgt, d.inner, d.columns,
                                                                   d.palette_groups, d.palette_group_columns);
   } else {
     if (tile)
-      palette_expand_kernel<T, 6, true><<<blocks, threads, 0, s>>>(codes, pal, tgt, d.inner, d.columns,
+      launch_kernel(palette_expand_kernel<T, 6, true>, blocks, threads, 0, s, codes, pal, tgt, d.inner, d.columns,
                                                                  d.palette_groups, d.palette_group_columns);
     else
-      palette_expand_kernel<T, 6, false><<<blocks, threads, 0, s>>>(codes, pal, tgt, d.inner, d.columns,
+      launch_kernel(palette_expand_kernel<T, 6, false>, blocks, threads, 0, s, codes, pal, tgt, d.inner, d.columns,
                                                                   d.palette_groups, d.palette_group_columns);
   }
 }

@@ -263,6 +263,19 @@ __device__ __forceinline__ void tc_commit_pair(uint32_t bar_cluster_addr) {
                : "memory");
 }
 
+// --------------------------------------- programmatic dependent launch
+// Every kernel of this library is launched with programmatic stream
+// serialization (launch_kernel in pk_internal.h), so the next kernel of a
+// stream (or captured graph) may be scheduled while this one's last CTAs
+// still run.  pdl_entry() lets our dependents launch early and then waits
+// until every kernel this one depends on has completed and its memory is
+// visible; each kernel calls it before it reads or writes any buffer that
+// another kernel touches.
+__device__ __forceinline__ void pdl_entry() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // -------------------------------------------------------------- math bits
 // SiLU exactly as the reference epilogue writes it:
 // v / (1 + exp(-clamp(v, -20, 20)))  (src/webgpu/kernels/gemm.ts:2018-2032).

@@ -22,6 +22,27 @@ struct DeviceCtx {
 int set_error(int code, const char* fmt, ...);
 int cuda_error(cudaError_t err, const char* what);
 
+// Launch with programmatic stream serialization: the kernel may be scheduled
+// while the previous kernel of the stream finishes its last CTAs, and waits
+// for it in pdl_entry() (pk_common.cuh) -- which every kernel of this
+// library calls before touching shared buffers.  In a captured graph this
+// becomes a programmatic dependency edge.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                                 Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 struct GemmArgs {
   int precision = PK_FP16;
   int64_t rows = 0, inner = 0, columns = 0;

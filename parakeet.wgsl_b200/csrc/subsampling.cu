@@ -100,6 +100,7 @@ __global__ void __launch_bounds__(256, 2) conv0_dw2_kernel(const float* __restri
                                                            const T* __restrict__ wd, const float* __restrict__ bd,
                                                            const uint32_t* __restrict__ feature_lengths,
                                                            T* __restrict__ out) {
+  pdl_entry();
   extern __shared__ __align__(16) float sub_smem[];
   float* in_s = sub_smem;                                 // [C0_IN_ROWS][129]
   float* ring = sub_smem + C0_IN_FLOATS;                  // [3][64][C0_PITCH], 16-byte aligned
@@ -303,6 +304,7 @@ __global__ void __launch_bounds__(256) depthwise_kernel(const T* __restrict__ in
                                                         const uint32_t* __restrict__ feature_lengths,
                                                         T* __restrict__ out, int batch, int ih, int iw,
                                                         int channels, int steps) {
+  pdl_entry();
   const int oh = (ih - 1) / 2 + 1, ow = (iw - 1) / 2 + 1;
   const int cv = channels / 8;
   const int64_t total = (int64_t)batch * oh * ow * cv;
@@ -345,6 +347,7 @@ __global__ void __launch_bounds__(256) depthwise_kernel(const T* __restrict__ in
 template <typename T>
 __global__ void time_mask_kernel(T* __restrict__ values, const uint32_t* __restrict__ feature_lengths, int height,
                                  int row_elems, int steps) {
+  pdl_entry();
   const int frame = blockIdx.x, b = blockIdx.y;
   if (frame < sub_len((int)feature_lengths[b], steps)) return;
   T* row = values + ((size_t)b * height + frame) * row_elems;
@@ -358,13 +361,13 @@ int launch_subsampling_conv0_dw2(int precision, int batch, const float* features
   if (precision == PK_FP16) {
     int st = set_max_dynamic_smem(reinterpret_cast<const void*>(conv0_dw2_kernel<__half>), C0_SMEM);
     if (st != PK_OK) return st;
-    conv0_dw2_kernel<__half><<<grid, 256, C0_SMEM, stream>>>(features, static_cast<const __half*>(conv0_w), conv0_b,
+    launch_kernel(conv0_dw2_kernel<__half>, grid, 256, C0_SMEM, stream, features, static_cast<const __half*>(conv0_w), conv0_b,
                                                              static_cast<const __half*>(dw_w), dw_b, feature_lengths,
                                                              static_cast<__half*>(out));
   } else {
     int st = set_max_dynamic_smem(reinterpret_cast<const void*>(conv0_dw2_kernel<float>), C0_SMEM);
     if (st != PK_OK) return st;
-    conv0_dw2_kernel<float><<<grid, 256, C0_SMEM, stream>>>(features, static_cast<const float*>(conv0_w), conv0_b,
+    launch_kernel(conv0_dw2_kernel<float>, grid, 256, C0_SMEM, stream, features, static_cast<const float*>(conv0_w), conv0_b,
                                                             static_cast<const float*>(dw_w), dw_b, feature_lengths,
                                                             static_cast<float*>(out));
   }
@@ -379,11 +382,11 @@ int launch_subsampling_depthwise(int precision, int batch, int ih, int iw, int c
   const int64_t total = (int64_t)batch * oh * ow * (channels / 8);
   const unsigned blocks = (unsigned)((total + 255) / 256);
   if (precision == PK_FP16)
-    depthwise_kernel<__half><<<blocks, 256, 0, stream>>>(static_cast<const __half*>(input),
+    launch_kernel(depthwise_kernel<__half>, blocks, 256, 0, stream, static_cast<const __half*>(input),
                                                          static_cast<const __half*>(w), b, feature_lengths,
                                                          static_cast<__half*>(out), batch, ih, iw, channels, steps);
   else
-    depthwise_kernel<float><<<blocks, 256, 0, stream>>>(static_cast<const float*>(input),
+    launch_kernel(depthwise_kernel<float>, blocks, 256, 0, stream, static_cast<const float*>(input),
                                                         static_cast<const float*>(w), b, feature_lengths,
                                                         static_cast<float*>(out), batch, ih, iw, channels, steps);
   return cuda_error(cudaGetLastError(), "subsampling depthwise launch");
@@ -393,10 +396,10 @@ int launch_subsampling_time_mask(int precision, int batch, int height, int width
                                  const uint32_t* feature_lengths, int steps, cudaStream_t stream) {
   const dim3 grid(height, batch);
   if (precision == PK_FP16)
-    time_mask_kernel<__half><<<grid, 256, 0, stream>>>(static_cast<__half*>(values), feature_lengths, height,
+    launch_kernel(time_mask_kernel<__half>, grid, 256, 0, stream, static_cast<__half*>(values), feature_lengths, height,
                                                        width * channels, steps);
   else
-    time_mask_kernel<float><<<grid, 256, 0, stream>>>(static_cast<float*>(values), feature_lengths, height,
+    launch_kernel(time_mask_kernel<float>, grid, 256, 0, stream, static_cast<float*>(values), feature_lengths, height,
                                                       width * channels, steps);
   return cuda_error(cudaGetLastError(), "subsampling time mask launch");
 }
