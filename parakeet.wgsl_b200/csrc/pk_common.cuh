@@ -271,9 +271,13 @@ __device__ __forceinline__ void tc_commit_pair(uint32_t bar_cluster_addr) {
 // until every kernel this one depends on has completed and its memory is
 // visible; each kernel calls it before it reads or writes any buffer that
 // another kernel touches.
-__device__ __forceinline__ void pdl_entry() {
+__device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_entry() {
+  pdl_launch_dependents();
+  pdl_wait();
 }
 
 // -------------------------------------------------------------- math bits

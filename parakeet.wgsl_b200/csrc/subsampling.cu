@@ -32,7 +32,8 @@ constexpr int C0_PITCH = C0_CG + 4;  // padded channel pitch of the conv0 ring (
 // The input strip is padded to a multiple of 4 floats so the conv0 ring and
 // the depthwise taps that follow it start on 16-byte boundaries (float4).
 constexpr int C0_IN_FLOATS = (C0_IN_ROWS * C0_IN_PITCH + 3) / 4 * 4;
-constexpr int C0_RING_FLOATS = 3 * SUB_CW * C0_PITCH;
+constexpr int C0_RING = 5;  // conv0 rows 2oy-1 .. 2oy+3 for two depthwise rows per pass
+constexpr int C0_RING_FLOATS = C0_RING * SUB_CW * C0_PITCH;
 constexpr int C0_SMEM = (C0_IN_FLOATS + C0_RING_FLOATS + 9 * C0_CG + C0_CG) * 4;
 static_assert(C0_IN_FLOATS % 4 == 0 && C0_PITCH % 4 == 0 && C0_RING_FLOATS % 4 == 0,
               "conv0 ring must stay 16-byte aligned");
@@ -115,11 +116,19 @@ __global__ void __launch_bounds__(256, 2) conv0_dw2_kernel(const float* __restri
   const int vin = sub_len(raw, 1), vout = sub_len(raw, 2);
   const int y_first = 2 * oy0 - 1;       // first conv0 row of the strip
   const int iy_first = 2 * y_first - 1;  // first input time sample
+  // Stage the strip's input with asynchronous 4-byte copies, all in flight at
+  // once (zero-filled outside the utterance); consecutive threads walk time,
+  // which is contiguous in the feature-major log-mel.
   for (int i = tid; i < C0_IN_ROWS * SUB_IW; i += 256) {
-    const int r = i % C0_IN_ROWS, x = i / C0_IN_ROWS;  // consecutive threads walk time (contiguous)
+    const int r = i % C0_IN_ROWS, x = i / C0_IN_ROWS;
     const int iy = iy_first + r;
-    in_s[r * C0_IN_PITCH + x] = (iy >= 0 && iy < SUB_IH) ? fbank[((size_t)b * SUB_IW + x) * SUB_IH + iy] : 0.0f;
+    const bool in_range = iy >= 0 && iy < SUB_IH;
+    const float* src = fbank + ((size_t)b * SUB_IW + x) * SUB_IH + (in_range ? iy : 0);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_addr(in_s + r * C0_IN_PITCH + x)),
+                 "l"(src), "r"(in_range ? 4 : 0)
+                 : "memory");
   }
+  asm volatile("cp.async.commit_group;" ::: "memory");
   for (int i = tid; i < 9 * C0_CG; i += 256) wd_s[i] = (float)wd[(i / C0_CG) * SUB_C + cbase + i % C0_CG];
   if (tid < C0_CG) bd_s[tid] = bd[cbase + tid];
   const int cg = tid >> 6;  // 8-channel group of this thread's conv0 outputs
@@ -153,6 +162,7 @@ __global__ void __launch_bounds__(256, 2) conv0_dw2_kernel(const float* __restri
       bb[nt][1] = __ldg(b0 + cbase + nt * 8 + 2 * mt + 1);
     }
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
 
   // conv0 row y, output positions x0 .. x0+15, all 32 channels, by one warp.
@@ -207,7 +217,7 @@ __global__ void __launch_bounds__(256, 2) conv0_dw2_kernel(const float* __restri
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[nt][e] = 0.0f;
     }
-    float* slot = ring + ((y + 3) % 3) * SUB_CW * C0_PITCH;
+    float* slot = ring + ((y + C0_RING) % C0_RING) * SUB_CW * C0_PITCH;
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt) {
       *reinterpret_cast<float2*>(slot + (x0 + mg) * C0_PITCH + nt * 8 + 2 * mt) = make_float2(acc[nt][0], acc[nt][1]);
@@ -216,7 +226,7 @@ __global__ void __launch_bounds__(256, 2) conv0_dw2_kernel(const float* __restri
     }
   };
 
-  // conv0 row y (3x3 stride 2 over the staged input) -> ring slot (y + 3) % 3.
+  // conv0 row y (3x3 stride 2 over the staged input) -> ring slot (y + 5) % 5.
   auto conv0_row = [&](int y) {
     float acc[8];
     if (y >= 0 && y < SUB_CH && y < vin) {
@@ -241,7 +251,7 @@ __global__ void __launch_bounds__(256, 2) conv0_dw2_kernel(const float* __restri
 #pragma unroll
       for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
     }
-    float* dst = ring + (((y + 3) % 3) * SUB_CW + x) * C0_PITCH + cg * 8;
+    float* dst = ring + (((y + C0_RING) % C0_RING) * SUB_CW + x) * C0_PITCH + cg * 8;
     *reinterpret_cast<float4*>(dst) = make_float4(acc[0], acc[1], acc[2], acc[3]);
     *reinterpret_cast<float4*>(dst + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
   };
@@ -251,19 +261,26 @@ __global__ void __launch_bounds__(256, 2) conv0_dw2_kernel(const float* __restri
   } else {
     conv0_row(y_first);
   }
+  // Two depthwise rows per pass: conv0 rows 2oy .. 2oy+3 (all 8 warps), one
+  // barrier, depthwise rows oy, oy+1 (all 256 threads), one barrier.
+  const int y_last = 2 * oy_end - 1;  // last conv0 row this strip needs
 #pragma unroll 1
-  for (int oy = oy0; oy < oy_end; ++oy) {
+  for (int oy = oy0; oy < oy_end; oy += 2) {
     if constexpr (kMma) {
-      conv0_mma(2 * oy + (warp >> 2), (warp & 3) * 16);  // 8 warps: 2 rows x 4 position tiles
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int y = 2 * oy + 2 * h + (warp >> 2);
+        if (y <= y_last) conv0_mma(y, (warp & 3) * 16);  // 8 warps: 2 rows x 4 position tiles
+      }
     } else {
-      conv0_row(2 * oy);
-      conv0_row(2 * oy + 1);
+      for (int y = 2 * oy; y <= min(2 * oy + 3, y_last); ++y) conv0_row(y);
     }
     __syncthreads();
-    if (tid < 128) {  // depthwise: thread = (channel group, output x)
-      const int dcg = tid >> 5, ox = tid & 31;
+    const int oyr = oy + (tid >> 7);  // depthwise: thread = (row, channel group, output x)
+    if (oyr < oy_end) {
+      const int dcg = (tid >> 5) & 3, ox = tid & 31;
       float acc[8];
-      if (oy >= vout) {
+      if (oyr >= vout) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
       } else {
@@ -271,13 +288,13 @@ __global__ void __launch_bounds__(256, 2) conv0_dw2_kernel(const float* __restri
         for (int j = 0; j < 8; ++j) acc[j] = bd_s[dcg * 8 + j];
 #pragma unroll
         for (int ky = 0; ky < 3; ++ky) {
-          const int iy = oy * 2 + ky - 1;
+          const int iy = oyr * 2 + ky - 1;
           if (iy < 0 || iy >= SUB_CH || iy >= vin) continue;
 #pragma unroll
           for (int kx = 0; kx < 3; ++kx) {
             const int ix = ox * 2 + kx - 1;
             if (ix < 0 || ix >= SUB_CW) continue;
-            const float* src = ring + (((iy + 3) % 3) * SUB_CW + ix) * C0_PITCH + dcg * 8;
+            const float* src = ring + (((iy + C0_RING) % C0_RING) * SUB_CW + ix) * C0_PITCH + dcg * 8;
             const float4 lo = *reinterpret_cast<const float4*>(src);
             const float4 hi = *reinterpret_cast<const float4*>(src + 4);
             const float* wk = wd_s + (ky * 3 + kx) * C0_CG + dcg * 8;
@@ -290,9 +307,9 @@ __global__ void __launch_bounds__(256, 2) conv0_dw2_kernel(const float* __restri
           }
         }
       }
-      store8<T>(out + (((size_t)b * SUB_OH + oy) * SUB_OW + ox) * SUB_C + cbase + dcg * 8, acc);
+      store8<T>(out + (((size_t)b * SUB_OH + oyr) * SUB_OW + ox) * SUB_C + cbase + dcg * 8, acc);
     }
-    __syncthreads();  // the next iteration overwrites the slot of row 2oy-1
+    __syncthreads();  // the next pass overwrites the slots of rows 2oy-1 .. 2oy+2
   }
 }
 
