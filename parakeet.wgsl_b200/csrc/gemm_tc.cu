@@ -589,7 +589,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc2_palette_gemm_kernel(const _
   cluster_sync();  // barriers of both CTAs initialised before any remote signal
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  pdl_entry();  // activations / residual / output are touched only after this
+  // Programmatic dependent launch: only the producer waits for the previous
+  // kernel (pdl_wait below), before its first activation / residual load;
+  // every other global access of this kernel (output stores) follows those
+  // loads through the pipeline barriers.  Weights are not written by kernels.
+  pdl_launch_dependents();
 
   // Residual GEMMs run KR extra k-steps first: B = the residual tile (the
   // pair's 256 output features as K), A = 1/res_scale times the identity
@@ -608,6 +612,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc2_palette_gemm_kernel(const _
       int last_round[S];
 #pragma unroll
       for (int s = 0; s < S; ++s) last_round[s] = -1;
+      // The first round's code tiles (weights only) load before the wait on
+      // the previous kernel, so their decode overlaps that kernel's tail.
+      auto issue_codes = [&](int s, int kb, int n_tile) {
+        if (kb < KR) {
+          mbar_arrive(&full_c[s]);  // no code tile: the decoders write an identity block
+        } else {
+          mbar_arrive_expect_tx(&full_c[s], L::CODE_BYTES);
+          tma_load_2d(sCodes + s * (L::CODE_BYTES / 4), &p.tmap_codes, &full_c[s], n_tile * L::WORDS_PER_ROW,
+                      (kb - KR) * TC_BK);
+        }
+      };
+      int ahead = 0;
+      if (pair < num_tiles)
+        for (; ahead < S && ahead < kb_count; ++ahead) issue_codes(ahead, ahead, (pair % pair_n_tiles) * 2 + (int)rank);
+      pdl_wait();
       uint32_t it = 0;
       bool ok = true;
       for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
@@ -623,15 +642,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc2_palette_gemm_kernel(const _
           if (leader) mbar_arrive_expect_tx(&full_b[s], 2 * L::A_BYTES);
           const uint32_t full_b_leader = mapa_shared(smem_addr(&full_b[s]), 0);
           const int y = m_tile * T + (int)rank * L::HALF_ROWS;
-          if (kb < KR) {
-            mbar_arrive(&full_c[s]);  // no code tile: the decoders write an identity block
+          if ((int)it >= ahead) issue_codes(s, kb, n_tile);
+          if (kb < KR)
             tma_load_2d_pair(sA + s * L::A_BYTES, &p.tmap_res, full_b_leader, np * 2 * TC_BM + kb * TC_BK, y);
-          } else {
-            mbar_arrive_expect_tx(&full_c[s], L::CODE_BYTES);
-            tma_load_2d(sCodes + s * (L::CODE_BYTES / 4), &p.tmap_codes, &full_c[s], n_tile * L::WORDS_PER_ROW,
-                        (kb - KR) * TC_BK);
+          else
             tma_load_2d_pair(sA + s * L::A_BYTES, &p.tmap_a, full_b_leader, (kb - KR) * TC_BK, y);
-          }
           last_round[s] = (int)round;
         }
       }
