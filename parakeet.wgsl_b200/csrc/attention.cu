@@ -140,10 +140,12 @@ __global__ void __launch_bounds__(ATT_THREADS) rel_attention_simt_kernel(
 
 int launch_rel_attention(const DeviceCtx& dev, int precision, int batch, int frames, const void* qkv,
                          const void* positions, const float* bias_u, const float* bias_v,
-                         const uint32_t* valid_lengths, void* context, cudaStream_t stream) {
+                         const uint32_t* valid_lengths, void* context, cudaStream_t stream,
+                         const void* positions_rowmajor) {
   (void)dev;
   if (precision == PK_FP16 && g_attention_route != 1)
-    return launch_rel_attention_tc(batch, frames, qkv, positions, bias_u, bias_v, valid_lengths, context, stream);
+    return launch_rel_attention_tc(batch, frames, qkv, positions_rowmajor ? positions_rowmajor : positions, bias_u,
+                                   bias_v, valid_lengths, context, stream, positions_rowmajor != nullptr);
   const dim3 grid((frames + ATT_QB - 1) / ATT_QB, 8, batch);
   if (precision == PK_FP16)
     launch_kernel(rel_attention_simt_kernel<__half>, grid, ATT_THREADS, 0, stream, 

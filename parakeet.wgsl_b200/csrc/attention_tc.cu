@@ -104,6 +104,10 @@ __device__ __forceinline__ void q_frags(uint32_t (&frag)[8][4], const __half* __
   }
 }
 
+// ROWMAJOR: positions as [8 heads][2T-1][128] (row-contiguous, re-laid out
+// once by the encoder); otherwise the package's head-vector-position-vec4
+// layout [8*32 vectors][2T-1][4].
+template <bool ROWMAJOR>
 __global__ void __launch_bounds__(ATHREADS, 2) rel_attention_flash_kernel(
     const __half* __restrict__ qkv, const __half* __restrict__ positions, const float* __restrict__ bias_u,
     const float* __restrict__ bias_v, const uint32_t* __restrict__ valid_lengths, __half* __restrict__ context,
@@ -157,12 +161,22 @@ __global__ void __launch_bounds__(ATHREADS, 2) rel_attention_flash_kernel(
       else *reinterpret_cast<uint4*>(Vs + jr * AS + c) = make_uint4(0, 0, 0, 0);
     }
     const int band0 = frames - AQ - q0 + j0;  // relative index of band row 0
-    for (int i = tid; i < APR * 32; i += ATHREADS) {
-      const int r = i % APR, vec = i / APR, rel = band0 + r;
-      if (rel >= 0 && rel < P)
-        cp_async8(smem_addr(Ps + r * AS + vec * 4), positions + ((size_t)(h * 32 + vec) * P + rel) * 4);
-      else
-        *reinterpret_cast<uint2*>(Ps + r * AS + vec * 4) = make_uint2(0, 0);
+    if constexpr (ROWMAJOR) {
+      for (int i = tid; i < APR * 16; i += ATHREADS) {
+        const int r = i >> 4, c = (i & 15) * 8, rel = band0 + r;
+        if (rel >= 0 && rel < P)
+          cp_async16(smem_addr(Ps + r * AS + c), positions + ((size_t)h * P + rel) * 128 + c);
+        else
+          *reinterpret_cast<uint4*>(Ps + r * AS + c) = make_uint4(0, 0, 0, 0);
+      }
+    } else {
+      for (int i = tid; i < APR * 32; i += ATHREADS) {
+        const int r = i % APR, vec = i / APR, rel = band0 + r;
+        if (rel >= 0 && rel < P)
+          cp_async8(smem_addr(Ps + r * AS + vec * 4), positions + ((size_t)(h * 32 + vec) * P + rel) * 4);
+        else
+          *reinterpret_cast<uint2*>(Ps + r * AS + vec * 4) = make_uint2(0, 0);
+      }
     }
     asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
     __syncthreads();
@@ -306,12 +320,36 @@ __global__ void __launch_bounds__(ATHREADS, 2) rel_attention_flash_kernel(
 
 }  // namespace
 
+// positions [8*32][P][4] (package layout) -> [8][P][128].
+__global__ void positions_rowmajor_kernel(const __half* __restrict__ pkg, __half* __restrict__ rm, int P) {
+  pdl_entry();
+  const int h = blockIdx.y, p = blockIdx.x, vec = threadIdx.x;
+  *reinterpret_cast<uint2*>(rm + ((size_t)h * P + p) * 128 + vec * 4) =
+      *reinterpret_cast<const uint2*>(pkg + ((size_t)(h * 32 + vec) * P + p) * 4);
+}
+
+int launch_positions_rowmajor(const void* pkg, void* rm, int frames, cudaStream_t stream) {
+  const int P = 2 * frames - 1;
+  return cuda_error(launch_kernel(positions_rowmajor_kernel, dim3(P, 8), dim3(32), 0, stream,
+                                  static_cast<const __half*>(pkg), static_cast<__half*>(rm), P),
+                    "positions_rowmajor launch");
+}
+
 int launch_rel_attention_tc(int batch, int frames, const void* qkv, const void* positions, const float* bias_u,
-                            const float* bias_v, const uint32_t* valid_lengths, void* context, cudaStream_t stream) {
-  const int st = set_max_dynamic_smem(reinterpret_cast<const void*>(rel_attention_flash_kernel), ASMEM);
-  if (st != PK_OK) return st;
+                            const float* bias_v, const uint32_t* valid_lengths, void* context, cudaStream_t stream,
+                            bool positions_rowmajor) {
   const dim3 grid((frames + AQ - 1) / AQ, 8, batch);
-  launch_kernel(rel_attention_flash_kernel, grid, ATHREADS, ASMEM, stream, 
+  if (positions_rowmajor) {
+    const int st = set_max_dynamic_smem(reinterpret_cast<const void*>(rel_attention_flash_kernel<true>), ASMEM);
+    if (st != PK_OK) return st;
+    launch_kernel(rel_attention_flash_kernel<true>, grid, ATHREADS, ASMEM, stream,
+                  static_cast<const __half*>(qkv), static_cast<const __half*>(positions), bias_u, bias_v,
+                  valid_lengths, static_cast<__half*>(context), frames);
+    return cuda_error(cudaGetLastError(), "rel_attention_flash launch");
+  }
+  const int st = set_max_dynamic_smem(reinterpret_cast<const void*>(rel_attention_flash_kernel<false>), ASMEM);
+  if (st != PK_OK) return st;
+  launch_kernel(rel_attention_flash_kernel<false>, grid, ATHREADS, ASMEM, stream, 
       static_cast<const __half*>(qkv), static_cast<const __half*>(positions), bias_u, bias_v, valid_lengths,
       static_cast<__half*>(context), frames);
   return cuda_error(cudaGetLastError(), "rel_attention_flash launch");

@@ -64,6 +64,7 @@ struct LayerRefs {
       *ln_out_b;
   MatrixRef ff1_l1, ff1_l2, qkv, o_proj, pw1, pw2, ff2_l1, ff2_l2;
   const void* positions;
+  const void* positions_rm = nullptr;  // FP16: [8][375][128] copy for the tensor-core attention
   const float *bias_u, *bias_v;
   const void* dw;
   const float *bn_scale, *bn_shift;
@@ -87,6 +88,7 @@ struct pk_encoder {
   void* p376 = nullptr;
   void* s188 = nullptr;      // [cap, 188, 16, 256]
   void* p188 = nullptr;
+  void* positions_rm = nullptr;  // FP16: every layer's positions, row-major per head
   std::vector<void*> checkpoints;  // optional per-layer outputs
   bool keep_checkpoints = false;
   // model references
@@ -230,7 +232,7 @@ int record_forward(pk_encoder* e, int batch, cudaStream_t s) {
     PK_TRY(launch_layernorm(prec, rows, kHidden, y, L.ln_att_w, L.ln_att_b, 1e-5f, scratch, s));
     PK_TRY(gemm(e, L.qkv, rows, scratch, qkv, PK_ACT_NONE, nullptr, nullptr, 1.0f, s));
     PK_TRY(launch_rel_attention(e->device->ctx, prec, batch, kFrames, qkv, L.positions, L.bias_u, L.bias_v,
-                                e->encoder_lengths, ctx, s));
+                                e->encoder_lengths, ctx, s, L.positions_rm));
     PK_TRY(gemm(e, L.o_proj, rows, ctx, scratch, PK_ACT_NONE, nullptr, y, 1.0f, s));
     PK_TRY(launch_layernorm(prec, rows, kHidden, scratch, L.ln_conv_w, L.ln_conv_b, 1e-5f, y, s));
     PK_TRY(gemm(e, L.pw1, rows, y, pw, PK_ACT_NONE, nullptr, nullptr, 1.0f, s));
@@ -264,7 +266,7 @@ void free_encoder(pk_encoder* e) {
   for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
   e->graphs.clear();
   void* bufs[] = {e->features, e->feature_lengths, e->encoder_lengths, e->slots[0], e->slots[1], e->big,
-                  e->projected, e->s376, e->p376, e->s188, e->p188};
+                  e->projected, e->s376, e->p376, e->s188, e->p188, e->positions_rm};
   for (void* b : bufs)
     if (b) cudaFree(b);
   for (void* b : e->checkpoints)
@@ -425,6 +427,26 @@ int pk_encoder_create(pk_device* device, pk_weights* weights, int precision, int
   if (err != cudaSuccess) {
     free_encoder(e.get());
     return cuda_error(err, "encoder host staging");
+  }
+  if (e->precision == PK_FP16) {
+    // The tensor-core attention reads each head's positions as contiguous
+    // 256-byte rows: re-lay the package's head-vector-position-vec4 tensors
+    // out once ([8][375][128] per layer).
+    const size_t per_layer = (size_t)8 * (2 * kFrames - 1) * 128 * sizeof(uint16_t);
+    err = cudaMalloc(&e->positions_rm, per_layer * kLayers);
+    for (int l = 0; l < kLayers && err == cudaSuccess; ++l) {
+      void* dst = static_cast<char*>(e->positions_rm) + per_layer * l;
+      if (launch_positions_rowmajor(e->layers[l].positions, dst, kFrames, e->capture_stream) != PK_OK) {
+        free_encoder(e.get());
+        return PK_E_CUDA;
+      }
+      e->layers[l].positions_rm = dst;
+    }
+    if (err == cudaSuccess) err = cudaStreamSynchronize(e->capture_stream);
+    if (err != cudaSuccess) {
+      free_encoder(e.get());
+      return cuda_error(err, "encoder positions re-layout");
+    }
   }
   *out = e.release();
   return PK_OK;

@@ -519,6 +519,11 @@ struct Tc2Layout {
   static constexpr int OFF_MISC = (OFF_BAR + NUM_BARS * 8 + 15) / 16 * 16;
   static constexpr int SMEM_BYTES = OFF_MISC + 32 + 1024;
   static constexpr int ACC_BUFS = 2 * T <= 512 ? 2 : 1;
+  // A single accumulator of two MMA sub-tiles is released per sub-tile
+  // (tm_empty[j]: sub-tile j drained), so the next tile's first stages can
+  // start on sub-tile 0 while the epilogue still drains sub-tile 1.
+  static constexpr bool SPLIT_RELEASE = ACC_BUFS == 1 && NSUB == 2;
+  static_assert(!SPLIT_RELEASE || BN_MMA % 32 == 0, "sub-tiles end on epilogue chunk boundaries");
   static constexpr uint32_t IDESC = umma_idesc_f16(2 * TC_BM, BN_MMA, /*A MN-major*/ 1, /*B K-major*/ 0);
   static constexpr uint32_t TMEM_COLS = ACC_BUFS * T <= 256 ? 256 : 512;
   static_assert(STAGES >= 3, "pipeline too shallow");
@@ -666,15 +671,44 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc2_palette_gemm_kernel(const _
       uint32_t it = 0;
       int tile_iter = 0;
       bool ok = true;
+      // MMAs of sub-tile j of stage s (four K=16 steps).
+      auto issue_sub = [&](int s, int kb, int j, uint32_t d_tmem) {
+        const uint32_t w_addr = smem_addr(sW + s * L::W_BYTES);
+        const uint32_t a_addr = smem_addr(sA + s * L::A_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < TC_BK / 16; ++kk) {
+          const uint64_t a_desc = umma_smem_desc(w_addr + kk * 2048, 8192, 1024, 2);
+          const uint64_t b_desc = umma_smem_desc(a_addr + j * L::SUB_ROWS * 128 + kk * 32, 16, 1024, 2);
+          tc_mma_f16_pair(d_tmem + (uint32_t)(j * BN_MMA), a_desc, b_desc, L::IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
+        }
+      };
       for (int tile = pair; tile < num_tiles && ok; tile += num_pairs, ++tile_iter) {
         const int acc = tile_iter % L::ACC_BUFS;
         const uint32_t acc_round = (uint32_t)(tile_iter / L::ACC_BUFS);
-        if (acc_round > 0 &&
-            !mbar_wait(&tm_empty[acc], (acc_round - 1) & 1, abort_flag, p.status, PK_STATUS_TIMEOUT_MMA)) {
+        // Split release: sub-tile 0's columns must be drained before this
+        // tile's first MMA; sub-tile 1's MMAs of the first stages wait (their
+        // stages held) until its columns are drained as well.
+        bool sub1_free = true;
+        int held = 0, held_kb0 = 0;  // stages it - held .. it - 1 hold sub-tile-1 MMAs, from k-step held_kb0
+        const uint32_t ph = (uint32_t)(tile_iter - 1) & 1;
+        if (L::SPLIT_RELEASE && tile_iter > 0) {
+          if (!mbar_wait(&tm_empty[0], ph, abort_flag, p.status, PK_STATUS_TIMEOUT_MMA)) break;
+          sub1_free = mbar_try_wait(&tm_empty[1], ph);
+        } else if (acc_round > 0 &&
+                   !mbar_wait(&tm_empty[acc], (acc_round - 1) & 1, abort_flag, p.status, PK_STATUS_TIMEOUT_MMA)) {
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * T);
+        auto flush_held = [&]() {  // sub-tile 1 of the held stages, in k order, then release them
+          for (int h = 0; h < held; ++h) {
+            const uint32_t hit = it - (uint32_t)held + (uint32_t)h;
+            issue_sub((int)(hit % S), held_kb0 + h, 1, d_tmem);
+            tc_commit_pair(smem_addr(&empty[hit % S]));
+            tc_commit_pair(peer(&empty[hit % S]));
+          }
+          held = 0;
+        };
         for (int kb = 0; kb < kb_count; ++kb, ++it) {
           const int s = it % S;
           const uint32_t round = it / S;
@@ -682,6 +716,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc2_palette_gemm_kernel(const _
               !mbar_wait(&full_dec[s], round & 1, abort_flag, p.status, PK_STATUS_TIMEOUT_MMA)) {
             ok = false;
             break;
+          }
+          if (!sub1_free) {
+            sub1_free = mbar_try_wait(&tm_empty[1], ph);
+            if (!sub1_free && held == S - 1) {  // the last free stage: wait for sub-tile 1's columns
+              if (!mbar_wait(&tm_empty[1], ph, abort_flag, p.status, PK_STATUS_TIMEOUT_MMA)) {
+                ok = false;
+                break;
+              }
+              sub1_free = true;
+            }
+            tc_fence_after();
+            if (sub1_free) {
+              flush_held();
+            } else {
+              if (held == 0) held_kb0 = kb;
+              issue_sub(s, kb, 0, d_tmem);
+              ++held;
+              continue;
+            }
           }
           tc_fence_after();
           const uint32_t w_addr = smem_addr(sW + s * L::W_BYTES);
@@ -699,14 +752,27 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc2_palette_gemm_kernel(const _
           tc_commit_pair(smem_addr(&empty[s]));
           tc_commit_pair(peer(&empty[s]));
         }
+        if (ok && held > 0) {  // a tile shorter than the held stages
+          if (!mbar_wait(&tm_empty[1], ph, abort_flag, p.status, PK_STATUS_TIMEOUT_MMA)) {
+            ok = false;
+          } else {
+            tc_fence_after();
+            flush_held();
+          }
+        }
         if (!ok) break;
         tc_commit_pair(smem_addr(&tm_full[acc]));
         tc_commit_pair(peer(&tm_full[acc]));
       }
-      // The last epilogue signals of each accumulator: the peer's bulk-copy
-      // signals must land before this CTA's shared memory is released.
-      for (int a = 0; a < L::ACC_BUFS && tile_iter > a; ++a)
-        mbar_wait_drain(&tm_empty[a], (uint32_t)((tile_iter - 1 - a) / L::ACC_BUFS) & 1, p.status);
+      // The last epilogue signals: the peer's bulk-copy signals must land
+      // before this CTA's shared memory is released.
+      if constexpr (L::SPLIT_RELEASE) {
+        if (tile_iter > 0)
+          for (int j = 0; j < 2; ++j) mbar_wait_drain(&tm_empty[j], (uint32_t)(tile_iter - 1) & 1, p.status);
+      } else {
+        for (int a = 0; a < L::ACC_BUFS && tile_iter > a; ++a)
+          mbar_wait_drain(&tm_empty[a], (uint32_t)((tile_iter - 1 - a) / L::ACC_BUFS) & 1, p.status);
+      }
       tc_commit_pair(smem_addr(drain));
       mbar_wait_drain(drain, 0, p.status);
     } else if (lane == 0) {
@@ -810,6 +876,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc2_palette_gemm_kernel(const _
         const int j = col / BN_MMA, c = col - j * BN_MMA;
         return m0 + (c < L::SUB_ROWS ? j * L::SUB_ROWS + c : L::HALF_ROWS + j * L::SUB_ROWS + c - L::SUB_ROWS);
       };
+      // Accumulator columns drained -> the leader's tm_empty[idx].
+      auto signal_empty = [&](int idx) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (!leader)
+            bulk_signal_cluster(payload_leader, signal_payload, SIGNAL_BYTES, tm_empty_leader + (uint32_t)(idx * 8));
+          else if (q == 0)
+            mbar_arrive_expect_tx(&tm_empty[idx], (TC_EPI_THREADS / 32) * SIGNAL_BYTES);
+          else
+            mbar_arrive(&tm_empty[idx]);
+        }
+      };
 #pragma unroll 2
       for (int ci = 0; ci < NCH; ++ci) {
         const int col0 = ci * 32;
@@ -819,19 +898,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc2_palette_gemm_kernel(const _
         uint32_t r[32];
         tc_ld_32x32b_x32(t_base + (uint32_t)col0, r);
         tc_wait_ld();
+        if (L::SPLIT_RELEASE && col0 + 32 == BN_MMA) signal_empty(0);  // sub-tile 0 read out of TMEM
         if (tok_a < p.rows || (split < 32 && tok_b < p.rows))
           pair_epilogue_chunk<EPI, ACT>(r, bias_v, p.res_scale, p.out + n, ld, p.rows, tok_a, split, tok_b);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        if (!leader)
-          bulk_signal_cluster(payload_leader, signal_payload, SIGNAL_BYTES, tm_empty_leader + (uint32_t)(acc * 8));
-        else if (q == 0)
-          mbar_arrive_expect_tx(&tm_empty[acc], (TC_EPI_THREADS / 32) * SIGNAL_BYTES);
-        else
-          mbar_arrive(&tm_empty[acc]);
-      }
+      signal_empty(L::SPLIT_RELEASE ? 1 : acc);
     }
   }
 

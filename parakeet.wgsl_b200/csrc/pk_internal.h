@@ -77,11 +77,16 @@ int launch_layernorm(int precision, int64_t rows, int64_t channels, const void* 
 // Two LayerNorms on 1024-wide rows: y1 = LN(x; g1, b1), y2 = LN(y1; g2, b2).
 int launch_layernorm_dual(int precision, int64_t rows, const void* x, const float* g1, const float* b1,
                           const float* g2, const float* b2, float eps, void* y1, void* y2, cudaStream_t stream);
+// positions_rowmajor (optional): the same positions re-laid out [8][2T-1][128]
+// by launch_positions_rowmajor, used by the tensor-core kernel when given.
 int launch_rel_attention(const DeviceCtx& dev, int precision, int batch, int frames, const void* qkv,
                          const void* positions, const float* bias_u, const float* bias_v,
-                         const uint32_t* valid_lengths, void* context, cudaStream_t stream);
+                         const uint32_t* valid_lengths, void* context, cudaStream_t stream,
+                         const void* positions_rowmajor = nullptr);
 int launch_rel_attention_tc(int batch, int frames, const void* qkv, const void* positions, const float* bias_u,
-                            const float* bias_v, const uint32_t* valid_lengths, void* context, cudaStream_t stream);
+                            const float* bias_v, const uint32_t* valid_lengths, void* context, cudaStream_t stream,
+                            bool positions_rowmajor);
+int launch_positions_rowmajor(const void* pkg, void* rm, int frames, cudaStream_t stream);
 int launch_conformer_conv(int precision, int batch, int frames, const void* pointwise, const void* dw,
                           const float* scale, const float* shift, const uint32_t* valid_lengths, void* out,
                           cudaStream_t stream);
