@@ -90,21 +90,22 @@ __device__ __forceinline__ uint32_t pack_h2(__half lo, __half hi) {
   return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
 }
 
-// One CTA: window b, a strip of C0_SR depthwise output rows, 32 channels.
-// The strip's input time samples (4*SR+3 of them, all 128 mel bins) are
-// staged once with coalesced loads; conv0 rows are produced in order into a
-// 3-row ring (rounded to the profile scalar, held as f32): each depthwise row
-// oy needs conv0 rows 2oy-1 .. 2oy+1, and consecutive rows share one.
-template <typename T>
-__global__ void __launch_bounds__(256, 2) conv0_dw2_kernel(const float* __restrict__ fbank,
-                                                           const T* __restrict__ w0, const float* __restrict__ b0,
-                                                           const T* __restrict__ wd, const float* __restrict__ bd,
-                                                           const uint32_t* __restrict__ feature_lengths,
-                                                           T* __restrict__ out) {
+// FP32 profile.  One CTA: window b, a strip of C0_SR depthwise output rows,
+// 32 channels.  The strip's input time samples (4*SR+3 of them, all 128 mel
+// bins) are staged once; conv0 rows are produced in order into a 5-row ring
+// (f32): depthwise row oy needs conv0 rows 2oy-1 .. 2oy+1, and consecutive
+// rows share one.
+__global__ void __launch_bounds__(256, 2) conv0_dw2_f32_kernel(const float* __restrict__ fbank,
+                                                               const float* __restrict__ w0,
+                                                               const float* __restrict__ b0,
+                                                               const float* __restrict__ wd,
+                                                               const float* __restrict__ bd,
+                                                               const uint32_t* __restrict__ feature_lengths,
+                                                               float* __restrict__ out) {
   pdl_entry();
   extern __shared__ __align__(16) float sub_smem[];
   float* in_s = sub_smem;                                 // [C0_IN_ROWS][129]
-  float* ring = sub_smem + C0_IN_FLOATS;                  // [3][64][C0_PITCH], 16-byte aligned
+  float* ring = sub_smem + C0_IN_FLOATS;                  // [5][64][C0_PITCH], 16-byte aligned
   float* wd_s = ring + C0_RING_FLOATS;                    // [9][32] depthwise taps
   float* bd_s = wd_s + 9 * C0_CG;                         // [32] depthwise bias
   const int b = blockIdx.z;
@@ -129,102 +130,18 @@ __global__ void __launch_bounds__(256, 2) conv0_dw2_kernel(const float* __restri
                  : "memory");
   }
   asm volatile("cp.async.commit_group;" ::: "memory");
-  for (int i = tid; i < 9 * C0_CG; i += 256) wd_s[i] = (float)wd[(i / C0_CG) * SUB_C + cbase + i % C0_CG];
+  for (int i = tid; i < 9 * C0_CG; i += 256) wd_s[i] = wd[(i / C0_CG) * SUB_C + cbase + i % C0_CG];
   if (tid < C0_CG) bd_s[tid] = bd[cbase + tid];
   const int cg = tid >> 6;  // 8-channel group of this thread's conv0 outputs
   const int c = cbase + cg * 8;
   const int x = tid & 63;
-  constexpr bool kMma = sizeof(T) == 2;
-  float w[9][8], bias[8];  // FP32 profile (the FP16 path keeps its weights as MMA fragments)
-  if constexpr (!kMma) {
+  float w[9][8], bias[8];
 #pragma unroll
-    for (int k = 0; k < 9; ++k) load8<T>(w0 + k * SUB_C + c, w[k]);
+  for (int k = 0; k < 9; ++k) load8<float>(w0 + k * SUB_C + c, w[k]);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) bias[j] = __ldg(b0 + c + j);
-  }
-  // FP16 profile: conv0 as a tensor-core GEMM, rows = 16 output positions of
-  // one conv0 row, k = the 9 taps (padded to 16), n = 8 channels.  The f32
-  // features are split into f16 hi + lo parts (two MMAs into the same f32
-  // accumulator), so the products keep f32-level precision; the weights are
-  // f16 in this profile.  Lane (g, t) holds weights of taps 2t, 2t+1, 2t+8,
-  // 2t+9 for channel cbase + 8 nt + g, and bias of channels 8 nt + 2t, +1.
-  const int lane = tid & 31, warp = tid >> 5, mg = lane >> 2, mt = lane & 3;
-  uint32_t bw[4][2];
-  float bb[4][2];
-  if constexpr (kMma) {
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
-      const int ch = cbase + nt * 8 + mg;
-      auto wv = [&](int k) { return k < 9 ? reinterpret_cast<const __half*>(w0)[k * SUB_C + ch] : __float2half(0.0f); };
-      bw[nt][0] = pack_h2(wv(2 * mt), wv(2 * mt + 1));
-      bw[nt][1] = pack_h2(wv(2 * mt + 8), wv(2 * mt + 9));
-      bb[nt][0] = __ldg(b0 + cbase + nt * 8 + 2 * mt);
-      bb[nt][1] = __ldg(b0 + cbase + nt * 8 + 2 * mt + 1);
-    }
-  }
+  for (int j = 0; j < 8; ++j) bias[j] = __ldg(b0 + c + j);
   asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
-
-  // conv0 row y, output positions x0 .. x0+15, all 32 channels, by one warp.
-  auto conv0_mma = [&](int y, int x0) {
-    float acc[4][4];
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
-      acc[nt][0] = acc[nt][2] = bb[nt][0];
-      acc[nt][1] = acc[nt][3] = bb[nt][1];
-    }
-    const bool live = y >= 0 && y < SUB_CH && y < vin;
-    if (live) {
-      const int xa = x0 + mg, xb = xa + 8;
-      float va[4], vb[4];  // taps 2t, 2t+1, 2t+8, 2t+9 at positions xa, xb
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int k = q < 2 ? 2 * mt + q : 2 * mt + 6 + q;
-        va[q] = vb[q] = 0.0f;
-        if (k < 9) {
-          const int ky = k / 3, kx = k % 3;
-          const float* rowp = in_s + (2 * y + ky - 1 - iy_first) * C0_IN_PITCH;
-          const int ia = 2 * xa + kx - 1, ib = 2 * xb + kx - 1;
-          if (ia >= 0) va[q] = rowp[ia];
-          vb[q] = rowp[ib];  // ib >= 15
-        }
-      }
-      uint32_t ahi[4], alo[4];
-      __half ha[4], hb[4], la[4], lb[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        ha[q] = __float2half_rn(va[q]);
-        hb[q] = __float2half_rn(vb[q]);
-        la[q] = __float2half_rn(va[q] - __half2float(ha[q]));
-        lb[q] = __float2half_rn(vb[q] - __half2float(hb[q]));
-      }
-      ahi[0] = pack_h2(ha[0], ha[1]), ahi[1] = pack_h2(hb[0], hb[1]);
-      ahi[2] = pack_h2(ha[2], ha[3]), ahi[3] = pack_h2(hb[2], hb[3]);
-      alo[0] = pack_h2(la[0], la[1]), alo[1] = pack_h2(lb[0], lb[1]);
-      alo[2] = pack_h2(la[2], la[3]), alo[3] = pack_h2(lb[2], lb[3]);
-#pragma unroll
-      for (int nt = 0; nt < 4; ++nt) {
-        mma_16816(acc[nt], ahi, bw[nt][0], bw[nt][1]);
-        mma_16816(acc[nt], alo, bw[nt][0], bw[nt][1]);
-      }
-#pragma unroll
-      for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[nt][e] = __half2float(__float2half_rn(fmaxf(acc[nt][e], 0.0f)));
-    } else {
-#pragma unroll
-      for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[nt][e] = 0.0f;
-    }
-    float* slot = ring + ((y + C0_RING) % C0_RING) * SUB_CW * C0_PITCH;
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
-      *reinterpret_cast<float2*>(slot + (x0 + mg) * C0_PITCH + nt * 8 + 2 * mt) = make_float2(acc[nt][0], acc[nt][1]);
-      *reinterpret_cast<float2*>(slot + (x0 + mg + 8) * C0_PITCH + nt * 8 + 2 * mt) =
-          make_float2(acc[nt][2], acc[nt][3]);
-    }
-  };
 
   // conv0 row y (3x3 stride 2 over the staged input) -> ring slot (y + 5) % 5.
   auto conv0_row = [&](int y) {
@@ -246,7 +163,7 @@ __global__ void __launch_bounds__(256, 2) conv0_dw2_kernel(const float* __restri
         }
       }
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j] = (float)(T)fmaxf(acc[j], 0.0f);  // rounded to the profile scalar
+      for (int j = 0; j < 8; ++j) acc[j] = fmaxf(acc[j], 0.0f);
     } else {
 #pragma unroll
       for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
@@ -256,25 +173,13 @@ __global__ void __launch_bounds__(256, 2) conv0_dw2_kernel(const float* __restri
     *reinterpret_cast<float4*>(dst + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
   };
 
-  if constexpr (kMma) {
-    if (warp < 4) conv0_mma(y_first, warp * 16);
-  } else {
-    conv0_row(y_first);
-  }
-  // Two depthwise rows per pass: conv0 rows 2oy .. 2oy+3 (all 8 warps), one
-  // barrier, depthwise rows oy, oy+1 (all 256 threads), one barrier.
+  conv0_row(y_first);
+  // Two depthwise rows per pass: conv0 rows 2oy .. 2oy+3, one barrier,
+  // depthwise rows oy, oy+1 (all 256 threads), one barrier.
   const int y_last = 2 * oy_end - 1;  // last conv0 row this strip needs
 #pragma unroll 1
   for (int oy = oy0; oy < oy_end; oy += 2) {
-    if constexpr (kMma) {
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int y = 2 * oy + 2 * h + (warp >> 2);
-        if (y <= y_last) conv0_mma(y, (warp & 3) * 16);  // 8 warps: 2 rows x 4 position tiles
-      }
-    } else {
-      for (int y = 2 * oy; y <= min(2 * oy + 3, y_last); ++y) conv0_row(y);
-    }
+    for (int y = 2 * oy; y <= min(2 * oy + 3, y_last); ++y) conv0_row(y);
     __syncthreads();
     const int oyr = oy + (tid >> 7);  // depthwise: thread = (row, channel group, output x)
     if (oyr < oy_end) {
@@ -307,9 +212,219 @@ __global__ void __launch_bounds__(256, 2) conv0_dw2_kernel(const float* __restri
           }
         }
       }
-      store8<T>(out + (((size_t)b * SUB_OH + oyr) * SUB_OW + ox) * SUB_C + cbase + dcg * 8, acc);
+      store8<float>(out + (((size_t)b * SUB_OH + oyr) * SUB_OW + ox) * SUB_C + cbase + dcg * 8, acc);
     }
     __syncthreads();  // the next pass overwrites the slots of rows 2oy-1 .. 2oy+2
+  }
+}
+
+// FP16 profile: same strip / channel tiling as the FP32 kernel.
+//
+// conv0 runs on tensor cores (mma.m16n8k16, f16 operands, f32 accumulate):
+// rows = 16 positions of one conv0 row, n = 8 channels, k = the 9 taps as six
+// pairs of horizontally adjacent input samples -- (ky, kx 0..1) and (ky, kx 2)
+// with a zero-weight partner -- so every A-fragment register is one aligned
+// 4-byte shared load.  The f32 features enter as f16 hi + lo parts (two MMAs
+// into one f32 accumulator), so the products keep f32-level precision.
+//
+// Input planes: after the f32 strip is staged (mel bin c at float index
+// c + 1 of its row, bins -1 and 128 zero), each 8-byte slot s -- bins 2s-1
+// and 2s -- is rewritten in place as {hi(2s-1), hi(2s), lo(2s-1), lo(2s)}.
+// The depthwise stage reads the conv0 ring as f16 (its values are rounded to
+// f16 by the reference already): thread = (output x, 4 channels), taps in
+// registers, one 8-byte load per tap; the 96-byte position pitch keeps the
+// stride-2 loads of a half-warp (2 positions x 8 channel groups) on distinct
+// banks.
+constexpr int C0H_ROW_WORDS = 138;  // 4-byte words per plane row (130 used; 138 % 32 == 10: conflict-free)
+constexpr int C0H_PLANE_BYTES = (C0_IN_ROWS * C0H_ROW_WORDS * 4 + 15) / 16 * 16;
+constexpr int C0H_POS = 48;  // halves per conv0 position in the ring (32 channels + 16 padding)
+constexpr int C0H_RING = 3;  // conv0 rows 2oy-1 .. 2oy+1 of one depthwise row
+constexpr int C0H_RING_HALVES = C0H_RING * SUB_CW * C0H_POS;
+constexpr int C0H_SMEM = C0H_PLANE_BYTES + C0H_RING_HALVES * 2 + 2 * C0_CG * 4;
+static_assert(C0H_PLANE_BYTES % 16 == 0 && (C0H_RING_HALVES * 2) % 16 == 0, "FP16 conv0 layout alignment");
+
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+  return v;
+}
+
+__global__ void __launch_bounds__(256, 3) conv0_dw2_f16_kernel(const float* __restrict__ fbank,
+                                                               const __half* __restrict__ w0,
+                                                               const float* __restrict__ b0,
+                                                               const __half* __restrict__ wd,
+                                                               const float* __restrict__ bd,
+                                                               const uint32_t* __restrict__ feature_lengths,
+                                                               __half* __restrict__ out) {
+  pdl_entry();
+  extern __shared__ __align__(16) float sub_smem[];
+  float* plane = sub_smem;  // [C0_IN_ROWS][C0H_ROW_WORDS]
+  __half* ring = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(sub_smem) + C0H_PLANE_BYTES);
+  float* bias0_s = reinterpret_cast<float*>(ring + C0H_RING_HALVES);  // [32] conv0 bias
+  float* biasd_s = bias0_s + C0_CG;                                    // [32] depthwise bias
+  const int b = blockIdx.z;
+  const int oy0 = blockIdx.y * C0_SR;
+  const int oy_end = min(oy0 + C0_SR, SUB_OH);
+  const int cbase = blockIdx.x * C0_CG;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int raw = (int)feature_lengths[b];
+  const int vin = sub_len(raw, 1), vout = sub_len(raw, 2);
+  const int y_first = 2 * oy0 - 1;       // first conv0 row of the strip
+  const int iy_first = 2 * y_first - 1;  // first input time sample
+  // Stage the strip: 4-byte asynchronous copies, all in flight at once,
+  // consecutive threads walking time (contiguous in the feature-major log-mel).
+  for (int i = tid; i < C0_IN_ROWS * SUB_IW; i += 256) {
+    const int r = i % C0_IN_ROWS, x = i / C0_IN_ROWS;
+    const int iy = iy_first + r;
+    const bool in_range = iy >= 0 && iy < SUB_IH;
+    const float* src = fbank + ((size_t)b * SUB_IW + x) * SUB_IH + (in_range ? iy : 0);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_addr(plane + r * C0H_ROW_WORDS + x + 1)),
+                 "l"(src), "r"(in_range ? 4 : 0)
+                 : "memory");
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  for (int r = tid; r < C0_IN_ROWS; r += 256) {  // mel bins -1 and 128
+    plane[r * C0H_ROW_WORDS] = 0.0f;
+    plane[r * C0H_ROW_WORDS + SUB_IW + 1] = 0.0f;
+  }
+  if (tid < C0_CG) {
+    bias0_s[tid] = b0[cbase + tid];
+    biasd_s[tid] = bd[cbase + tid];
+  }
+  const int g = lane >> 2, t = lane & 3;
+  // B fragments: lane (g, t) holds k = 2t, 2t+1 (pair t) and 2t+8, 2t+9
+  // (pair t + 4) of channel cbase + 8 nt + g.  Pair p < 6: ky = p / 2; even p
+  // = taps (ky, 0), (ky, 1); odd p = tap (ky, 2) and a zero weight.
+  uint32_t bw[4][2];
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt) {
+    const int ch = cbase + nt * 8 + g;
+    auto wtap = [&](int p, int second) {
+      if (p >= 6 || ((p & 1) && second)) return __float2half(0.0f);
+      const int ky = p >> 1, kx = (p & 1) ? 2 : second;
+      return w0[(ky * 3 + kx) * SUB_C + ch];
+    };
+    bw[nt][0] = pack_h2(wtap(t, 0), wtap(t, 1));
+    bw[nt][1] = pack_h2(wtap(t + 4, 0), wtap(t + 4, 1));
+  }
+  // Depthwise: thread = (output x, channels 4 dq .. 4 dq + 3).
+  const int ox = warp * 4 + (lane >> 3), dq = lane & 7;
+  float wdr[9][4];
+#pragma unroll
+  for (int k = 0; k < 9; ++k)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) wdr[k][j] = __half2float(wd[k * SUB_C + cbase + 4 * dq + j]);
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
+  // In place: f32 pairs -> {hi pair, lo pair}; consecutive threads walk rows.
+  for (int i = tid; i < C0_IN_ROWS * (SUB_IW / 2 + 1); i += 256) {
+    const int r = i % C0_IN_ROWS, sl = i / C0_IN_ROWS;
+    float2* slot = reinterpret_cast<float2*>(plane + r * C0H_ROW_WORDS) + sl;
+    const float2 v = *slot;
+    const __half2 hi = __floats2half2_rn(v.x, v.y);
+    const float2 hf = __half22float2(hi);
+    const __half2 lo = __floats2half2_rn(v.x - hf.x, v.y - hf.y);
+    uint2 packed;
+    packed.x = *reinterpret_cast<const uint32_t*>(&hi);
+    packed.y = *reinterpret_cast<const uint32_t*>(&lo);
+    *reinterpret_cast<uint2*>(slot) = packed;
+  }
+  __syncthreads();
+
+  const uint32_t plane_addr = smem_addr(plane);
+  // conv0 row y, output positions x0 .. x0+15, all 32 channels, by one warp
+  // -> ring slot y % 3 (ReLU, rounded to f16; rows past the valid length are
+  // zero).
+  auto conv0_mma = [&](int y, int x0) {
+    float acc[4][4];
+    const bool live = y >= 0 && y < SUB_CH && y < vin;
+    if (live) {
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        const float2 bb = *reinterpret_cast<const float2*>(bias0_s + nt * 8 + 2 * t);
+        acc[nt][0] = acc[nt][2] = bb.x;
+        acc[nt][1] = acc[nt][3] = bb.y;
+      }
+      // Pair t at rows ky = t / 2, slot x + (t & 1); pair t + 4 (t < 2) at ky = 2.
+      const int xa = x0 + g;
+      const uint32_t row0 = plane_addr + (uint32_t)((2 * y - 1 - iy_first) * C0H_ROW_WORDS * 4);
+      const uint32_t ra = row0 + (uint32_t)((t >> 1) * C0H_ROW_WORDS * 4 + (xa + (t & 1)) * 8);
+      const uint2 pa = lds64(ra), pb = lds64(ra + 64);  // positions xa, xa + 8
+      uint2 qa = make_uint2(0u, 0u), qb = make_uint2(0u, 0u);
+      if (t < 2) {
+        const uint32_t rq = row0 + (uint32_t)(2 * C0H_ROW_WORDS * 4 + (xa + t) * 8);
+        qa = lds64(rq);
+        qb = lds64(rq + 64);
+      }
+      const uint32_t ahi[4] = {pa.x, pb.x, qa.x, qb.x};
+      const uint32_t alo[4] = {pa.y, pb.y, qa.y, qb.y};
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        mma_16816(acc[nt], ahi, bw[nt][0], bw[nt][1]);
+        mma_16816(acc[nt], alo, bw[nt][0], bw[nt][1]);
+      }
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[nt][e] = fmaxf(acc[nt][e], 0.0f);
+    } else {
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[nt][e] = 0.0f;
+    }
+    __half* slot = ring + (y + C0H_RING) % C0H_RING * (SUB_CW * C0H_POS);
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      *reinterpret_cast<__half2*>(slot + (x0 + g) * C0H_POS + nt * 8 + 2 * t) =
+          __floats2half2_rn(acc[nt][0], acc[nt][1]);
+      *reinterpret_cast<__half2*>(slot + (x0 + g + 8) * C0H_POS + nt * 8 + 2 * t) =
+          __floats2half2_rn(acc[nt][2], acc[nt][3]);
+    }
+  };
+
+  if (warp < 4) conv0_mma(y_first, warp * 16);
+  const int y_last = 2 * oy_end - 1;  // last conv0 row this strip needs
+  // One depthwise row per pass: conv0 rows 2oy, 2oy+1 (8 warps = 2 rows x 4
+  // position tiles), one barrier, the depthwise row, one barrier.
+#pragma unroll 1
+  for (int oy = oy0; oy < oy_end; ++oy) {
+    const int y = 2 * oy + (warp >> 2);
+    if (y <= y_last) conv0_mma(y, (warp & 3) * 16);
+    __syncthreads();
+    float acc[4];
+    if (oy >= vout) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[j] = 0.0f;
+    } else {
+      const float4 bq = *reinterpret_cast<const float4*>(biasd_s + 4 * dq);
+      acc[0] = bq.x, acc[1] = bq.y, acc[2] = bq.z, acc[3] = bq.w;
+#pragma unroll
+      for (int ky = 0; ky < 3; ++ky) {
+        const int iy = oy * 2 + ky - 1;
+        if (iy < 0 || iy >= SUB_CH || iy >= vin) continue;
+        const __half* rowp = ring + (iy % C0H_RING) * (SUB_CW * C0H_POS) + 4 * dq;
+#pragma unroll
+        for (int kx = 0; kx < 3; ++kx) {
+          const int ix = ox * 2 + kx - 1;  // <= 63
+          if (ix < 0) continue;
+          const uint2 raw2 = *reinterpret_cast<const uint2*>(rowp + ix * C0H_POS);
+          const float2 v01 = __half22float2(*reinterpret_cast<const __half2*>(&raw2.x));
+          const float2 v23 = __half22float2(*reinterpret_cast<const __half2*>(&raw2.y));
+          const float* wk = wdr[ky * 3 + kx];
+          acc[0] = fmaf(v01.x, wk[0], acc[0]);
+          acc[1] = fmaf(v01.y, wk[1], acc[1]);
+          acc[2] = fmaf(v23.x, wk[2], acc[2]);
+          acc[3] = fmaf(v23.y, wk[3], acc[3]);
+        }
+      }
+    }
+    const __half2 o01 = __floats2half2_rn(acc[0], acc[1]), o23 = __floats2half2_rn(acc[2], acc[3]);
+    uint2 packed;
+    packed.x = *reinterpret_cast<const uint32_t*>(&o01);
+    packed.y = *reinterpret_cast<const uint32_t*>(&o23);
+    *reinterpret_cast<uint2*>(out + (((size_t)b * SUB_OH + oy) * SUB_OW + ox) * SUB_C + cbase + 4 * dq) = packed;
+    __syncthreads();  // the next pass overwrites the slots of rows 2oy-1, 2oy
   }
 }
 
@@ -376,17 +491,15 @@ int launch_subsampling_conv0_dw2(int precision, int batch, const float* features
                                  const uint32_t* feature_lengths, void* out, cudaStream_t stream) {
   const dim3 grid(SUB_C / C0_CG, C0_STRIPS, batch);
   if (precision == PK_FP16) {
-    int st = set_max_dynamic_smem(reinterpret_cast<const void*>(conv0_dw2_kernel<__half>), C0_SMEM);
+    int st = set_max_dynamic_smem(reinterpret_cast<const void*>(conv0_dw2_f16_kernel), C0H_SMEM);
     if (st != PK_OK) return st;
-    launch_kernel(conv0_dw2_kernel<__half>, grid, 256, C0_SMEM, stream, features, static_cast<const __half*>(conv0_w), conv0_b,
-                                                             static_cast<const __half*>(dw_w), dw_b, feature_lengths,
-                                                             static_cast<__half*>(out));
+    launch_kernel(conv0_dw2_f16_kernel, grid, 256, C0H_SMEM, stream, features, static_cast<const __half*>(conv0_w),
+                  conv0_b, static_cast<const __half*>(dw_w), dw_b, feature_lengths, static_cast<__half*>(out));
   } else {
-    int st = set_max_dynamic_smem(reinterpret_cast<const void*>(conv0_dw2_kernel<float>), C0_SMEM);
+    int st = set_max_dynamic_smem(reinterpret_cast<const void*>(conv0_dw2_f32_kernel), C0_SMEM);
     if (st != PK_OK) return st;
-    launch_kernel(conv0_dw2_kernel<float>, grid, 256, C0_SMEM, stream, features, static_cast<const float*>(conv0_w), conv0_b,
-                                                            static_cast<const float*>(dw_w), dw_b, feature_lengths,
-                                                            static_cast<float*>(out));
+    launch_kernel(conv0_dw2_f32_kernel, grid, 256, C0_SMEM, stream, features, static_cast<const float*>(conv0_w),
+                  conv0_b, static_cast<const float*>(dw_w), dw_b, feature_lengths, static_cast<float*>(out));
   }
   return cuda_error(cudaGetLastError(), "subsampling conv0+dw2 launch");
 }
