@@ -369,11 +369,17 @@ def run_kernel(args):
         desc = L.GemmDesc(L.FP16, m, k, n, bits, 1, n, L.ACT[args.act], 0, 1.0, None, None, a.data_ptr(),
                           dev(codes["data"]).value, dev(lut["data"]).value, c.data_ptr())
         launch = lambda: L.call("pk_palette_gemm", device.handle, ctypes.byref(desc), None)  # noqa: E731
-    elif args.kernel == "attention":
+    elif args.kernel in ("attention", "attention-mma"):
+        # "attention": the tcgen05 kernel on row-major positions (the encoder's
+        # path); "attention-mma": the mma.sync kernel on the package layout.
         b = int(args.shape or BATCH)
         qkv = torch.randn((b * FRAMES, 3072), dtype=torch.float16, device="cuda")
         ctx = torch.empty((b * FRAMES, 1024), dtype=torch.float16, device="cuda")
-        pos = dev((0.5 * rng.standard_normal((8, 32, 375, 4))).astype(np.float16))
+        pos_np = (0.5 * rng.standard_normal((8, 32, 375, 4))).astype(np.float16)
+        if args.kernel == "attention":
+            pos_np = np.ascontiguousarray(pos_np.transpose(0, 2, 1, 3).reshape(8, 375, 128))
+        pk.kernels.set_attention_route("tcgen05-rowmajor" if args.kernel == "attention" else "mma")
+        pos = dev(pos_np)
         u = dev((0.02 * rng.standard_normal((8, 128))).astype(np.float32))
         v = dev((0.02 * rng.standard_normal((8, 128))).astype(np.float32))
         lens = dev(np.full(b, FRAMES, np.uint32))
@@ -388,6 +394,18 @@ def run_kernel(args):
         bb = dev(np.zeros(1024, np.float32))
         launch = lambda: L.call("pk_layernorm", device.handle, L.FP16, rows, 1024,  # noqa: E731
                                 ctypes.c_void_p(x.data_ptr()), g, bb, 1e-5, ctypes.c_void_p(y.data_ptr()), None)
+    elif args.kernel == "subsampling":
+        b = int(args.shape or BATCH)
+        fb = torch.randn((b, 128, 1501), dtype=torch.float32, device="cuda")
+        out = torch.empty((b, 376, 32, 256), dtype=torch.float16, device="cuda")
+        w0 = dev((0.3 * rng.standard_normal((3, 3, 256))).astype(np.float16))
+        b0 = dev((0.02 * rng.standard_normal(256)).astype(np.float32))
+        wd = dev((0.1 * rng.standard_normal((3, 3, 256))).astype(np.float16))
+        bd = dev((0.02 * rng.standard_normal(256)).astype(np.float32))
+        lens = dev(np.full(b, 1501, np.uint32))
+        launch = lambda: L.call("pk_subsampling_conv0_dw2", device.handle, L.FP16, b,  # noqa: E731
+                                ctypes.c_void_p(fb.data_ptr()), w0, b0, wd, bd, lens,
+                                ctypes.c_void_p(out.data_ptr()), None)
     elif args.kernel == "conv":
         b = int(args.shape or BATCH)
         gin = torch.randn((b * FRAMES, 2048), dtype=torch.float16, device="cuda")
@@ -423,7 +441,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
-    ap.add_argument("--kernel", choices=["gemm", "attention", "layernorm", "conv"],
+    ap.add_argument("--kernel", choices=["gemm", "attention", "attention-mma", "layernorm", "conv", "subsampling"],
                     help="profiling target: launch one operator only")
     ap.add_argument("--shape", default="", help="gemm: M,K,N,BITS; attention/conv: batch; layernorm: rows")
     ap.add_argument("--act", default="none", choices=["none", "silu", "relu"])

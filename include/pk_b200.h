@@ -204,8 +204,11 @@ int pk_debug_set_gemm_route(int route);
  * 128 / 192 / 256 = single-CTA tile, -256 / -384 / -512 = CTA-pair tile
  * (used where N is a multiple of 256, else the 256-token single-CTA tile). */
 int pk_debug_set_gemm_tile(int tile);
-/* Test hook (no reference counterpart): 0 = automatic (tensor-core attention
- * for the FP16 package), 1 = CUDA-core attention kernel. */
+/* Test hook (no reference counterpart): 0 = automatic (FP16: the tcgen05
+ * attention where positions are held row-major -- the encoder -- else the
+ * mma.sync tensor-core kernel), 1 = CUDA-core attention kernel, 2 = the
+ * mma.sync kernel, 3 = the tcgen05 kernel reading `positions` of
+ * pk_rel_attention as row-major [8][2T-1][128] instead of the package layout. */
 int pk_debug_set_attention_route(int route);
 
 #ifdef __cplusplus

@@ -142,7 +142,13 @@ int launch_rel_attention(const DeviceCtx& dev, int precision, int batch, int fra
                          const void* positions, const float* bias_u, const float* bias_v,
                          const uint32_t* valid_lengths, void* context, cudaStream_t stream,
                          const void* positions_rowmajor) {
-  (void)dev;
+  if (precision == PK_FP16 && g_attention_route == 3)
+    return launch_rel_attention_umma(dev, batch, frames, qkv, positions, bias_u, bias_v, valid_lengths, context,
+                                     stream);
+  if (precision == PK_FP16 && g_attention_route == 0 &&
+      rel_attention_umma_supported(dev, frames, qkv, positions_rowmajor, context))
+    return launch_rel_attention_umma(dev, batch, frames, qkv, positions_rowmajor, bias_u, bias_v, valid_lengths,
+                                     context, stream);
   if (precision == PK_FP16 && g_attention_route != 1)
     return launch_rel_attention_tc(batch, frames, qkv, positions_rowmajor ? positions_rowmajor : positions, bias_u,
                                    bias_v, valid_lengths, context, stream, positions_rowmajor != nullptr);

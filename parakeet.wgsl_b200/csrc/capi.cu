@@ -227,7 +227,7 @@ int pk_debug_set_gemm_tile(int tile) {
 }
 
 int pk_debug_set_attention_route(int route) {
-  if (route < 0 || route > 1) return set_error(PK_E_INVALID, "route must be 0 or 1");
+  if (route < 0 || route > 3) return set_error(PK_E_INVALID, "route must be 0, 1, 2 or 3");
   g_attention_route = route;
   return PK_OK;
 }

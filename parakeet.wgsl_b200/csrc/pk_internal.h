@@ -87,6 +87,12 @@ int launch_rel_attention_tc(int batch, int frames, const void* qkv, const void* 
                             const float* bias_v, const uint32_t* valid_lengths, void* context, cudaStream_t stream,
                             bool positions_rowmajor);
 int launch_positions_rowmajor(const void* pkg, void* rm, int frames, cudaStream_t stream);
+// tcgen05 attention (FP16, frames <= 192, positions row-major [8][2T-1][128]).
+bool rel_attention_umma_supported(const DeviceCtx& dev, int frames, const void* qkv, const void* positions_rowmajor,
+                                  const void* context);
+int launch_rel_attention_umma(const DeviceCtx& dev, int batch, int frames, const void* qkv,
+                              const void* positions_rowmajor, const float* bias_u, const float* bias_v,
+                              const uint32_t* valid_lengths, void* context, cudaStream_t stream);
 int launch_conformer_conv(int precision, int batch, int frames, const void* pointwise, const void* dw,
                           const float* scale, const float* shift, const uint32_t* valid_lengths, void* out,
                           cudaStream_t stream);
@@ -103,7 +109,10 @@ int launch_subsampling_time_mask(int precision, int batch, int height, int width
 // 2 = force the tensor-core GEMM (fails if the shape is unsupported).
 extern int g_gemm_route;
 extern int g_gemm_tile;
-// Debug / test knob: 0 = automatic (tensor cores for FP16), 1 = CUDA-core attention.
+// Debug / test knob: 0 = automatic (FP16: the tcgen05 kernel when row-major
+// positions are at hand, else the mma.sync kernel), 1 = CUDA-core attention,
+// 2 = the mma.sync kernel, 3 = the tcgen05 kernel with `positions` already
+// row-major [8][2T-1][128].
 extern int g_attention_route;
 
 }  // namespace pk

@@ -536,5 +536,7 @@ def set_gemm_tile(tile: int) -> None:
 
 
 def set_attention_route(route: str) -> None:
-    """Test hook: "auto" (tensor cores for FP16) or "simt"."""
-    _lib.call("pk_debug_set_attention_route", {"auto": 0, "simt": 1}[route])
+    """Test hook: "auto" (tensor cores for FP16), "simt" (CUDA cores), "mma"
+    (the mma.sync kernel) or "tcgen05-rowmajor" (the tcgen05 kernel, with the
+    positions argument given row-major [8][2T-1][128])."""
+    _lib.call("pk_debug_set_attention_route", {"auto": 0, "simt": 1, "mma": 2, "tcgen05-rowmajor": 3}[route])

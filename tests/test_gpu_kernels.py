@@ -327,6 +327,43 @@ def test_rel_attention_simt_route_matches_tensor_core(pk, oracle, device):
     assert rel(outs[0], outs[1]) < 5e-3
 
 
+@pytest.mark.parametrize("frames,lengths", [(188, [188, 150, 1]), (192, [192, 130]), (77, [77, 40]),
+                                            (129, [129, 128])])
+def test_rel_attention_tcgen05(pk, oracle, device, frames, lengths):
+    """FP16 tcgen05 kernel (positions row-major, as the encoder holds them)
+    against the oracle and against the mma.sync kernel."""
+    import torch
+
+    batch = len(lengths)
+    rng = np.random.default_rng(frames + sum(lengths))
+    P = 2 * frames - 1
+    qkv = rng.standard_normal((batch * frames, 3072)).astype(np.float16)
+    pos = (0.5 * rng.standard_normal((8, 32, P, 4))).astype(np.float16)
+    pos_rm = np.ascontiguousarray(pos.transpose(0, 2, 1, 3).reshape(8, P, 128))
+    u = (0.02 * rng.standard_normal((8, 128))).astype(np.float32)
+    v = (0.02 * rng.standard_normal((8, 128))).astype(np.float32)
+    lens = np.array(lengths, np.uint32)
+    outs = []
+    for route, positions in (("tcgen05-rowmajor", pos_rm), ("mma", pos), ("tcgen05-rowmajor", pos_rm)):
+        ctx = torch.full((batch * frames, 1024), float("nan"), dtype=torch.float16, device="cuda")
+        pk.kernels.set_attention_route(route)
+        try:
+            pk._lib.call("pk_rel_attention", device.handle, pk._lib.FP16, batch, frames, vp(cuda(qkv)),
+                         vp(cuda(positions)), vp(cuda(u)), vp(cuda(v)), vp(cuda(lens)), vp(ctx), None)
+        finally:
+            pk.kernels.set_attention_route("auto")
+        outs.append(host(ctx))
+    assert device.status() == 0
+    ref = oracle.rel_attention(qkv, pos, u, v, lens, batch, frames)
+    got = outs[0]
+    assert np.isfinite(got).all()
+    assert rel(got, ref) < FP16_TOL / 4
+    assert rel(got, outs[1]) < 5e-3
+    np.testing.assert_array_equal(got, outs[2])  # deterministic
+    for b, L in enumerate(lengths):
+        assert np.all(got.reshape(batch, frames, 1024)[b, L:] == 0)
+
+
 def test_rel_attention_rejects_long_windows(pk, device):
     x = cuda(np.zeros(8, np.float32))
     with pytest.raises(pk.PkError, match="PK_E_SHAPE"):
