@@ -27,9 +27,9 @@
 // leaves through a TMA store of the f16 tile staged in shared memory.
 //
 // The per-row shift of BD (row r reads its key j at column 127 - r + j) is a
-// skewed read: each warp loads the 64 BD columns its 32 rows need for 32 keys,
-// writes them column-major to a per-warp scratch and reads the diagonal back
-// (both directions conflict-free).
+// skewed read: each warp loads the 64 BD columns its 32 rows need for 32 keys;
+// every thread parks its row's 64 values in shared memory and reads back the
+// 32 it needs at its own offset (both directions conflict-free).
 //
 // Threads: 8 warps; warp w reads TMEM lanes 32 (w % 4) .. +31 (query rows) and
 // handles keys [96 (w / 4), +96) of them in the softmax and dims
@@ -61,7 +61,7 @@ constexpr int U_MISC = U_BAR + 64;             // TMEM slot, abort flag
 constexpr int U_SMEM = U_MISC + 16 + 1024;     // + alignment slack
 static_assert(U_PB % 1024 == 0 && (UKEYS * 128) % 1024 == 0 && (UBAND / 2 * 128) % 1024 == 0,
               "swizzled operands must start on 1024-byte boundaries");
-static_assert(8 * 32 * 64 * 4 <= 2 * UBAND * 128, "per-warp shift scratch fits in the band region");
+static_assert(8 * 32 * 68 * 4 <= 2 * UBAND * 128, "per-thread shift scratch rows fit in the band region");
 
 constexpr uint32_t IDESC_S = umma_idesc_f16(UQ, UKEYS, 0, 0);
 constexpr uint32_t IDESC_BD = umma_idesc_f16(UQ, UBAND / 2, 0, 0);
@@ -167,11 +167,10 @@ __global__ void __launch_bounds__(UTHREADS, 1) rel_attention_umma_kernel(const _
   {
     const int c8 = tid & 15;
     float ub[8], vb[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      ub[k] = __ldg(p.bias_u + h * 128 + c8 * 8 + k);
-      vb[k] = __ldg(p.bias_v + h * 128 + c8 * 8 + k);
-    }
+    *reinterpret_cast<float4*>(ub) = __ldg(reinterpret_cast<const float4*>(p.bias_u + h * 128 + c8 * 8));
+    *reinterpret_cast<float4*>(ub + 4) = __ldg(reinterpret_cast<const float4*>(p.bias_u + h * 128 + c8 * 8 + 4));
+    *reinterpret_cast<float4*>(vb) = __ldg(reinterpret_cast<const float4*>(p.bias_v + h * 128 + c8 * 8));
+    *reinterpret_cast<float4*>(vb + 4) = __ldg(reinterpret_cast<const float4*>(p.bias_v + h * 128 + c8 * 8 + 4));
     bool qok = mbar_wait(bar_q, 0, abort_flag, p.status, PK_STATUS_TIMEOUT_TMA);
 #pragma unroll 4
     for (int r = tid >> 4; r < UQ && qok; r += UTHREADS / 16) {
@@ -235,35 +234,56 @@ __global__ void __launch_bounds__(UTHREADS, 1) rel_attention_umma_kernel(const _
   const uint32_t t_row = tmem_base + ((uint32_t)(qd * 32) << 16);
   const float scale = 0.08838834764831845f * 1.4426950408889634f;  // log2(e) / sqrt(128): base-2 softmax
   if (ok) {
-    // ---- scores = (S + shifted BD) * scale, masked; written back over S
-    float* scr = reinterpret_cast<float*>(sm + U_PB) + warp * (64 * 32);
+    // ---- scores = (S + shifted BD) * scale, masked; written back over S.
+    // Row r needs BD window entry 31 - lane + jj for key jc + jj: the thread
+    // parks its 64 window values in its own scratch row (16-byte stores, row
+    // pitch 68 floats: conflict-free both ways) and reads them back shifted.
+    // The next chunk's TMEM loads are issued before this chunk's arithmetic.
+    const uint32_t scr_row = smem_addr(sm + U_PB) + (uint32_t)((warp * 32 + lane) * 68 * 4);
     float mx = -3.402823466e+38f;
-#pragma unroll 1
-    for (int c = 0; c < 3; ++c) {
-      const int jc = kh * 96 + c * 32;
-      uint32_t sv[32], d0[32], d1[32];
+    uint32_t sa[32], sb[32], d0[32], d1[32];
+    auto load_chunk = [&](int jc, uint32_t(&sv)[32]) {
       const uint32_t cb = (uint32_t)(UKEYS + 96 - 32 * qd + jc);  // band rows 96 - 32 qd + jc .. +63
       tc_ld_32x32b_x32(t_row + (uint32_t)jc, sv);
       tc_ld_32x32b_x32(t_row + cb, d0);
       tc_ld_32x32b_x32(t_row + cb + 32, d1);
+    };
+    auto score_chunk = [&](int c, uint32_t(&sv)[32], uint32_t(&next)[32]) {
+      const int jc = kh * 96 + c * 32;
       tc_wait_ld();
 #pragma unroll
-      for (int k = 0; k < 32; ++k) {
-        scr[k * 32 + lane] = __uint_as_float(d0[k]);
-        scr[(k + 32) * 32 + lane] = __uint_as_float(d1[k]);
+      for (int k = 0; k < 8; ++k) {
+        sts128(scr_row + k * 16, d0[4 * k], d0[4 * k + 1], d0[4 * k + 2], d0[4 * k + 3]);
+        sts128(scr_row + 128 + k * 16, d1[4 * k], d1[4 * k + 1], d1[4 * k + 2], d1[4 * k + 3]);
       }
-      __syncwarp();
+      if (c < 2) load_chunk(jc + 32, next);
+      const uint32_t rd = scr_row + (uint32_t)((31 - lane) * 4);
+      if (jc + 32 <= valid) {
 #pragma unroll
-      for (int jj = 0; jj < 32; ++jj) {
-        const float bd = scr[(31 - lane + jj) * 32 + lane];  // band row 127 - r + j
-        float v = (__uint_as_float(sv[jj]) + bd) * scale;
-        if (jc + jj >= valid) v = -3.402823466e+38f;
-        mx = fmaxf(mx, v);
-        sv[jj] = __float_as_uint(v);
+        for (int jj = 0; jj < 32; ++jj) {
+          float bd;
+          asm volatile("ld.shared.f32 %0, [%1];" : "=f"(bd) : "r"(rd + jj * 4));
+          const float v = (__uint_as_float(sv[jj]) + bd) * scale;
+          mx = fmaxf(mx, v);
+          sv[jj] = __float_as_uint(v);
+        }
+      } else {
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) {
+          float bd;
+          asm volatile("ld.shared.f32 %0, [%1];" : "=f"(bd) : "r"(rd + jj * 4));
+          float v = (__uint_as_float(sv[jj]) + bd) * scale;
+          if (jc + jj >= valid) v = -3.402823466e+38f;
+          mx = fmaxf(mx, v);
+          sv[jj] = __float_as_uint(v);
+        }
       }
-      __syncwarp();
       tc_st_32x32b_x32(t_row + (uint32_t)jc, sv);
-    }
+    };
+    load_chunk(kh * 96, sa);
+    score_chunk(0, sa, sb);
+    score_chunk(1, sb, sa);
+    score_chunk(2, sa, sb);
     tc_wait_st();
     red_max[kh * UQ + r] = mx;
     __syncthreads();
@@ -271,20 +291,28 @@ __global__ void __launch_bounds__(UTHREADS, 1) rel_attention_umma_kernel(const _
     // ---- probabilities (f16) into the A operand of the PV MMA; f32 row sums
     float sum = 0.0f;
     const uint32_t pbuf = smem_addr(sm + U_P);
-#pragma unroll 1
-    for (int c = 0; c < 3; ++c) {
+    auto prob_chunk = [&](int c, uint32_t(&sv)[32], uint32_t(&next)[32]) {
       const int jc = kh * 96 + c * 32;
-      uint32_t sv[32];
-      tc_ld_32x32b_x32(t_row + (uint32_t)jc, sv);
       tc_wait_ld();
+      if (c < 2) tc_ld_32x32b_x32(t_row + (uint32_t)(jc + 32), next);
       uint32_t pk[16];
+      if (jc + 32 <= valid) {
 #pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        const int j = jc + 2 * e;
-        const float p0 = j < valid ? ex2f(__uint_as_float(sv[2 * e]) - mx) : 0.0f;
-        const float p1 = j + 1 < valid ? ex2f(__uint_as_float(sv[2 * e + 1]) - mx) : 0.0f;
-        sum += p0 + p1;
-        pk[e] = pack_h2f(p0, p1);
+        for (int e = 0; e < 16; ++e) {
+          const float p0 = ex2f(__uint_as_float(sv[2 * e]) - mx);
+          const float p1 = ex2f(__uint_as_float(sv[2 * e + 1]) - mx);
+          sum += p0 + p1;
+          pk[e] = pack_h2f(p0, p1);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int j = jc + 2 * e;
+          const float p0 = j < valid ? ex2f(__uint_as_float(sv[2 * e]) - mx) : 0.0f;
+          const float p1 = j + 1 < valid ? ex2f(__uint_as_float(sv[2 * e + 1]) - mx) : 0.0f;
+          sum += p0 + p1;
+          pk[e] = pack_h2f(p0, p1);
+        }
       }
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -292,7 +320,11 @@ __global__ void __launch_bounds__(UTHREADS, 1) rel_attention_umma_kernel(const _
         sts128(pbuf + (uint32_t)((key0 >> 6) * (UQ * 128)) + sw128(r, (key0 >> 3) & 7), pk[4 * q], pk[4 * q + 1],
                pk[4 * q + 2], pk[4 * q + 3]);
       }
-    }
+    };
+    tc_ld_32x32b_x32(t_row + (uint32_t)(kh * 96), sa);
+    prob_chunk(0, sa, sb);
+    prob_chunk(1, sb, sa);
+    prob_chunk(2, sa, sb);
     red_sum[kh * UQ + r] = sum;
     fence_proxy_async_smem();
   }
