@@ -6,7 +6,7 @@
 //   s_ij = ((q_i+u).k_j + (q_i+v).p[T-1-i+j]) / sqrt(128), keys j >= valid
 //   excluded, f32 softmax over keys, ctx_i = sum_j prob_ij v_j, rows i >= valid
 //   zero.
-// One CTA = (128 queries, head, window), windows of at most 192 frames:
+// A tile = (128 queries, head, window), windows of at most 192 frames:
 //   S  = (Q+u) . K^T       M=128, N=192 keys          TMEM columns [0, 192)
 //   BD = (Q+v) . Pband^T   M=128, N=320 band rows     TMEM columns [192, 512)
 //        band row rr holds relative position T-128-q0+rr, so query row r and
@@ -31,11 +31,15 @@
 // every thread parks its row's 64 values in shared memory and reads back the
 // 32 it needs at its own offset (both directions conflict-free).
 //
+// Persistent CTAs, one per SM (shared memory ~195 KB, TMEM all 512 columns),
+// walk the tiles; the next tile's operands load while this one finishes: the
+// band once the scores are formed, Q once PV has consumed the probabilities,
+// K once the context tile staged over V has been stored.
 // Threads: 8 warps; warp w reads TMEM lanes 32 (w % 4) .. +31 (query rows) and
 // handles keys [96 (w / 4), +96) of them in the softmax and dims
 // [64 (w / 4), +64) in the epilogue.  Thread 0 issues the TMA loads and MMAs.
-// Shared memory (~195 KB) and TMEM (all 512 columns) hold one CTA per SM.
 #include <cuda.h>
+#include <algorithm>
 #include <cudaTypedefs.h>
 
 #include "pk_common.cuh"
@@ -57,8 +61,8 @@ constexpr int U_KV = 65536;                    // K (then V): 2 dim blocks x 192
 constexpr int U_PB = U_KV + 2 * UKEYS * 128;   // positional band: 2 dim blocks x 320 rows x 128 B
 constexpr int U_RED = U_PB + 2 * UBAND * 128;  // row max [2][128], row sum [2][128]
 constexpr int U_BAR = U_RED + 4 * UQ * 4;      // 6 mbarriers
-constexpr int U_MISC = U_BAR + 64;             // TMEM slot, abort flag
-constexpr int U_SMEM = U_MISC + 16 + 1024;     // + alignment slack
+constexpr int U_MISC = U_BAR + 64;             // TMEM slot, abort flag, barrier arm counts
+constexpr int U_SMEM = U_MISC + 64 + 1024;     // + alignment slack
 static_assert(U_PB % 1024 == 0 && (UKEYS * 128) % 1024 == 0 && (UBAND / 2 * 128) % 1024 == 0,
               "swizzled operands must start on 1024-byte boundaries");
 static_assert(8 * 32 * 68 * 4 <= 2 * UBAND * 128, "per-thread shift scratch rows fit in the band region");
@@ -78,6 +82,7 @@ struct UmmaAttnParams {
   __half* context;
   unsigned int* status;
   int frames;
+  int batch;
 };
 
 __device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
@@ -105,34 +110,28 @@ __global__ void __launch_bounds__(UTHREADS, 1) rel_attention_umma_kernel(const _
   pdl_entry();
   extern __shared__ uint8_t u_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(u_raw) + 1023) & ~uintptr_t(1023));
-  const int q0 = blockIdx.x * UQ, h = blockIdx.y, b = blockIdx.z;
   const int T = p.frames;
+  const int qtiles = (T + UQ - 1) / UQ;
+  const int num_tiles = qtiles * 8 * p.batch;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int valid = min((int)p.valid_lengths[b], T);
-  const size_t row0 = (size_t)b * T;
-  const int qend = min(q0 + UQ, T);
-  if (q0 >= valid) {  // whole block masked: zero its context rows
-    for (int i = tid; i < (qend - q0) * 16; i += UTHREADS) {
-      const int q = q0 + i / 16, c = (i % 16) * 8;
-      *reinterpret_cast<uint4*>(p.context + (row0 + q) * 1024 + h * 128 + c) = make_uint4(0, 0, 0, 0);
-    }
-    return;
-  }
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + U_BAR);
-  uint64_t* bar_ld = bars;      // K + band landed
-  uint64_t* bar_s = bars + 1;   // S MMAs done (K may be overwritten)
-  uint64_t* bar_bd = bars + 2;  // S and BD MMAs done
+  // Each barrier completes once per tile (phase parity = tile iteration & 1).
+  uint64_t* bar_q = bars;       // Q landed
+  uint64_t* bar_k = bars + 1;   // K landed
+  uint64_t* bar_pb = bars + 2;  // band landed
   uint64_t* bar_v = bars + 3;   // V landed
-  uint64_t* bar_o = bars + 4;   // PV MMAs done
-  uint64_t* bar_q = bars + 5;   // Q landed
+  uint64_t* bar_sb = bars + 4;  // S and BD MMAs done
+  uint64_t* bar_o = bars + 5;   // PV MMAs done
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + U_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + U_MISC + 4);
   float* red_max = reinterpret_cast<float*>(sm + U_RED);
   float* red_sum = red_max + 2 * UQ;
-  const int band0 = T - UQ - q0;  // relative position of band row 0
 
   if (tid == 0) {
-    for (int i = 0; i < 6; ++i) mbar_init(&bars[i], 1);
+    for (int i = 0; i < 6; ++i) {
+      mbar_init(&bars[i], 1);
+      reinterpret_cast<uint32_t*>(sm + U_MISC + 16)[i] = 0;
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -144,96 +143,132 @@ __global__ void __launch_bounds__(UTHREADS, 1) rel_attention_umma_kernel(const _
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  bool issued_ld = false, issued_v = false, issued_mma = false, issued_pv = false;
-  if (tid == 0) {
+
+  // Tile t = (query tile, head, window), query tile fastest.
+  auto tile_of = [&](int t, int& q0, int& h, int& b) {
+    q0 = (t % qtiles) * UQ;
+    h = (t / qtiles) % 8;
+    b = t / (qtiles * 8);
+  };
+  // Loads and MMA commits are issued by thread 0, which counts each
+  // barrier's arms for the unwind.
+  uint32_t* arms = reinterpret_cast<uint32_t*>(sm + U_MISC + 16);  // thread 0 only
+  auto load_q = [&](int t) {
+    int q0, h, b;
+    tile_of(t, q0, h, b);
+    mbar_arrive_expect_tx(bar_q, 2 * UQ * 128);
+    for (int kb = 0; kb < 2; ++kb) tma_load_3d(sm + U_QU + kb * UQ * 128, &p.tmap_q, bar_q, h * 128 + kb * 64, q0, b);
+    ++arms[0];
+  };
+  auto load_kv = [&](int t, uint64_t* bar, int col0, int idx) {  // col0 1024: K, 2048: V
+    int q0, h, b;
+    tile_of(t, q0, h, b);
+    mbar_arrive_expect_tx(bar, 2 * UKEYS * 128);
+    for (int kb = 0; kb < 2; ++kb)
+      tma_load_3d(sm + U_KV + kb * UKEYS * 128, &p.tmap_kv, bar, col0 + h * 128 + kb * 64, 0, b);
+    ++arms[idx];
+  };
+  auto load_band = [&](int t) {
+    int q0, h, b;
+    tile_of(t, q0, h, b);
+    const int band0 = T - UQ - q0;  // relative position of band row 0
+    mbar_arrive_expect_tx(bar_pb, 2 * UBAND * 128);
+    for (int kb = 0; kb < 2; ++kb)
+      for (int half = 0; half < 2; ++half)
+        tma_load_3d(sm + U_PB + kb * UBAND * 128 + half * (UBAND / 2) * 128, &p.tmap_pos, bar_pb, kb * 64,
+                    band0 + half * (UBAND / 2), h);
+    ++arms[2];
+  };
+  if (tid == 0 && (int)blockIdx.x < num_tiles) {
     tma_prefetch_desc(&p.tmap_q);
     tma_prefetch_desc(&p.tmap_kv);
     tma_prefetch_desc(&p.tmap_pos);
     tma_prefetch_desc(&p.tmap_ctx);
-    mbar_arrive_expect_tx(bar_q, 2 * UQ * 128);
-    for (int kb = 0; kb < 2; ++kb) tma_load_3d(sm + U_QU + kb * UQ * 128, &p.tmap_q, bar_q, h * 128 + kb * 64, q0, b);
-    mbar_arrive_expect_tx(bar_ld, 2 * UKEYS * 128 + 2 * UBAND * 128);
-    for (int kb = 0; kb < 2; ++kb) {
-      tma_load_3d(sm + U_KV + kb * UKEYS * 128, &p.tmap_kv, bar_ld, 1024 + h * 128 + kb * 64, 0, b);
-      for (int half = 0; half < 2; ++half)
-        tma_load_3d(sm + U_PB + kb * UBAND * 128 + half * (UBAND / 2) * 128, &p.tmap_pos, bar_ld, kb * 64,
-                    band0 + half * (UBAND / 2), h);
-    }
-    issued_ld = true;
+    load_q(blockIdx.x);
+    load_kv(blockIdx.x, bar_k, 1024, 1);
+    load_band(blockIdx.x);
   }
-  // (Q+u) in place and (Q+v) beside it, rounded to f16, in the same swizzled
-  // K-major layout (rows past the window arrive as zero and stay zero).  Each
-  // thread keeps one 8-dim chunk column, so its biases are loaded once.
-  {
-    const int c8 = tid & 15;
-    float ub[8], vb[8];
-    *reinterpret_cast<float4*>(ub) = __ldg(reinterpret_cast<const float4*>(p.bias_u + h * 128 + c8 * 8));
-    *reinterpret_cast<float4*>(ub + 4) = __ldg(reinterpret_cast<const float4*>(p.bias_u + h * 128 + c8 * 8 + 4));
-    *reinterpret_cast<float4*>(vb) = __ldg(reinterpret_cast<const float4*>(p.bias_v + h * 128 + c8 * 8));
-    *reinterpret_cast<float4*>(vb + 4) = __ldg(reinterpret_cast<const float4*>(p.bias_v + h * 128 + c8 * 8 + 4));
-    bool qok = mbar_wait(bar_q, 0, abort_flag, p.status, PK_STATUS_TIMEOUT_TMA);
-#pragma unroll 4
-    for (int r = tid >> 4; r < UQ && qok; r += UTHREADS / 16) {
-      const uint32_t off = (uint32_t)((c8 >> 3) * (UQ * 128)) + sw128(r, c8 & 7);
-      const uint4 raw = *reinterpret_cast<const uint4*>(sm + U_QU + off);
-      const __half2* hv = reinterpret_cast<const __half2*>(&raw);
-      const bool live = q0 + r < T;
-      uint32_t qu[4], qv[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float2 f = __half22float2(hv[k]);
-        qu[k] = live ? pack_h2f(f.x + ub[2 * k], f.y + ub[2 * k + 1]) : 0u;
-        qv[k] = live ? pack_h2f(f.x + vb[2 * k], f.y + vb[2 * k + 1]) : 0u;
-      }
-      sts128(smem_addr(sm + U_QU + off), qu[0], qu[1], qu[2], qu[3]);
-      sts128(smem_addr(sm + U_QV + off), qv[0], qv[1], qv[2], qv[3]);
-    }
-  }
-  fence_proxy_async_smem();  // the threads' writes become visible to the tensor core
-  __syncthreads();
-
-  if (tid == 0) {
-    if (mbar_wait(bar_ld, 0, abort_flag, p.status, PK_STATUS_TIMEOUT_TMA)) {
-      tc_fence_after();
-      const uint32_t qu = smem_addr(sm + U_QU), qv = smem_addr(sm + U_QV);
-      const uint32_t kbase = smem_addr(sm + U_KV), pbase = smem_addr(sm + U_PB);
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {  // 8 K=16 steps over the 128 dims
-        const uint32_t ko = (uint32_t)((ks >> 2) * (UQ * 128) + (ks & 3) * 32);
-        tc_mma_f16(tmem_base, umma_smem_desc(qu + ko, 16, 1024, 2),
-                   umma_smem_desc(kbase + (uint32_t)((ks >> 2) * UKEYS * 128 + (ks & 3) * 32), 16, 1024, 2),
-                   IDESC_S, ks > 0 ? 1u : 0u);
-      }
-      tc_commit(bar_s);
-#pragma unroll
-      for (int half = 0; half < 2; ++half)
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          const uint32_t ko = (uint32_t)((ks >> 2) * (UQ * 128) + (ks & 3) * 32);
-          const uint32_t bo = (uint32_t)((ks >> 2) * UBAND * 128 + half * (UBAND / 2) * 128 + (ks & 3) * 32);
-          tc_mma_f16(tmem_base + (uint32_t)(UKEYS + half * (UBAND / 2)), umma_smem_desc(qv + ko, 16, 1024, 2),
-                     umma_smem_desc(pbase + bo, 16, 1024, 2), IDESC_BD, ks > 0 ? 1u : 0u);
-        }
-      tc_commit(bar_bd);
-      issued_mma = true;
-      // V replaces K once the S MMAs have read it.
-      if (mbar_wait(bar_s, 0, abort_flag, p.status, PK_STATUS_TIMEOUT_MMA)) {
-        mbar_arrive_expect_tx(bar_v, 2 * UKEYS * 128);
-        for (int kb = 0; kb < 2; ++kb)
-          tma_load_3d(sm + U_KV + kb * UKEYS * 128, &p.tmap_kv, bar_v, 2048 + h * 128 + kb * 64, 0, b);
-        issued_v = true;
-      }
-    }
-  }
-  bool ok = mbar_wait(bar_bd, 0, abort_flag, p.status, PK_STATUS_TIMEOUT_MMA);
-  ok = __syncthreads_and(ok) != 0;
-  tc_fence_after();
 
   const int qd = warp & 3, kh = warp >> 2;
   const int r = qd * 32 + lane;  // query row in the tile
   const uint32_t t_row = tmem_base + ((uint32_t)(qd * 32) << 16);
   const float scale = 0.08838834764831845f * 1.4426950408889634f;  // log2(e) / sqrt(128): base-2 softmax
-  if (ok) {
+  uint32_t it = 0;
+#pragma unroll 1
+  for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
+    const uint32_t ph = it & 1;
+    int q0, h, b;
+    tile_of(t, q0, h, b);
+    const int valid = min((int)p.valid_lengths[b], T);
+    const int tn = t + (int)gridDim.x;
+    const bool has_next = tn < num_tiles;
+    // ---- (Q+u) in place and (Q+v) beside it, rounded to f16, in the same
+    // swizzled K-major layout (rows past the window stay zero).  Each thread
+    // keeps one 8-dim chunk column, so its biases load once per tile.
+    bool ok;
+    {
+      const int c8 = tid & 15;
+      float ub[8], vb[8];
+      *reinterpret_cast<float4*>(ub) = __ldg(reinterpret_cast<const float4*>(p.bias_u + h * 128 + c8 * 8));
+      *reinterpret_cast<float4*>(ub + 4) = __ldg(reinterpret_cast<const float4*>(p.bias_u + h * 128 + c8 * 8 + 4));
+      *reinterpret_cast<float4*>(vb) = __ldg(reinterpret_cast<const float4*>(p.bias_v + h * 128 + c8 * 8));
+      *reinterpret_cast<float4*>(vb + 4) = __ldg(reinterpret_cast<const float4*>(p.bias_v + h * 128 + c8 * 8 + 4));
+      ok = mbar_wait(bar_q, ph, abort_flag, p.status, PK_STATUS_TIMEOUT_TMA);
+#pragma unroll 4
+      for (int rr = tid >> 4; rr < UQ && ok; rr += UTHREADS / 16) {
+        const uint32_t off = (uint32_t)((c8 >> 3) * (UQ * 128)) + sw128(rr, c8 & 7);
+        const uint4 raw = *reinterpret_cast<const uint4*>(sm + U_QU + off);
+        const __half2* hv = reinterpret_cast<const __half2*>(&raw);
+        const bool live = q0 + rr < T;
+        uint32_t qu[4], qv[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = __half22float2(hv[k]);
+          qu[k] = live ? pack_h2f(f.x + ub[2 * k], f.y + ub[2 * k + 1]) : 0u;
+          qv[k] = live ? pack_h2f(f.x + vb[2 * k], f.y + vb[2 * k + 1]) : 0u;
+        }
+        sts128(smem_addr(sm + U_QU + off), qu[0], qu[1], qu[2], qu[3]);
+        sts128(smem_addr(sm + U_QV + off), qv[0], qv[1], qv[2], qv[3]);
+      }
+    }
+    fence_proxy_async_smem();  // the threads' writes become visible to the tensor core
+    ok = __syncthreads_and(ok) != 0;
+    if (!ok) break;
+    // ---- BD = (Q+v) . band^T as soon as the band is in, then S = (Q+u) . K^T
+    if (tid == 0) {
+      const uint32_t qu = smem_addr(sm + U_QU), qv = smem_addr(sm + U_QV);
+      const uint32_t kbase = smem_addr(sm + U_KV), pbase = smem_addr(sm + U_PB);
+      if (mbar_wait(bar_pb, ph, abort_flag, p.status, PK_STATUS_TIMEOUT_TMA)) {
+        tc_fence_after();
+#pragma unroll
+        for (int half = 0; half < 2; ++half)
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {  // 8 K=16 steps over the 128 dims
+            const uint32_t ko = (uint32_t)((ks >> 2) * (UQ * 128) + (ks & 3) * 32);
+            const uint32_t bo = (uint32_t)((ks >> 2) * UBAND * 128 + half * (UBAND / 2) * 128 + (ks & 3) * 32);
+            tc_mma_f16(tmem_base + (uint32_t)(UKEYS + half * (UBAND / 2)), umma_smem_desc(qv + ko, 16, 1024, 2),
+                       umma_smem_desc(pbase + bo, 16, 1024, 2), IDESC_BD, ks > 0 ? 1u : 0u);
+          }
+        if (mbar_wait(bar_k, ph, abort_flag, p.status, PK_STATUS_TIMEOUT_TMA)) {
+          tc_fence_after();
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {
+            const uint32_t ko = (uint32_t)((ks >> 2) * (UQ * 128) + (ks & 3) * 32);
+            tc_mma_f16(tmem_base, umma_smem_desc(qu + ko, 16, 1024, 2),
+                       umma_smem_desc(kbase + (uint32_t)((ks >> 2) * UKEYS * 128 + (ks & 3) * 32), 16, 1024, 2),
+                       IDESC_S, ks > 0 ? 1u : 0u);
+          }
+        }
+        tc_commit(bar_sb);  // also after a failed K wait: the BD MMAs must drain
+        ++arms[4];
+      }
+    }
+    ok = mbar_wait(bar_sb, ph, abort_flag, p.status, PK_STATUS_TIMEOUT_MMA);
+    ok = __syncthreads_and(ok && *abort_flag == 0) != 0;  // thread 0's own flag covers a failed K wait
+    if (!ok) break;
+    tc_fence_after();
+    if (tid == 0) load_kv(t, bar_v, 2048, 3);  // V replaces K, which the S MMAs have read
+    {
     // ---- scores = (S + shifted BD) * scale, masked; written back over S.
     // Row r needs BD window entry 31 - lane + jj for key jc + jj: the thread
     // parks its 64 window values in its own scratch row (16-byte stores, row
@@ -286,7 +321,9 @@ __global__ void __launch_bounds__(UTHREADS, 1) rel_attention_umma_kernel(const _
     score_chunk(2, sa, sb);
     tc_wait_st();
     red_max[kh * UQ + r] = mx;
+    fence_proxy_async_smem();  // scratch writes ordered before the next band's TMA writes
     __syncthreads();
+    if (tid == 0 && has_next) load_band(tn);  // the BD MMAs and the scratch are done with the band region
     mx = fmaxf(red_max[r], red_max[UQ + r]);
     // ---- probabilities (f16) into the A operand of the PV MMA; f32 row sums
     float sum = 0.0f;
@@ -328,68 +365,69 @@ __global__ void __launch_bounds__(UTHREADS, 1) rel_attention_umma_kernel(const _
     red_sum[kh * UQ + r] = sum;
     fence_proxy_async_smem();
   }
-  tc_fence_before();
-  __syncthreads();
-  if (tid == 0 && ok && issued_v) {
-    if (mbar_wait(bar_v, 0, abort_flag, p.status, PK_STATUS_TIMEOUT_TMA)) {
-      tc_fence_after();
-      const uint32_t pbuf = smem_addr(sm + U_P), vbase = smem_addr(sm + U_KV);
+    tc_fence_before();
+    __syncthreads();
+    // ---- O = P . V
+    if (tid == 0) {
+      if (mbar_wait(bar_v, ph, abort_flag, p.status, PK_STATUS_TIMEOUT_TMA)) {
+        tc_fence_after();
+        const uint32_t pbuf = smem_addr(sm + U_P), vbase = smem_addr(sm + U_KV);
 #pragma unroll
-      for (int ks = 0; ks < UKEYS / 16; ++ks) {
-        const uint32_t ao = (uint32_t)((ks >> 2) * (UQ * 128) + (ks & 3) * 32);
-        tc_mma_f16(tmem_base, umma_smem_desc(pbuf + ao, 16, 1024, 2),
-                   umma_smem_desc(vbase + (uint32_t)(ks * 2048), UKEYS * 128, 1024, 2), IDESC_PV,
-                   ks > 0 ? 1u : 0u);
+        for (int ks = 0; ks < UKEYS / 16; ++ks) {
+          const uint32_t ao = (uint32_t)((ks >> 2) * (UQ * 128) + (ks & 3) * 32);
+          tc_mma_f16(tmem_base, umma_smem_desc(pbuf + ao, 16, 1024, 2),
+                     umma_smem_desc(vbase + (uint32_t)(ks * 2048), UKEYS * 128, 1024, 2), IDESC_PV,
+                     ks > 0 ? 1u : 0u);
+        }
+        tc_commit(bar_o);
+        ++arms[5];
       }
-      tc_commit(bar_o);
-      issued_pv = true;
     }
-  }
-  if (ok) ok = mbar_wait(bar_o, 0, abort_flag, p.status, PK_STATUS_TIMEOUT_EPILOGUE);
-  ok = __syncthreads_and(ok) != 0;
-  tc_fence_after();
-  if (ok) {
-    // ---- epilogue: warp w stages dims [64 (w / 4), +64) of its 32 rows (f16,
-    // swizzled, over the consumed probabilities); one TMA store per dim block
-    // (rows past the window are clipped by the tensor bounds).
-    const int dh = warp >> 2;
-    uint32_t o0[32], o1[32];
-    tc_ld_32x32b_x32(t_row + (uint32_t)(dh * 64), o0);
-    tc_ld_32x32b_x32(t_row + (uint32_t)(dh * 64 + 32), o1);
-    tc_wait_ld();
-    const bool live = q0 + r < valid;
-    const float inv = live ? 1.0f / (red_sum[r] + red_sum[UQ + r]) : 0.0f;  // rows past valid: zero
-    const uint32_t obuf = smem_addr(sm + U_P + dh * (UQ * 128));
+    ok = mbar_wait(bar_o, ph, abort_flag, p.status, PK_STATUS_TIMEOUT_EPILOGUE);
+    ok = __syncthreads_and(ok) != 0;
+    if (!ok) break;
+    tc_fence_after();
+    if (tid == 0 && has_next) load_q(tn);  // the probabilities are consumed
+    {
+      // ---- epilogue: warp w stages dims [64 (w / 4), +64) of its 32 rows
+      // (f16, swizzled) over the consumed V; one TMA store per dim block (rows
+      // past the window are clipped by the tensor bounds).
+      const int dh = warp >> 2;
+      uint32_t o0[32], o1[32];
+      tc_ld_32x32b_x32(t_row + (uint32_t)(dh * 64), o0);
+      tc_ld_32x32b_x32(t_row + (uint32_t)(dh * 64 + 32), o1);
+      tc_wait_ld();
+      const bool live = q0 + r < valid;
+      const float inv = live ? 1.0f / (red_sum[r] + red_sum[UQ + r]) : 0.0f;  // rows past valid: zero
+      const uint32_t obuf = smem_addr(sm + U_KV + dh * (UQ * 128));
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const uint32_t(&o)[32] = q < 4 ? o0 : o1;
-      const int e = (q & 3) * 8;
-      sts128(obuf + sw128(r, q), pack_h2f(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv),
-             pack_h2f(__uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv),
-             pack_h2f(__uint_as_float(o[e + 4]) * inv, __uint_as_float(o[e + 5]) * inv),
-             pack_h2f(__uint_as_float(o[e + 6]) * inv, __uint_as_float(o[e + 7]) * inv));
+      for (int q = 0; q < 8; ++q) {
+        const uint32_t(&o)[32] = q < 4 ? o0 : o1;
+        const int e = (q & 3) * 8;
+        sts128(obuf + sw128(r, q), pack_h2f(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv),
+               pack_h2f(__uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv),
+               pack_h2f(__uint_as_float(o[e + 4]) * inv, __uint_as_float(o[e + 5]) * inv),
+               pack_h2f(__uint_as_float(o[e + 6]) * inv, __uint_as_float(o[e + 7]) * inv));
+      }
+      fence_proxy_async_smem();
     }
-    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();  // O read out of TMEM (the next tile's MMAs may overwrite it) and staged
+    if (tid == 0) {
+      for (int kb = 0; kb < 2; ++kb)
+        tma_store_3d(&p.tmap_ctx, sm + U_KV + kb * (UQ * 128), h * 128 + kb * 64, q0, b);
+      bulk_commit_group();
+      bulk_wait_group_read_all();  // the staging has been read: K of the next tile may land there
+      if (has_next) load_kv(tn, bar_k, 1024, 1);
+    }
   }
-  __syncthreads();
-  if (tid == 0 && ok) {
-    for (int kb = 0; kb < 2; ++kb) tma_store_3d(&p.tmap_ctx, sm + U_P + kb * (UQ * 128), h * 128 + kb * 64, q0, b);
-    bulk_commit_group();
-    bulk_wait_group_all();
-  }
-  // Unwind: loads and MMAs this CTA issued have landed before its shared
-  // memory and TMEM are released (immediate on the normal path).
+  // Unwind: every load and MMA commit this CTA armed has completed, and its
+  // stores are done, before shared memory and TMEM are released (immediate on
+  // the normal path).
   if (tid == 0) {
-    if (issued_ld) {
-      mbar_wait_drain(bar_q, 0, p.status);
-      mbar_wait_drain(bar_ld, 0, p.status);
-    }
-    if (issued_mma) {
-      mbar_wait_drain(bar_s, 0, p.status);
-      mbar_wait_drain(bar_bd, 0, p.status);
-    }
-    if (issued_v) mbar_wait_drain(bar_v, 0, p.status);
-    if (issued_pv) mbar_wait_drain(bar_o, 0, p.status);
+    for (int i = 0; i < 6; ++i)
+      if (arms[i] > 0) mbar_wait_drain(&bars[i], (arms[i] - 1) & 1, p.status);
+    bulk_wait_group_all();
   }
   tc_fence_before();
   __syncthreads();
@@ -455,10 +493,12 @@ int launch_rel_attention_umma(const DeviceCtx& dev, int batch, int frames, const
   p.valid_lengths = valid_lengths;
   p.context = static_cast<__half*>(context);
   p.status = dev.status;
+  p.batch = batch;
   p.frames = frames;
   const int st = set_max_dynamic_smem(reinterpret_cast<const void*>(rel_attention_umma_kernel), U_SMEM);
   if (st != PK_OK) return st;
-  const dim3 grid((frames + UQ - 1) / UQ, 8, batch);
+  const int num_tiles = (frames + UQ - 1) / UQ * 8 * batch;
+  const dim3 grid((unsigned)std::min(num_tiles, dev.sm_count));  // persistent: one CTA per SM
   return cuda_error(launch_kernel(rel_attention_umma_kernel, grid, dim3(UTHREADS), U_SMEM, stream, p),
                     "rel_attention_umma launch");
 }
