@@ -42,6 +42,15 @@ constexpr int TC_STAGES = 4;
 constexpr int TC_DECODE_WARPS = 8;
 constexpr int TC_FIRST_EPI_WARP = 2 + TC_DECODE_WARPS;  // 10: warps 10..13 cover TMEM lane quarters 2,3,0,1
 constexpr int TC_THREADS = (TC_FIRST_EPI_WARP + 4) * 32;  // 448
+// CTA-pair kernel: one more warp (14) issues the code-tile loads, so that
+// activation and code boxes come from different threads (a thread's TMA
+// boxes are serviced one after another, ~0.3 us each).
+constexpr int TC2_CODE_WARP = TC_FIRST_EPI_WARP + 4;
+// ... and a second epilogue warp per TMEM lane quadrant (warps 15-18) takes
+// every other 32-column chunk, halving the accumulator drain that the next
+// tile's first MMAs wait for.
+constexpr int TC2_EPI_WARPS = 8;
+constexpr int TC2_THREADS = (TC2_CODE_WARP + 1 + 4) * 32;  // 608
 constexpr int TC_EPI_THREADS = 128;
 
 // EPI_RESIDUAL adds res_scale * acc to a residual loaded in the epilogue;
@@ -536,7 +545,7 @@ struct Tc2Layout {
 };
 
 template <int BN_MMA, int NSUB, int BITS, int EPI, int ACT>
-__global__ void __launch_bounds__(TC_THREADS, 1) tc2_palette_gemm_kernel(const __grid_constant__ TcGemmParams p) {
+__global__ void __launch_bounds__(TC2_THREADS, 1) tc2_palette_gemm_kernel(const __grid_constant__ TcGemmParams p) {
   using L = Tc2Layout<BN_MMA, NSUB, BITS>;
   constexpr int S = L::STAGES;
   constexpr int T = L::T;
@@ -575,7 +584,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc2_palette_gemm_kernel(const _
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tm_full[a], 1);
-      mbar_init(&tm_empty[a], TC_EPI_THREADS / 32);  // + SIGNAL_BYTES per peer epilogue warp
+      mbar_init(&tm_empty[a], TC2_EPI_WARPS);  // + SIGNAL_BYTES per peer epilogue warp
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -594,10 +603,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc2_palette_gemm_kernel(const _
   cluster_sync();  // barriers of both CTAs initialised before any remote signal
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  // Programmatic dependent launch: only the producer waits for the previous
-  // kernel (pdl_wait below), before its first activation / residual load;
-  // every other global access of this kernel (output stores) follows those
-  // loads through the pipeline barriers.  Weights are not written by kernels.
+  // Programmatic dependent launch: only the activation producer waits for
+  // the previous kernel (pdl_wait below), before its first activation /
+  // residual load; every other global access of this kernel (output stores)
+  // follows those loads through the pipeline barriers.  Weights are not
+  // written by kernels, so the code-tile producer does not wait.
   pdl_launch_dependents();
 
   // Residual GEMMs run KR extra k-steps first: B = the residual tile (the
@@ -612,31 +622,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc2_palette_gemm_kernel(const _
   const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer (both CTAs)
+    // ------------------------------------------------- activation producer (both CTAs)
     if (lane == 0) {
       int last_round[S];
 #pragma unroll
       for (int s = 0; s < S; ++s) last_round[s] = -1;
-      // The first round's code tiles (weights only) load before the wait on
-      // the previous kernel, so their decode overlaps that kernel's tail.
-      auto issue_codes = [&](int s, int kb, int n_tile) {
-        if (kb < KR) {
-          mbar_arrive(&full_c[s]);  // no code tile: the decoders write an identity block
-        } else {
-          mbar_arrive_expect_tx(&full_c[s], L::CODE_BYTES);
-          tma_load_2d(sCodes + s * (L::CODE_BYTES / 4), &p.tmap_codes, &full_c[s], n_tile * L::WORDS_PER_ROW,
-                      (kb - KR) * TC_BK);
-        }
-      };
-      int ahead = 0;
-      if (pair < num_tiles)
-        for (; ahead < S && ahead < kb_count; ++ahead) issue_codes(ahead, ahead, (pair % pair_n_tiles) * 2 + (int)rank);
       pdl_wait();
       uint32_t it = 0;
       bool ok = true;
       for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
         const int np = tile % pair_n_tiles, m_tile = tile / pair_n_tiles;
-        const int n_tile = np * 2 + (int)rank;  // this CTA's 128-feature tile
         for (int kb = 0; kb < kb_count; ++kb, ++it) {
           const int s = it % S;
           const uint32_t round = it / S;
@@ -647,7 +642,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc2_palette_gemm_kernel(const _
           if (leader) mbar_arrive_expect_tx(&full_b[s], 2 * L::A_BYTES);
           const uint32_t full_b_leader = mapa_shared(smem_addr(&full_b[s]), 0);
           const int y = m_tile * T + (int)rank * L::HALF_ROWS;
-          if ((int)it >= ahead) issue_codes(s, kb, n_tile);
           if (kb < KR)
             tma_load_2d_pair(sA + s * L::A_BYTES, &p.tmap_res, full_b_leader, np * 2 * TC_BM + kb * TC_BK, y);
           else
@@ -655,13 +649,46 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc2_palette_gemm_kernel(const _
           last_round[s] = (int)round;
         }
       }
-      // Unwind: this CTA's code tiles must have landed (the B halves are
-      // tracked by the leader's barriers, which its MMA thread drains).
-      for (int s = 0; s < S; ++s)
-        if (last_round[s] >= 0) mbar_wait_drain(&full_c[s], (uint32_t)last_round[s] & 1, p.status);
+      // Unwind: the B halves are tracked by the leader's barriers, which its
+      // MMA thread drains; the leader's producer also waits for its own.
       if (leader)
         for (int s = 0; s < S; ++s)
           if (last_round[s] >= 0) mbar_wait_drain(&full_b[s], (uint32_t)last_round[s] & 1, p.status);
+    }
+  } else if (warp == TC2_CODE_WARP) {
+    // -------------------------------------------------- code-tile producer (both CTAs)
+    // Weights are not written by kernels, so this warp does not wait for the
+    // previous kernel: the first round's code tiles load (and decode) during
+    // its tail.
+    if (lane == 0) {
+      int last_round[S];
+#pragma unroll
+      for (int s = 0; s < S; ++s) last_round[s] = -1;
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
+        const int np = tile % pair_n_tiles;
+        const int n_tile = np * 2 + (int)rank;  // this CTA's 128-feature tile
+        for (int kb = 0; kb < kb_count; ++kb, ++it) {
+          const int s = it % S;
+          const uint32_t round = it / S;
+          if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1, abort_flag, p.status, PK_STATUS_TIMEOUT_TMA)) {
+            ok = false;
+            break;
+          }
+          if (kb < KR) {
+            mbar_arrive(&full_c[s]);  // no code tile: the decoders write an identity block
+          } else {
+            mbar_arrive_expect_tx(&full_c[s], L::CODE_BYTES);
+            tma_load_2d(sCodes + s * (L::CODE_BYTES / 4), &p.tmap_codes, &full_c[s], n_tile * L::WORDS_PER_ROW,
+                        (kb - KR) * TC_BK);
+          }
+          last_round[s] = (int)round;
+        }
+      }
+      // Unwind: this CTA's code tiles must have landed.
+      for (int s = 0; s < S; ++s)
+        if (last_round[s] >= 0) mbar_wait_drain(&full_c[s], (uint32_t)last_round[s] & 1, p.status);
     }
   } else if (warp == 1) {
     if (lane == 0 && leader) {
@@ -850,6 +877,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc2_palette_gemm_kernel(const _
   } else {
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int q = warp & 3;
+    const int eset = warp < TC2_CODE_WARP ? 0 : 1;  // chunks eset, eset + 2, ...
     const uint32_t tm_empty_leader = mapa_shared(smem_addr(tm_empty), 0);
     const uint32_t payload_leader = mapa_shared(signal_payload, 0);
     constexpr int NCH = T / 32;
@@ -883,14 +911,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc2_palette_gemm_kernel(const _
         if (lane == 0) {
           if (!leader)
             bulk_signal_cluster(payload_leader, signal_payload, SIGNAL_BYTES, tm_empty_leader + (uint32_t)(idx * 8));
-          else if (q == 0)
-            mbar_arrive_expect_tx(&tm_empty[idx], (TC_EPI_THREADS / 32) * SIGNAL_BYTES);
+          else if (q == 0 && eset == 0)
+            mbar_arrive_expect_tx(&tm_empty[idx], TC2_EPI_WARPS * SIGNAL_BYTES);
           else
             mbar_arrive(&tm_empty[idx]);
         }
       };
 #pragma unroll 2
-      for (int ci = 0; ci < NCH; ++ci) {
+      for (int ci = eset; ci < NCH; ci += 2) {
         const int col0 = ci * 32;
         const int split = min(32, (col0 / L::SUB_ROWS + 1) * L::SUB_ROWS - col0);
         const int tok_a = col_token(col0);
@@ -898,7 +926,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc2_palette_gemm_kernel(const _
         uint32_t r[32];
         tc_ld_32x32b_x32(t_base + (uint32_t)col0, r);
         tc_wait_ld();
-        if (L::SPLIT_RELEASE && col0 + 32 == BN_MMA) signal_empty(0);  // sub-tile 0 read out of TMEM
+        // This warp's last chunk of sub-tile 0 read out of TMEM.
+        if (L::SPLIT_RELEASE && col0 < BN_MMA && col0 + 64 >= BN_MMA) signal_empty(0);
         if (tok_a < p.rows || (split < 32 && tok_b < p.rows))
           pair_epilogue_chunk<EPI, ACT>(r, bias_v, p.res_scale, p.out + n, ld, p.rows, tok_a, split, tok_b);
       }
@@ -1033,7 +1062,7 @@ static int launch_tc2_spec(const DeviceCtx& dev, const TcGemmParams& p, cudaStre
   attr[0].val.clusterDim.z = 1;
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see launch_kernel
   attr[1].val.programmaticStreamSerializationAllowed = 1;
-  cfg.blockDim = dim3(TC_THREADS);
+  cfg.blockDim = dim3(TC2_THREADS);
   cfg.dynamicSmemBytes = L::SMEM_BYTES;
   cfg.stream = stream;
   cfg.attrs = attr;
