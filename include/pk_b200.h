@@ -126,6 +126,25 @@ int pk_rel_attention(pk_device* device, int precision, int batch, int frames, co
                      const void* positions, const float* bias_u, const float* bias_v,
                      const uint32_t* valid_lengths, void* context, pk_stream stream);
 
+/* Allocation-free FP16 relative-position attention.  No counterpart in the
+ * reference: it exists for callers that may not allocate device memory (a
+ * host with its own fixed device pool, a process under a scheduler-set memory
+ * cap, a harness that must see every allocation up front), which cannot open a
+ * pk_device either.  It takes no handle and runs on the calling thread's
+ * current device.  Arguments mean what they mean for pk_rel_attention (package
+ * position layout, 1 <= frames <= 192; qkv, positions and context 16-byte
+ * aligned).  The positions are re-laid out into a fixed 784,640-byte scratch
+ * array that the library holds on every GPU that loads it; no cudaMalloc,
+ * cudaFree or allocating library call is made.  Calls whose GPU work overlaps
+ * race on that array: serialise them.  The first call on a device resolves
+ * the array's address; make it before any stream capture.  wait_status
+ * (host, optional): when given, the call waits for the stream and stores the
+ * kernel's status bits (0 = every bounded wait completed; non-zero returns
+ * PK_E_TIMEOUT). */
+int pk_rel_attention_noalloc(int batch, int frames, const void* qkv, const void* positions,
+                             const float* bias_u, const float* bias_v, const uint32_t* valid_lengths,
+                             void* context, uint32_t* wait_status, pk_stream stream);
+
 /* Fused GLU + depthwise k9 + folded BN + SiLU (src/webgpu/kernels/
  * conformer-conv.ts:471-575); replaces FusedConformerConvKernel
  * (:174-351).  pointwise [B*T, 2048]; dw [9, 1024]; scale/shift f32 [1024];

@@ -25,7 +25,8 @@ DTYPE_F16, DTYPE_F32, DTYPE_U32 = 0, 1, 2
 # Every symbol include/pk_b200.h declares.
 EXPORTED = (
     "pk_last_error", "pk_version", "pk_device_open", "pk_device_close", "pk_device_status",
-    "pk_palette_expand", "pk_palette_gemm", "pk_layernorm", "pk_rel_attention", "pk_conformer_conv",
+    "pk_palette_expand", "pk_palette_gemm", "pk_layernorm", "pk_rel_attention", "pk_rel_attention_noalloc",
+    "pk_conformer_conv",
     "pk_subsampling_conv0_dw2", "pk_subsampling_depthwise", "pk_subsampling_time_mask",
     "pk_weights_upload", "pk_weights_release", "pk_encoder_create", "pk_encoder_forward",
     "pk_encoder_set_checkpoints", "pk_encoder_checkpoint", "pk_encoder_destroy", "pk_debug_set_gemm_route",
@@ -93,6 +94,7 @@ def load() -> ctypes.CDLL:
             "pk_palette_gemm": [vp, ctypes.POINTER(GemmDesc), vp],
             "pk_layernorm": [vp, i32, i64, i64, vp, vp, vp, f32, vp, vp],
             "pk_rel_attention": [vp, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp],
+            "pk_rel_attention_noalloc": [i32, i32, vp, vp, vp, vp, vp, vp, ctypes.POINTER(ctypes.c_uint32), vp],
             "pk_conformer_conv": [vp, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp],
             "pk_subsampling_conv0_dw2": [vp, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp],
             "pk_subsampling_depthwise": [vp, i32, i32, i32, i32, i32, vp, vp, vp, vp, i32, vp, vp],
