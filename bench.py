@@ -177,6 +177,51 @@ def time_gemms(pk, device, batch, stream, reps=5):
     return total_flops, total_ms, detail
 
 
+MAX_TOKENS_PER_WINDOW = 2048  # the reference engine's decoder capacity (src/runtime/webgpu-engine.ts:84)
+
+
+def decoder_buffers(pk, device, enc, precision="fp16", seed=0):
+    """PersistentTdtDecoderKernel over `enc` [batch, frames, 640] with synthetic
+    decoder weights; returns (dispatch, descriptor dict)."""
+    import torch
+
+    K = pk.kernels
+    b, t = enc.shape[0], enc.shape[1]
+    dec = pk.synthetic.make_decoder(precision, seed=seed)
+    model = {n: K.GpuTensor.from_record(n, r) for n, r in dec.items()}
+    kern = K.PersistentTdtDecoderKernel.create(device, None, model, precision)
+    u32 = lambda v: torch.full((b,), v, dtype=torch.int32, device="cuda")  # noqa: E731
+    out = lambda: torch.zeros((b, MAX_TOKENS_PER_WINDOW), dtype=torch.int32, device="cuda")  # noqa: E731
+    d = dict(encoder_projected=enc, encoded_lengths=u32(t), decode_starts=u32(0), decode_ends=u32(t),
+             flush_finals=u32(0), tokens=out(), token_frames=out(), token_durations=out(),
+             metadata=torch.zeros(2 * b, dtype=torch.int32, device="cuda"), batch_size=b, frames=t,
+             max_tokens=MAX_TOKENS_PER_WINDOW, model=model)
+    return kern.create_dispatch(d), d
+
+
+def time_decoder(pk, device, enc, stream, reps=3):
+    """CUDA-event time of one greedy TDT decode of the batch on `stream`."""
+    import torch
+
+    disp, d = decoder_buffers(pk, device, enc)
+    with torch.cuda.stream(stream):
+        disp.encode(stream)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(reps):
+            disp.encode(stream)
+        end.record(stream)
+    end.synchronize()
+    ms = start.elapsed_time(end) / reps
+    b = enc.shape[0]
+    counts = d["metadata"][:b].cpu().numpy()
+    return {"kernel": "tdt_decoder_kernel (one 4-CTA cluster per window)", "windows": b,
+            "ms_per_batch": round(ms, 3), "windows_per_s": round(b / (ms * 1e-3), 1),
+            "audio_s_per_s": round(b * WINDOW_SECONDS / (ms * 1e-3), 1),
+            "tokens_per_window": round(float(counts.mean()), 1), "joint_steps_bound": "<= 10 x 188 per window",
+            "weights": "synthetic random-init decoder (blank-biased head)"}
+
+
 def cpu_baseline(pk, package, window_count=1):
     """Oracle (reference algorithm, f16-accumulating GEMMs) on `window_count` windows."""
     from oracle import oracle
@@ -293,6 +338,10 @@ def run_ours(args):
     barrier()
     e2e_ms = max_over_ranks(t_start.elapsed_time(t_end) / args.steps)
 
+    # ---- TDT greedy decoding of this batch's encoder output (synthetic decoder weights)
+    dec_info = time_decoder(pk, device, out.view(BATCH, FRAMES, 640), stream, reps=max(1, min(args.steps, 5)))
+    barrier()
+
     # ---- dominant kernel: palette GEMMs of one step, timed live
     with torch.cuda.stream(stream):
         gemm_flops, gemm_ms, gemm_detail = time_gemms(pk, device, BATCH, stream)
@@ -325,6 +374,7 @@ def run_ours(args):
                          "peak_kind": f"bf16 dense burst, {peak_kind}",
                          "gemm_ms_per_step": round(gemm_ms, 3), "gemm_tflop_per_step": round(gemm_flops / 1e12, 3)},
             "gemm_shapes": gemm_detail,
+            "decoder": dec_info,
             "cpu_baseline": None if cpu_value is None else {
                 "value": round(cpu_value, 3), "unit": UNIT, "cores": int(os.environ.get("OMP_NUM_THREADS", cores)),
                 "kind": "port", "sample": f"1 window x 24 layers, oracle reference mode, {cpu_dt:.1f} s"},
@@ -417,6 +467,11 @@ def run_kernel(args):
         launch = lambda: L.call("pk_conformer_conv", device.handle, L.FP16, b, FRAMES,  # noqa: E731
                                 ctypes.c_void_p(gin.data_ptr()), dw, sc, sh, lens, ctypes.c_void_p(out.data_ptr()),
                                 None)
+    elif args.kernel == "decoder":
+        b = int(args.shape or BATCH)
+        enc = torch.randn((b, FRAMES, 640), dtype=torch.float16, device="cuda")
+        disp, d = decoder_buffers(pk, device, enc)
+        launch = lambda: disp.encode()  # noqa: E731
     else:
         raise SystemExit(f"unknown kernel {args.kernel}")
     for _ in range(args.steps):
@@ -441,9 +496,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
-    ap.add_argument("--kernel", choices=["gemm", "attention", "attention-mma", "layernorm", "conv", "subsampling"],
+    ap.add_argument("--kernel", choices=["gemm", "attention", "attention-mma", "layernorm", "conv", "subsampling",
+                                         "decoder"],
                     help="profiling target: launch one operator only")
-    ap.add_argument("--shape", default="", help="gemm: M,K,N,BITS; attention/conv: batch; layernorm: rows")
+    ap.add_argument("--shape", default="", help="gemm: M,K,N,BITS; attention/conv/decoder: batch; layernorm: rows")
     ap.add_argument("--act", default="none", choices=["none", "silu", "relu"])
     args = ap.parse_args()
     if args.kernel:

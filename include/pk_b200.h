@@ -169,6 +169,42 @@ int pk_subsampling_time_mask(pk_device* device, int precision, int batch, int he
                              int channels, void* values, const uint32_t* feature_lengths, int steps,
                              pk_stream stream);
 
+/* Persistent greedy TDT decoder (prediction net: 2-layer LSTM 640 + projector;
+ * joint: relu(encoder + predictor) -> head 640 x 1032 = 1025 tokens (blank
+ * 1024) + 5 durations {0..4}).  Mirrors TdtDecoderDescriptor (src/webgpu/
+ * kernels/tdt-decoder.ts:54-82) with the decoder tensors of the package
+ * (requireDecoderWeights, :367-420); replaces PersistentTdtDecoderKernel.create
+ * + createDispatch + TdtDecoderDispatch.encode (:155-330, :84-149).  All
+ * pointers are device pointers; weights and the encoder input are f16
+ * (PK_FP16) or f32 (PK_FP32), biases f32; weight, embedding and encoder
+ * pointers 16-byte aligned.  The decoder state lives on chip, so the
+ * reference's state / predictorScratch arena slices have no counterpart. */
+typedef struct pk_tdt_desc {
+  int precision;                      /* PK_FP16 or PK_FP32 */
+  int batch;                          /* windows */
+  int frames;                         /* encoder frames per window (stride of encoder_projected) */
+  int max_tokens;                     /* output capacity per window */
+  const void* encoder_projected;      /* [batch, frames, 640] (after encoder_projector) */
+  const uint32_t* encoded_lengths;    /* u32 [batch] */
+  const uint32_t* decode_starts;      /* u32 [batch]: first frame each decoder consumes */
+  const uint32_t* decode_ends;        /* u32 [batch]: exclusive frame bound */
+  const uint32_t* flush_finals;       /* u32 [batch]: nonzero runs the bounded end-of-stream flush */
+  const void* embedding;              /* decoder.embedding.weight [1025, 640] */
+  const void* lstm_weight0;           /* decoder.lstm.weight_l0 [1280, 2560] (input-hidden-k-by-ifgo) */
+  const float* lstm_bias0;            /* decoder.lstm.bias_l0 [2560] */
+  const void* lstm_weight1;           /* decoder.lstm.weight_l1 [1280, 2560] */
+  const float* lstm_bias1;            /* decoder.lstm.bias_l1 [2560] */
+  const void* projector_weight;       /* decoder.decoder_projector.weight [640, 640] (k-by-output) */
+  const float* projector_bias;        /* decoder.decoder_projector.bias [640] */
+  const void* head_weight;            /* joint.head.weight [640, 1032] (k-by-output, padded) */
+  const float* head_bias;             /* joint.head.bias [1032] */
+  uint32_t* tokens;                   /* u32 [batch, max_tokens] */
+  uint32_t* token_frames;             /* u32 [batch, max_tokens]: encoder frame of each emission */
+  uint32_t* token_durations;          /* u32 [batch, max_tokens] */
+  uint32_t* metadata;                 /* u32 [2 * batch]: token counts, then status flags (1 = overflow) */
+} pk_tdt_desc;
+int pk_tdt_decode(pk_device* device, const pk_tdt_desc* desc, pk_stream stream);
+
 /* ------------------------------------------------------------ model + graph
  * One named tensor of a weight package (ParakeetTensorRecord,
  * src/model/manifest.ts; runtime layouts src/model/runtime-plan.ts:26-37). */

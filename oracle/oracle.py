@@ -57,6 +57,7 @@ def lib() -> ctypes.CDLL:
         _lib.or_subsampling_conv0_dw2.argtypes = [i32, i64, vp, vp, vp, vp, vp, vp, vp]
         _lib.or_subsampling_depthwise.argtypes = [i32, i64, i64, i64, i64, vp, vp, vp, vp, i32, vp]
         _lib.or_subsampling_time_mask.argtypes = [i32, i64, i64, i64, i64, vp, vp, i32]
+        _lib.or_tdt_decode.argtypes = [i32, i64, i64, i64, vp, vp, vp, vp, vp] + [vp] * 9 + [vp] * 4
     return _lib
 
 
@@ -281,3 +282,30 @@ def rel_frobenius(actual: np.ndarray, expected: np.ndarray) -> float:
     e = np.asarray(expected, dtype=np.float64)
     denom = np.linalg.norm(e)
     return float(np.linalg.norm(a - e) / (denom if denom > 0 else 1.0))
+
+
+DECODER_ORDER = ("decoder.embedding.weight", "decoder.lstm.weight_l0", "decoder.lstm.bias_l0",
+                 "decoder.lstm.weight_l1", "decoder.lstm.bias_l1", "decoder.decoder_projector.weight",
+                 "decoder.decoder_projector.bias", "joint.head.weight", "joint.head.bias")
+
+
+def tdt_decode(enc, lengths, decoder, *, max_tokens=376, starts=None, ends=None, flush=None):
+    """Greedy TDT decoding of ``enc`` [batch, frames, 640] (f16 -> FP16 package,
+    f32 -> FP32) with the decoder tensors ``decoder`` (name -> array), restating
+    src/webgpu/kernels/tdt-decoder.ts.  Returns (tokens, frames, durations,
+    counts, status) with the first three u32 [batch, max_tokens]."""
+    enc = np.ascontiguousarray(enc)
+    prec = FP16 if enc.dtype == np.float16 else FP32
+    batch, frames = enc.shape[0], enc.shape[1]
+    u32 = lambda a, d: np.ascontiguousarray(np.full(batch, d, np.uint32) if a is None else np.asarray(a, np.uint32))
+    lengths = u32(lengths, frames)
+    starts, ends, flush = u32(starts, 0), u32(ends, frames), u32(flush, 0)
+    ws = [np.ascontiguousarray(decoder[n]) for n in DECODER_ORDER]
+    tokens = np.zeros((batch, max_tokens), np.uint32)
+    tframes = np.zeros_like(tokens)
+    durs = np.zeros_like(tokens)
+    meta = np.zeros(2 * batch, np.uint32)
+    ptr = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+    lib().or_tdt_decode(prec, batch, frames, max_tokens, ptr(enc), ptr(lengths), ptr(starts), ptr(ends),
+                        ptr(flush), *[ptr(w) for w in ws], ptr(tokens), ptr(tframes), ptr(durs), ptr(meta))
+    return tokens, tframes, durs, meta[:batch].copy(), meta[batch:].copy()

@@ -462,4 +462,222 @@ void or_subsampling_time_mask(int prec, int64_t batch, int64_t height, int64_t w
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Persistent TDT greedy decoder (src/webgpu/kernels/tdt-decoder.ts:1076-2000,
+// the subgroup shader; one sequence at a time -- the shader pairs two
+// sequences per workgroup only to share weight loads, with no arithmetic
+// shared between them).
+//
+// FP16 package (prec 0): every LSTM gate is two f16 FMA chains in increasing
+// input index -- even indices starting from f16(bias), odd indices from 0 --
+// summed in f16 (wgslLstmAccumulate / wgslLstmStore, :596-671); each chain
+// input is f16(x).  The head is one f16 FMA chain per output starting from
+// f16(bias) (wgslFp16PairedHeadBody, :1005-1057) that skips an input index
+// whose f32 value is +0 as long as no -0 or NaN input has been seen.  The
+// projection is an f32 FMA chain over f32(h1) and f32(weight) (:1435-1456).
+// An f16 FMA is emulated with a single rounding: the product of two f16
+// values and the sum with an f16 addend are formed exactly in double, then
+// rounded once to f16 (a fused f16 FMA, as Apple GPUs and CUDA's HFMA2 do).
+// FP32 package (prec 1): the same chains in f32 with fmaf (:682-700, :864-878).
+// Gate nonlinearities: sigmoid(v) = 1/(1+exp(-clamp(v,+-20))), tanh of a value
+// clamped to +-10 (:1310-1326); cell = fma(f, c, i*g), h = o*tanh(cell).
+// Argmax: the largest score (NaN -> -FLT_MAX), lowest id on ties
+// (choose_better, :1478-1486); tokens 0..1023 plus blank 1024, durations from
+// outputs 1025..1029 (wgslHeadArgmaxAndReduce, :769-830).
+// Control: tdt-decoder.ts:1702-1990 (main loop, at most 10 symbols per frame,
+// then the bounded end-of-stream flush).
+// ---------------------------------------------------------------------------
+namespace tdt {
+constexpr int H = 640, G = 2560, KIN = 1280, NOUT = 1032, BLANK = 1024, MAXSYM = 10;
+
+static inline float hfma(float a, float b, float c) {
+  return (float)(half_t)((double)a * (double)b + (double)c);
+}
+static inline float hadd(float a, float b) { return (float)(half_t)((double)a + (double)b); }
+// exp / tanh are taken correctly rounded to f32 (the double-precision
+// functions, rounded once); the shader's f32 versions are backend-defined to
+// a few ulp, and the CUDA decoder uses the same correctly rounded values.
+static inline float sig(float v) {
+  const float b = std::min(std::max(v, -20.0f), 20.0f);
+  return 1.0f / (1.0f + (float)std::exp((double)-b));
+}
+static inline float stanh(float v) { return (float)std::tanh((double)std::min(std::max(v, -10.0f), 10.0f)); }
+
+struct Weights {
+  int prec;
+  const void *emb, *w0, *w1, *pw, *hw;
+  const float *b0, *b1, *pb, *hb;
+};
+
+struct Seq {
+  std::vector<float> h0, c0, h1, c1, proj;
+  Seq() : h0(H, 0.f), c0(H, 0.f), h1(H, 0.f), c1(H, 0.f), proj(H, 0.f) {}
+};
+
+// One LSTM layer: gates from `x` (KIN inputs, only the first `limit` used),
+// then the cell update of (h, c) in place.
+static void lstm_layer(const Weights& W, const void* w, const float* bias, const float* x, int limit,
+                       std::vector<float>& h, std::vector<float>& c) {
+  std::vector<float> gate(G);
+  const int p = W.prec;
+  for (int o = 0; o < G; ++o) {
+    float even, odd = 0.0f;
+    if (p == 0) {
+      even = round_h(bias[o]);
+      for (int k = 0; k < limit; k += 2) {
+        even = hfma(round_h(x[k]), ld(w, 0, (size_t)k * G + o), even);
+        odd = hfma(round_h(x[k + 1]), ld(w, 0, (size_t)(k + 1) * G + o), odd);
+      }
+      gate[o] = hadd(even, odd);
+    } else {
+      even = bias[o];
+      for (int k = 0; k < limit; k += 2) {
+        even = std::fma(x[k], ld(w, 1, (size_t)k * G + o), even);
+        odd = std::fma(x[k + 1], ld(w, 1, (size_t)(k + 1) * G + o), odd);
+      }
+      gate[o] = even + odd;
+    }
+  }
+  for (int ch = 0; ch < H; ++ch) {
+    const float i = sig(gate[ch]), f = sig(gate[H + ch]), g = stanh(gate[2 * H + ch]), o = sig(gate[3 * H + ch]);
+    const float cell = std::fma(f, c[ch], i * g);
+    c[ch] = cell;
+    h[ch] = o * stanh(cell);
+  }
+}
+
+// prepare_predictor + commit (the committed state always equals the last
+// candidate, so the state is advanced in place).
+static void predict(const Weights& W, Seq& s, int token, bool initial) {
+  std::vector<float> x(KIN, 0.0f);
+  if (!initial) {
+    for (int k = 0; k < H; ++k) x[k] = ld(W.emb, W.prec, (size_t)token * H + k);
+    for (int k = 0; k < H; ++k) x[H + k] = s.h0[k];
+    lstm_layer(W, W.w0, W.b0, x.data(), KIN, s.h0, s.c0);
+  } else {
+    lstm_layer(W, W.w0, W.b0, x.data(), 0, s.h0, s.c0);  // SOS: zero input and state
+  }
+  for (int k = 0; k < H; ++k) x[k] = s.h0[k];
+  for (int k = 0; k < H; ++k) x[H + k] = s.h1[k];
+  lstm_layer(W, W.w1, W.b1, x.data(), initial ? H : KIN, s.h1, s.c1);
+  for (int o = 0; o < H; ++o) {
+    float acc = W.pb[o];
+    for (int k = 0; k < H; ++k) acc = std::fma(s.h1[k], ld(W.pw, W.prec, (size_t)k * H + o), acc);
+    s.proj[o] = acc;
+  }
+}
+
+static inline float sanitize(float v) { return v != v ? -3.402823466e38f : v; }
+static inline bool better(float lv, uint32_t lid, float rv, uint32_t rid) {
+  return rv > lv || (rv == lv && rid < lid);
+}
+
+static void joint(const Weights& W, const Seq& s, const void* enc_row, uint32_t* token, uint32_t* duration) {
+  const int p = W.prec;
+  std::vector<float> jin(H);
+  for (int k = 0; k < H; ++k) jin[k] = std::max(ld(enc_row, p, k) + s.proj[k], 0.0f);
+  std::vector<float> acc(NOUT);
+  for (int o = 0; o < NOUT; ++o) acc[o] = p == 0 ? round_h(W.hb[o]) : W.hb[o];
+  bool safe = true;
+  for (int k = 0; k < H; ++k) {
+    uint32_t bits;
+    std::memcpy(&bits, &jin[k], 4);
+    const bool nan = (bits & 0x7fffffffu) > 0x7f800000u;
+    safe = safe && !(bits == 0x80000000u || nan);
+    if (safe && bits == 0u) continue;
+    if (p == 0) {
+      const float xk = round_h(jin[k]);
+      for (int o = 0; o < NOUT; ++o) acc[o] = hfma(xk, ld(W.hw, 0, (size_t)k * NOUT + o), acc[o]);
+    } else {
+      for (int o = 0; o < NOUT; ++o) acc[o] = std::fma(jin[k], ld(W.hw, 1, (size_t)k * NOUT + o), acc[o]);
+    }
+  }
+  float tv = -3.402823466e38f, dv = -3.402823466e38f;
+  uint32_t tid = 0xffffffffu, did = 0xffffffffu;
+  for (uint32_t o = 0; o <= (uint32_t)BLANK; ++o)
+    if (better(tv, tid, sanitize(acc[o]), o)) tv = sanitize(acc[o]), tid = o;
+  for (uint32_t d = 0; d < 5; ++d)
+    if (better(dv, did, sanitize(acc[BLANK + 1 + d]), d)) dv = sanitize(acc[BLANK + 1 + d]), did = d;
+  *token = tid;
+  *duration = did;
+}
+}  // namespace tdt
+
+// Decodes `batch` sequences.  enc: [batch, frames, 640] profile scalar;
+// lengths/starts/ends/flush: u32 [batch]; outputs tokens / token_frames /
+// token_durations u32 [batch, max_tokens]; metadata u32 [2*batch] = counts
+// then status flags (bit 0 = more tokens than max_tokens).
+void or_tdt_decode(int prec, int64_t batch, int64_t frames, int64_t max_tokens, const void* enc,
+                   const uint32_t* lengths, const uint32_t* starts, const uint32_t* ends, const uint32_t* flush,
+                   const void* embedding, const void* lstm0, const float* bias0, const void* lstm1,
+                   const float* bias1, const void* proj_w, const float* proj_b, const void* head_w,
+                   const float* head_b, uint32_t* tokens, uint32_t* token_frames, uint32_t* token_durations,
+                   uint32_t* metadata) {
+  using namespace tdt;
+  const Weights W{prec, embedding, lstm0, lstm1, proj_w, head_w, bias0, bias1, proj_b, head_b};
+  const size_t es = prec == 0 ? 2 : 4;
+#pragma omp parallel for schedule(dynamic, 1)
+  for (int64_t b = 0; b < batch; ++b) {
+    Seq s;
+    uint32_t count = 0, status = 0, sym = 0;
+    const uint32_t enc_len = std::min(std::min(lengths[b], (uint32_t)frames), ends[b]);
+    uint32_t t = std::min(starts[b], enc_len);
+    auto row = [&](uint32_t tt) {
+      return static_cast<const void*>(static_cast<const char*>(enc) + ((size_t)b * frames + tt) * H * es);
+    };
+    auto emit = [&](uint32_t tok, uint32_t frame, uint32_t dur) {
+      if (count < (uint32_t)max_tokens) {
+        const size_t o = (size_t)b * max_tokens + count;
+        tokens[o] = tok;
+        token_frames[o] = frame;
+        token_durations[o] = dur;
+        ++count;
+      } else {
+        status |= 1u;
+      }
+    };
+    if (t < enc_len) predict(W, s, 0, true);
+    while (t < enc_len) {
+      uint32_t tok, dur;
+      joint(W, s, row(t), &tok, &dur);
+      const bool nonblank = tok != (uint32_t)BLANK;
+      if (nonblank) emit(tok, t, dur);
+      sym += 1;
+      if (dur != 0) {
+        t += dur;
+        sym = 0;
+      } else if (!nonblank || sym >= (uint32_t)MAXSYM) {
+        t += 1;
+        sym = 0;
+      }
+      if (nonblank) predict(W, s, (int)tok, false);
+    }
+    if (flush[b] != 0 && starts[b] < enc_len) {
+      uint32_t fsym = 0, blanks = 0, ft = t;
+      const uint32_t len_c = std::min(lengths[b], (uint32_t)frames);
+      while (fsym < (uint32_t)MAXSYM && blanks < 5) {
+        const uint32_t v = fsym % 3;
+        if (v == 0) t = std::min(ft, len_c - 1);
+        else if (v == 1) t = std::min(enc_len - 1, (uint32_t)frames - 1);
+        else t = std::min(std::max(enc_len, 2u) - 2, (uint32_t)frames - 1);
+        uint32_t tok, dur;
+        joint(W, s, row(t), &tok, &dur);
+        const bool nonblank = tok != (uint32_t)BLANK;
+        if (!nonblank) {
+          blanks += 1;
+        } else {
+          blanks = 0;
+          emit(tok, std::min(ft, enc_len - 1), dur);
+        }
+        ft = std::min(ft + std::max(1u, dur), enc_len);
+        fsym += 1;
+        if (nonblank) predict(W, s, (int)tok, false);
+      }
+    }
+    metadata[b] = count;
+    metadata[batch + b] = status;
+  }
+}
+
 }  // extern "C"

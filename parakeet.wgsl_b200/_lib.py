@@ -27,7 +27,7 @@ EXPORTED = (
     "pk_last_error", "pk_version", "pk_device_open", "pk_device_close", "pk_device_status",
     "pk_palette_expand", "pk_palette_gemm", "pk_layernorm", "pk_rel_attention", "pk_rel_attention_noalloc",
     "pk_conformer_conv",
-    "pk_subsampling_conv0_dw2", "pk_subsampling_depthwise", "pk_subsampling_time_mask",
+    "pk_subsampling_conv0_dw2", "pk_subsampling_depthwise", "pk_subsampling_time_mask", "pk_tdt_decode",
     "pk_weights_upload", "pk_weights_release", "pk_encoder_create", "pk_encoder_forward",
     "pk_encoder_set_checkpoints", "pk_encoder_checkpoint", "pk_encoder_destroy", "pk_debug_set_gemm_route",
     "pk_debug_set_gemm_tile", "pk_debug_set_attention_route",
@@ -60,6 +60,16 @@ class GemmDesc(ctypes.Structure):
         ("bias", ctypes.c_void_p), ("residual", ctypes.c_void_p), ("a", ctypes.c_void_p),
         ("codes", ctypes.c_void_p), ("palette", ctypes.c_void_p), ("c", ctypes.c_void_p),
     ]
+
+
+class TdtDesc(ctypes.Structure):
+    _fields_ = [
+        ("precision", ctypes.c_int), ("batch", ctypes.c_int), ("frames", ctypes.c_int),
+        ("max_tokens", ctypes.c_int),
+    ] + [(n, ctypes.c_void_p) for n in (
+        "encoder_projected", "encoded_lengths", "decode_starts", "decode_ends", "flush_finals", "embedding",
+        "lstm_weight0", "lstm_bias0", "lstm_weight1", "lstm_bias1", "projector_weight", "projector_bias",
+        "head_weight", "head_bias", "tokens", "token_frames", "token_durations", "metadata")]
 
 
 class TensorDesc(ctypes.Structure):
@@ -99,6 +109,7 @@ def load() -> ctypes.CDLL:
             "pk_subsampling_conv0_dw2": [vp, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp],
             "pk_subsampling_depthwise": [vp, i32, i32, i32, i32, i32, vp, vp, vp, vp, i32, vp, vp],
             "pk_subsampling_time_mask": [vp, i32, i32, i32, i32, i32, vp, vp, i32, vp],
+            "pk_tdt_decode": [vp, ctypes.POINTER(TdtDesc), vp],
             "pk_weights_upload": [vp, ctypes.POINTER(TensorDesc), i32, ctypes.POINTER(vp)],
             "pk_weights_release": [vp],
             "pk_encoder_create": [vp, vp, i32, i32, ctypes.POINTER(vp)],

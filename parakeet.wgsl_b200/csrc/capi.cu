@@ -256,6 +256,28 @@ int pk_rel_attention(pk_device* device, int precision, int batch, int frames, co
                               context, as_stream(stream));
 }
 
+int pk_tdt_decode(pk_device* device, const pk_tdt_desc* d, pk_stream stream) {
+  if (!device || !d) return set_error(PK_E_INVALID, "null argument");
+  if (d->precision != PK_FP16 && d->precision != PK_FP32) return set_error(PK_E_INVALID, "unknown precision");
+  if (d->batch <= 0 || d->batch > 16383) return set_error(PK_E_SHAPE, "Invalid TDT decoder batchSize");
+  if (d->frames <= 0 || d->frames > (1 << 20)) return set_error(PK_E_SHAPE, "Invalid TDT decoder frames");
+  if (d->max_tokens <= 0 || (int64_t)d->max_tokens * d->batch > ((int64_t)1 << 31))
+    return set_error(PK_E_SHAPE, "Invalid TDT decoder maxTokens");
+  const void* ptrs[] = {d->encoder_projected, d->encoded_lengths, d->decode_starts, d->decode_ends,
+                        d->flush_finals, d->embedding, d->lstm_weight0, d->lstm_bias0, d->lstm_weight1,
+                        d->lstm_bias1, d->projector_weight, d->projector_bias, d->head_weight, d->head_bias,
+                        d->tokens, d->token_frames, d->token_durations, d->metadata};
+  for (const void* q : ptrs)
+    if (!q) return set_error(PK_E_INVALID, "TDT decoder pointer is null");
+  const void* aligned16[] = {d->encoder_projected, d->embedding, d->lstm_weight0, d->lstm_weight1,
+                             d->projector_weight, d->head_weight};
+  for (const void* q : aligned16)
+    if (reinterpret_cast<uintptr_t>(q) & 15)
+      return set_error(PK_E_LAYOUT, "TDT decoder weights and encoder input must be 16-byte aligned");
+  cudaSetDevice(device->ctx.ordinal);
+  return launch_tdt_decode(device->ctx, *d, as_stream(stream));
+}
+
 int pk_conformer_conv(pk_device* device, int precision, int batch, int frames, const void* pointwise,
                       const void* dw_weights, const float* bn_scale, const float* bn_shift,
                       const uint32_t* valid_lengths, void* out, pk_stream stream) {

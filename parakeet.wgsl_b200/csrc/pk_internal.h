@@ -105,6 +105,8 @@ int launch_subsampling_depthwise(int precision, int batch, int ih, int iw, int c
 int launch_subsampling_time_mask(int precision, int batch, int height, int width, int channels, void* values,
                                  const uint32_t* feature_lengths, int steps, cudaStream_t stream);
 
+int launch_tdt_decode(const DeviceCtx& dev, const pk_tdt_desc& d, cudaStream_t stream);
+
 // Debug / test knob: 0 = automatic kernel choice, 1 = force the SIMT GEMM,
 // 2 = force the tensor-core GEMM (fails if the shape is unsupported).
 extern int g_gemm_route;

@@ -388,6 +388,97 @@ class RelativeAttentionKernel:
         return disp
 
 
+# --------------------------------------------------------------------- TDT decoder
+
+# requireDecoderWeights (src/webgpu/kernels/tdt-decoder.ts:367-420): name ->
+# (weight dtype follows the profile?, storage shape, layout).
+TDT_DECODER_TENSORS = {
+    "decoder.embedding.weight": (True, (1025, 640), "token-by-channel-row-major"),
+    "decoder.lstm.weight_l0": (True, (1280, 2560), "input-hidden-k-by-ifgo-row-major-vec4"),
+    "decoder.lstm.bias_l0": (False, (2560,), "ifgo-gates"),
+    "decoder.lstm.weight_l1": (True, (1280, 2560), "input-hidden-k-by-ifgo-row-major-vec4"),
+    "decoder.lstm.bias_l1": (False, (2560,), "ifgo-gates"),
+    "decoder.decoder_projector.weight": (True, (640, 640), "k-by-output-row-major-vec4"),
+    "decoder.decoder_projector.bias": (False, (640,), "output-channel"),
+    "joint.head.weight": (True, (640, 1032), "k-by-output-row-major-vec4"),
+    "joint.head.bias": (False, (1032,), "output-channel-padded-vec4"),
+}
+TDT_DECODER_OVERFLOW = 1
+
+
+def plan_tdt_decoder_execution(batch_size: int) -> dict:
+    """planTdtDecoderExecution (tdt-decoder.ts:39-52), restated for this engine:
+    one 4-CTA cluster per window; the predictor state stays on chip."""
+    if not isinstance(batch_size, int) or batch_size <= 0:
+        raise RangeError("TDT decoder batchSize must be a positive integer")
+    return {"clusters": batch_size, "ctas": 4 * batch_size, "predictor_scratch_bytes": 0}
+
+
+class PersistentTdtDecoderKernel:
+    """PersistentTdtDecoderKernel (src/webgpu/kernels/tdt-decoder.ts:155-330):
+    greedy TDT decoding of whole windows in one persistent launch."""
+
+    def __init__(self, device: Device, weights: dict, profile: str):
+        self.device, self.weights, self.profile = device, weights, profile
+
+    @staticmethod
+    def create(device: Device, arena=None, model: dict | None = None,
+               profile: str = "fp16") -> "PersistentTdtDecoderKernel":
+        """model: name -> GpuTensor holding the decoder tensors of the package."""
+        _precision(profile)
+        if model is None:
+            raise ParakeetError("TDT decoder requires the decoder tensors of a package")
+        wdtype = "float16" if profile == "fp16" else "float32"
+        resident = {}
+        for name, (profiled, shape, layout) in TDT_DECODER_TENSORS.items():
+            if name not in model:
+                raise ParakeetError(f"Missing decoder tensor {name}")
+            t = model[name]
+            want = wdtype if profiled else "float32"
+            if t.dtype != want or tuple(t.shape) != shape or t.layout != layout:
+                raise ParakeetError(f"Unexpected decoder tensor {t.layout} [{','.join(map(str, t.shape))}]")
+            resident[name] = t
+        return PersistentTdtDecoderKernel(device, resident, profile)
+
+    def create_dispatch(self, d: dict) -> _Dispatch:
+        """d (TdtDecoderDescriptor, tdt-decoder.ts:54-82): label, encoder_projected,
+        encoded_lengths, decode_starts, decode_ends, flush_finals, tokens, token_frames,
+        token_durations, metadata, batch_size, frames, max_tokens."""
+        for key in ("batch_size", "frames", "max_tokens"):
+            v = d[key]
+            if not isinstance(v, int) or v <= 0:
+                raise RangeError(f"Invalid TDT decoder {key}")
+        b, t, m = d["batch_size"], d["frames"], d["max_tokens"]
+        esize = 2 if self.profile == "fp16" else 4
+        need = {"encoder_projected": b * t * 640 * esize, "encoded_lengths": b * 4, "decode_starts": b * 4,
+                "decode_ends": b * 4, "flush_finals": b * 4, "tokens": b * m * 4, "token_frames": b * m * 4,
+                "token_durations": b * m * 4, "metadata": b * 2 * 4}
+        for key, nbytes in need.items():
+            buf = d[key]
+            if buf.numel() * buf.element_size() < nbytes:
+                raise RangeError(f"{key} is too small for TDT decoding")
+        disp = _Dispatch(d.get("label", "parakeet-persistent-tdt-decode"))
+        kernel = self
+        w = self.weights
+
+        def encode(stream=None, timestamp_writes=None, active_batch_size: int | None = None):
+            disp._alive()
+            batch = b if active_batch_size is None else active_batch_size
+            if not isinstance(batch, int) or batch <= 0 or batch > b:
+                raise RangeError(f"{disp.label} active batch must be in [1, {b}]")
+            desc = _lib.TdtDesc(_precision(kernel.profile), batch, t, m, *[_ptr(x) for x in (
+                d["encoder_projected"], d["encoded_lengths"], d["decode_starts"], d["decode_ends"],
+                d["flush_finals"], w["decoder.embedding.weight"], w["decoder.lstm.weight_l0"],
+                w["decoder.lstm.bias_l0"], w["decoder.lstm.weight_l1"], w["decoder.lstm.bias_l1"],
+                w["decoder.decoder_projector.weight"], w["decoder.decoder_projector.bias"],
+                w["joint.head.weight"], w["joint.head.bias"], d["tokens"], d["token_frames"],
+                d["token_durations"], d["metadata"])])
+            _lib.call("pk_tdt_decode", kernel.device.handle, ctypes.byref(desc), _stream_handle(stream))
+
+        disp.encode = encode
+        return disp
+
+
 # --------------------------------------------------------------------- conformer conv
 
 class FusedConformerConvKernel:

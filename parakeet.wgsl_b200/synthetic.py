@@ -136,3 +136,50 @@ def make_features(batch: int, seed: int = 0, mean: float = -4.0, std: float = 2.
     """Log-mel features f32 [batch, 128, 1501] feature-major, i.i.d. N(mean, std^2)."""
     rng = np.random.default_rng(seed)
     return rng.normal(mean, std, size=(batch, 128, 1501)).astype(np.float32)
+
+
+# Decoder tensors read by the persistent TDT decoder (src/webgpu/kernels/tdt-decoder.ts:367-420;
+# packed by model/convert.py:1608-1703): name -> (logical shape, layout, weight dtype?).
+DECODER_HIDDEN = 640
+DECODER_TOKENS = 1025          # 1024 vocabulary tokens + blank (id 1024)
+DECODER_HEAD_OUTPUTS = 1032    # 1025 tokens + 5 durations, padded to a multiple of 4
+DECODER_TENSORS = {
+    "decoder.embedding.weight": ((1025, 640), "token-by-channel-row-major", True),
+    "decoder.lstm.weight_l0": ((1280, 2560), "input-hidden-k-by-ifgo-row-major-vec4", True),
+    "decoder.lstm.bias_l0": ((2560,), "ifgo-gates", False),
+    "decoder.lstm.weight_l1": ((1280, 2560), "input-hidden-k-by-ifgo-row-major-vec4", True),
+    "decoder.lstm.bias_l1": ((2560,), "ifgo-gates", False),
+    "decoder.decoder_projector.weight": ((640, 640), "k-by-output-row-major-vec4", True),
+    "decoder.decoder_projector.bias": ((640,), "output-channel", False),
+    "joint.head.weight": ((640, 1032), "k-by-output-row-major-vec4", True),
+    "joint.head.bias": ((1032,), "output-channel-padded-vec4", False),
+}
+
+
+def make_decoder(precision: str = "fp16", seed: int = 0, blank_bias: float = 1.5) -> dict:
+    """Random-init TDT decoder tensors (prediction net + joint head).
+
+    LSTM weights U(+-1/sqrt(640)) (PyTorch's LSTM default), embedding N(0, 1),
+    projector U(+-1/sqrt(640)), head N(0, 0.1); the blank logit's bias is raised
+    by ``blank_bias`` so greedy decoding emits a realistic mix of blanks and
+    tokens.  The two padding outputs of the head are zero."""
+    rng = np.random.default_rng(seed)
+    dt = _np_dtype(precision)
+    a = 1.0 / np.sqrt(DECODER_HIDDEN)
+    head = rng.normal(0.0, 0.1, size=(640, 1032)).astype(np.float32)
+    head[:, 1030:] = 0.0
+    head_bias = rng.normal(0.0, 0.1, size=1032).astype(np.float32)
+    head_bias[1024] += blank_bias
+    head_bias[1030:] = 0.0
+    data = {
+        "decoder.embedding.weight": rng.normal(0.0, 1.0, size=(1025, 640)).astype(dt),
+        "decoder.lstm.weight_l0": rng.uniform(-a, a, size=(1280, 2560)).astype(dt),
+        "decoder.lstm.bias_l0": rng.uniform(-2 * a, 2 * a, size=2560).astype(np.float32),
+        "decoder.lstm.weight_l1": rng.uniform(-a, a, size=(1280, 2560)).astype(dt),
+        "decoder.lstm.bias_l1": rng.uniform(-2 * a, 2 * a, size=2560).astype(np.float32),
+        "decoder.decoder_projector.weight": rng.uniform(-a, a, size=(640, 640)).astype(dt),
+        "decoder.decoder_projector.bias": rng.uniform(-a, a, size=640).astype(np.float32),
+        "joint.head.weight": head.astype(dt),
+        "joint.head.bias": head_bias,
+    }
+    return {name: _rec(data[name], shape, layout) for name, (shape, layout, _) in DECODER_TENSORS.items()}

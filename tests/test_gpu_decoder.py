@@ -1,0 +1,93 @@
+"""GPU parity of the persistent TDT decoder (pk_tdt_decode) against the CPU
+oracle, through the C ABI and the operator mirror.
+
+Bar (north_star): greedy TDT tokens agree on >= 99% of encoder frames.  The
+kernel replays the shader's arithmetic (f16 FMA chains with the same split
+and order, f32 projection chain, same skip and tie rules), so the sequences
+are expected to be identical; the test reports exact agreement and asserts
+the frame bar."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from decoder_util import forced_decoder, frame_agreement
+from gpu_util import cuda, host
+
+pytestmark = pytest.mark.gpu
+
+FRAME_BAR = 0.99
+
+
+def _run_gpu(pk, device, enc, lengths, dec, precision, max_tokens, starts=None, ends=None, flush=None):
+    import torch
+
+    K = pk.kernels
+    b, t = enc.shape[0], enc.shape[1]
+    u32 = lambda a, d: cuda(np.asarray(np.full(b, d) if a is None else a, np.uint32))
+    wdtype = "float16" if precision == "fp16" else "float32"
+    model = {name: K.GpuTensor(name, wdtype if profiled else "float32", shape, layout, cuda(dec[name]))
+             for name, (profiled, shape, layout) in K.TDT_DECODER_TENSORS.items()}
+    kern = K.PersistentTdtDecoderKernel.create(device, None, model, precision)
+    out = lambda: torch.full((b, max_tokens), 0xEEEE, dtype=torch.int32, device="cuda")
+    d = dict(encoder_projected=cuda(enc), encoded_lengths=u32(lengths, t), decode_starts=u32(starts, 0),
+             decode_ends=u32(ends, t), flush_finals=u32(flush, 0), tokens=out(), token_frames=out(),
+             token_durations=out(), metadata=torch.full((2 * b,), -1, dtype=torch.int32, device="cuda"),
+             batch_size=b, frames=t, max_tokens=max_tokens)
+    disp = kern.create_dispatch(d)
+    disp.encode()
+    u = np.uint32
+    meta = host(d["metadata"], u)
+    return host(d["tokens"], u), host(d["token_frames"], u), host(d["token_durations"], u), meta[:b], meta[b:]
+
+
+def _compare(got, ref, lengths):
+    tok, fr, du, cnt, st = got
+    rtok, rfr, rdu, rcnt, rst = ref
+    agree = frame_agreement(tok, fr, cnt, rtok, rfr, rcnt, lengths)
+    exact = all(cnt[b] == rcnt[b] and np.array_equal(tok[b, :cnt[b]], rtok[b, :rcnt[b]]) and
+                np.array_equal(fr[b, :cnt[b]], rfr[b, :rcnt[b]]) and np.array_equal(du[b, :cnt[b]], rdu[b, :rcnt[b]])
+                for b in range(len(lengths)))
+    print(f"decoder: frame agreement {agree:.4f}, exact {exact}, counts {list(cnt)} vs {list(rcnt)}")
+    return agree, exact
+
+
+@pytest.mark.parametrize("precision", ["fp16", "fp32"])
+def test_tdt_decoder_matches_oracle(pk, oracle, device, precision):
+    dt = np.float16 if precision == "fp16" else np.float32
+    rng = np.random.default_rng(11)
+    enc = rng.normal(0, 1, (4, 188, 640)).astype(dt)
+    dec = {k: v["data"] for k, v in pk.synthetic.make_decoder(precision, seed=3).items()}
+    kw = dict(starts=[0, 0, 10, 0], ends=[188, 188, 100, 188], flush=[0, 1, 0, 1])
+    lengths = [188, 150, 188, 5]
+    got = _run_gpu(pk, device, enc, lengths, dec, precision, 400, **kw)
+    ref = oracle.tdt_decode(enc, lengths, dec, max_tokens=400, **kw)
+    assert device.status() == 0
+    assert list(got[4]) == list(ref[4])
+    agree, _ = _compare(got, ref, [min(L, e) for L, e in zip(lengths, kw["ends"])])
+    assert agree >= FRAME_BAR
+
+
+@pytest.mark.parametrize("token,duration,max_tokens,flush", [(1024, 3, 8, 0), (7, 0, 64, 0), (7, 0, 15, 0),
+                                                             (9, 2, 32, 1)])
+def test_tdt_decoder_control_paths(pk, oracle, device, token, duration, max_tokens, flush):
+    """Blank skipping, the 10-symbol cap, overflow and the end-of-stream flush."""
+    enc = np.random.default_rng(4).normal(0, 1, (2, 12, 640)).astype(np.float16)
+    dec = forced_decoder(pk, "fp16", token, duration)
+    got = _run_gpu(pk, device, enc, [12, 5], dec, "fp16", max_tokens, flush=[flush, flush])
+    ref = oracle.tdt_decode(enc, [12, 5], dec, max_tokens=max_tokens, flush=[flush, flush])
+    assert list(got[3]) == list(ref[3]) and list(got[4]) == list(ref[4])
+    for b in range(2):
+        n = int(ref[3][b])
+        assert np.array_equal(got[0][b, :n], ref[0][b, :n]) and np.array_equal(got[1][b, :n], ref[1][b, :n])
+
+
+def test_tdt_decoder_rejects_bad_descriptors(pk, device):
+    K = pk.kernels
+    with pytest.raises(K.RangeError):
+        K.plan_tdt_decoder_execution(0)
+    import ctypes
+
+    desc = pk._lib.TdtDesc(0, 0, 188, 10)
+    with pytest.raises(pk.PkError, match="PK_E_SHAPE"):
+        pk._lib.call("pk_tdt_decode", device.handle, ctypes.byref(desc), None)
