@@ -222,6 +222,29 @@ def time_decoder(pk, device, enc, stream, reps=3):
             "weights": "synthetic random-init decoder (blank-biased head)"}
 
 
+def time_logmel(pk, device, stream, reps=5):
+    """CUDA-event time of the log-mel front end for one batch of 15 s windows."""
+    import torch
+
+    pcm = (0.1 * torch.randn((BATCH, 240_000), device="cuda")).contiguous()
+    valid = torch.full((BATCH,), 240_000, dtype=torch.int32, device="cuda")
+    feats = torch.empty((BATCH, 128, 1501), dtype=torch.float32, device="cuda")
+    fb = pk.kernels.ParakeetFbank(device)
+    with torch.cuda.stream(stream):
+        fb.compute_batch(pcm, valid, out=feats, stream=stream)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(reps):
+            fb.compute_batch(pcm, valid, out=feats, stream=stream)
+        end.record(stream)
+    end.synchronize()
+    ms = start.elapsed_time(end) / reps
+    moved = pcm.numel() * 4 + 3 * feats.numel() * 4  # PCM read, raw write, normalize read + write
+    return {"kernels": "logmel_raw_kernel + logmel_normalize_kernel", "windows": BATCH,
+            "us_per_batch": round(ms * 1e3, 1), "audio_s_per_s": round(BATCH * WINDOW_SECONDS / (ms * 1e-3), 1),
+            "hbm_bytes_per_batch": moved, "achieved_gbs": round(moved / (ms * 1e-3) / 1e9, 1)}
+
+
 def cpu_baseline(pk, package, window_count=1):
     """Oracle (reference algorithm, f16-accumulating GEMMs) on `window_count` windows."""
     from oracle import oracle
@@ -338,6 +361,10 @@ def run_ours(args):
     barrier()
     e2e_ms = max_over_ranks(t_start.elapsed_time(t_end) / args.steps)
 
+    # ---- log-mel front end for this batch (32 x 240 000 samples of PCM)
+    lm_info = time_logmel(pk, device, stream)
+    barrier()
+
     # ---- TDT greedy decoding of this batch's encoder output (synthetic decoder weights)
     dec_info = time_decoder(pk, device, out.view(BATCH, FRAMES, 640), stream, reps=max(1, min(args.steps, 5)))
     barrier()
@@ -375,6 +402,7 @@ def run_ours(args):
                          "gemm_ms_per_step": round(gemm_ms, 3), "gemm_tflop_per_step": round(gemm_flops / 1e12, 3)},
             "gemm_shapes": gemm_detail,
             "decoder": dec_info,
+            "logmel": lm_info,
             "cpu_baseline": None if cpu_value is None else {
                 "value": round(cpu_value, 3), "unit": UNIT, "cores": int(os.environ.get("OMP_NUM_THREADS", cores)),
                 "kind": "port", "sample": f"1 window x 24 layers, oracle reference mode, {cpu_dt:.1f} s"},
@@ -467,6 +495,13 @@ def run_kernel(args):
         launch = lambda: L.call("pk_conformer_conv", device.handle, L.FP16, b, FRAMES,  # noqa: E731
                                 ctypes.c_void_p(gin.data_ptr()), dw, sc, sh, lens, ctypes.c_void_p(out.data_ptr()),
                                 None)
+    elif args.kernel == "logmel":
+        b = int(args.shape or BATCH)
+        pcm = (0.1 * torch.randn((b, 240_000), device="cuda")).contiguous()
+        valid = torch.full((b,), 240_000, dtype=torch.int32, device="cuda")
+        fb = pk.kernels.ParakeetFbank(device)
+        feats = torch.empty((b, 128, 1501), dtype=torch.float32, device="cuda")
+        launch = lambda: fb.compute_batch(pcm, valid, out=feats)  # noqa: E731
     elif args.kernel == "decoder":
         b = int(args.shape or BATCH)
         enc = torch.randn((b, FRAMES, 640), dtype=torch.float16, device="cuda")
@@ -497,7 +532,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
     ap.add_argument("--kernel", choices=["gemm", "attention", "attention-mma", "layernorm", "conv", "subsampling",
-                                         "decoder"],
+                                         "decoder", "logmel"],
                     help="profiling target: launch one operator only")
     ap.add_argument("--shape", default="", help="gemm: M,K,N,BITS; attention/conv/decoder: batch; layernorm: rows")
     ap.add_argument("--act", default="none", choices=["none", "silu", "relu"])

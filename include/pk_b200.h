@@ -169,6 +169,20 @@ int pk_subsampling_time_mask(pk_device* device, int precision, int batch, int he
                              int channels, void* values, const uint32_t* feature_lengths, int steps,
                              pk_stream stream);
 
+/* Log-mel front end: the reference's native front end, parakeet_fbank_
+ * compute_item (src/cpp/fbank/parakeet_fbank.cpp:596-653; wrapper
+ * ParakeetFbankWasm, src/audio/fbank-wasm.ts:158), for a whole batch at once.
+ * samples: device f32 [batch, sample_count] (16 kHz PCM, the physical window
+ * arena, 160 <= sample_count <= 240000); valid_samples: device u32 [batch]
+ * (values above sample_count are treated as sample_count); features: device
+ * f32 [batch, 128, sample_count / 160 + 1] feature-major, normalized over the
+ * floor(valid / 160) valid frames and zero beyond them -- the encoder's input
+ * layout.  The reference's raw-frame reuse between overlapping windows only
+ * skips recomputing identical frames and has no counterpart.  The first call
+ * on a device uploads constant tables; make it before any stream capture. */
+int pk_logmel(pk_device* device, int batch, int sample_count, const float* samples,
+              const uint32_t* valid_samples, float* features, pk_stream stream);
+
 /* Persistent greedy TDT decoder (prediction net: 2-layer LSTM 640 + projector;
  * joint: relu(encoder + predictor) -> head 640 x 1032 = 1025 tokens (blank
  * 1024) + 5 durations {0..4}).  Mirrors TdtDecoderDescriptor (src/webgpu/

@@ -37,6 +37,15 @@ def build() -> Path:
     return _LIB_PATH
 
 
+def build_reference() -> bool:
+    """Build oracle/_ref (the reference's own log-mel front end) when the
+    reference checkout is present; a no-op otherwise.  Returns availability."""
+    src = Path(os.environ.get("PARAKEET_REFERENCE", "/root/reference")) / "src" / "cpp" / "fbank" / "parakeet_fbank.cpp"
+    if src.exists():
+        subprocess.run(["make", "-s", "-C", str(_HERE), "ref", f"REFERENCE={src.parents[3]}"], check=True)
+    return (_HERE / "_ref" / "libparakeet_fbank.so").exists()
+
+
 def lib() -> ctypes.CDLL:
     global _lib
     if _lib is None:
@@ -57,6 +66,9 @@ def lib() -> ctypes.CDLL:
         _lib.or_subsampling_conv0_dw2.argtypes = [i32, i64, vp, vp, vp, vp, vp, vp, vp]
         _lib.or_subsampling_depthwise.argtypes = [i32, i64, i64, i64, i64, vp, vp, vp, vp, i32, vp]
         _lib.or_subsampling_time_mask.argtypes = [i32, i64, i64, i64, i64, vp, vp, i32]
+        _lib.or_logmel.argtypes = [i64, i64, vp, vp, vp]
+        _lib.or_logmel_tables.argtypes = [vp] * 6 + [i32]
+        _lib.or_logmel_tables.restype = i32
         _lib.or_tdt_decode.argtypes = [i32, i64, i64, i64, vp, vp, vp, vp, vp] + [vp] * 9 + [vp] * 4
     return _lib
 
@@ -309,3 +321,62 @@ def tdt_decode(enc, lengths, decoder, *, max_tokens=376, starts=None, ends=None,
     lib().or_tdt_decode(prec, batch, frames, max_tokens, ptr(enc), ptr(lengths), ptr(starts), ptr(ends),
                         ptr(flush), *[ptr(w) for w in ws], ptr(tokens), ptr(tframes), ptr(durs), ptr(meta))
     return tokens, tframes, durs, meta[:batch].copy(), meta[batch:].copy()
+
+
+def logmel(samples, valid):
+    """Log-mel features f32 [batch, 128, sample_count // 160 + 1] of PCM
+    ``samples`` f32 [batch, sample_count] with ``valid`` samples per window
+    (restating src/cpp/fbank/parakeet_fbank.cpp)."""
+    samples = np.ascontiguousarray(samples, np.float32)
+    b, n = samples.shape
+    valid = np.ascontiguousarray(valid, np.uint32)
+    out = np.zeros((b, 128, n // 160 + 1), np.float32)
+    ptr = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+    lib().or_logmel(b, n, ptr(samples), ptr(valid), ptr(out))
+    return out
+
+
+_REF_FBANK = _HERE / "_ref" / "libparakeet_fbank.so"
+
+
+def reference_fbank_available() -> bool:
+    return _REF_FBANK.exists()
+
+
+def reference_fbank(samples, valid):
+    """The reference's own front end (oracle/_ref, built by ``make -C oracle ref``
+    from src/cpp/fbank/parakeet_fbank.cpp): one parakeet_fbank_compute_item per
+    window, no raw-frame reuse.  Same shapes as ``logmel``."""
+    samples = np.ascontiguousarray(samples, np.float32)
+    b, n = samples.shape
+    L = ctypes.CDLL(str(_REF_FBANK))
+    L.parakeet_fbank_input_ptr.restype = ctypes.c_void_p
+    L.parakeet_fbank_output_ptr.restype = ctypes.c_void_p
+    assert L.parakeet_fbank_init() == 1
+    frames = n // 160 + 1
+    out = np.zeros((b, 128, frames), np.float32)
+    inp = (ctypes.c_float * 240000).from_address(L.parakeet_fbank_input_ptr())
+    outp = (ctypes.c_float * (128 * 1501)).from_address(L.parakeet_fbank_output_ptr())
+    for i in range(b):
+        L.parakeet_fbank_reset_reuse()
+        if L.parakeet_fbank_begin_batch(1, n) != frames:
+            raise ValueError("reference rejected the window shape")
+        ctypes.memmove(inp, samples[i].ctypes.data, n * 4)
+        if L.parakeet_fbank_compute_item(0, int(valid[i]), 0) != frames:
+            raise ValueError("reference rejected the window")
+        out[i] = np.frombuffer(outp, np.float32, count=128 * frames).reshape(128, frames)
+        L.parakeet_fbank_finish_batch()
+    return out
+
+
+def logmel_tables():
+    """(hann [512], twiddle re [256], im [256], first [128], count [128], packed weights)."""
+    h = np.zeros(512, np.float32)
+    tr = np.zeros(256, np.float32)
+    ti = np.zeros(256, np.float32)
+    first = np.zeros(128, np.int32)
+    count = np.zeros(128, np.int32)
+    packed = np.zeros(2048, np.float32)
+    ptr = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+    n = lib().or_logmel_tables(ptr(h), ptr(tr), ptr(ti), ptr(first), ptr(count), ptr(packed), 2048)
+    return h, tr, ti, first, count, packed[:n].copy()

@@ -680,4 +680,175 @@ void or_tdt_decode(int prec, int64_t batch, int64_t frames, int64_t max_tokens, 
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Log-mel front end (src/cpp/fbank/parakeet_fbank.cpp): per window,
+// floor(valid/160) frames of a centered 512-point STFT over a 400-sample
+// Hann window (periodic = false, centered in the 512 frame), preemphasis 0.97
+// applied in double inside each frame's samples (the first sample of the
+// window kept), radix-2 decimation-in-time FFT in f32 on bit-reversed input
+// with a twiddle-free first butterfly per block (:195-240), power in double,
+// 128 Slaney mel filters (Slaney-normalized, f32 weights from double, :139-186)
+// summed in double in bin order, log(energy + 2^-24) in double, then
+// per-window per-bin normalization over the valid frames with an unbiased
+// standard deviation (+1e-5), zero beyond them (:486-521).  The reference's
+// raw-frame reuse between overlapping windows only skips recomputing frames
+// whose result is identical, so every frame is computed here.
+// ---------------------------------------------------------------------------
+namespace lm {
+constexpr int kFft = 512, kBins = 257, kWin = 400, kHop = 160, kMels = 128, kSr = 16000;
+constexpr double kPi = 3.14159265358979323846264338327950288;
+
+struct Tables {
+  float hann[kFft];
+  float tw_re[kFft / 2], tw_im[kFft / 2];
+  int rev[kFft];
+  float mel[kMels][kBins];
+  int first[kMels], last[kMels];
+  Tables() {
+    for (int i = 0; i < kFft; ++i) hann[i] = 0.0f;
+    for (int i = 0; i < kWin; ++i)
+      hann[(kFft - kWin) / 2 + i] = (float)(0.5 * (1.0 - std::cos(2.0 * kPi * (double)i / (double)(kWin - 1))));
+    for (int i = 0; i < kFft / 2; ++i) {
+      const double ph = (-2.0 * kPi * (double)i) / (double)kFft;
+      tw_re[i] = (float)std::cos(ph);
+      tw_im[i] = (float)std::sin(ph);
+    }
+    for (int i = 0; i < kFft; ++i) {
+      int r = 0;
+      for (int b = 0; b < 9; ++b) r |= ((i >> b) & 1) << (8 - b);
+      rev[i] = r;
+    }
+    auto to_mel = [](double f) {
+      const double lin = 200.0 / 3.0, ft = 1000.0, mt = ft / lin, step = 0.06875177742094912;
+      return f >= ft ? mt + std::log(f / ft) / step : f / lin;
+    };
+    auto to_hz = [](double m) {
+      const double lin = 200.0 / 3.0, ft = 1000.0, mt = ft / lin, step = 0.06875177742094912;
+      return m >= mt ? ft * std::exp(step * (m - mt)) : m * lin;
+    };
+    double freq[kBins], pts[kMels + 2];
+    for (int b = 0; b < kBins; ++b) freq[b] = ((double)kSr * 0.5 * b) / (double)(kBins - 1);
+    const double m0 = to_mel(0.0), m1 = to_mel(kSr * 0.5);
+    for (int i = 0; i < kMels + 2; ++i) pts[i] = to_hz(m0 + (m1 - m0) * i / (kMels + 1));
+    for (int m = 0; m < kMels; ++m) {
+      const double norm = 2.0 / (pts[m + 2] - pts[m]);
+      first[m] = -1;
+      last[m] = -1;
+      for (int b = 0; b < kBins; ++b) {
+        const double down = (freq[b] - pts[m]) / (pts[m + 1] - pts[m]);
+        const double up = (pts[m + 2] - freq[b]) / (pts[m + 2] - pts[m + 1]);
+        double tri = down < up ? down : up;
+        if (tri < 0.0) tri = 0.0;
+        mel[m][b] = (float)(tri * norm);
+        if (mel[m][b] > 0.0f) {
+          if (first[m] < 0) first[m] = b;
+          last[m] = b;
+        }
+      }
+      if (first[m] < 0) first[m] = 0, last[m] = -1;
+    }
+  }
+};
+
+static const Tables& tables() {
+  static const Tables t;
+  return t;
+}
+
+// One frame's 128 raw log-mel values; `n` samples are real, the rest zero.
+static void raw_frame(const float* x, int n, int frame, float* out /* [128], stride ostride */, int64_t ostride) {
+  const Tables& T = tables();
+  float re[kFft], im[kFft];
+  for (int i = 0; i < kFft; ++i) re[i] = im[i] = 0.0f;
+  const int center = frame * kHop;
+  const int lo = std::max(0, center - kWin / 2), hi = std::min(n, center + kWin / 2);
+  for (int src = lo; src < hi; ++src) {
+    const double e = src == 0 ? (double)x[0] : (double)x[src] - (double)0.97f * (double)x[src - 1];
+    const int fi = src - center + kFft / 2;
+    re[T.rev[fi]] = (float)(e * (double)T.hann[fi]);
+  }
+  for (int len = 2; len <= kFft; len <<= 1) {
+    const int half = len >> 1, step = kFft / len;
+    for (int blk = 0; blk < kFft; blk += len) {
+      {
+        const float rr = re[blk + half], ri = im[blk + half], lr = re[blk], li = im[blk];
+        re[blk] = lr + rr;
+        im[blk] = li + ri;
+        re[blk + half] = lr - rr;
+        im[blk + half] = li - ri;
+      }
+      for (int j = 1; j < half; ++j) {
+        const int l = blk + j, r = l + half, t = j * step;
+        const float rr = re[r], ri = im[r];
+        const float xr = T.tw_re[t] * rr - T.tw_im[t] * ri;
+        const float xi = T.tw_re[t] * ri + T.tw_im[t] * rr;
+        const float lr = re[l], li = im[l];
+        re[l] = lr + xr;
+        im[l] = li + xi;
+        re[r] = lr - xr;
+        im[r] = li - xi;
+      }
+    }
+  }
+  double pw[kBins];
+  for (int b = 0; b < kBins; ++b) pw[b] = (double)re[b] * (double)re[b] + (double)im[b] * (double)im[b];
+  for (int m = 0; m < kMels; ++m) {
+    double en = 0.0;
+    for (int b = T.first[m]; b <= T.last[m]; ++b) en += (double)T.mel[m][b] * pw[b];
+    out[m * ostride] = (float)std::log(en + 1.0 / 16777216.0);
+  }
+}
+}  // namespace lm
+
+// samples f32 [batch, sample_count]; valid u32 [batch] (<= sample_count);
+// features f32 [batch, 128, sample_count / 160 + 1] feature-major.
+void or_logmel(int64_t batch, int64_t sample_count, const float* samples, const uint32_t* valid, float* features) {
+  using namespace lm;
+  const int64_t frames = sample_count / kHop + 1;
+  tables();
+#pragma omp parallel for schedule(dynamic, 1)
+  for (int64_t b = 0; b < batch; ++b) {
+    const int n = (int)valid[b];
+    const int nf = n / kHop;
+    float* f = features + (size_t)b * kMels * frames;
+    const float* x = samples + (size_t)b * sample_count;
+    for (int t = 0; t < nf; ++t) raw_frame(x, n, t, f + t, frames);
+    for (int m = 0; m < kMels; ++m) {
+      float* row = f + (size_t)m * frames;
+      double sum = 0.0;
+      for (int t = 0; t < nf; ++t) sum += (double)row[t];
+      const double mean = nf > 0 ? sum / (double)nf : 0.0;
+      double sq = 0.0;
+      for (int t = 0; t < nf; ++t) {
+        const double d = (double)row[t] - mean;
+        sq += d * d;
+      }
+      const double sd = nf > 1 ? std::sqrt(sq / (double)(nf - 1)) : 0.0;
+      const double inv = 1.0 / (sd + 1.0e-5);
+      for (int t = 0; t < nf; ++t) row[t] = (float)(((double)row[t] - mean) * inv);
+      for (int64_t t = nf; t < frames; ++t) row[t] = 0.0f;
+    }
+  }
+}
+
+// The tables the CUDA front end uploads: hann [512], twiddles re/im [256],
+// mel filter bins first/count [128] and the packed nonzero weights.
+int or_logmel_tables(float* hann, float* tw_re, float* tw_im, int* first, int* count, float* packed, int capacity) {
+  const lm::Tables& T = lm::tables();
+  std::memcpy(hann, T.hann, sizeof(T.hann));
+  std::memcpy(tw_re, T.tw_re, sizeof(T.tw_re));
+  std::memcpy(tw_im, T.tw_im, sizeof(T.tw_im));
+  int n = 0;
+  for (int m = 0; m < lm::kMels; ++m) {
+    first[m] = T.first[m];
+    count[m] = T.last[m] - T.first[m] + 1;
+    for (int b = T.first[m]; b <= T.last[m]; ++b) {
+      if (n < capacity) packed[n] = T.mel[m][b];
+      ++n;
+    }
+  }
+  return n;
+}
+
 }  // extern "C"

@@ -28,6 +28,7 @@ EXPORTED = (
     "pk_palette_expand", "pk_palette_gemm", "pk_layernorm", "pk_rel_attention", "pk_rel_attention_noalloc",
     "pk_conformer_conv",
     "pk_subsampling_conv0_dw2", "pk_subsampling_depthwise", "pk_subsampling_time_mask", "pk_tdt_decode",
+    "pk_logmel",
     "pk_weights_upload", "pk_weights_release", "pk_encoder_create", "pk_encoder_forward",
     "pk_encoder_set_checkpoints", "pk_encoder_checkpoint", "pk_encoder_destroy", "pk_debug_set_gemm_route",
     "pk_debug_set_gemm_tile", "pk_debug_set_attention_route",
@@ -110,6 +111,7 @@ def load() -> ctypes.CDLL:
             "pk_subsampling_depthwise": [vp, i32, i32, i32, i32, i32, vp, vp, vp, vp, i32, vp, vp],
             "pk_subsampling_time_mask": [vp, i32, i32, i32, i32, i32, vp, vp, i32, vp],
             "pk_tdt_decode": [vp, ctypes.POINTER(TdtDesc), vp],
+            "pk_logmel": [vp, i32, i32, vp, vp, vp, vp],
             "pk_weights_upload": [vp, ctypes.POINTER(TensorDesc), i32, ctypes.POINTER(vp)],
             "pk_weights_release": [vp],
             "pk_encoder_create": [vp, vp, i32, i32, ctypes.POINTER(vp)],

@@ -256,6 +256,16 @@ int pk_rel_attention(pk_device* device, int precision, int batch, int frames, co
                               context, as_stream(stream));
 }
 
+int pk_logmel(pk_device* device, int batch, int sample_count, const float* samples, const uint32_t* valid_samples,
+              float* features, pk_stream stream) {
+  if (!device || !samples || !valid_samples || !features) return set_error(PK_E_INVALID, "null argument");
+  if (batch <= 0 || batch > 65535) return set_error(PK_E_SHAPE, "batchSize must be in [1, 65535]");
+  if (sample_count < 160 || sample_count > 240000)
+    return set_error(PK_E_SHAPE, "sampleCount must be in [160, 240000] (hop 160, at most 1501 frames)");
+  cudaSetDevice(device->ctx.ordinal);
+  return launch_logmel(batch, sample_count, samples, valid_samples, features, as_stream(stream));
+}
+
 int pk_tdt_decode(pk_device* device, const pk_tdt_desc* d, pk_stream stream) {
   if (!device || !d) return set_error(PK_E_INVALID, "null argument");
   if (d->precision != PK_FP16 && d->precision != PK_FP32) return set_error(PK_E_INVALID, "unknown precision");

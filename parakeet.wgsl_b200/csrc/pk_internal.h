@@ -106,6 +106,8 @@ int launch_subsampling_time_mask(int precision, int batch, int height, int width
                                  const uint32_t* feature_lengths, int steps, cudaStream_t stream);
 
 int launch_tdt_decode(const DeviceCtx& dev, const pk_tdt_desc& d, cudaStream_t stream);
+int launch_logmel(int batch, int sample_count, const float* samples, const uint32_t* valid_samples, float* features,
+                  cudaStream_t stream);
 
 // Debug / test knob: 0 = automatic kernel choice, 1 = force the SIMT GEMM,
 // 2 = force the tensor-core GEMM (fails if the shape is unsupported).

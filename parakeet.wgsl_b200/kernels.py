@@ -388,6 +388,52 @@ class RelativeAttentionKernel:
         return disp
 
 
+# --------------------------------------------------------------------- log-mel front end
+
+PARAKEET_FBANK_HOP_SAMPLES = 160
+PARAKEET_FBANK_BINS = 128
+PARAKEET_FBANK_MAX_SAMPLES = 240_000
+
+
+def parakeet_feature_frame_count(sample_count: int) -> int:
+    """parakeetFeatureFrameCount (src/audio/fbank-wasm.ts:133-139)."""
+    if not isinstance(sample_count, int) or sample_count < 0:
+        raise RangeError("sampleCount must be a non-negative safe integer")
+    return sample_count // PARAKEET_FBANK_HOP_SAMPLES + 1
+
+
+def parakeet_valid_feature_frame_count(sample_count: int) -> int:
+    """parakeetValidFeatureFrameCount (src/audio/fbank-wasm.ts:141-147)."""
+    if not isinstance(sample_count, int) or sample_count < 0:
+        raise RangeError("sampleCount must be a non-negative safe integer")
+    return sample_count // PARAKEET_FBANK_HOP_SAMPLES
+
+
+class ParakeetFbank:
+    """The log-mel front end (ParakeetFbankWasm, src/audio/fbank-wasm.ts:158)
+    on the GPU: a whole batch of windows per call instead of one item at a time."""
+
+    def __init__(self, device: Device):
+        self.device = device
+
+    def compute_batch(self, samples, valid_samples, out=None, stream=None):
+        """samples: CUDA f32 [batch, sample_count]; valid_samples: CUDA int32/uint32
+        [batch]; returns (or fills) CUDA f32 [batch, 128, sample_count // 160 + 1]."""
+        if samples.dim() != 2 or samples.dtype != torch.float32:
+            raise RangeError("samples must be f32 [batch, sample_count]")
+        batch, count = samples.shape
+        if count < PARAKEET_FBANK_HOP_SAMPLES or count > PARAKEET_FBANK_MAX_SAMPLES:
+            raise RangeError("sampleCount must be in [160, 240000]")
+        if valid_samples.numel() < batch:
+            raise RangeError("validSampleCount needs one entry per window")
+        frames = parakeet_feature_frame_count(count)
+        if out is None:
+            out = torch.empty((batch, PARAKEET_FBANK_BINS, frames), dtype=torch.float32, device=samples.device)
+        _lib.call("pk_logmel", self.device.handle, batch, count, _ptr(samples), _ptr(valid_samples), _ptr(out),
+                  _stream_handle(stream))
+        return out
+
+
 # --------------------------------------------------------------------- TDT decoder
 
 # requireDecoderWeights (src/webgpu/kernels/tdt-decoder.ts:367-420): name ->
