@@ -10,10 +10,10 @@ The directory name contains a dot, so import it through ``load()`` in
 ``__graft_entry__`` or with ``importlib`` under the module name
 ``parakeet_wgsl_b200``.
 """
-from . import _lib, runtime_plan, synthetic, windows  # noqa: F401
+from . import _lib, runtime_plan, stitch, synthetic, windows  # noqa: F401
 from ._lib import PkError  # noqa: F401
 
-__all__ = ["_lib", "runtime_plan", "synthetic", "windows", "PkError", "kernels", "encoder"]
+__all__ = ["_lib", "runtime_plan", "stitch", "synthetic", "windows", "PkError", "kernels", "encoder"]
 
 
 def __getattr__(name):

@@ -1,0 +1,368 @@
+"""Host-side merge of independently decoded windows into one token stream.
+
+Restates ``src/runtime/stitch.ts`` (the reference's port of FluidAudio's
+ChunkProcessor merge): window-local TDT emissions are placed on the source
+timeline (``globalize_tdt_tokens``, stitch.ts:69-99), then consecutive windows
+are spliced at their 2 s overlap by the first applicable method -- disjoint
+(no overlap), the longest contiguous run of matching tokens, their longest
+common subsequence, or a timestamp midpoint (``merge_token_streams``,
+:247-343) -- with word-boundary-aware splicing when token pieces are known
+(:470-592).  ``snapshot`` clamps timestamps to be non-decreasing
+(:209-237) and collapses case-only duplicate words at seams (:641-713).
+
+This is the host half of the multi-GPU design: windows are encoded and
+decoded on whichever GPU holds them, and only their token lists meet here.
+"""
+from __future__ import annotations
+
+import unicodedata
+from dataclasses import dataclass, replace
+from typing import Callable, Optional, Sequence
+
+from .windows import ENCODER_FRAME_SAMPLES, OVERLAP_SAMPLES, WindowPlan
+
+TokenPieceResolver = Callable[[int], Optional[str]]
+
+
+@dataclass(frozen=True)
+class TimedToken:
+    token_id: int
+    start_sample: int
+    end_sample: int
+    duration_frames: int  # raw TDT duration (seam-gap repair keeps it)
+
+
+@dataclass(frozen=True)
+class EmittedToken:
+    """One decoder emission in window-local encoder frames (TdtEmittedToken)."""
+    token_id: int
+    frame_index: int
+    duration_frames: int
+
+
+@dataclass(frozen=True)
+class DecodedTokenWindow:
+    index: int
+    start_sample: int  # logical emission range, not the physical read range
+    end_sample: int
+    tokens: tuple
+
+
+@dataclass(frozen=True)
+class StitchTrace:
+    left_window_index: int
+    right_window_index: int
+    method: str  # "disjoint" | "contiguous" | "lcs" | "midpoint"
+    overlap_start_sample: int
+    overlap_end_sample: int
+
+
+@dataclass(frozen=True)
+class StitchedTokens:
+    tokens: tuple
+    trace: tuple
+
+
+def globalize_tdt_tokens(tokens: Sequence[EmittedToken], window: WindowPlan) -> list[TimedToken]:
+    """Window-local frames -> source samples (1 280 per encoder frame); tokens
+    outside the window's logical emission range (hidden context, an end-aligned
+    window's backfill) are dropped and ends clamp to the range."""
+    out = []
+    for t in tokens:
+        start = window.timestamp_offset_sample + t.frame_index * ENCODER_FRAME_SAMPLES
+        end = start + t.duration_frames * ENCODER_FRAME_SAMPLES
+        if start < window.emission_start_sample or start >= window.emission_end_sample:
+            continue
+        out.append(TimedToken(t.token_id, start, min(end, window.emission_end_sample), t.duration_frames))
+    return out
+
+
+def stitch_token_windows(windows: Sequence[DecodedTokenWindow],
+                         token_piece: Optional[TokenPieceResolver] = None) -> StitchedTokens:
+    ordered = sorted(windows, key=lambda w: (w.start_sample, w.index))
+    acc = IncrementalStitchAccumulator(token_piece=token_piece, collect_trace=True)
+    for w in ordered:
+        acc.append(w)
+    return acc.snapshot()
+
+
+class IncrementalStitchAccumulator:
+    """Streaming form of ``stitch_token_windows`` for windows appended in
+    (start_sample, index) order; ``snapshot`` finalizes a copy."""
+
+    def __init__(self, token_piece: Optional[TokenPieceResolver] = None, collect_trace: bool = False):
+        self._piece = token_piece if token_piece is not None else (lambda _tid: None)
+        self._has_pieces = token_piece is not None
+        self._trace: Optional[list] = [] if collect_trace else None
+        self._merged: list = []
+        self._previous: Optional[DecodedTokenWindow] = None
+
+    def append(self, window: DecodedTokenWindow) -> None:
+        _validate_window(window)
+        prev = self._previous
+        if prev is None:
+            self._merged = list(window.tokens)
+            self._previous = window
+            return
+        if (prev.start_sample, prev.index) > (window.start_sample, window.index):
+            raise ValueError("incremental stitch windows must be appended in chronological order")
+        tokens, method = _merge_token_streams(self._merged, list(window.tokens), self._piece, self._has_pieces)
+        self._merged = tokens
+        if self._trace is not None:
+            self._trace.append(StitchTrace(prev.index, window.index, method, window.start_sample,
+                                           min(prev.end_sample, window.end_sample)))
+        self._previous = window
+
+    def snapshot(self) -> StitchedTokens:
+        tokens = enforce_monotonic_token_times(self._merged)
+        if len(tokens) > 1 and self._has_pieces:
+            tokens = collapse_seam_word_duplicates(tokens, self._piece)
+        return StitchedTokens(tuple(tokens), tuple(self._trace) if self._trace is not None else ())
+
+
+def enforce_monotonic_token_times(tokens: Sequence[TimedToken]) -> list[TimedToken]:
+    """Keep the merged text order; shift any token that starts before its
+    predecessor forward by the difference (start and end together)."""
+    if not tokens:
+        return []
+    out = [tokens[0]]
+    last = tokens[0].start_sample
+    for t in tokens[1:]:
+        if t.start_sample >= last:
+            out.append(t)
+            last = t.start_sample
+        else:
+            shift = last - t.start_sample
+            out.append(replace(t, start_sample=last, end_sample=t.end_sample + shift))
+    return out
+
+
+def _merge_token_streams(left, right, piece, has_pieces):
+    if not left:
+        return list(right), "disjoint"
+    if not right:
+        return list(left), "disjoint"
+    left_end = left[-1].start_sample + ENCODER_FRAME_SAMPLES
+    right_start = right[0].start_sample
+    if left_end <= right_start:
+        return left + right, "disjoint"
+    ov_left = [(i, t) for i, t in enumerate(left)
+               if t.start_sample + ENCODER_FRAME_SAMPLES > right_start - OVERLAP_SAMPLES]
+    ov_right = [(i, t) for i, t in enumerate(right) if t.start_sample < left_end + OVERLAP_SAMPLES]
+    if len(ov_left) < 2 or len(ov_right) < 2:
+        return _merge_by_midpoint(left, right, left_end, right_start, piece, has_pieces), "midpoint"
+
+    def matches(a, b):
+        return (token_ids_match(a[1].token_id, b[1].token_id, piece)
+                and abs(a[1].start_sample - b[1].start_sample) < OVERLAP_SAMPLES / 2)
+
+    run = _longest_contiguous(ov_left, ov_right, matches)
+    if len(run) >= max(len(ov_left) // 2, 1):
+        return _merge_using_matches(run, ov_left, ov_right, left, right, piece, has_pieces), "contiguous"
+    lcs = _longest_common_subsequence(ov_left, ov_right, matches)
+    if not lcs:
+        return _merge_by_midpoint(left, right, left_end, right_start, piece, has_pieces), "midpoint"
+    return _merge_using_matches(lcs, ov_left, ov_right, left, right, piece, has_pieces), "lcs"
+
+
+def _longest_contiguous(left, right, matches):
+    best: list = []
+    for lo in range(len(left)):
+        for ro in range(len(right)):
+            if not matches(left[lo], right[ro]):
+                continue
+            cur = []
+            lc, rc = lo, ro
+            while lc < len(left) and rc < len(right) and matches(left[lc], right[rc]):
+                cur.append((lc, rc))
+                lc += 1
+                rc += 1
+            if len(cur) > len(best):  # the first run in scan order wins ties
+                best = cur
+    return best
+
+
+def _longest_common_subsequence(left, right, matches):
+    w = len(right) + 1
+    table = [0] * ((len(left) + 1) * w)
+    for lc in range(1, len(left) + 1):
+        for rc in range(1, len(right) + 1):
+            cell = lc * w + rc
+            if matches(left[lc - 1], right[rc - 1]):
+                table[cell] = table[(lc - 1) * w + rc - 1] + 1
+            else:
+                table[cell] = max(table[(lc - 1) * w + rc], table[lc * w + rc - 1])
+    rev = []
+    lc, rc = len(left), len(right)
+    while lc > 0 and rc > 0:
+        if matches(left[lc - 1], right[rc - 1]):
+            rev.append((lc - 1, rc - 1))
+            lc -= 1
+            rc -= 1
+        elif table[(lc - 1) * w + rc] > table[lc * w + rc - 1]:
+            lc -= 1
+        else:
+            rc -= 1  # backtracking tie rule
+    rev.reverse()
+    return rev
+
+
+def _merge_using_matches(pairs, ov_left, ov_right, left, right, piece, has_pieces):
+    li = [ov_left[a][0] for a, _ in pairs]
+    ri = [ov_right[b][0] for _, b in pairs]
+    out = list(left[:li[0]])
+    for m in range(len(pairs)):
+        out.append(left[li[m]])
+        if m == len(pairs) - 1:
+            continue
+        lgap = left[li[m] + 1:li[m + 1]]
+        rgap = right[ri[m] + 1:ri[m + 1]]
+        out.extend(rgap if len(rgap) > len(lgap) else lgap)
+    last_right = ri[-1]
+    if last_right + 1 >= len(right):
+        return out
+    tail = right[last_right + 1:]
+    if not has_pieces or is_splice_safe_token(tail[0].token_id, piece):
+        out.extend(tail)
+        return out
+    word_start = _word_initial_index(right, last_right, piece)
+    if word_start is not None and _pop_seam_word(out, piece):
+        out.extend(right[word_start:])
+        return out
+    cursor = li[-1] + 1
+    while cursor < len(left) and not is_splice_safe_token(left[cursor].token_id, piece):
+        out.append(left[cursor])
+        cursor += 1
+    resume = next((i for i, t in enumerate(tail) if is_splice_safe_token(t.token_id, piece)), -1)
+    out.extend(tail[resume:] if resume >= 0 else tail)  # a glued word beats dropping the tail
+    return out
+
+
+def _word_initial_index(stream, ending_at, piece):
+    for i in range(ending_at, -1, -1):
+        if is_splice_safe_token(stream[i].token_id, piece):
+            return i
+    return None
+
+
+def _pop_seam_word(out, piece) -> bool:
+    for i in range(len(out) - 1, -1, -1):
+        if is_splice_safe_token(out[i].token_id, piece):
+            del out[i:]
+            return True
+    return False
+
+
+def _merge_by_midpoint(left, right, left_end, right_start, piece, has_pieces):
+    cutoff = (left_end + right_start) / 2
+    le = next((i for i, t in enumerate(left) if t.start_sample >= cutoff), len(left))
+    rs = next((i for i, t in enumerate(right) if t.start_sample >= cutoff), len(right))
+    if has_pieces and le > 0:
+        while le < len(left) and not is_splice_safe_token(left[le].token_id, piece):
+            le += 1
+    if has_pieces:
+        safe = rs
+        while safe < len(right) and not is_splice_safe_token(right[safe].token_id, piece):
+            safe += 1
+        if safe < len(right):  # keep the original cutoff when no safe right token exists
+            rs = safe
+    return list(left[:le]) + list(right[rs:])
+
+
+def _is_punct_or_symbol(ch: str) -> bool:
+    return unicodedata.category(ch)[0] in ("P", "S")
+
+
+def _starts_word(piece: str) -> bool:
+    return piece.startswith("▁") or piece.startswith(" ")
+
+
+def is_splice_safe_token(token_id: int, piece: TokenPieceResolver) -> bool:
+    p = piece(token_id)
+    if not p:
+        return False
+    return _starts_word(p) or all(_is_punct_or_symbol(c) for c in p)
+
+
+def is_punctuation_only_token(token_id: int, piece: TokenPieceResolver) -> bool:
+    p = piece(token_id)
+    return bool(p) and all(_is_punct_or_symbol(c) for c in p)
+
+
+def token_ids_match(a: int, b: int, piece: TokenPieceResolver) -> bool:
+    if a == b:
+        return True
+    pa, pb = piece(a), piece(b)
+    return pa is not None and pb is not None and pa.lower() == pb.lower()
+
+
+def collapse_seam_word_duplicates(tokens: Sequence[TimedToken], piece: TokenPieceResolver) -> list[TimedToken]:
+    """Drop one of two adjacent words that differ only in case and start within
+    the overlap of each other (keeping the lowercase form when it comes
+    second), unless the first ends a sentence."""
+    if len(tokens) < 2:
+        return list(tokens)
+    words = []
+    for t in tokens:
+        p = piece(t.token_id) or ""
+        if not words or _starts_word(p):
+            words.append({"tokens": [t], "start": t.start_sample})
+        else:
+            words[-1]["tokens"].append(t)
+    for w in words:
+        text = "".join(_strip_prefix(piece(t.token_id) or "") for t in w["tokens"])
+        core = text
+        while core and (unicodedata.category(core[0])[0] == "P" or core[0].isspace()):
+            core = core[1:]
+        while core and (unicodedata.category(core[-1])[0] == "P" or core[-1].isspace()):
+            core = core[:-1]
+        w["core"] = core
+        w["ends"] = text.endswith((".", "?", "!", ":"))
+    keep = [True] * len(words)
+    last = -1
+    for i, cur in enumerate(words):
+        if last < 0:
+            last = i
+            continue
+        prev = words[last]
+        dup = (prev["core"] and cur["core"] and prev["core"] != cur["core"]
+               and prev["core"].lower() == cur["core"].lower()
+               and unicodedata.category(cur["core"][0])[0] == "L" and not prev["ends"]
+               and cur["start"] - prev["start"] <= OVERLAP_SAMPLES)
+        if not dup:
+            last = i
+            continue
+        if cur["core"] == cur["core"].lower() and prev["core"] != prev["core"].lower():
+            keep[last] = False
+            last = i
+        else:
+            keep[i] = False
+    out = []
+    for i, w in enumerate(words):
+        if keep[i]:
+            out.extend(w["tokens"])
+    return out
+
+
+def _strip_prefix(p: str) -> str:
+    return p[1:] if _starts_word(p) else p
+
+
+def _validate_window(w: DecodedTokenWindow) -> None:
+    for name, v in (("window index", w.index), ("window startSample", w.start_sample),
+                    ("window endSample", w.end_sample)):
+        if not isinstance(v, int) or v < 0:
+            raise ValueError(f"{name} must be a non-negative safe integer")
+    if w.end_sample < w.start_sample:
+        raise ValueError("window endSample must not precede startSample")
+    prev = None
+    for t in w.tokens:
+        for name, v in (("tokenId", t.token_id), ("token startSample", t.start_sample),
+                        ("token endSample", t.end_sample), ("token durationFrames", t.duration_frames)):
+            if not isinstance(v, int) or v < 0:
+                raise ValueError(f"{name} must be a non-negative safe integer")
+        if t.end_sample < t.start_sample:
+            raise ValueError("token endSample must not precede startSample")
+        if prev is not None and t.start_sample < prev:
+            raise ValueError("tokens must be sorted by startSample")
+        prev = t.start_sample
