@@ -69,6 +69,8 @@ def lib() -> ctypes.CDLL:
         _lib.or_logmel.argtypes = [i64, i64, vp, vp, vp]
         _lib.or_logmel_tables.argtypes = [vp] * 6 + [i32]
         _lib.or_logmel_tables.restype = i32
+        _lib.or_hfma_selfcheck.argtypes = [i64, ctypes.c_uint64]
+        _lib.or_hfma_selfcheck.restype = i64
         _lib.or_tdt_decode.argtypes = [i32, i64, i64, i64, vp, vp, vp, vp, vp] + [vp] * 9 + [vp] * 4
     return _lib
 

@@ -491,10 +491,32 @@ void or_subsampling_time_mask(int prec, int64_t batch, int64_t height, int64_t w
 namespace tdt {
 constexpr int H = 640, G = 2560, KIN = 1280, NOUT = 1032, BLANK = 1024, MAXSYM = 10;
 
-static inline float hfma(float a, float b, float c) {
+// a*b + c and a + b for f16 operands, rounded once to f16.  The product of
+// two f16 values is exact in f32; TwoSum gives the exact error of the f32 sum,
+// which then rounds to odd (an inexact result with an even last bit moves one
+// ulp toward the exact value); rounding that to f16 (11 bits, far fewer than
+// f32's 24) is the correctly rounded f16 result.
+static inline float sum_round_odd(float p, float c) {
+  const float s = p + c;
+  const float bp = s - c;
+  const float err = (p - bp) + (c - (s - bp));
+  uint32_t bits;
+  std::memcpy(&bits, &s, 4);
+  // Branch-free (so the loops vectorize): move only when inexact and even;
+  // s != 0 whenever err != 0.
+  const uint32_t move = (uint32_t)(err != 0.0f) & ~bits & 1u;
+  const uint32_t away = (uint32_t)((err > 0.0f) == (s > 0.0f));
+  bits += move * (away ? 1u : 0xffffffffu);
+  float r;
+  std::memcpy(&r, &bits, 4);
+  return r;
+}
+static inline float hfma(float a, float b, float c) { return (float)(half_t)sum_round_odd(a * b, c); }
+static inline float hadd(float a, float b) { return (float)(half_t)sum_round_odd(a, b); }
+// The same operation through double (an exact sum), kept to cross-check.
+static inline float hfma_double(float a, float b, float c) {
   return (float)(half_t)((double)a * (double)b + (double)c);
 }
-static inline float hadd(float a, float b) { return (float)(half_t)((double)a + (double)b); }
 // exp / tanh are taken correctly rounded to f32 (the double-precision
 // functions, rounded once); the shader's f32 versions are backend-defined to
 // a few ulp, and the CUDA decoder uses the same correctly rounded values.
@@ -521,23 +543,34 @@ static void lstm_layer(const Weights& W, const void* w, const float* bias, const
                        std::vector<float>& h, std::vector<float>& c) {
   std::vector<float> gate(G);
   const int p = W.prec;
-  for (int o = 0; o < G; ++o) {
-    float even, odd = 0.0f;
-    if (p == 0) {
-      even = round_h(bias[o]);
-      for (int k = 0; k < limit; k += 2) {
-        even = hfma(round_h(x[k]), ld(w, 0, (size_t)k * G + o), even);
-        odd = hfma(round_h(x[k + 1]), ld(w, 0, (size_t)(k + 1) * G + o), odd);
-      }
-      gate[o] = hadd(even, odd);
-    } else {
-      even = bias[o];
-      for (int k = 0; k < limit; k += 2) {
-        even = std::fma(x[k], ld(w, 1, (size_t)k * G + o), even);
-        odd = std::fma(x[k + 1], ld(w, 1, (size_t)(k + 1) * G + o), odd);
-      }
-      gate[o] = even + odd;
+  // Each thread owns a block of outputs and walks the inputs in increasing
+  // order, so every output's two chains keep the shader's order.
+#pragma omp parallel for schedule(static)
+  for (int o0 = 0; o0 < G; o0 += 256) {
+    float even[256], odd[256];
+    for (int i = 0; i < 256; ++i) {
+      even[i] = p == 0 ? round_h(bias[o0 + i]) : bias[o0 + i];
+      odd[i] = 0.0f;
     }
+    for (int k = 0; k < limit; k += 2) {
+      if (p == 0) {
+        const float xe = round_h(x[k]), xo = round_h(x[k + 1]);
+        const uint16_t* re = (const uint16_t*)w + (size_t)k * G + o0;
+        const uint16_t* ro = re + G;
+        for (int i = 0; i < 256; ++i) {
+          even[i] = hfma(xe, h2f(re[i]), even[i]);
+          odd[i] = hfma(xo, h2f(ro[i]), odd[i]);
+        }
+      } else {
+        const float* re = (const float*)w + (size_t)k * G + o0;
+        const float* ro = re + G;
+        for (int i = 0; i < 256; ++i) {
+          even[i] = std::fma(x[k], re[i], even[i]);
+          odd[i] = std::fma(x[k + 1], ro[i], odd[i]);
+        }
+      }
+    }
+    for (int i = 0; i < 256; ++i) gate[o0 + i] = p == 0 ? hadd(even[i], odd[i]) : even[i] + odd[i];
   }
   for (int ch = 0; ch < H; ++ch) {
     const float i = sig(gate[ch]), f = sig(gate[H + ch]), g = stanh(gate[2 * H + ch]), o = sig(gate[3 * H + ch]);
@@ -579,18 +612,26 @@ static void joint(const Weights& W, const Seq& s, const void* enc_row, uint32_t*
   for (int k = 0; k < H; ++k) jin[k] = std::max(ld(enc_row, p, k) + s.proj[k], 0.0f);
   std::vector<float> acc(NOUT);
   for (int o = 0; o < NOUT; ++o) acc[o] = p == 0 ? round_h(W.hb[o]) : W.hb[o];
+  std::vector<char> skip(H);
   bool safe = true;
   for (int k = 0; k < H; ++k) {
     uint32_t bits;
     std::memcpy(&bits, &jin[k], 4);
     const bool nan = (bits & 0x7fffffffu) > 0x7f800000u;
     safe = safe && !(bits == 0x80000000u || nan);
-    if (safe && bits == 0u) continue;
-    if (p == 0) {
-      const float xk = round_h(jin[k]);
-      for (int o = 0; o < NOUT; ++o) acc[o] = hfma(xk, ld(W.hw, 0, (size_t)k * NOUT + o), acc[o]);
-    } else {
-      for (int o = 0; o < NOUT; ++o) acc[o] = std::fma(jin[k], ld(W.hw, 1, (size_t)k * NOUT + o), acc[o]);
+    skip[k] = safe && bits == 0u;
+  }
+#pragma omp parallel for schedule(static)
+  for (int o0 = 0; o0 < NOUT; o0 += 129) {  // 8 blocks of outputs, inputs in increasing order
+    const int o1 = std::min(o0 + 129, NOUT);
+    for (int k = 0; k < H; ++k) {
+      if (skip[k]) continue;
+      if (p == 0) {
+        const float xk = round_h(jin[k]);
+        for (int o = o0; o < o1; ++o) acc[o] = hfma(xk, ld(W.hw, 0, (size_t)k * NOUT + o), acc[o]);
+      } else {
+        for (int o = o0; o < o1; ++o) acc[o] = std::fma(jin[k], ld(W.hw, 1, (size_t)k * NOUT + o), acc[o]);
+      }
     }
   }
   float tv = -3.402823466e38f, dv = -3.402823466e38f;
@@ -603,6 +644,31 @@ static void joint(const Weights& W, const Seq& s, const void* enc_row, uint32_t*
   *duration = did;
 }
 }  // namespace tdt
+
+// Self-check of the f16 FMA emulation: how many of n seeded operand triples
+// (f16 values over the whole finite range) round differently through
+// round-to-odd f32 and through double.
+int64_t or_hfma_selfcheck(int64_t n, uint64_t seed) {
+  uint64_t x = seed | 1;
+  auto next = [&]() {
+    x ^= x << 13;
+    x ^= x >> 7;
+    x ^= x << 17;
+    return x;
+  };
+  auto h = [&]() {
+    uint16_t bits = (uint16_t)next();
+    if ((bits & 0x7c00u) == 0x7c00u) bits &= 0xbbffu;  // no inf / NaN
+    return h2f(bits);
+  };
+  int64_t bad = 0;
+  for (int64_t i = 0; i < n; ++i) {
+    const float a = h(), b = h(), c = h();
+    const float r1 = tdt::hfma(a, b, c), r2 = tdt::hfma_double(a, b, c);
+    if (std::memcmp(&r1, &r2, 4) != 0 && !(r1 != r1 && r2 != r2)) ++bad;
+  }
+  return bad;
+}
 
 // Decodes `batch` sequences.  enc: [batch, frames, 640] profile scalar;
 // lengths/starts/ends/flush: u32 [batch]; outputs tokens / token_frames /
@@ -617,8 +683,7 @@ void or_tdt_decode(int prec, int64_t batch, int64_t frames, int64_t max_tokens, 
   using namespace tdt;
   const Weights W{prec, embedding, lstm0, lstm1, proj_w, head_w, bias0, bias1, proj_b, head_b};
   const size_t es = prec == 0 ? 2 : 4;
-#pragma omp parallel for schedule(dynamic, 1)
-  for (int64_t b = 0; b < batch; ++b) {
+  for (int64_t b = 0; b < batch; ++b) {  // the chains inside each step run in parallel
     Seq s;
     uint32_t count = 0, status = 0, sym = 0;
     const uint32_t enc_len = std::min(std::min(lengths[b], (uint32_t)frames), ends[b]);
