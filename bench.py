@@ -245,6 +245,28 @@ def time_logmel(pk, device, stream, reps=5):
             "hbm_bytes_per_batch": moved, "achieved_gbs": round(moved / (ms * 1e-3) / 1e9, 1)}
 
 
+def time_transcribe(pk, device, package, seconds=60.0, reps=2):
+    """Wall time of engine.transcribe on `seconds` of synthetic PCM (host
+    buffers in and out; window plan, log-mel, encoder, decoder, merge)."""
+    import torch
+
+    full = dict(package)
+    full.update(pk.synthetic.make_decoder("fp16", seed=0))
+    eng = pk.engine.ParakeetEngine(device, full, "fp16", capacity=BATCH)
+    pcm = pk.synthetic.make_pcm(seconds, seed=4)
+    eng.transcribe(pcm)  # warm-up
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        res = eng.transcribe(pcm)
+    dt = (time.perf_counter() - t0) / reps
+    windows = len(pk.windows.plan_stateless_windows(len(pcm)))
+    eng.destroy()
+    return {"workload": f"config4: {seconds:.0f} s synthetic PCM (pink noise + modulated tones), {windows} windows",
+            "s_per_run": round(dt, 4), "audio_s_per_s": round(seconds / dt, 1), "tokens": len(res.tokens),
+            "note": "random-init weights; the decoder's token count (not real speech) sets most of the time"}
+
+
 def cpu_baseline(pk, package, window_count=1):
     """Oracle (reference algorithm, f16-accumulating GEMMs) on `window_count` windows."""
     from oracle import oracle
@@ -369,6 +391,10 @@ def run_ours(args):
     dec_info = time_decoder(pk, device, out.view(BATCH, FRAMES, 640), stream, reps=max(1, min(args.steps, 5)))
     barrier()
 
+    # ---- end-to-end transcription (config 4): 60 s of PCM through the engine
+    tr_info = time_transcribe(pk, device, package) if rank == 0 else None
+    barrier()
+
     # ---- dominant kernel: palette GEMMs of one step, timed live
     with torch.cuda.stream(stream):
         gemm_flops, gemm_ms, gemm_detail = time_gemms(pk, device, BATCH, stream)
@@ -403,6 +429,7 @@ def run_ours(args):
             "gemm_shapes": gemm_detail,
             "decoder": dec_info,
             "logmel": lm_info,
+            "transcribe": tr_info,
             "cpu_baseline": None if cpu_value is None else {
                 "value": round(cpu_value, 3), "unit": UNIT, "cores": int(os.environ.get("OMP_NUM_THREADS", cores)),
                 "kind": "port", "sample": f"1 window x 24 layers, oracle reference mode, {cpu_dt:.1f} s"},

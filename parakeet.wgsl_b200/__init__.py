@@ -13,11 +13,11 @@ The directory name contains a dot, so import it through ``load()`` in
 from . import _lib, runtime_plan, stitch, synthetic, windows  # noqa: F401
 from ._lib import PkError  # noqa: F401
 
-__all__ = ["_lib", "runtime_plan", "stitch", "synthetic", "windows", "PkError", "kernels", "encoder"]
+__all__ = ["_lib", "runtime_plan", "stitch", "synthetic", "windows", "PkError", "kernels", "encoder", "engine"]
 
 
 def __getattr__(name):
-    if name in ("kernels", "encoder"):
+    if name in ("kernels", "encoder", "engine"):
         import importlib
 
         return importlib.import_module(f"{__name__}.{name}")

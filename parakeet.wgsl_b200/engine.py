@@ -1,0 +1,165 @@
+"""Inference engine: PCM windows in, decoded tokens out, on one GPU.
+
+Mirrors the engine seam the reference's worker runtime calls
+(``ParakeetInferenceEngine``, src/runtime/worker.ts:114-153) as implemented
+by ``createRawWebGpuParakeetEngine(...).transcribeWindows``
+(src/runtime/webgpu-engine.ts:578-880): per batch of at most ``capacity``
+windows the PCM arena is copied in, the log-mel front end, the 24-layer
+encoder graph and the persistent TDT decoder run back to back on one stream,
+and the token lists come back to the host.  ``transcribe`` adds the
+reference's long-form flow around it: the stateless window plan
+(src/runtime/chunking.ts:174-302), batching, timestamp globalization and the
+overlap merge (src/runtime/stitch.ts).  ``transcribe_sharded`` splits the
+window plan across ranks (one GPU each); only the token lists travel to rank
+0, which merges them -- the hot path has no collective.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Sequence
+
+import numpy as np
+
+from . import stitch as st
+from . import windows as wp
+from .encoder import ModelWeights, ParakeetEncoderGraph, derive_encoder_valid_length
+from .kernels import (Device, GpuTensor, ParakeetFbank, PersistentTdtDecoderKernel, RangeError,
+                      TDT_DECODER_TENSORS)
+
+try:
+    import torch
+except ImportError:  # pragma: no cover
+    torch = None
+
+WINDOW_SAMPLES = wp.WINDOW_SAMPLES
+MAX_TOKENS_PER_WINDOW = 2048  # src/runtime/webgpu-engine.ts:84
+
+
+@dataclass(frozen=True)
+class WindowResult:
+    """EngineWindowResult: one window's emissions in window-local frames."""
+    tokens: tuple  # of stitch.EmittedToken
+    overflow: bool
+
+
+class ParakeetEngine:
+    def __init__(self, device: Device, package: dict, precision: str = "fp16", capacity: int = 32,
+                 max_tokens: int = MAX_TOKENS_PER_WINDOW, keep_intermediates: bool = False):
+        """package: encoder + decoder tensors (name -> record), as produced by
+        the reference converter or ``synthetic.make_package`` + ``make_decoder``."""
+        self.device, self.precision, self.capacity, self.max_tokens = device, precision, capacity, max_tokens
+        dec_names = set(TDT_DECODER_TENSORS)
+        missing = sorted(dec_names - set(package))
+        if missing:
+            raise RangeError(f"package lacks decoder tensors: {', '.join(missing)}")
+        self.weights = ModelWeights(device, {k: v for k, v in package.items() if k not in dec_names})
+        self.graph = ParakeetEncoderGraph.create(device, self.weights, precision, capacity)
+        cuda = f"cuda:{device.ordinal}"
+        self._decoder_tensors = {n: GpuTensor.from_record(n, package[n], cuda) for n in dec_names}
+        self.decoder = PersistentTdtDecoderKernel.create(device, None, self._decoder_tensors, precision)
+        self.fbank = ParakeetFbank(device)
+        i32 = dict(dtype=torch.int32, device=cuda)
+        self._pcm = torch.zeros((capacity, WINDOW_SAMPLES), dtype=torch.float32, device=cuda)
+        self._pcm_host = torch.zeros((capacity, WINDOW_SAMPLES), dtype=torch.float32).pin_memory()
+        # Rows: valid samples, encoder lengths, decode starts, decode ends, flush flags.
+        self._control_host = torch.zeros((5, capacity), dtype=torch.int32).pin_memory()
+        self._control = torch.zeros((5, capacity), **i32)
+        self._features = torch.zeros((capacity, 128, 1501), dtype=torch.float32, device=cuda)
+        self._tokens = torch.zeros((3, capacity, max_tokens), **i32)
+        self._meta = torch.zeros(2 * capacity, **i32)
+        self._tokens_host = torch.zeros((3, capacity, max_tokens), dtype=torch.int32).pin_memory()
+        self._meta_host = torch.zeros(2 * capacity, dtype=torch.int32).pin_memory()
+        self._dispatch = self.decoder.create_dispatch(dict(
+            encoder_projected=self.graph.decoder_input(), encoded_lengths=self._control[1],
+            decode_starts=self._control[2], decode_ends=self._control[3], flush_finals=self._control[4],
+            tokens=self._tokens[0], token_frames=self._tokens[1], token_durations=self._tokens[2],
+            metadata=self._meta, batch_size=capacity, frames=188, max_tokens=max_tokens))
+        self.keep_intermediates = keep_intermediates
+        self.last: dict = {}
+
+    def transcribe_windows(self, windows: Sequence[tuple], stream=None) -> list[WindowResult]:
+        """windows: (samples f32 [<= 240 000], WindowPlan) per window, 1..capacity."""
+        b = len(windows)
+        if not 0 < b <= self.capacity:
+            raise RangeError(f"Engine batch must contain 1-{self.capacity} windows")
+        stream = torch.cuda.current_stream() if stream is None else stream
+        pcm = self._pcm_host[:b]
+        pcm.zero_()
+        ctrl = self._control_host
+        lengths = []
+        for i, (samples, plan) in enumerate(windows):
+            samples = np.asarray(samples, dtype=np.float32)
+            if samples.ndim != 1 or samples.shape[0] > WINDOW_SAMPLES or plan.valid_sample_count > samples.shape[0]:
+                raise RangeError(f"Window {i} must hold its {plan.valid_sample_count} valid samples in at most "
+                                 f"{WINDOW_SAMPLES}")
+            pcm[i, : samples.shape[0]] = torch.from_numpy(samples)
+            feature_frames = max(1, plan.valid_sample_count // wp.HOP_SAMPLES)
+            enc_len = derive_encoder_valid_length(feature_frames)
+            if plan.decode_start_frame > enc_len:
+                raise RangeError(f"Window {i} decoder start exceeds its {enc_len} encoder frames")
+            lengths.append(feature_frames)
+            ctrl[0, i] = plan.valid_sample_count
+            ctrl[1, i] = enc_len
+            ctrl[2, i] = plan.decode_start_frame
+            ctrl[3, i] = plan.decode_end_frame
+            ctrl[4, i] = int(plan.flush_final)
+        with torch.cuda.stream(stream):
+            self._pcm[:b].copy_(pcm, non_blocking=True)
+            self._control.copy_(ctrl, non_blocking=True)
+            self.fbank.compute_batch(self._pcm[:b], self._control[0, :b], out=self._features[:b], stream=stream)
+            projected, _ = self.graph.encode(self._features[:b], lengths, stream=stream)
+            self._dispatch.encode(stream, active_batch_size=b)
+            self._tokens_host[:, :b].copy_(self._tokens[:, :b], non_blocking=True)
+            self._meta_host.copy_(self._meta, non_blocking=True)
+        stream.synchronize()
+        if self.keep_intermediates:
+            self.last = {"features": self._features[:b].cpu().numpy(),
+                         "projected": projected.view(b, 188, 640).cpu().numpy(),
+                         "encoded_lengths": ctrl[1, :b].numpy().copy()}
+        tok, fr, du = (self._tokens_host[k, :b].numpy() for k in range(3))
+        counts = self._meta_host[:b].numpy()
+        flags = self._meta_host[self.capacity:self.capacity + b].numpy()
+        out = []
+        for i in range(b):
+            n = min(int(counts[i]), self.max_tokens)
+            out.append(WindowResult(tuple(st.EmittedToken(int(tok[i, j]), int(fr[i, j]), int(du[i, j]))
+                                          for j in range(n)), bool(flags[i] & 1)))
+        return out
+
+    def decode_plans(self, pcm: np.ndarray, plans: Sequence[wp.WindowPlan], stream=None) -> list:
+        """Runs `plans` in capacity-sized batches; returns a DecodedTokenWindow per plan."""
+        decoded = []
+        for start in range(0, len(plans), self.capacity):
+            chunk = plans[start:start + self.capacity]
+            batch = [(pcm[p.source_start_sample:p.source_end_sample], p) for p in chunk]
+            for plan, res in zip(chunk, self.transcribe_windows(batch, stream)):
+                toks = st.globalize_tdt_tokens(res.tokens, plan)
+                decoded.append(st.DecodedTokenWindow(plan.index, plan.emission_start_sample,
+                                                     plan.emission_end_sample, tuple(toks)))
+        return decoded
+
+    def transcribe(self, pcm: np.ndarray, token_piece=None, stream=None) -> st.StitchedTokens:
+        """Long-form transcription of 16 kHz mono f32 PCM on this GPU."""
+        pcm = np.ascontiguousarray(pcm, dtype=np.float32)
+        plans = wp.plan_stateless_windows(int(pcm.shape[0]))
+        return st.stitch_token_windows(self.decode_plans(pcm, plans, stream), token_piece)
+
+    def destroy(self) -> None:
+        self.graph.destroy()
+        self.weights.release()
+
+
+def transcribe_sharded(engine, pcm: np.ndarray, rank: int, world_size: int, gather, token_piece=None):
+    """Multi-GPU long-form transcription: this rank decodes its contiguous
+    share of the window plan with its own `engine` (its own GPU);
+    `gather(obj)` brings every rank's decoded windows to rank 0 (for example
+    torch.distributed's gather_object), which merges them.  Returns the merged
+    tokens on rank 0 and None elsewhere."""
+    pcm = np.ascontiguousarray(pcm, dtype=np.float32)
+    plans = wp.plan_stateless_windows(int(pcm.shape[0]))
+    mine = [plans[i] for i in wp.shard_windows(len(plans), world_size, rank)]
+    decoded = engine.decode_plans(pcm, mine) if mine else []
+    gathered = gather(decoded)
+    if rank != 0:
+        return None
+    return st.stitch_token_windows([w for part in gathered for w in part], token_piece)

@@ -183,3 +183,26 @@ def make_decoder(precision: str = "fp16", seed: int = 0, blank_bias: float = 1.5
         "joint.head.bias": head_bias,
     }
     return {name: _rec(data[name], shape, layout) for name, (shape, layout, _) in DECODER_TENSORS.items()}
+
+
+def make_pcm(seconds: float, seed: int = 0, sample_rate: int = 16_000) -> np.ndarray:
+    """Seeded synthetic speech-band audio as 16 kHz f32 PCM with PCM16
+    quantization: pink (1/f) noise plus six amplitude-modulated tones between
+    100 and 4000 Hz (the benchmark's stand-in for real recordings)."""
+    rng = np.random.default_rng(seed)
+    n = int(round(seconds * sample_rate))
+    spec = np.fft.rfft(rng.standard_normal(n))
+    f = np.fft.rfftfreq(n, 1.0 / sample_rate)
+    spec[1:] /= np.sqrt(f[1:])
+    spec[0] = 0.0
+    pink = np.fft.irfft(spec, n)
+    pink /= max(np.abs(pink).max(), 1e-12)
+    t = np.arange(n) / sample_rate
+    tones = np.zeros(n)
+    for freq in rng.uniform(100.0, 4000.0, size=6):
+        am = 0.5 * (1.0 + np.sin(2 * np.pi * rng.uniform(0.5, 4.0) * t + rng.uniform(0, 2 * np.pi)))
+        tones += am * np.sin(2 * np.pi * freq * t + rng.uniform(0, 2 * np.pi))
+    tones /= 6.0
+    x = 0.3 * pink + 0.4 * tones
+    pcm16 = np.clip(np.round(x * 32767.0), -32768, 32767).astype(np.int16)
+    return pcm16.astype(np.float32) / 32768.0
