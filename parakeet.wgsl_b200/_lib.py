@@ -31,7 +31,7 @@ EXPORTED = (
     "pk_logmel",
     "pk_weights_upload", "pk_weights_release", "pk_encoder_create", "pk_encoder_forward",
     "pk_encoder_set_checkpoints", "pk_encoder_checkpoint", "pk_encoder_destroy", "pk_debug_set_gemm_route",
-    "pk_debug_set_gemm_tile", "pk_debug_set_attention_route",
+    "pk_debug_set_gemm_tile", "pk_debug_set_attention_route", "pk_debug_set_decoder_route",
 )
 
 
@@ -122,6 +122,7 @@ def load() -> ctypes.CDLL:
             "pk_debug_set_gemm_route": [i32],
             "pk_debug_set_gemm_tile": [i32],
             "pk_debug_set_attention_route": [i32],
+            "pk_debug_set_decoder_route": [i32],
         }
         for name, args in sig.items():
             fn = getattr(lib, name)

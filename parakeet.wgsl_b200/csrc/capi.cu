@@ -26,6 +26,7 @@ static thread_local std::string t_last_error;
 int g_gemm_route = 0;
 int g_gemm_tile = 0;
 int g_attention_route = 0;
+int g_decoder_route = 0;
 
 int set_error(int code, const char* fmt, ...) {
   char buf[1024];
@@ -128,6 +129,11 @@ int pk_device_open(int ordinal, pk_device** out) {
     return cuda_error(e, "cudaMalloc(status)");
   }
   cudaMemset(d->ctx.status, 0, sizeof(unsigned int));
+  if ((e = cudaMalloc(&d->ctx.tdt_exchange, kTdtExchangeBytes)) != cudaSuccess) {
+    cudaFree(d->ctx.status);
+    delete d;
+    return cuda_error(e, "cudaMalloc(decoder exchange)");
+  }
   *out = d;
   return PK_OK;
 }
@@ -137,6 +143,7 @@ int pk_device_close(pk_device* device) {
   if (!device->closed) {
     cudaSetDevice(device->ctx.ordinal);
     cudaFree(device->ctx.status);
+    cudaFree(device->ctx.tdt_exchange);
     device->closed = true;
   }
   delete device;
@@ -285,7 +292,17 @@ int pk_tdt_decode(pk_device* device, const pk_tdt_desc* d, pk_stream stream) {
     if (reinterpret_cast<uintptr_t>(q) & 15)
       return set_error(PK_E_LAYOUT, "TDT decoder weights and encoder input must be 16-byte aligned");
   cudaSetDevice(device->ctx.ordinal);
+  if (g_decoder_route != 1) {
+    const int st = launch_tdt_resident(device->ctx, *d, as_stream(stream));
+    if (st != PK_E_SHAPE || g_decoder_route == 2) return st;
+  }
   return launch_tdt_decode(device->ctx, *d, as_stream(stream));
+}
+
+int pk_debug_set_decoder_route(int route) {
+  if (route < 0 || route > 2) return set_error(PK_E_INVALID, "decoder route must be 0, 1 or 2");
+  g_decoder_route = route;
+  return PK_OK;
 }
 
 int pk_conformer_conv(pk_device* device, int precision, int batch, int frames, const void* pointwise,

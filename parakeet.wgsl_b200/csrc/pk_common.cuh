@@ -327,4 +327,18 @@ __device__ __forceinline__ float sigmoid_ref(float v) {
   return 1.0f / (1.0f + expf(-b));
 }
 
+// The TDT decoders' gate nonlinearities (src/webgpu/kernels/tdt-decoder.ts:
+// 1310-1326): sigmoid of a value clamped to +-20, tanh of a value clamped to
+// +-10.  The shader's f32 exp / tanh are accurate to a few ulp and
+// backend-defined; here (and in the CPU restatement) they are the correctly
+// rounded f32 values, taken from the double-precision functions, so the two
+// agree bit for bit.
+__device__ __forceinline__ float tdt_sigmoid(float v) {
+  const float b = fminf(fmaxf(v, -20.0f), 20.0f);
+  return 1.0f / (1.0f + __double2float_rn(exp(-(double)b)));
+}
+__device__ __forceinline__ float tdt_tanh(float v) {
+  return __double2float_rn(tanh((double)fminf(fmaxf(v, -10.0f), 10.0f)));
+}
+
 }  // namespace pk

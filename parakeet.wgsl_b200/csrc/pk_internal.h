@@ -16,7 +16,13 @@ struct DeviceCtx {
   int max_smem_optin = 0;
   unsigned int* status = nullptr;  // device word; kernels OR PK_STATUS_* bits into it
   void* encode_tiled = nullptr;    // cuTensorMapEncodeTiled
+  void* tdt_exchange = nullptr;    // resident decoder's cross-CTA exchange area (kTdtExchangeBytes)
 };
+
+// Bytes of the resident TDT decoder's exchange area (hidden / projection
+// vectors, argmax partials and the grid-barrier counter for up to 32 windows),
+// allocated with the device handle.
+constexpr size_t kTdtExchangeBytes = 512 * 1024;
 
 // Thread-local error reporting.
 int set_error(int code, const char* fmt, ...);
@@ -106,6 +112,11 @@ int launch_subsampling_time_mask(int precision, int batch, int height, int width
                                  const uint32_t* feature_lengths, int steps, cudaStream_t stream);
 
 int launch_tdt_decode(const DeviceCtx& dev, const pk_tdt_desc& d, cudaStream_t stream);
+// Resident FP16 decoder (all windows in lockstep on 128 co-resident CTAs);
+// returns PK_E_SHAPE when it does not apply (then the cluster kernel runs).
+int launch_tdt_resident(const DeviceCtx& dev, const pk_tdt_desc& d, cudaStream_t stream);
+// Test knob: 0 = automatic, 1 = cluster kernel only, 2 = resident kernel only.
+extern int g_decoder_route;
 int launch_logmel(int batch, int sample_count, const float* samples, const uint32_t* valid_samples, float* features,
                   cudaStream_t stream);
 

@@ -232,17 +232,8 @@ __device__ __forceinline__ bool better(float lv, uint32_t li, float rv, uint32_t
   return rv > lv || (rv == lv && ri < li);
 }
 __device__ __forceinline__ float sanitize(float v) { return v != v ? TNEG : v; }
-// The shader's f32 exp / tanh are accurate to a few ulp and backend-defined;
-// here (and in the CPU restatement) they are the correctly rounded f32 values,
-// taken from the double-precision functions, so both sides agree bit for bit.
-__device__ __forceinline__ float exp_cr(float v) { return __double2float_rn(exp((double)v)); }
-__device__ __forceinline__ float sig_ref(float v) {
-  const float b = fminf(fmaxf(v, -20.0f), 20.0f);
-  return 1.0f / (1.0f + exp_cr(-b));
-}
-__device__ __forceinline__ float tanh_ref(float v) {
-  return __double2float_rn(tanh((double)fminf(fmaxf(v, -10.0f), 10.0f)));
-}
+__device__ __forceinline__ float sig_ref(float v) { return tdt_sigmoid(v); }
+__device__ __forceinline__ float tanh_ref(float v) { return tdt_tanh(v); }
 
 // Ring position shared by the producer and every consumer warp (each keeps
 // its own copy; all walk the same stage sequence).

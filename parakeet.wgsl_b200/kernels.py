@@ -677,3 +677,9 @@ def set_attention_route(route: str) -> None:
     (the mma.sync kernel) or "tcgen05-rowmajor" (the tcgen05 kernel, with the
     positions argument given row-major [8][2T-1][128])."""
     _lib.call("pk_debug_set_attention_route", {"auto": 0, "simt": 1, "mma": 2, "tcgen05-rowmajor": 3}[route])
+
+
+def set_decoder_route(route: str) -> None:
+    """Test hook: "auto" (the resident FP16 decoder where it applies),
+    "cluster" (one 4-CTA cluster per window) or "resident"."""
+    _lib.call("pk_debug_set_decoder_route", {"auto": 0, "cluster": 1, "resident": 2}[route])

@@ -52,8 +52,17 @@ def _compare(got, ref, lengths):
     return agree, exact
 
 
+@pytest.fixture(params=["cluster", "resident"])
+def route(pk, request):
+    pk.kernels.set_decoder_route(request.param)
+    yield request.param
+    pk.kernels.set_decoder_route("auto")
+
+
 @pytest.mark.parametrize("precision", ["fp16", "fp32"])
-def test_tdt_decoder_matches_oracle(pk, oracle, device, precision):
+def test_tdt_decoder_matches_oracle(pk, oracle, device, precision, route):
+    if route == "resident" and precision == "fp32":
+        pytest.skip("the resident decoder holds FP16 weights only")
     dt = np.float16 if precision == "fp16" else np.float32
     rng = np.random.default_rng(11)
     enc = rng.normal(0, 1, (4, 188, 640)).astype(dt)
@@ -70,7 +79,7 @@ def test_tdt_decoder_matches_oracle(pk, oracle, device, precision):
 
 @pytest.mark.parametrize("token,duration,max_tokens,flush", [(1024, 3, 8, 0), (7, 0, 64, 0), (7, 0, 15, 0),
                                                              (9, 2, 32, 1)])
-def test_tdt_decoder_control_paths(pk, oracle, device, token, duration, max_tokens, flush):
+def test_tdt_decoder_control_paths(pk, oracle, device, token, duration, max_tokens, flush, route):
     """Blank skipping, the 10-symbol cap, overflow and the end-of-stream flush."""
     enc = np.random.default_rng(4).normal(0, 1, (2, 12, 640)).astype(np.float16)
     dec = forced_decoder(pk, "fp16", token, duration)
@@ -91,3 +100,32 @@ def test_tdt_decoder_rejects_bad_descriptors(pk, device):
     desc = pk._lib.TdtDesc(0, 0, 188, 10)
     with pytest.raises(pk.PkError, match="PK_E_SHAPE"):
         pk._lib.call("pk_tdt_decode", device.handle, ctypes.byref(desc), None)
+
+
+def test_resident_and_cluster_decoders_agree_on_32_windows(pk, device):
+    """32 windows (the resident kernel's capacity) with ragged lengths, start /
+    end ranges and flushes: both kernels return identical tokens, frames,
+    durations, counts and flags."""
+    rng = np.random.default_rng(21)
+    b = 32
+    enc = rng.normal(0, 1, (b, 188, 640)).astype(np.float16)
+    dec = {k: v["data"] for k, v in pk.synthetic.make_decoder("fp16", seed=5).items()}
+    lengths = rng.integers(1, 189, size=b).tolist()
+    starts = [int(rng.integers(0, 3)) for _ in range(b)]
+    ends = [int(rng.integers(150, 189)) for _ in range(b)]
+    flush = [int(i % 3 == 0) for i in range(b)]
+    outs = []
+    for r in ("cluster", "resident"):
+        pk.kernels.set_decoder_route(r)
+        try:
+            outs.append(_run_gpu(pk, device, enc, lengths, dec, "fp16", 2048, starts=starts, ends=ends, flush=flush))
+        finally:
+            pk.kernels.set_decoder_route("auto")
+    assert device.status() == 0
+    (t0, f0, d0, c0, s0), (t1, f1, d1, c1, s1) = outs
+    assert list(c0) == list(c1) and list(s0) == list(s1)
+    for w in range(b):
+        n = int(c0[w])
+        assert np.array_equal(t0[w, :n], t1[w, :n]) and np.array_equal(f0[w, :n], f1[w, :n])
+        assert np.array_equal(d0[w, :n], d1[w, :n])
+    print(f"decoder: 32-window agreement, {int(np.sum(c0))} tokens")
