@@ -17,6 +17,8 @@ from __future__ import annotations
 
 import unicodedata
 from dataclasses import dataclass, replace
+
+import numpy as np
 from typing import Callable, Optional, Sequence
 
 from .windows import ENCODER_FRAME_SAMPLES, OVERLAP_SAMPLES, WindowPlan
@@ -152,54 +154,72 @@ def _merge_token_streams(left, right, piece, has_pieces):
     if len(ov_left) < 2 or len(ov_right) < 2:
         return _merge_by_midpoint(left, right, left_end, right_start, piece, has_pieces), "midpoint"
 
-    def matches(a, b):
-        return (token_ids_match(a[1].token_id, b[1].token_id, piece)
-                and abs(a[1].start_sample - b[1].start_sample) < OVERLAP_SAMPLES / 2)
-
-    run = _longest_contiguous(ov_left, ov_right, matches)
+    m = _match_matrix(ov_left, ov_right, piece, has_pieces)
+    run = _longest_contiguous(m)
     if len(run) >= max(len(ov_left) // 2, 1):
         return _merge_using_matches(run, ov_left, ov_right, left, right, piece, has_pieces), "contiguous"
-    lcs = _longest_common_subsequence(ov_left, ov_right, matches)
+    lcs = _longest_common_subsequence(m)
     if not lcs:
         return _merge_by_midpoint(left, right, left_end, right_start, piece, has_pieces), "midpoint"
     return _merge_using_matches(lcs, ov_left, ov_right, left, right, piece, has_pieces), "lcs"
 
 
-def _longest_contiguous(left, right, matches):
-    best: list = []
-    for lo in range(len(left)):
-        for ro in range(len(right)):
-            if not matches(left[lo], right[ro]):
-                continue
-            cur = []
-            lc, rc = lo, ro
-            while lc < len(left) and rc < len(right) and matches(left[lc], right[rc]):
-                cur.append((lc, rc))
-                lc += 1
-                rc += 1
-            if len(cur) > len(best):  # the first run in scan order wins ties
-                best = cur
-    return best
+def _match_matrix(ov_left, ov_right, piece, has_pieces) -> np.ndarray:
+    """m[i, j]: overlap tokens i (left) and j (right) match -- same id (or the
+    same piece ignoring case) and starts less than half the overlap apart."""
+    lid = np.array([t.token_id for _, t in ov_left], dtype=np.int64)
+    rid = np.array([t.token_id for _, t in ov_right], dtype=np.int64)
+    same = lid[:, None] == rid[None, :]
+    if has_pieces:
+        codes: dict = {}
+
+        def code(tid):
+            p = piece(tid)
+            return -1 if p is None else codes.setdefault(p.lower(), len(codes))
+
+        lc = np.array([code(t.token_id) for _, t in ov_left], dtype=np.int64)
+        rc = np.array([code(t.token_id) for _, t in ov_right], dtype=np.int64)
+        same |= (lc[:, None] == rc[None, :]) & (lc[:, None] >= 0)
+    ls = np.array([t.start_sample for _, t in ov_left], dtype=np.int64)
+    rs = np.array([t.start_sample for _, t in ov_right], dtype=np.int64)
+    return same & (np.abs(ls[:, None] - rs[None, :]) * 2 < OVERLAP_SAMPLES)
 
 
-def _longest_common_subsequence(left, right, matches):
-    w = len(right) + 1
-    table = [0] * ((len(left) + 1) * w)
-    for lc in range(1, len(left) + 1):
-        for rc in range(1, len(right) + 1):
-            cell = lc * w + rc
-            if matches(left[lc - 1], right[rc - 1]):
-                table[cell] = table[(lc - 1) * w + rc - 1] + 1
+def _longest_contiguous(m: np.ndarray):
+    """The longest diagonal run of matches; among equal lengths the first run
+    start in row-major scan order (the reference's scan keeps the first)."""
+    n, k = m.shape
+    runs = np.zeros((n + 1, k + 1), dtype=np.int32)
+    for i in range(n - 1, -1, -1):
+        runs[i, :k] = np.where(m[i], runs[i + 1, 1:] + 1, 0)
+    best = int(runs[:n, :k].max(initial=0))
+    if best == 0:
+        return []
+    flat = int(np.argmax(runs[:n, :k] == best))
+    i, j = divmod(flat, k)
+    return [(i + d, j + d) for d in range(best)]
+
+
+def _longest_common_subsequence(m: np.ndarray):
+    n, k = m.shape
+    rows = m.tolist()
+    table = [[0] * (k + 1) for _ in range(n + 1)]
+    for lc in range(1, n + 1):
+        prev, cur, row = table[lc - 1], table[lc], rows[lc - 1]
+        for rc in range(1, k + 1):
+            if row[rc - 1]:
+                cur[rc] = prev[rc - 1] + 1
             else:
-                table[cell] = max(table[(lc - 1) * w + rc], table[lc * w + rc - 1])
+                a, b = prev[rc], cur[rc - 1]
+                cur[rc] = a if a > b else b
     rev = []
-    lc, rc = len(left), len(right)
+    lc, rc = n, k
     while lc > 0 and rc > 0:
-        if matches(left[lc - 1], right[rc - 1]):
+        if rows[lc - 1][rc - 1]:
             rev.append((lc - 1, rc - 1))
             lc -= 1
             rc -= 1
-        elif table[(lc - 1) * w + rc] > table[lc * w + rc - 1]:
+        elif table[lc - 1][rc] > table[lc][rc - 1]:
             lc -= 1
         else:
             rc -= 1  # backtracking tie rule
