@@ -273,13 +273,23 @@ __device__ void lstm_chains(RSmem& s, const __half (*w)[RW_STRIDE], const float*
         uint4 xv[RCHUNK];
 #pragma unroll
         for (int j = 0; j < RCHUNK; ++j) xv[j] = *reinterpret_cast<const uint4*>(&s.in.x2[k0 + 2 * j + par][grp * 4]);
+        if (!recurrent) {  // plain chains: nothing to keep
 #pragma unroll
-        for (int j = 0; j < RCHUNK; ++j) {
-          const __half2 wv = __half2half2(__ushort_as_half((unsigned short)(par ? ww[j] >> 16 : ww[j] & 0xffffu)));
-          const uint32_t xs[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
+          for (int j = 0; j < RCHUNK; ++j) {
+            const __half2 wv = __half2half2(__ushort_as_half((unsigned short)(par ? ww[j] >> 16 : ww[j] & 0xffffu)));
+            acc[0] = __hfma2(bits_h2(xv[j].x), wv, acc[0]);
+            acc[1] = __hfma2(bits_h2(xv[j].y), wv, acc[1]);
+            acc[2] = __hfma2(bits_h2(xv[j].z), wv, acc[2]);
+            acc[3] = __hfma2(bits_h2(xv[j].w), wv, acc[3]);
+          }
+        } else {
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            acc[i] = keep_mask(acc[i], __hfma2(bits_h2(xs[i]), wv, acc[i]), recurrent ? keep_rec[i] : 0u);
+          for (int j = 0; j < RCHUNK; ++j) {
+            const __half2 wv = __half2half2(__ushort_as_half((unsigned short)(par ? ww[j] >> 16 : ww[j] & 0xffffu)));
+            const uint32_t xs[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[i] = keep_mask(acc[i], __hfma2(bits_h2(xs[i]), wv, acc[i]), keep_rec[i]);
+          }
         }
       }
     }
@@ -449,9 +459,14 @@ __device__ void joint_partials(RSmem& s, const RParams& p, int slot) {
         const __half* wh = reinterpret_cast<const __half*>(&wq);
         const uint32_t xs[RCHUNK] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
         const uint32_t ms[RCHUNK] = {ma.x, ma.y, ma.z, ma.w, mb.x, mb.y, mb.z, mb.w};
+        if ((ma.x | ma.y | ma.z | ma.w | mb.x | mb.y | mb.z | mb.w) == 0u) {  // no skipped input here
 #pragma unroll
-        for (int j = 0; j < RCHUNK; ++j)
-          acc = keep_mask(acc, __hfma2(bits_h2(xs[j]), __half2half2(wh[j]), acc), ms[j]);
+          for (int j = 0; j < RCHUNK; ++j) acc = __hfma2(bits_h2(xs[j]), __half2half2(wh[j]), acc);
+        } else {
+#pragma unroll
+          for (int j = 0; j < RCHUNK; ++j)
+            acc = keep_mask(acc, __hfma2(bits_h2(xs[j]), __half2half2(wh[j]), acc), ms[j]);
+        }
       }
     }
     const float2 v01 = __half22float2(acc);
