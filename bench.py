@@ -268,6 +268,74 @@ def time_transcribe(pk, device, package, seconds=60.0, reps=2):
             "note": "random-init weights; the decoder's token count (not real speech) sets most of the time"}
 
 
+# Config 5 variants: (precision, palette policy, seconds of audio).  FP32 runs a
+# shorter stretch so the default benchmark stays within minutes.
+LONGFORM_VARIANTS = (("fp16", "mixed", 3600.0), ("fp16", "all5", 3600.0), ("fp32", "mixed", 600.0),
+                     ("fp32", "all5", 600.0))
+
+
+def longform_pcm(pk, seconds, seed=5, distinct=5):
+    """`seconds` of synthetic PCM built from `distinct` different 60 s
+    make_pcm blocks in rotation (a full-length make_pcm of an hour costs
+    about 40 s of host time)."""
+    blocks = [pk.synthetic.make_pcm(60.0, seed=seed + i) for i in range(distinct)]
+    n = int(round(seconds * 16_000))
+    reps = -(-n // blocks[0].shape[0])
+    return np.concatenate([blocks[i % distinct] for i in range(reps)])[:n]
+
+
+def time_longform(pk, device, rank, world, stream):
+    """engine.transcribe_sharded on synthetic audio, host PCM in and merged
+    tokens out: each rank decodes its contiguous share of the window plan on
+    its own GPU; the token lists meet on rank 0 (a host gather, no collective
+    on the hot path), which merges them.  Time: CUDA events on each rank's
+    stream around its share, the gather and the merge; max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    def gather(obj):
+        if world == 1:
+            return [obj]
+        parts = [None] * world if rank == 0 else None
+        dist.gather_object(obj, parts, dst=0)
+        return parts
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    out = []
+    for precision, policy, seconds in LONGFORM_VARIANTS:
+        package = pk.synthetic.make_package(precision, bits_policy=policy, seed=0)
+        package.update(pk.synthetic.make_decoder(precision, seed=0))
+        eng = pk.engine.ParakeetEngine(device, package, precision, capacity=BATCH)
+        del package
+        pcm = longform_pcm(pk, seconds)
+        with torch.cuda.stream(stream):
+            eng.transcribe(pcm[:30 * 16_000])  # warm-up
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record(stream)
+            res = pk.engine.transcribe_sharded(eng, pcm, rank, world, gather)
+            end.record(stream)
+            end.synchronize()
+        ms = max_over_ranks(start.elapsed_time(end))
+        windows = len(pk.windows.plan_stateless_windows(len(pcm)))
+        eng.destroy()
+        out.append({"precision": precision, "palette_bits": policy, "audio_s": seconds, "windows": windows,
+                    "s": round(ms / 1e3, 3), "audio_s_per_s": round(seconds / (ms / 1e3), 1),
+                    "tokens": None if res is None else len(res.tokens)})
+    return {"workload": "config5: synthetic PCM (five 60 s pink-noise + tone blocks in rotation), window plan "
+                        "sharded over ranks, host PCM in, merged tokens out",
+            "n_gpus": world, "variants": out,
+            "note": "random-init weights; decoded token counts are not real speech and set most of the time"}
+
+
 def cpu_baseline(pk, package, window_count=1):
     """Oracle (reference algorithm, f16-accumulating GEMMs) on `window_count` windows."""
     from oracle import oracle
@@ -396,6 +464,10 @@ def run_ours(args):
     tr_info = time_transcribe(pk, device, package) if rank == 0 else None
     barrier()
 
+    # ---- long-form (config 5): one hour's window plan sharded across all ranks
+    lf_info = None if args.skip_longform else time_longform(pk, device, rank, world, stream)
+    barrier()
+
     # ---- dominant kernel: palette GEMMs of one step, timed live
     with torch.cuda.stream(stream):
         gemm_flops, gemm_ms, gemm_detail = time_gemms(pk, device, BATCH, stream)
@@ -431,6 +503,7 @@ def run_ours(args):
             "decoder": dec_info,
             "logmel": lm_info,
             "transcribe": tr_info,
+            "longform": lf_info,
             "cpu_baseline": None if cpu_value is None else {
                 "value": round(cpu_value, 3), "unit": UNIT, "cores": int(os.environ.get("OMP_NUM_THREADS", cores)),
                 "kind": "port", "sample": f"1 window x 24 layers, oracle reference mode, {cpu_dt:.1f} s"},
@@ -559,6 +632,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
+    ap.add_argument("--skip-longform", action="store_true")
     ap.add_argument("--kernel", choices=["gemm", "attention", "attention-mma", "layernorm", "conv", "subsampling",
                                          "decoder", "logmel"],
                     help="profiling target: launch one operator only")

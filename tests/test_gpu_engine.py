@@ -18,11 +18,13 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 
-def test_engine_matches_oracle_stage_by_stage(pk, oracle, device):
-    package = pk.synthetic.make_package("fp16", seed=0)
-    decoder = pk.synthetic.make_decoder("fp16", seed=0)
+@pytest.mark.parametrize("precision", ["fp16", "fp32"])
+def test_engine_matches_oracle_stage_by_stage(pk, oracle, device, precision):
+    dtype = np.float16 if precision == "fp16" else np.float32
+    package = pk.synthetic.make_package(precision, seed=0)
+    decoder = pk.synthetic.make_decoder(precision, seed=0)
     package.update(decoder)
-    eng = pk.engine.ParakeetEngine(device, package, "fp16", capacity=4, keep_intermediates=True)
+    eng = pk.engine.ParakeetEngine(device, package, precision, capacity=4, keep_intermediates=True)
     try:
         pcm = pk.synthetic.make_pcm(20.0, seed=3)
         result = eng.transcribe(pcm)
@@ -39,15 +41,15 @@ def test_engine_matches_oracle_stage_by_stage(pk, oracle, device):
 
         lengths = [max(1, int(v) // 160) for v in valid]
         proj = eng.last["projected"]
-        ref_proj, ref_lens = oracle.encoder(package, feats, lengths, np.float16, acc_mode=1)
+        ref_proj, ref_lens = oracle.encoder(package, feats, lengths, dtype, acc_mode=1)
         err = oracle.rel_frobenius(proj.reshape(-1, 640), ref_proj)
-        print(f"engine: encoder rel-Frobenius {err:.2e} vs wide oracle")
+        print(f"engine {precision}: encoder rel-Frobenius {err:.2e} vs wide oracle")
         assert err < 2e-2
         assert list(eng.last["encoded_lengths"]) == [int(v) for v in ref_lens]
 
         dec = {n: r["data"] for n, r in decoder.items()}
         tok, fr, du, cnt, flags = oracle.tdt_decode(
-            proj.astype(np.float16), eng.last["encoded_lengths"], dec, max_tokens=eng.max_tokens,
+            proj.astype(dtype), eng.last["encoded_lengths"], dec, max_tokens=eng.max_tokens,
             starts=[p.decode_start_frame for p in plans], ends=[p.decode_end_frame for p in plans],
             flush=[int(p.flush_final) for p in plans])
         st = pk.stitch
@@ -57,7 +59,7 @@ def test_engine_matches_oracle_stage_by_stage(pk, oracle, device):
             windows.append(st.DecodedTokenWindow(p.index, p.emission_start_sample, p.emission_end_sample,
                                                  tuple(st.globalize_tdt_tokens(emitted, p))))
         ref = st.stitch_token_windows(windows)
-        print(f"engine: {len(result.tokens)} merged tokens, methods {[t.method for t in result.trace]}")
+        print(f"engine {precision}: {len(result.tokens)} merged tokens, methods {[t.method for t in result.trace]}")
         assert result.tokens == ref.tokens
         assert result.trace == ref.trace
         assert device.status() == 0
