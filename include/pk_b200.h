@@ -61,8 +61,9 @@ int pk_version(void);
  * createRawWebGpuParakeetEngine (src/runtime/webgpu-engine.ts:1062-1120). */
 int pk_device_open(int ordinal, pk_device** out);
 int pk_device_close(pk_device* device);
-/* Reads and clears the device status word (bit 0..4: a bounded wait inside a
- * kernel expired).  Replaces the uncapturederror listener / throwGpuError
+/* Reads and clears the device status word (bits 0..5: a bounded wait inside a
+ * kernel expired -- 0 TMA/mbarrier, 1 MMA, 2 decode, 3 epilogue, 4 unwind
+ * drain, 5 grid barrier).  Replaces the uncapturederror listener / throwGpuError
  * (src/runtime/webgpu-engine.ts:274, :959).  Synchronizes the device. */
 int pk_device_status(pk_device* device, uint32_t* status_bits);
 
@@ -287,6 +288,19 @@ int pk_debug_set_attention_route(int route);
  * cluster kernel only, 2 = the resident kernel only (PK_E_SHAPE where it does
  * not apply). */
 int pk_debug_set_decoder_route(int route);
+
+/* Test hook (no reference counterpart; the reference's device-loss path is the
+ * uncapturederror listener, src/runtime/webgpu-engine.ts:274): makes one of
+ * the library's bounded device waits run out, with a limit of `limit_ms`
+ * (1..2000) instead of the 4 s production limit, and synchronizes `stream`.
+ * kind 0: an mbarrier wait whose producer arrives (completes; no status bit);
+ * 1: an mbarrier wait that nothing completes (status bit 0);
+ * 2: a grid barrier of a two-CTA cooperative launch that both CTAs reach;
+ * 3: the same barrier with one CTA returning before it (status bit 5).
+ * Returns PK_OK once the probe kernel has finished; a wait that ran out shows
+ * up as PK_E_TIMEOUT from the next pk_device_status, as in production.  The
+ * probe traps, faults and hangs nothing: the context stays usable. */
+int pk_debug_wait_probe(pk_device* device, int kind, uint32_t limit_ms, pk_stream stream);
 
 #ifdef __cplusplus
 }

@@ -32,6 +32,7 @@ EXPORTED = (
     "pk_weights_upload", "pk_weights_release", "pk_encoder_create", "pk_encoder_forward",
     "pk_encoder_set_checkpoints", "pk_encoder_checkpoint", "pk_encoder_destroy", "pk_debug_set_gemm_route",
     "pk_debug_set_gemm_tile", "pk_debug_set_attention_route", "pk_debug_set_decoder_route",
+    "pk_debug_wait_probe",
 )
 
 
@@ -123,6 +124,7 @@ def load() -> ctypes.CDLL:
             "pk_debug_set_gemm_tile": [i32],
             "pk_debug_set_attention_route": [i32],
             "pk_debug_set_decoder_route": [i32],
+            "pk_debug_wait_probe": [vp, i32, ctypes.c_uint32, vp],
         }
         for name, args in sig.items():
             fn = getattr(lib, name)

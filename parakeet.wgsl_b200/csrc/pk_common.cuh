@@ -22,6 +22,7 @@
 #define PK_STATUS_TIMEOUT_DECODE 4u
 #define PK_STATUS_TIMEOUT_EPILOGUE 8u
 #define PK_STATUS_TIMEOUT_DRAIN 16u
+#define PK_STATUS_TIMEOUT_GRID 32u
 
 namespace pk {
 
@@ -76,21 +77,61 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 }
 
 // Wait for the phase with the given parity to complete.  Returns false (and
-// raises *abort and the status bit) when the wait exceeds PK_WAIT_NS or when
+// raises *abort and the status bit) when the wait exceeds `limit_ns` or when
 // another role of this CTA has already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                          unsigned int* status, unsigned int bit) {
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                              unsigned int* status, unsigned int bit, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = global_timer_ns();
   while (true) {
     if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
     if (*abort) return false;
-    if (global_timer_ns() - start > PK_WAIT_NS) {
+    if (global_timer_ns() - start > limit_ns) {
       *abort = 1;
       if (status) atomicOr(status, bit);
       return false;
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                          unsigned int* status, unsigned int bit) {
+  return mbar_wait_for(bar, parity, abort, status, bit, PK_WAIT_NS);
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_u32(const unsigned int* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// One thread per CTA of a cooperative launch: arrive on the grid barrier
+// counter `ctr` and wait until it reaches `target` (gridDim.x times the
+// barrier's generation).  Bounded: after `limit_ns`, or once any CTA has
+// raised *abort_flag, it stops waiting; on expiry it raises *abort_flag (later
+// barriers then no longer wait) and ORs `bit` into the status word.  Returns
+// whether every CTA arrived.
+__device__ __forceinline__ bool grid_arrive_wait(unsigned int* ctr, volatile unsigned int* abort_flag,
+                                                 unsigned int target, unsigned int* status, unsigned int bit,
+                                                 uint64_t limit_ns) {
+  __threadfence();
+  atomicAdd(ctr, 1u);
+  const uint64_t t0 = global_timer_ns();
+  bool ok = true;
+  while (ld_acquire_u32(ctr) < target) {
+    if (*abort_flag) {
+      ok = false;
+      break;
+    }
+    if (global_timer_ns() - t0 > limit_ns) {
+      *abort_flag = 1u;
+      if (status) atomicOr(status, bit);
+      ok = false;
+      break;
+    }
+    __nanosleep(64);
+  }
+  __threadfence();
+  return ok;
 }
 
 // Bounded drain wait used on the unwind path (short limit, no abort check).

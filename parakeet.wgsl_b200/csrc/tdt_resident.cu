@@ -139,34 +139,14 @@ struct RParams {
   int batch, frames, max_tokens;
 };
 
-__device__ __forceinline__ uint32_t ld_acquire_u32(const unsigned int* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
 // Grid barrier of the cooperative launch; bounded (a wait that expires sets
 // the abort flag and a status bit, after which barriers no longer wait).
 __device__ void grid_sync(RSmem& s, const RParams& p) {
   __syncthreads();
   if (threadIdx.x == 0) {
     unsigned int* ctr = reinterpret_cast<unsigned int*>(p.xchg + XSYNC);
-    volatile unsigned int* abort_flag = ctr + 1;
     s.gen += 1;
-    const unsigned int target = s.gen * gridDim.x;
-    __threadfence();
-    atomicAdd(ctr, 1u);
-    const uint64_t t0 = global_timer_ns();
-    while (ld_acquire_u32(ctr) < target) {
-      if (*abort_flag) break;
-      if (global_timer_ns() - t0 > PK_WAIT_NS) {
-        *abort_flag = 1u;
-        atomicOr(p.status, PK_STATUS_TIMEOUT_EPILOGUE);
-        break;
-      }
-      __nanosleep(64);
-    }
-    __threadfence();
+    grid_arrive_wait(ctr, ctr + 1, s.gen * gridDim.x, p.status, PK_STATUS_TIMEOUT_GRID, PK_WAIT_NS);
   }
   __syncthreads();
 }

@@ -149,17 +149,49 @@ class ParakeetEngine:
         self.weights.release()
 
 
+class ShardFailure(RuntimeError):
+    """A sharded transcription failed on one or more ranks, or its gather did.
+    ``failures`` maps each failed rank to its error ("ErrorType: message");
+    a failed gather (a rank that left, a collective that timed out) has the
+    key None."""
+
+    def __init__(self, failures: dict):
+        self.failures = dict(failures)
+        super().__init__("; ".join(("gather" if r is None else f"rank {r}") + f": {m}"
+                                   for r, m in sorted(self.failures.items(), key=lambda kv: (kv[0] is None, kv[0]))))
+
+
 def transcribe_sharded(engine, pcm: np.ndarray, rank: int, world_size: int, gather, token_piece=None):
     """Multi-GPU long-form transcription: this rank decodes its contiguous
     share of the window plan with its own `engine` (its own GPU);
-    `gather(obj)` brings every rank's decoded windows to rank 0 (for example
-    torch.distributed's gather_object), which merges them.  Returns the merged
-    tokens on rank 0 and None elsewhere."""
+    `gather(obj)` brings every rank's object to rank 0 (for example
+    torch.distributed's gather_object), which merges the decoded windows.
+    Returns the merged tokens on rank 0 and None elsewhere.
+
+    Failures do not hang the other ranks: a rank whose decode raises (a
+    PkError such as PK_E_TIMEOUT from a bounded device wait, a RangeError)
+    still takes the gather step, carrying its error instead of its windows,
+    and then re-raises; rank 0 raises ShardFailure naming every failed rank.
+    A gather that itself fails (a rank that exited, a process-group timeout)
+    raises ShardFailure on the ranks that see it."""
     pcm = np.ascontiguousarray(pcm, dtype=np.float32)
     plans = wp.plan_stateless_windows(int(pcm.shape[0]))
     mine = [plans[i] for i in wp.shard_windows(len(plans), world_size, rank)]
-    decoded = engine.decode_plans(pcm, mine) if mine else []
-    gathered = gather(decoded)
+    error = None
+    try:
+        payload = ("ok", engine.decode_plans(pcm, mine) if mine else [])
+    except Exception as exc:  # reported through the gather, re-raised below
+        error = exc
+        payload = ("error", f"{type(exc).__name__}: {exc}")
+    try:
+        gathered = gather(payload)
+    except Exception as exc:
+        raise ShardFailure({None: f"{type(exc).__name__}: {exc}"}) from exc
     if rank != 0:
+        if error is not None:
+            raise error
         return None
-    return st.stitch_token_windows([w for part in gathered for w in part], token_piece)
+    failures = {r: part[1] for r, part in enumerate(gathered) if part[0] != "ok"}
+    if failures:
+        raise ShardFailure(failures) from error
+    return st.stitch_token_windows([w for part in gathered for w in part[1]], token_piece)

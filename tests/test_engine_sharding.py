@@ -1,7 +1,11 @@
 """Sharded long-form transcription on the host (engine.transcribe_sharded):
 world_size-2 gloo ranks on CPU, each decoding its contiguous share of the
 window plan with a deterministic stand-in engine; rank 0's merge equals the
-single-rank merge.  The GPU engine itself is covered by test_gpu_engine.py."""
+single-rank merge.  Failure detection, made on the host: a rank whose engine
+returns an injected PK_E_TIMEOUT, and a rank that exits before the gather --
+rank 0 reports ShardFailure and no process hangs.  The GPU engine itself is
+covered by test_gpu_engine.py; the device side of a timeout by
+test_gpu_fault.py."""
 from __future__ import annotations
 
 import os
@@ -65,3 +69,83 @@ def test_two_rank_merge_equals_single_rank(pk, tmp_path):
     single = pk.engine.transcribe_sharded(FakeEngine(pk), pcm, 0, 1, lambda obj: [obj])
     assert got == [(t.token_id, t.start_sample) for t in single.tokens]
     assert len(got) > 0
+
+
+class FailingEngine(FakeEngine):
+    """decode_plans that fails the way a bounded device wait reports it."""
+
+    def decode_plans(self, pcm, plans, stream=None):
+        raise self.pk.PkError(-7, "injected: a bounded device wait expired (status bits 0x1)")
+
+
+def _failing_rank(rank, world, port, out_dir, mode):
+    import sys
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import __graft_entry__
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
+    pk = __graft_entry__.load()
+    outcome = "returned"
+    if mode == "exits" and rank == 1:
+        outcome = "left"  # leaves between steps: nothing of this rank is in flight
+    else:
+        engine = FailingEngine(pk) if (mode == "raises" and rank == 1) else FakeEngine(pk)
+
+        def gather(obj):
+            parts = [None] * world if rank == 0 else None
+            dist.gather_object(obj, parts, dst=0)
+            return parts
+
+        try:
+            pk.engine.transcribe_sharded(engine, np.zeros(16_000 * 100, np.float32), rank, world, gather)
+        except Exception as exc:  # recorded for the test
+            outcome = f"{type(exc).__name__}|{exc}"
+    with open(os.path.join(out_dir, f"rank{rank}.txt"), "w") as f:
+        f.write(outcome)
+    if outcome == "returned":
+        dist.destroy_process_group()
+
+
+def _run_ranks(tmp_path, mode, deadline_s=60.0):
+    import socket
+    import time
+
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.start_processes(_failing_rank, args=(2, port, str(tmp_path), mode), nprocs=2, join=False,
+                             start_method="spawn")
+    t0 = time.monotonic()
+    while not ctx.join(timeout=1.0):
+        if time.monotonic() - t0 > deadline_s:
+            for p in ctx.processes:
+                p.kill()
+            raise AssertionError(f"ranks still running after {deadline_s} s ({mode})")
+    return [(tmp_path / f"rank{r}.txt").read_text() for r in range(2)], time.monotonic() - t0
+
+
+def test_rank_with_injected_timeout_is_reported_on_rank0(tmp_path):
+    (r0, r1), _ = _run_ranks(tmp_path, "raises")
+    kind, msg = r0.split("|", 1)
+    assert kind == "ShardFailure"
+    assert msg.startswith("rank 1: PkError: PK_E_TIMEOUT: injected"), msg
+    assert r1.startswith("PkError|PK_E_TIMEOUT")
+
+
+def test_rank_that_exits_before_the_gather_is_detected(tmp_path):
+    (r0, r1), elapsed = _run_ranks(tmp_path, "exits")
+    assert r1 == "left"
+    assert r0.startswith("ShardFailure|gather: "), r0
+    assert elapsed < 60.0
+
+
+def test_shard_failure_message_orders_ranks_then_gather(pk):
+    err = pk.engine.ShardFailure({3: "B", None: "C", 1: "A"})
+    assert str(err) == "rank 1: A; rank 3: B; gather: C"
