@@ -79,6 +79,15 @@ class ParakeetEngine:
 
     def transcribe_windows(self, windows: Sequence[tuple], stream=None) -> list[WindowResult]:
         """windows: (samples f32 [<= 240 000], WindowPlan) per window, 1..capacity."""
+        out = []
+        for tok, fr, du, overflow in self._run_batch(windows, stream):
+            out.append(WindowResult(tuple(st.EmittedToken(*e) for e in zip(tok.tolist(), fr.tolist(), du.tolist())),
+                                    overflow))
+        return out
+
+    def _run_batch(self, windows: Sequence[tuple], stream=None) -> list:
+        """One batch through log-mel, encoder and decoder; per window its
+        (token ids, frames, durations) arrays and overflow flag."""
         b = len(windows)
         if not 0 < b <= self.capacity:
             raise RangeError(f"Engine batch must contain 1-{self.capacity} windows")
@@ -122,8 +131,7 @@ class ParakeetEngine:
         out = []
         for i in range(b):
             n = min(int(counts[i]), self.max_tokens)
-            out.append(WindowResult(tuple(st.EmittedToken(int(tok[i, j]), int(fr[i, j]), int(du[i, j]))
-                                          for j in range(n)), bool(flags[i] & 1)))
+            out.append((tok[i, :n].copy(), fr[i, :n].copy(), du[i, :n].copy(), bool(flags[i] & 1)))
         return out
 
     def decode_plans(self, pcm: np.ndarray, plans: Sequence[wp.WindowPlan], stream=None) -> list:
@@ -132,8 +140,8 @@ class ParakeetEngine:
         for start in range(0, len(plans), self.capacity):
             chunk = plans[start:start + self.capacity]
             batch = [(pcm[p.source_start_sample:p.source_end_sample], p) for p in chunk]
-            for plan, res in zip(chunk, self.transcribe_windows(batch, stream)):
-                toks = st.globalize_tdt_tokens(res.tokens, plan)
+            for plan, (tok, fr, du, _) in zip(chunk, self._run_batch(batch, stream)):
+                toks = st.globalize_tdt_arrays(tok, fr, du, plan)
                 decoded.append(st.DecodedTokenWindow(plan.index, plan.emission_start_sample,
                                                      plan.emission_end_sample, tuple(toks)))
         return decoded

@@ -16,7 +16,7 @@ decoded on whichever GPU holds them, and only their token lists meet here.
 from __future__ import annotations
 
 import unicodedata
-from dataclasses import dataclass, replace
+from dataclasses import dataclass
 
 import numpy as np
 from typing import Callable, Optional, Sequence
@@ -79,6 +79,19 @@ def globalize_tdt_tokens(tokens: Sequence[EmittedToken], window: WindowPlan) -> 
     return out
 
 
+def globalize_tdt_arrays(token_ids, frames, durations, window: WindowPlan) -> list[TimedToken]:
+    """globalize_tdt_tokens on the decoder's output arrays (token ids,
+    window-local frames, durations; one entry per emission): the same tokens,
+    without building an EmittedToken per emission first."""
+    frames = np.asarray(frames, dtype=np.int64)
+    durations = np.asarray(durations, dtype=np.int64)
+    start = window.timestamp_offset_sample + frames * ENCODER_FRAME_SAMPLES
+    end = np.minimum(start + durations * ENCODER_FRAME_SAMPLES, window.emission_end_sample)
+    keep = (start >= window.emission_start_sample) & (start < window.emission_end_sample)
+    ids = np.asarray(token_ids, dtype=np.int64)[keep].tolist()
+    return [TimedToken(*f) for f in zip(ids, start[keep].tolist(), end[keep].tolist(), durations[keep].tolist())]
+
+
 def stitch_token_windows(windows: Sequence[DecodedTokenWindow],
                          token_piece: Optional[TokenPieceResolver] = None) -> StitchedTokens:
     ordered = sorted(windows, key=lambda w: (w.start_sample, w.index))
@@ -97,6 +110,10 @@ class IncrementalStitchAccumulator:
         self._has_pieces = token_piece is not None
         self._trace: Optional[list] = [] if collect_trace else None
         self._merged: list = []
+        # start_sample of every merged token, in list order (the first
+        # len(self._merged) entries): the overlap scans of each merge read
+        # this array instead of the growing token list.
+        self._starts = np.zeros(1024, dtype=np.int64)
         self._previous: Optional[DecodedTokenWindow] = None
 
     def append(self, window: DecodedTokenWindow) -> None:
@@ -104,16 +121,29 @@ class IncrementalStitchAccumulator:
         prev = self._previous
         if prev is None:
             self._merged = list(window.tokens)
+            self._set_starts(0)
             self._previous = window
             return
         if (prev.start_sample, prev.index) > (window.start_sample, window.index):
             raise ValueError("incremental stitch windows must be appended in chronological order")
-        tokens, method = _merge_token_streams(self._merged, list(window.tokens), self._piece, self._has_pieces)
-        self._merged = tokens
+        n = len(self._merged)
+        method, keep = _merge_token_streams(self._merged, self._starts[:n], list(window.tokens), self._piece,
+                                            self._has_pieces)
+        self._set_starts(keep)
         if self._trace is not None:
             self._trace.append(StitchTrace(prev.index, window.index, method, window.start_sample,
                                            min(prev.end_sample, window.end_sample)))
         self._previous = window
+
+    def _set_starts(self, keep: int) -> None:
+        """Refreshes the start array after a merge left the first `keep`
+        merged tokens in place."""
+        n = len(self._merged)
+        if n > self._starts.shape[0]:
+            grown = np.zeros(max(n, 2 * self._starts.shape[0]), dtype=np.int64)
+            grown[:keep] = self._starts[:keep]
+            self._starts = grown
+        self._starts[keep:n] = _start_array(self._merged[keep:])
 
     def snapshot(self) -> StitchedTokens:
         tokens = enforce_monotonic_token_times(self._merged)
@@ -135,33 +165,43 @@ def enforce_monotonic_token_times(tokens: Sequence[TimedToken]) -> list[TimedTok
             last = t.start_sample
         else:
             shift = last - t.start_sample
-            out.append(replace(t, start_sample=last, end_sample=t.end_sample + shift))
+            out.append(TimedToken(t.token_id, last, t.end_sample + shift, t.duration_frames))
     return out
 
 
-def _merge_token_streams(left, right, piece, has_pieces):
+def _start_array(tokens) -> np.ndarray:
+    return np.fromiter((t.start_sample for t in tokens), dtype=np.int64, count=len(tokens))
+
+
+def _merge_token_streams(left, left_starts, right, piece, has_pieces):
+    """Merges `right` (one window's tokens) into the merged stream `left` in
+    place; `left_starts` holds left's start samples.  Returns (method, keep):
+    the first `keep` tokens of the result are left's own first `keep`."""
     if not left:
-        return list(right), "disjoint"
+        left.extend(right)
+        return "disjoint", 0
     if not right:
-        return list(left), "disjoint"
+        return "disjoint", len(left)
     left_end = left[-1].start_sample + ENCODER_FRAME_SAMPLES
     right_start = right[0].start_sample
     if left_end <= right_start:
-        return left + right, "disjoint"
-    ov_left = [(i, t) for i, t in enumerate(left)
-               if t.start_sample + ENCODER_FRAME_SAMPLES > right_start - OVERLAP_SAMPLES]
+        keep = len(left)
+        left.extend(right)
+        return "disjoint", keep
+    ov_left = [(int(i), left[i]) for i in
+               np.flatnonzero(left_starts + ENCODER_FRAME_SAMPLES > right_start - OVERLAP_SAMPLES)]
     ov_right = [(i, t) for i, t in enumerate(right) if t.start_sample < left_end + OVERLAP_SAMPLES]
     if len(ov_left) < 2 or len(ov_right) < 2:
-        return _merge_by_midpoint(left, right, left_end, right_start, piece, has_pieces), "midpoint"
+        return "midpoint", _merge_by_midpoint(left, left_starts, right, left_end, right_start, piece, has_pieces)
 
     m = _match_matrix(ov_left, ov_right, piece, has_pieces)
     run = _longest_contiguous(m)
     if len(run) >= max(len(ov_left) // 2, 1):
-        return _merge_using_matches(run, ov_left, ov_right, left, right, piece, has_pieces), "contiguous"
+        return "contiguous", _merge_using_matches(run, ov_left, ov_right, left, right, piece, has_pieces)
     lcs = _longest_common_subsequence(m)
     if not lcs:
-        return _merge_by_midpoint(left, right, left_end, right_start, piece, has_pieces), "midpoint"
-    return _merge_using_matches(lcs, ov_left, ov_right, left, right, piece, has_pieces), "lcs"
+        return "midpoint", _merge_by_midpoint(left, left_starts, right, left_end, right_start, piece, has_pieces)
+    return "lcs", _merge_using_matches(lcs, ov_left, ov_right, left, right, piece, has_pieces)
 
 
 def _match_matrix(ov_left, ov_right, piece, has_pieces) -> np.ndarray:
@@ -201,25 +241,32 @@ def _longest_contiguous(m: np.ndarray):
 
 
 def _longest_common_subsequence(m: np.ndarray):
+    """LCS of the match matrix with the reference's backtracking tie rule.
+    The DP table L is held as one bit row per left token (Hyyro's
+    bit-parallel LCS): bit j of row i is set when L(i, j+1) == L(i, j), so
+    L(i, j) = j - popcount(row_i & (2^j - 1)); a row follows from the
+    previous one in three big-integer operations."""
     n, k = m.shape
-    rows = m.tolist()
-    table = [[0] * (k + 1) for _ in range(n + 1)]
-    for lc in range(1, n + 1):
-        prev, cur, row = table[lc - 1], table[lc], rows[lc - 1]
-        for rc in range(1, k + 1):
-            if row[rc - 1]:
-                cur[rc] = prev[rc - 1] + 1
-            else:
-                a, b = prev[rc], cur[rc - 1]
-                cur[rc] = a if a > b else b
+    full = (1 << k) - 1
+    packed = np.packbits(m, axis=1, bitorder="little")
+    rows = [full]
+    v = full
+    for i in range(n):
+        u = v & int.from_bytes(packed[i].tobytes(), "little")
+        v = ((v + u) | (v - u)) & full
+        rows.append(v)
+
+    def table(i, j):
+        return j - (rows[i] & ((1 << j) - 1)).bit_count()
+
     rev = []
     lc, rc = n, k
     while lc > 0 and rc > 0:
-        if rows[lc - 1][rc - 1]:
+        if m[lc - 1, rc - 1]:
             rev.append((lc - 1, rc - 1))
             lc -= 1
             rc -= 1
-        elif table[lc - 1][rc] > table[lc][rc - 1]:
+        elif table(lc - 1, rc) > table(lc, rc - 1):
             lc -= 1
         else:
             rc -= 1  # backtracking tie rule
@@ -227,10 +274,15 @@ def _longest_common_subsequence(m: np.ndarray):
     return rev
 
 
-def _merge_using_matches(pairs, ov_left, ov_right, left, right, piece, has_pieces):
-    li = [ov_left[a][0] for a, _ in pairs]
+def _merge_using_matches(pairs, ov_left, ov_right, out, right, piece, has_pieces):
+    """Splices `right` into `out` (the merged stream, edited in place) at the
+    matched pairs; returns how many leading tokens of `out` are unchanged."""
+    base = ov_left[pairs[0][0]][0]
+    left = out[base:]  # left[x] below is the stream's token base + x
+    del out[base:]
+    li = [ov_left[a][0] - base for a, _ in pairs]
     ri = [ov_right[b][0] for _, b in pairs]
-    out = list(left[:li[0]])
+    keep = base + 1  # the first matched token follows the untouched prefix, unless the seam-word pop cuts into it
     for m in range(len(pairs)):
         out.append(left[li[m]])
         if m == len(pairs) - 1:
@@ -240,22 +292,23 @@ def _merge_using_matches(pairs, ov_left, ov_right, left, right, piece, has_piece
         out.extend(rgap if len(rgap) > len(lgap) else lgap)
     last_right = ri[-1]
     if last_right + 1 >= len(right):
-        return out
+        return keep
     tail = right[last_right + 1:]
     if not has_pieces or is_splice_safe_token(tail[0].token_id, piece):
         out.extend(tail)
-        return out
+        return keep
     word_start = _word_initial_index(right, last_right, piece)
     if word_start is not None and _pop_seam_word(out, piece):
+        keep = min(keep, len(out))
         out.extend(right[word_start:])
-        return out
+        return keep
     cursor = li[-1] + 1
     while cursor < len(left) and not is_splice_safe_token(left[cursor].token_id, piece):
         out.append(left[cursor])
         cursor += 1
     resume = next((i for i, t in enumerate(tail) if is_splice_safe_token(t.token_id, piece)), -1)
     out.extend(tail[resume:] if resume >= 0 else tail)  # a glued word beats dropping the tail
-    return out
+    return keep
 
 
 def _word_initial_index(stream, ending_at, piece):
@@ -273,9 +326,12 @@ def _pop_seam_word(out, piece) -> bool:
     return False
 
 
-def _merge_by_midpoint(left, right, left_end, right_start, piece, has_pieces):
+def _merge_by_midpoint(left, left_starts, right, left_end, right_start, piece, has_pieces):
+    """Cuts `left` (edited in place) and `right` at the timestamp midpoint of
+    their overlap; returns how many leading tokens of `left` are unchanged."""
     cutoff = (left_end + right_start) / 2
-    le = next((i for i, t in enumerate(left) if t.start_sample >= cutoff), len(left))
+    at_or_after = np.flatnonzero(left_starts >= cutoff)
+    le = int(at_or_after[0]) if at_or_after.size else len(left)
     rs = next((i for i, t in enumerate(right) if t.start_sample >= cutoff), len(right))
     if has_pieces and le > 0:
         while le < len(left) and not is_splice_safe_token(left[le].token_id, piece):
@@ -286,7 +342,9 @@ def _merge_by_midpoint(left, right, left_end, right_start, piece, has_pieces):
             safe += 1
         if safe < len(right):  # keep the original cutoff when no safe right token exists
             rs = safe
-    return list(left[:le]) + list(right[rs:])
+    del left[le:]
+    left.extend(right[rs:])
+    return le
 
 
 def _is_punct_or_symbol(ch: str) -> bool:

@@ -229,3 +229,47 @@ def test_half_overlap_timestamp_tolerance(st):
         win(st, 0, 0, 240_000, [tok(st, 1, 210_000), tok(st, 2, 220_000)]),
         win(st, 1, 208_000, 448_000, [tok(st, 1, 211_400), tok(st, 2, 221_400)])])
     assert r.trace[0].method == "contiguous"
+
+
+def test_globalize_arrays_equals_per_token_globalize(st, pk):
+    import numpy as np
+
+    rng = np.random.default_rng(7)
+    plans = pk.windows.plan_stateless_windows(16_000 * 95 + 1234)
+    for plan in plans:
+        n = int(rng.integers(0, 400))
+        frames = np.sort(rng.integers(0, 188, n)).astype(np.int32)
+        ids = rng.integers(0, 1030, n).astype(np.int32)
+        durs = rng.integers(0, 5, n).astype(np.int32)
+        emitted = [st.EmittedToken(int(a), int(b), int(c)) for a, b, c in zip(ids, frames, durs)]
+        assert st.globalize_tdt_arrays(ids, frames, durs, plan) == st.globalize_tdt_tokens(emitted, plan)
+
+
+def _lcs_plain(m):
+    """Textbook LCS table over a boolean match matrix, then the merge's
+    backtracking (diagonal on a match; up only when strictly larger)."""
+    n, k = len(m), len(m[0]) if m else 0
+    table = [[0] * (k + 1) for _ in range(n + 1)]
+    for i in range(1, n + 1):
+        for j in range(1, k + 1):
+            table[i][j] = table[i - 1][j - 1] + 1 if m[i - 1][j - 1] else max(table[i - 1][j], table[i][j - 1])
+    out, i, j = [], n, k
+    while i > 0 and j > 0:
+        if m[i - 1][j - 1]:
+            out.append((i - 1, j - 1))
+            i, j = i - 1, j - 1
+        elif table[i - 1][j] > table[i][j - 1]:
+            i -= 1
+        else:
+            j -= 1
+    return out[::-1]
+
+
+def test_bit_parallel_lcs_equals_textbook_table(st):
+    import numpy as np
+
+    rng = np.random.default_rng(3)
+    for trial in range(400):
+        n, k = int(rng.integers(1, 70)), int(rng.integers(1, 70))
+        m = rng.random((n, k)) < (0.04, 0.3, 0.85)[trial % 3]
+        assert st._longest_common_subsequence(m) == _lcs_plain(m.tolist()), trial
