@@ -81,7 +81,7 @@ class ParakeetEngine:
         """windows: (samples f32 [<= 240 000], WindowPlan) per window, 1..capacity."""
         out = []
         for tok, fr, du, overflow in self._run_batch(windows, stream):
-            out.append(WindowResult(tuple(st.EmittedToken(*e) for e in zip(tok.tolist(), fr.tolist(), du.tolist())),
+            out.append(WindowResult(tuple(map(st.EmittedToken._make, zip(tok.tolist(), fr.tolist(), du.tolist()))),
                                     overflow))
         return out
 
@@ -171,10 +171,13 @@ class ShardFailure(RuntimeError):
 
 def transcribe_sharded(engine, pcm: np.ndarray, rank: int, world_size: int, gather, token_piece=None):
     """Multi-GPU long-form transcription: this rank decodes its contiguous
-    share of the window plan with its own `engine` (its own GPU);
-    `gather(obj)` brings every rank's object to rank 0 (for example
-    torch.distributed's gather_object), which merges the decoded windows.
-    Returns the merged tokens on rank 0 and None elsewhere.
+    share of the window plan with its own `engine` (its own GPU) and merges
+    its own windows (stitch.stitch_partial); `gather(obj)` brings every
+    rank's partial stream, packed as arrays, to rank 0 (for example
+    torch.distributed's gather_object), which joins them at the rank seams
+    (IncrementalStitchAccumulator.extend -- the same tokens and trace as
+    merging every window on one rank).  Returns the merged tokens on rank 0
+    and None elsewhere.
 
     Failures do not hang the other ranks: a rank whose decode raises (a
     PkError such as PK_E_TIMEOUT from a bounded device wait, a RangeError)
@@ -187,7 +190,7 @@ def transcribe_sharded(engine, pcm: np.ndarray, rank: int, world_size: int, gath
     mine = [plans[i] for i in wp.shard_windows(len(plans), world_size, rank)]
     error = None
     try:
-        payload = ("ok", engine.decode_plans(pcm, mine) if mine else [])
+        payload = ("ok", st.stitch_partial(engine.decode_plans(pcm, mine) if mine else [], token_piece))
     except Exception as exc:  # reported through the gather, re-raised below
         error = exc
         payload = ("error", f"{type(exc).__name__}: {exc}")
@@ -202,4 +205,7 @@ def transcribe_sharded(engine, pcm: np.ndarray, rank: int, world_size: int, gath
     failures = {r: part[1] for r, part in enumerate(gathered) if part[0] != "ok"}
     if failures:
         raise ShardFailure(failures) from error
-    return st.stitch_token_windows([w for part in gathered for w in part[1]], token_piece)
+    acc = st.IncrementalStitchAccumulator(token_piece=token_piece, collect_trace=True)
+    for _, part in gathered:  # rank order is window order: the shards are contiguous
+        acc.extend(part)
+    return acc.snapshot()

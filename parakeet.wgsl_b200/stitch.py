@@ -15,31 +15,46 @@ decoded on whichever GPU holds them, and only their token lists meet here.
 """
 from __future__ import annotations
 
+import gc
 import unicodedata
+from contextlib import contextmanager
 from dataclasses import dataclass
+from typing import Callable, NamedTuple, Optional, Sequence
 
 import numpy as np
-from typing import Callable, Optional, Sequence
 
 from .windows import ENCODER_FRAME_SAMPLES, OVERLAP_SAMPLES, WindowPlan
 
 TokenPieceResolver = Callable[[int], Optional[str]]
 
 
-@dataclass(frozen=True)
-class TimedToken:
+class TimedToken(NamedTuple):
+    """One token on the source timeline (an immutable record; a named tuple
+    because a long-form merge builds hundreds of thousands of them)."""
     token_id: int
     start_sample: int
     end_sample: int
     duration_frames: int  # raw TDT duration (seam-gap repair keeps it)
 
 
-@dataclass(frozen=True)
-class EmittedToken:
+class EmittedToken(NamedTuple):
     """One decoder emission in window-local encoder frames (TdtEmittedToken)."""
     token_id: int
     frame_index: int
     duration_frames: int
+
+
+@contextmanager
+def _gc_paused():
+    """Bulk record construction without the cyclic collector's passes (the
+    records hold only ints, so they cannot form cycles)."""
+    was_enabled = gc.isenabled()
+    gc.disable()
+    try:
+        yield
+    finally:
+        if was_enabled:
+            gc.enable()
 
 
 @dataclass(frozen=True)
@@ -89,7 +104,9 @@ def globalize_tdt_arrays(token_ids, frames, durations, window: WindowPlan) -> li
     end = np.minimum(start + durations * ENCODER_FRAME_SAMPLES, window.emission_end_sample)
     keep = (start >= window.emission_start_sample) & (start < window.emission_end_sample)
     ids = np.asarray(token_ids, dtype=np.int64)[keep].tolist()
-    return [TimedToken(*f) for f in zip(ids, start[keep].tolist(), end[keep].tolist(), durations[keep].tolist())]
+    with _gc_paused():
+        return list(map(TimedToken._make, zip(ids, start[keep].tolist(), end[keep].tolist(),
+                                              durations[keep].tolist())))
 
 
 def stitch_token_windows(windows: Sequence[DecodedTokenWindow],
@@ -118,22 +135,54 @@ class IncrementalStitchAccumulator:
 
     def append(self, window: DecodedTokenWindow) -> None:
         _validate_window(window)
+        self._merge_in(window, list(window.tokens))
+
+    def _merge_in(self, window: DecodedTokenWindow, right: list) -> int:
+        """Merges `right` -- `window`'s tokens, or a partial stream that
+        starts with `window` -- after the previous window; returns the merge's
+        keep count (-1 for the first window)."""
         prev = self._previous
         if prev is None:
-            self._merged = list(window.tokens)
+            self._merged = right
             self._set_starts(0)
             self._previous = window
-            return
+            return -1
         if (prev.start_sample, prev.index) > (window.start_sample, window.index):
             raise ValueError("incremental stitch windows must be appended in chronological order")
         n = len(self._merged)
-        method, keep = _merge_token_streams(self._merged, self._starts[:n], list(window.tokens), self._piece,
-                                            self._has_pieces)
+        method, keep = _merge_token_streams(self._merged, self._starts[:n], right, self._piece, self._has_pieces)
         self._set_starts(keep)
         if self._trace is not None:
             self._trace.append(StitchTrace(prev.index, window.index, method, window.start_sample,
                                            min(prev.end_sample, window.end_sample)))
         self._previous = window
+        return keep
+
+    def extend(self, part: "PartialStitch") -> None:
+        """Appends a run of windows that `stitch_partial` merged on its own
+        (on another rank); the result is exactly that of appending the run's
+        windows one by one.  The partial stream is spliced in at its first
+        seam when that seam and the run's own merges cannot see each other's
+        tokens (checked here and in stitch_partial); otherwise the run's
+        windows are appended one by one."""
+        if not part.window_meta.shape[0]:
+            return
+        windows = None
+        if part.local_ok and not self._has_pieces and part.window_meta.shape[0] > 1:
+            n = len(self._merged)
+            seam_free = self._previous is None or n == 0 or (
+                int(self._starts[:n].max()) <= part.guard
+                and self._merged[-1].start_sample + ENCODER_FRAME_SAMPLES + OVERLAP_SAMPLES <= part.guard + 1)
+            if seam_free:
+                first, last = part.window(0, with_tokens=False), part.window(-1, with_tokens=False)
+                self._merge_in(first, part.token_list())
+                if self._trace is not None:
+                    self._trace.extend(part.trace)
+                self._previous = last
+                return
+        windows = part.windows()
+        for w in windows:
+            self.append(w)
 
     def _set_starts(self, keep: int) -> None:
         """Refreshes the start array after a merge left the first `keep`
@@ -146,26 +195,110 @@ class IncrementalStitchAccumulator:
         self._starts[keep:n] = _start_array(self._merged[keep:])
 
     def snapshot(self) -> StitchedTokens:
-        tokens = enforce_monotonic_token_times(self._merged)
+        tokens = enforce_monotonic_token_times(self._merged, self._starts[:len(self._merged)])
         if len(tokens) > 1 and self._has_pieces:
             tokens = collapse_seam_word_duplicates(tokens, self._piece)
         return StitchedTokens(tuple(tokens), tuple(self._trace) if self._trace is not None else ())
 
 
-def enforce_monotonic_token_times(tokens: Sequence[TimedToken]) -> list[TimedToken]:
+@dataclass(frozen=True)
+class PartialStitch:
+    """A contiguous run of decoded windows merged on its own, packed as
+    arrays for sending between ranks (see stitch_partial).
+
+    window_meta: int64 [windows, 4] (index, start_sample, end_sample, token
+    count); window_tokens / tokens: int64 [n, 4] (token_id, start_sample,
+    end_sample, duration_frames) of the windows' own tokens and of the merged
+    run; trace: the run's internal StitchTrace entries.  `guard` and
+    `local_ok` are the splice conditions of IncrementalStitchAccumulator.extend."""
+    window_meta: np.ndarray
+    window_tokens: np.ndarray
+    tokens: np.ndarray
+    trace: tuple
+    guard: int
+    local_ok: bool
+
+    def token_list(self) -> list:
+        with _gc_paused():
+            return list(map(TimedToken._make, self.tokens.tolist()))
+
+    def window(self, i: int, with_tokens: bool = True) -> DecodedTokenWindow:
+        index, start, end, count = self.window_meta[i].tolist()
+        toks = ()
+        if with_tokens:
+            offset = int(self.window_meta[:i % self.window_meta.shape[0], 3].sum())
+            toks = tuple(map(TimedToken._make, self.window_tokens[offset:offset + count].tolist()))
+        return DecodedTokenWindow(index, start, end, toks)
+
+    def windows(self) -> list:
+        out, offset = [], 0
+        with _gc_paused():
+            for index, start, end, count in self.window_meta.tolist():
+                rows = self.window_tokens[offset:offset + count].tolist()
+                out.append(DecodedTokenWindow(index, start, end, tuple(map(TimedToken._make, rows))))
+                offset += count
+        return out
+
+
+def _token_rows(tokens) -> np.ndarray:
+    rows = np.array([(t.token_id, t.start_sample, t.end_sample, t.duration_frames) for t in tokens],
+                    dtype=np.int64)
+    return rows.reshape(-1, 4)
+
+
+def stitch_partial(windows: Sequence[DecodedTokenWindow],
+                   token_piece: Optional[TokenPieceResolver] = None) -> PartialStitch:
+    """Merges a contiguous, chronological run of windows on its own, for a
+    later IncrementalStitchAccumulator.extend.  Splicing the run's merged
+    stream in at its first seam gives the same tokens and trace as appending
+    its windows one by one when (checked here; `local_ok`):
+
+    * every token lies inside its window's [start_sample, end_sample);
+    * with G = (second window's start_sample) - overlap - one frame (`guard`),
+      the run's later merges never look at tokens starting at or before G,
+      so the first window's tokens up to G -- its first h tokens -- stay
+      the run's first h tokens; h >= 1 and the first window has tokens after G;
+    * every merge of the run leaves more than h tokens;
+
+    and (checked by extend) the stream it joins starts no token after G and
+    its last token's overlap reach ends by G.  Without token pieces only."""
+    windows = list(windows)
+    meta = np.array([(w.index, w.start_sample, w.end_sample, len(w.tokens)) for w in windows],
+                    dtype=np.int64).reshape(-1, 4)
+    raw = _token_rows([t for w in windows for t in w.tokens])
+    acc = IncrementalStitchAccumulator(token_piece, collect_trace=True)
+    ok = token_piece is None and len(windows) > 1
+    guard = 0
+    if ok:
+        guard = windows[1].start_sample - OVERLAP_SAMPLES - ENCODER_FRAME_SAMPLES
+        ok = all(w.start_sample <= t.start_sample < w.end_sample for w in windows for t in w.tokens)
+        head = sum(1 for t in windows[0].tokens if t.start_sample <= guard)
+        ok = ok and 1 <= head < len(windows[0].tokens)
+    for i, w in enumerate(windows):
+        acc.append(w)
+        if ok and i > 0 and len(acc._merged) <= head:
+            ok = False
+    merged = _token_rows(acc._merged)
+    trace = tuple(acc._trace)
+    return PartialStitch(meta, raw, merged, trace, int(guard), bool(ok))
+
+
+def enforce_monotonic_token_times(tokens: Sequence[TimedToken], starts: Optional[np.ndarray] = None) -> list[TimedToken]:
     """Keep the merged text order; shift any token that starts before its
-    predecessor forward by the difference (start and end together)."""
+    predecessor forward by the difference (start and end together).  Each
+    token's new start is the running maximum of the starts so far.
+    `starts`, when given, holds the tokens' start samples."""
     if not tokens:
         return []
-    out = [tokens[0]]
-    last = tokens[0].start_sample
-    for t in tokens[1:]:
-        if t.start_sample >= last:
-            out.append(t)
-            last = t.start_sample
-        else:
-            shift = last - t.start_sample
-            out.append(TimedToken(t.token_id, last, t.end_sample + shift, t.duration_frames))
+    if starts is None:
+        starts = _start_array(tokens)
+    clamped = np.maximum.accumulate(starts)
+    out = list(tokens)
+    with _gc_paused():
+        for i in np.flatnonzero(clamped != starts).tolist():
+            t = out[i]
+            shift = int(clamped[i]) - t.start_sample
+            out[i] = TimedToken(t.token_id, t.start_sample + shift, t.end_sample + shift, t.duration_frames)
     return out
 
 
@@ -229,6 +362,22 @@ def _longest_contiguous(m: np.ndarray):
     """The longest diagonal run of matches; among equal lengths the first run
     start in row-major scan order (the reference's scan keeps the first)."""
     n, k = m.shape
+    if n * k <= 1024:  # small overlaps: plain lists beat per-row numpy calls
+        rows = m.tolist()
+        below = [0] * (k + 1)
+        best, bi, bj = 0, n, 0
+        for i in range(n - 1, -1, -1):
+            row, here = rows[i], [0] * (k + 1)
+            for j in range(k):
+                if row[j]:
+                    run = below[j + 1] + 1
+                    here[j] = run
+                    # rows are visited bottom-up, columns left to right: the
+                    # first run start in row-major order wins a tie
+                    if run > best or (run == best and i < bi):
+                        best, bi, bj = run, i, j
+            below = here
+        return [(bi + d, bj + d) for d in range(best)]
     runs = np.zeros((n + 1, k + 1), dtype=np.int32)
     for i in range(n - 1, -1, -1):
         runs[i, :k] = np.where(m[i], runs[i + 1, 1:] + 1, 0)
@@ -433,14 +582,22 @@ def _validate_window(w: DecodedTokenWindow) -> None:
             raise ValueError(f"{name} must be a non-negative safe integer")
     if w.end_sample < w.start_sample:
         raise ValueError("window endSample must not precede startSample")
-    prev = None
+    prev = -1
     for t in w.tokens:
-        for name, v in (("tokenId", t.token_id), ("token startSample", t.start_sample),
-                        ("token endSample", t.end_sample), ("token durationFrames", t.duration_frames)):
-            if not isinstance(v, int) or v < 0:
-                raise ValueError(f"{name} must be a non-negative safe integer")
-        if t.end_sample < t.start_sample:
-            raise ValueError("token endSample must not precede startSample")
-        if prev is not None and t.start_sample < prev:
-            raise ValueError("tokens must be sorted by startSample")
-        prev = t.start_sample
+        a, start, end, dur = t.token_id, t.start_sample, t.end_sample, t.duration_frames
+        # Fast path: plain ints in order; anything else takes the full check.
+        if not (type(a) is int and type(start) is int and type(end) is int and type(dur) is int
+                and a >= 0 and dur >= 0 and prev <= start <= end):
+            _check_token(t, prev)
+        prev = start
+
+
+def _check_token(t: TimedToken, prev: int) -> None:
+    for name, v in (("tokenId", t.token_id), ("token startSample", t.start_sample),
+                    ("token endSample", t.end_sample), ("token durationFrames", t.duration_frames)):
+        if not isinstance(v, int) or v < 0:
+            raise ValueError(f"{name} must be a non-negative safe integer")
+    if t.end_sample < t.start_sample:
+        raise ValueError("token endSample must not precede startSample")
+    if t.start_sample < prev:
+        raise ValueError("tokens must be sorted by startSample")

@@ -67,7 +67,10 @@ def test_two_rank_merge_equals_single_rank(pk, tmp_path):
     got = eval(out.read_text())  # noqa: S307 - written by this test
     pcm = np.zeros(16_000 * 100, np.float32)
     single = pk.engine.transcribe_sharded(FakeEngine(pk), pcm, 0, 1, lambda obj: [obj])
+    plans = pk.windows.plan_stateless_windows(len(pcm))
+    sequential = pk.stitch.stitch_token_windows(FakeEngine(pk).decode_plans(pcm, plans))
     assert got == [(t.token_id, t.start_sample) for t in single.tokens]
+    assert single.tokens == sequential.tokens and single.trace == sequential.trace
     assert len(got) > 0
 
 

@@ -273,3 +273,100 @@ def test_bit_parallel_lcs_equals_textbook_table(st):
         n, k = int(rng.integers(1, 70)), int(rng.integers(1, 70))
         m = rng.random((n, k)) < (0.04, 0.3, 0.85)[trial % 3]
         assert st._longest_common_subsequence(m) == _lcs_plain(m.tolist()), trial
+
+
+def test_small_and_large_contiguous_runs_agree(st):
+    import numpy as np
+
+    def plain(m):
+        n, k = m.shape
+        best, at = 0, None
+        for i in range(n):  # row-major: the first start of the longest run
+            for j in range(k):
+                run = 0
+                while i + run < n and j + run < k and m[i + run, j + run]:
+                    run += 1
+                if run > best:
+                    best, at = run, (i, j)
+        return [] if at is None else [(at[0] + d, at[1] + d) for d in range(best)]
+
+    rng = np.random.default_rng(11)
+    for trial in range(300):
+        n, k = int(rng.integers(1, 60)), int(rng.integers(1, 60))
+        m = rng.random((n, k)) < (0.05, 0.4, 0.9)[trial % 3]
+        assert st._longest_contiguous(m) == plain(m), trial
+
+
+def test_monotonic_clamp_equals_sequential_rule(st):
+    import random
+
+    random.seed(4)
+    for _ in range(200):
+        toks = [st.TimedToken(random.randint(0, 9), s, s + random.randint(0, 3000), 1)
+                for s in (random.randint(0, 50_000) for _ in range(random.randint(0, 60)))]
+        expect, last = [], None
+        for t in toks:
+            if last is None or t.start_sample >= last:
+                expect.append(t)
+                last = t.start_sample
+            else:
+                expect.append(st.TimedToken(t.token_id, last, t.end_sample + last - t.start_sample,
+                                            t.duration_frames))
+        assert st.enforce_monotonic_token_times(toks) == expect
+
+
+def _random_decoded_windows(st, wp, rng):
+    """Windows of a random-length plan with random tokens inside each
+    emission range: empty, sparse, speech-like and dense windows, some with a
+    silent head or tail."""
+    import numpy as np
+
+    plans = wp.plan_stateless_windows(int(rng.uniform(20, 300) * 16_000))
+    density = rng.choice([0.0, 0.05, 0.3, 1.0, 3.0])
+    out = []
+    for p in plans:
+        lo, hi = p.emission_start_sample, p.emission_end_sample
+        n = int(rng.poisson(density * (hi - lo) / 1280))
+        if rng.random() < 0.2:
+            cut = int(rng.integers(lo, hi))
+            starts = np.sort(rng.integers(lo, cut, n) if rng.random() < 0.5 else rng.integers(cut, hi, n))
+        else:
+            starts = np.sort(rng.integers(lo, hi, n))
+        ids = rng.integers(0, int(rng.choice([3, 30, 1024])), n)
+        toks = tuple(st.TimedToken(int(a), int(s), int(min(s + 1280 * int(rng.integers(0, 5)), hi)), 1)
+                     for a, s in zip(ids, starts))
+        out.append(st.DecodedTokenWindow(p.index, lo, hi, toks))
+    return out
+
+
+def test_partial_streams_joined_at_rank_seams_equal_one_fold(st, pk):
+    """stitch_partial per contiguous shard + IncrementalStitchAccumulator.extend
+    (the multi-rank merge) gives exactly the one-rank merge: tokens and trace."""
+    import numpy as np
+
+    wp = pk.windows
+    spliced = 0
+    for trial in range(120):
+        wins = _random_decoded_windows(st, wp, np.random.default_rng(trial))
+        ref = st.stitch_token_windows(wins)
+        for world in (2, 3, 8):
+            acc = st.IncrementalStitchAccumulator(collect_trace=True)
+            for r in range(world):
+                part = st.stitch_partial([wins[i] for i in wp.shard_windows(len(wins), world, r)])
+                spliced += part.local_ok
+                acc.extend(part)
+            got = acc.snapshot()
+            assert got.tokens == ref.tokens and got.trace == ref.trace, (trial, world)
+    assert spliced > 100  # the splice path itself is exercised, not only the window-by-window fallback
+
+
+def test_partial_stitch_round_trips_windows(st, pk):
+    import numpy as np
+
+    wins = _random_decoded_windows(st, pk.windows, np.random.default_rng(5))
+    part = st.stitch_partial(wins)
+    assert part.windows() == wins
+    assert part.window(-1, with_tokens=True) == wins[-1]
+    acc = st.IncrementalStitchAccumulator(collect_trace=True)
+    acc.extend(part)
+    assert acc.snapshot() == st.stitch_token_windows(wins)
