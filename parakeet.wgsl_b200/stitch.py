@@ -160,29 +160,31 @@ class IncrementalStitchAccumulator:
 
     def extend(self, part: "PartialStitch") -> None:
         """Appends a run of windows that `stitch_partial` merged on its own
-        (on another rank); the result is exactly that of appending the run's
-        windows one by one.  The partial stream is spliced in at its first
-        seam when that seam and the run's own merges cannot see each other's
-        tokens (checked here and in stitch_partial); otherwise the run's
-        windows are appended one by one."""
-        if not part.window_meta.shape[0]:
+        (on another rank, with the same token_piece); the result is exactly
+        that of appending the run's windows one by one.  The partial stream is
+        spliced in at its first seam when that seam and the run's own merges
+        cannot see each other's tokens (checked here and in stitch_partial);
+        otherwise the run's windows are appended one by one."""
+        count = part.window_meta.shape[0]
+        if not count:
             return
-        windows = None
-        if part.local_ok and not self._has_pieces and part.window_meta.shape[0] > 1:
-            n = len(self._merged)
-            seam_free = self._previous is None or n == 0 or (
-                int(self._starts[:n].max()) <= part.guard
-                and self._merged[-1].start_sample + ENCODER_FRAME_SAMPLES + OVERLAP_SAMPLES <= part.guard + 1)
-            if seam_free:
-                first, last = part.window(0, with_tokens=False), part.window(-1, with_tokens=False)
-                self._merge_in(first, part.token_list())
-                if self._trace is not None:
-                    self._trace.extend(part.trace)
-                self._previous = last
-                return
-        windows = part.windows()
-        for w in windows:
-            self.append(w)
+        n = len(self._merged)
+        # Splicing is exact outright into an empty stream (the run's own fold,
+        # or a disjoint join) and for a one-window run (an append); otherwise
+        # it needs the locality conditions.
+        splice = self._previous is None or n == 0 or count == 1 or (
+            part.local_ok and not self._has_pieces
+            and int(self._starts[:n].max()) <= part.guard
+            and self._merged[-1].start_sample + ENCODER_FRAME_SAMPLES + OVERLAP_SAMPLES <= part.guard + 1)
+        if not splice:
+            for w in part.windows():
+                self.append(w)
+            return
+        first, last = part.window(0, with_tokens=False), part.window(-1, with_tokens=False)
+        self._merge_in(first, part.token_list())
+        if self._trace is not None:
+            self._trace.extend(part.trace)
+        self._previous = last
 
     def _set_starts(self, keep: int) -> None:
         """Refreshes the start array after a merge left the first `keep`

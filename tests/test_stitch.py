@@ -360,6 +360,23 @@ def test_partial_streams_joined_at_rank_seams_equal_one_fold(st, pk):
     assert spliced > 100  # the splice path itself is exercised, not only the window-by-window fallback
 
 
+def test_partial_streams_with_token_pieces_equal_one_fold(st, pk):
+    import numpy as np
+
+    vocab = ["\u2581a", "\u2581A", "b", "\u2581c", ",", "\u2581C", "d", "\u2581e", "f"]
+    piece = lambda tid: vocab[tid % len(vocab)]  # noqa: E731
+    for trial in range(40):
+        wins = _random_decoded_windows(st, pk.windows, np.random.default_rng(1000 + trial))
+        ref = st.stitch_token_windows(wins, piece)
+        for world in (2, 5):
+            acc = st.IncrementalStitchAccumulator(token_piece=piece, collect_trace=True)
+            for r in range(world):
+                acc.extend(st.stitch_partial([wins[i] for i in pk.windows.shard_windows(len(wins), world, r)],
+                                             piece))
+            got = acc.snapshot()
+            assert got.tokens == ref.tokens and got.trace == ref.trace, (trial, world)
+
+
 def test_partial_stitch_round_trips_windows(st, pk):
     import numpy as np
 
