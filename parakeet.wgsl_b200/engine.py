@@ -177,7 +177,8 @@ def transcribe_sharded(engine, pcm: np.ndarray, rank: int, world_size: int, gath
     torch.distributed's gather_object), which joins them at the rank seams
     (IncrementalStitchAccumulator.extend -- the same tokens and trace as
     merging every window on one rank).  Returns the merged tokens on rank 0
-    and None elsewhere.
+    and None elsewhere.  With world_size 1 it is ``engine.transcribe`` (no
+    gather; errors propagate as they are).
 
     Failures do not hang the other ranks: a rank whose decode raises (a
     PkError such as PK_E_TIMEOUT from a bounded device wait, a RangeError)
@@ -187,6 +188,8 @@ def transcribe_sharded(engine, pcm: np.ndarray, rank: int, world_size: int, gath
     raises ShardFailure on the ranks that see it."""
     pcm = np.ascontiguousarray(pcm, dtype=np.float32)
     plans = wp.plan_stateless_windows(int(pcm.shape[0]))
+    if world_size == 1:
+        return st.stitch_token_windows(engine.decode_plans(pcm, plans), token_piece)
     mine = [plans[i] for i in wp.shard_windows(len(plans), world_size, rank)]
     error = None
     try:

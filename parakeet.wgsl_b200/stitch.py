@@ -243,9 +243,8 @@ class PartialStitch:
 
 
 def _token_rows(tokens) -> np.ndarray:
-    rows = np.array([(t.token_id, t.start_sample, t.end_sample, t.duration_frames) for t in tokens],
-                    dtype=np.int64)
-    return rows.reshape(-1, 4)
+    """int64 [n, 4] rows of TimedTokens (named tuples, so numpy reads them as rows)."""
+    return np.array(tokens, dtype=np.int64).reshape(-1, 4)
 
 
 def stitch_partial(windows: Sequence[DecodedTokenWindow],
@@ -273,7 +272,8 @@ def stitch_partial(windows: Sequence[DecodedTokenWindow],
     guard = 0
     if ok:
         guard = windows[1].start_sample - OVERLAP_SAMPLES - ENCODER_FRAME_SAMPLES
-        ok = all(w.start_sample <= t.start_sample < w.end_sample for w in windows for t in w.tokens)
+        lo, hi = (np.repeat(meta[:, c], meta[:, 3]) for c in (1, 2))
+        ok = bool(np.all((lo <= raw[:, 1]) & (raw[:, 1] < hi)))
         head = sum(1 for t in windows[0].tokens if t.start_sample <= guard)
         ok = ok and 1 <= head < len(windows[0].tokens)
     for i, w in enumerate(windows):
