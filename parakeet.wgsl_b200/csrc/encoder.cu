@@ -80,7 +80,14 @@ struct pk_encoder {
   float* features = nullptr;
   uint32_t* feature_lengths = nullptr;
   uint32_t* encoder_lengths = nullptr;
-  uint32_t* host_lengths = nullptr;  // pinned [2 * capacity]
+  // Pinned staging of the per-batch lengths: a ring of kLengthSlots buffers of
+  // [2 * capacity], each reused only after the event recorded behind its
+  // uploads has completed, so a caller may queue the next batch before the
+  // previous one has started on the GPU.
+  static constexpr int kLengthSlots = 4;
+  uint32_t* host_lengths = nullptr;  // pinned [kLengthSlots][2 * capacity]
+  cudaEvent_t length_uploaded[kLengthSlots] = {};
+  int length_slot = 0;
   void* slots[2] = {nullptr, nullptr};
   void* big = nullptr;       // [cap*188, 4096]
   void* projected = nullptr; // [cap*188, 640]
@@ -272,6 +279,8 @@ void free_encoder(pk_encoder* e) {
   for (void* b : e->checkpoints)
     if (b) cudaFree(b);
   if (e->host_lengths) cudaFreeHost(e->host_lengths);
+  for (cudaEvent_t ev : e->length_uploaded)
+    if (ev) cudaEventDestroy(ev);
   if (e->capture_stream) cudaStreamDestroy(e->capture_stream);
 }
 
@@ -422,7 +431,9 @@ int pk_encoder_create(pk_device* device, pk_weights* weights, int precision, int
       return cuda_error(err, "cudaMalloc(encoder arena)");
     }
   }
-  cudaError_t err = cudaMallocHost(&e->host_lengths, 2 * cap * sizeof(uint32_t));
+  cudaError_t err = cudaMallocHost(&e->host_lengths, pk_encoder::kLengthSlots * 2 * cap * sizeof(uint32_t));
+  for (int i = 0; i < pk_encoder::kLengthSlots && err == cudaSuccess; ++i)
+    err = cudaEventCreateWithFlags(&e->length_uploaded[i], cudaEventDisableTiming);
   if (err == cudaSuccess) err = cudaStreamCreateWithFlags(&e->capture_stream, cudaStreamNonBlocking);
   if (err != cudaSuccess) {
     free_encoder(e.get());
@@ -486,18 +497,22 @@ int pk_encoder_forward(pk_encoder* e, const float* features, int features_on_dev
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // Lengths: raw feature frames and the derived three-times stride-2 encoder
   // lengths (deriveEncoderValidLengths, encoder.ts:441-479).
+  const int slot = e->length_slot;
+  e->length_slot = (slot + 1) % pk_encoder::kLengthSlots;
+  PK_TRY(cuda_error(cudaEventSynchronize(e->length_uploaded[slot]), "length staging slot"));
+  uint32_t* staged = e->host_lengths + (size_t)slot * 2 * e->capacity;
   for (int i = 0; i < batch; ++i) {
-    e->host_lengths[i] = feature_lengths[i];
-    e->host_lengths[e->capacity + i] = (uint32_t)sub_len((int)feature_lengths[i], 3);
+    staged[i] = feature_lengths[i];
+    staged[e->capacity + i] = (uint32_t)sub_len((int)feature_lengths[i], 3);
   }
   if (encoded_lengths)
-    for (int i = 0; i < batch; ++i) encoded_lengths[i] = e->host_lengths[e->capacity + i];
-  PK_TRY(cuda_error(cudaMemcpyAsync(e->feature_lengths, e->host_lengths, batch * sizeof(uint32_t),
-                                    cudaMemcpyHostToDevice, s),
+    for (int i = 0; i < batch; ++i) encoded_lengths[i] = staged[e->capacity + i];
+  PK_TRY(cuda_error(cudaMemcpyAsync(e->feature_lengths, staged, batch * sizeof(uint32_t), cudaMemcpyHostToDevice, s),
                     "upload feature lengths"));
-  PK_TRY(cuda_error(cudaMemcpyAsync(e->encoder_lengths, e->host_lengths + e->capacity, batch * sizeof(uint32_t),
+  PK_TRY(cuda_error(cudaMemcpyAsync(e->encoder_lengths, staged + e->capacity, batch * sizeof(uint32_t),
                                     cudaMemcpyHostToDevice, s),
                     "upload encoder lengths"));
+  PK_TRY(cuda_error(cudaEventRecord(e->length_uploaded[slot], s), "record length upload"));
   const size_t feat_bytes = (size_t)batch * kFeatureBins * kFeatureFrames * sizeof(float);
   PK_TRY(cuda_error(cudaMemcpyAsync(e->features, features, feat_bytes,
                                     features_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s),

@@ -60,15 +60,20 @@ class ParakeetEngine:
         self.fbank = ParakeetFbank(device)
         i32 = dict(dtype=torch.int32, device=cuda)
         self._pcm = torch.zeros((capacity, WINDOW_SAMPLES), dtype=torch.float32, device=cuda)
-        self._pcm_host = torch.zeros((capacity, WINDOW_SAMPLES), dtype=torch.float32).pin_memory()
-        # Rows: valid samples, encoder lengths, decode starts, decode ends, flush flags.
-        self._control_host = torch.zeros((5, capacity), dtype=torch.int32).pin_memory()
         self._control = torch.zeros((5, capacity), **i32)
         self._features = torch.zeros((capacity, 128, 1501), dtype=torch.float32, device=cuda)
         self._tokens = torch.zeros((3, capacity, max_tokens), **i32)
         self._meta = torch.zeros(2 * capacity, **i32)
-        self._tokens_host = torch.zeros((3, capacity, max_tokens), dtype=torch.int32).pin_memory()
-        self._meta_host = torch.zeros(2 * capacity, dtype=torch.int32).pin_memory()
+        # Two pinned host slots: while the GPU runs one batch, the host stages
+        # the next batch's PCM in the other (decode_plans pipelines batches).
+        # Control rows: valid samples, encoder lengths, decode starts, decode
+        # ends, flush flags.
+        self._slots = [dict(
+            pcm=torch.zeros((capacity, WINDOW_SAMPLES), dtype=torch.float32).pin_memory(),
+            control=torch.zeros((5, capacity), dtype=torch.int32).pin_memory(),
+            tokens=torch.zeros((3, capacity, max_tokens), dtype=torch.int32).pin_memory(),
+            meta=torch.zeros(2 * capacity, dtype=torch.int32).pin_memory(),
+            done=torch.cuda.Event()) for _ in range(2)]
         self._dispatch = self.decoder.create_dispatch(dict(
             encoder_projected=self.graph.decoder_input(), encoded_lengths=self._control[1],
             decode_starts=self._control[2], decode_ends=self._control[3], flush_finals=self._control[4],
@@ -88,20 +93,27 @@ class ParakeetEngine:
     def _run_batch(self, windows: Sequence[tuple], stream=None) -> list:
         """One batch through log-mel, encoder and decoder; per window its
         (token ids, frames, durations) arrays and overflow flag."""
+        return self._collect(self._submit(windows, stream, 0))
+
+    def _submit(self, windows: Sequence[tuple], stream, slot: int):
+        """Stages a batch in host slot `slot` and queues its copies and
+        kernels on `stream` without waiting for them."""
         b = len(windows)
         if not 0 < b <= self.capacity:
             raise RangeError(f"Engine batch must contain 1-{self.capacity} windows")
         stream = torch.cuda.current_stream() if stream is None else stream
-        pcm = self._pcm_host[:b]
-        pcm.zero_()
-        ctrl = self._control_host
+        host = self._slots[slot]
+        pcm, ctrl = host["pcm"], host["control"]
         lengths = []
         for i, (samples, plan) in enumerate(windows):
             samples = np.asarray(samples, dtype=np.float32)
             if samples.ndim != 1 or samples.shape[0] > WINDOW_SAMPLES or plan.valid_sample_count > samples.shape[0]:
                 raise RangeError(f"Window {i} must hold its {plan.valid_sample_count} valid samples in at most "
                                  f"{WINDOW_SAMPLES}")
-            pcm[i, : samples.shape[0]] = torch.from_numpy(samples)
+            n = samples.shape[0]
+            pcm[i, :n] = torch.from_numpy(samples)
+            if n < WINDOW_SAMPLES:
+                pcm[i, n:].zero_()
             feature_frames = max(1, plan.valid_sample_count // wp.HOP_SAMPLES)
             enc_len = derive_encoder_valid_length(feature_frames)
             if plan.decode_start_frame > enc_len:
@@ -113,21 +125,29 @@ class ParakeetEngine:
             ctrl[3, i] = plan.decode_end_frame
             ctrl[4, i] = int(plan.flush_final)
         with torch.cuda.stream(stream):
-            self._pcm[:b].copy_(pcm, non_blocking=True)
+            self._pcm[:b].copy_(pcm[:b], non_blocking=True)
             self._control.copy_(ctrl, non_blocking=True)
             self.fbank.compute_batch(self._pcm[:b], self._control[0, :b], out=self._features[:b], stream=stream)
             projected, _ = self.graph.encode(self._features[:b], lengths, stream=stream)
             self._dispatch.encode(stream, active_batch_size=b)
-            self._tokens_host[:, :b].copy_(self._tokens[:, :b], non_blocking=True)
-            self._meta_host.copy_(self._meta, non_blocking=True)
-        stream.synchronize()
+            host["tokens"][:, :b].copy_(self._tokens[:, :b], non_blocking=True)
+            host["meta"].copy_(self._meta, non_blocking=True)
+            host["done"].record(stream)
         if self.keep_intermediates:
+            stream.synchronize()
             self.last = {"features": self._features[:b].cpu().numpy(),
                          "projected": projected.view(b, 188, 640).cpu().numpy(),
                          "encoded_lengths": ctrl[1, :b].numpy().copy()}
-        tok, fr, du = (self._tokens_host[k, :b].numpy() for k in range(3))
-        counts = self._meta_host[:b].numpy()
-        flags = self._meta_host[self.capacity:self.capacity + b].numpy()
+        return slot, b
+
+    def _collect(self, ticket) -> list:
+        """Waits for a submitted batch and reads its tokens from its slot."""
+        slot, b = ticket
+        host = self._slots[slot]
+        host["done"].synchronize()
+        tok, fr, du = (host["tokens"][k, :b].numpy() for k in range(3))
+        counts = host["meta"][:b].numpy()
+        flags = host["meta"][self.capacity:self.capacity + b].numpy()
         out = []
         for i in range(b):
             n = min(int(counts[i]), self.max_tokens)
@@ -135,15 +155,28 @@ class ParakeetEngine:
         return out
 
     def decode_plans(self, pcm: np.ndarray, plans: Sequence[wp.WindowPlan], stream=None) -> list:
-        """Runs `plans` in capacity-sized batches; returns a DecodedTokenWindow per plan."""
+        """Runs `plans` in capacity-sized batches; returns a DecodedTokenWindow
+        per plan.  Batches are pipelined: batch i+1 is staged on the host and
+        queued while the GPU runs batch i, and batch i's tokens are read and
+        globalized while batch i+1 runs."""
         decoded = []
-        for start in range(0, len(plans), self.capacity):
-            chunk = plans[start:start + self.capacity]
-            batch = [(pcm[p.source_start_sample:p.source_end_sample], p) for p in chunk]
-            for plan, (tok, fr, du, _) in zip(chunk, self._run_batch(batch, stream)):
+
+        def finish(chunk, ticket):
+            for plan, (tok, fr, du, _) in zip(chunk, self._collect(ticket)):
                 toks = st.globalize_tdt_arrays(tok, fr, du, plan)
                 decoded.append(st.DecodedTokenWindow(plan.index, plan.emission_start_sample,
                                                      plan.emission_end_sample, tuple(toks)))
+
+        pending = None
+        for k, start in enumerate(range(0, len(plans), self.capacity)):
+            chunk = plans[start:start + self.capacity]
+            batch = [(pcm[p.source_start_sample:p.source_end_sample], p) for p in chunk]
+            ticket = self._submit(batch, stream, k % 2)
+            if pending is not None:
+                finish(*pending)
+            pending = (chunk, ticket)
+        if pending is not None:
+            finish(*pending)
         return decoded
 
     def transcribe(self, pcm: np.ndarray, token_piece=None, stream=None) -> st.StitchedTokens:

@@ -65,3 +65,29 @@ def test_engine_matches_oracle_stage_by_stage(pk, oracle, device, precision):
         assert device.status() == 0
     finally:
         eng.destroy()
+
+
+def test_pipelined_batches_equal_one_batch_at_a_time(pk, device):
+    """decode_plans queues batch i+1 before reading batch i (two host slots);
+    every window's tokens equal a synchronous transcribe_windows of its
+    batch, and the encoder's length staging is not overwritten in flight."""
+    package = pk.synthetic.make_package("fp16", seed=0, bits_policy="all5")
+    package.update(pk.synthetic.make_decoder("fp16", seed=0))
+    eng = pk.engine.ParakeetEngine(device, package, "fp16", capacity=3)
+    try:
+        pcm = pk.synthetic.make_pcm(100.0, seed=9)
+        plans = pk.windows.plan_stateless_windows(len(pcm))
+        assert len(plans) >= 7  # at least three batches of up to 3
+        piped = eng.decode_plans(pcm, plans)
+        one_by_one = []
+        for start in range(0, len(plans), 3):
+            chunk = plans[start:start + 3]
+            res = eng.transcribe_windows([(pcm[p.source_start_sample:p.source_end_sample], p) for p in chunk])
+            for p, r in zip(chunk, res):
+                one_by_one.append(pk.stitch.DecodedTokenWindow(
+                    p.index, p.emission_start_sample, p.emission_end_sample,
+                    tuple(pk.stitch.globalize_tdt_tokens(r.tokens, p))))
+        assert piped == one_by_one
+        assert device.status() == 0
+    finally:
+        eng.destroy()
