@@ -154,18 +154,22 @@ class ParakeetEngine:
             out.append((tok[i, :n].copy(), fr[i, :n].copy(), du[i, :n].copy(), bool(flags[i] & 1)))
         return out
 
-    def decode_plans(self, pcm: np.ndarray, plans: Sequence[wp.WindowPlan], stream=None) -> list:
+    def decode_plans(self, pcm: np.ndarray, plans: Sequence[wp.WindowPlan], stream=None, on_window=None) -> list:
         """Runs `plans` in capacity-sized batches; returns a DecodedTokenWindow
         per plan.  Batches are pipelined: batch i+1 is staged on the host and
-        queued while the GPU runs batch i, and batch i's tokens are read and
-        globalized while batch i+1 runs."""
+        queued while the GPU runs batch i, and batch i's tokens are read,
+        globalized and handed to `on_window` (in plan order; a merge, for
+        instance) while batch i+1 runs."""
         decoded = []
 
         def finish(chunk, ticket):
             for plan, (tok, fr, du, _) in zip(chunk, self._collect(ticket)):
                 toks = st.globalize_tdt_arrays(tok, fr, du, plan)
-                decoded.append(st.DecodedTokenWindow(plan.index, plan.emission_start_sample,
-                                                     plan.emission_end_sample, tuple(toks)))
+                window = st.DecodedTokenWindow(plan.index, plan.emission_start_sample, plan.emission_end_sample,
+                                               tuple(toks))
+                decoded.append(window)
+                if on_window is not None:
+                    on_window(window)
 
         pending = None
         for k, start in enumerate(range(0, len(plans), self.capacity)):
@@ -183,11 +187,25 @@ class ParakeetEngine:
         """Long-form transcription of 16 kHz mono f32 PCM on this GPU."""
         pcm = np.ascontiguousarray(pcm, dtype=np.float32)
         plans = wp.plan_stateless_windows(int(pcm.shape[0]))
-        return st.stitch_token_windows(self.decode_plans(pcm, plans, stream), token_piece)
+        acc = st.IncrementalStitchAccumulator(token_piece=token_piece, collect_trace=True)
+        _decode_into(self, pcm, plans, acc.append, stream)
+        return acc.snapshot()
 
     def destroy(self) -> None:
         self.graph.destroy()
         self.weights.release()
+
+
+def _decode_into(engine, pcm, plans, sink, stream=None) -> None:
+    """Decodes `plans` and feeds each DecodedTokenWindow to `sink` in the
+    merge's (emission start, index) order -- as each batch finishes, while
+    the GPU runs the next one, when the plan is already in that order."""
+    keys = [(p.emission_start_sample, p.index) for p in plans]
+    if all(a <= b for a, b in zip(keys, keys[1:])):
+        engine.decode_plans(pcm, plans, stream, on_window=sink)
+        return
+    for w in sorted(engine.decode_plans(pcm, plans, stream), key=lambda w: (w.start_sample, w.index)):
+        sink(w)
 
 
 class ShardFailure(RuntimeError):
@@ -222,11 +240,16 @@ def transcribe_sharded(engine, pcm: np.ndarray, rank: int, world_size: int, gath
     pcm = np.ascontiguousarray(pcm, dtype=np.float32)
     plans = wp.plan_stateless_windows(int(pcm.shape[0]))
     if world_size == 1:
-        return st.stitch_token_windows(engine.decode_plans(pcm, plans), token_piece)
+        acc = st.IncrementalStitchAccumulator(token_piece=token_piece, collect_trace=True)
+        _decode_into(engine, pcm, plans, acc.append)
+        return acc.snapshot()
     mine = [plans[i] for i in wp.shard_windows(len(plans), world_size, rank)]
     error = None
     try:
-        payload = ("ok", st.stitch_partial(engine.decode_plans(pcm, mine) if mine else [], token_piece))
+        builder = st.PartialStitchBuilder(token_piece)
+        if mine:
+            _decode_into(engine, pcm, mine, builder.append)
+        payload = ("ok", builder.finish())
     except Exception as exc:  # reported through the gather, re-raised below
         error = exc
         payload = ("error", f"{type(exc).__name__}: {exc}")

@@ -247,6 +247,41 @@ def _token_rows(tokens) -> np.ndarray:
     return np.array(tokens, dtype=np.int64).reshape(-1, 4)
 
 
+class PartialStitchBuilder:
+    """Incremental form of stitch_partial: windows are appended in order (as
+    their batches finish decoding) and `finish` packs the run."""
+
+    def __init__(self, token_piece: Optional[TokenPieceResolver] = None):
+        self._acc = IncrementalStitchAccumulator(token_piece, collect_trace=True)
+        self._windows: list = []
+        self._ok = token_piece is None
+        self._guard = 0
+        self._head = 0
+
+    def append(self, window: DecodedTokenWindow) -> None:
+        self._acc.append(window)
+        self._windows.append(window)
+        if len(self._windows) == 2 and self._ok:
+            self._guard = window.start_sample - OVERLAP_SAMPLES - ENCODER_FRAME_SAMPLES
+            first = self._windows[0].tokens
+            self._head = sum(1 for t in first if t.start_sample <= self._guard)
+            self._ok = 1 <= self._head < len(first)
+        if len(self._windows) > 1 and self._ok and len(self._acc._merged) <= self._head:
+            self._ok = False
+
+    def finish(self) -> PartialStitch:
+        windows = self._windows
+        meta = np.array([(w.index, w.start_sample, w.end_sample, len(w.tokens)) for w in windows],
+                        dtype=np.int64).reshape(-1, 4)
+        raw = _token_rows([t for w in windows for t in w.tokens])
+        ok = self._ok and len(windows) > 1
+        if ok:
+            lo, hi = (np.repeat(meta[:, c], meta[:, 3]) for c in (1, 2))
+            ok = bool(np.all((lo <= raw[:, 1]) & (raw[:, 1] < hi)))
+        return PartialStitch(meta, raw, _token_rows(self._acc._merged), tuple(self._acc._trace),
+                             int(self._guard), bool(ok))
+
+
 def stitch_partial(windows: Sequence[DecodedTokenWindow],
                    token_piece: Optional[TokenPieceResolver] = None) -> PartialStitch:
     """Merges a contiguous, chronological run of windows on its own, for a
@@ -263,26 +298,10 @@ def stitch_partial(windows: Sequence[DecodedTokenWindow],
 
     and (checked by extend) the stream it joins starts no token after G and
     its last token's overlap reach ends by G.  Without token pieces only."""
-    windows = list(windows)
-    meta = np.array([(w.index, w.start_sample, w.end_sample, len(w.tokens)) for w in windows],
-                    dtype=np.int64).reshape(-1, 4)
-    raw = _token_rows([t for w in windows for t in w.tokens])
-    acc = IncrementalStitchAccumulator(token_piece, collect_trace=True)
-    ok = token_piece is None and len(windows) > 1
-    guard = 0
-    if ok:
-        guard = windows[1].start_sample - OVERLAP_SAMPLES - ENCODER_FRAME_SAMPLES
-        lo, hi = (np.repeat(meta[:, c], meta[:, 3]) for c in (1, 2))
-        ok = bool(np.all((lo <= raw[:, 1]) & (raw[:, 1] < hi)))
-        head = sum(1 for t in windows[0].tokens if t.start_sample <= guard)
-        ok = ok and 1 <= head < len(windows[0].tokens)
-    for i, w in enumerate(windows):
-        acc.append(w)
-        if ok and i > 0 and len(acc._merged) <= head:
-            ok = False
-    merged = _token_rows(acc._merged)
-    trace = tuple(acc._trace)
-    return PartialStitch(meta, raw, merged, trace, int(guard), bool(ok))
+    builder = PartialStitchBuilder(token_piece)
+    for w in windows:
+        builder.append(w)
+    return builder.finish()
 
 
 def enforce_monotonic_token_times(tokens: Sequence[TimedToken], starts: Optional[np.ndarray] = None) -> list[TimedToken]:

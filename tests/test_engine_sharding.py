@@ -19,13 +19,15 @@ class FakeEngine:
     def __init__(self, pk):
         self.pk = pk
 
-    def decode_plans(self, pcm, plans, stream=None):
+    def decode_plans(self, pcm, plans, stream=None, on_window=None):
         st = self.pk.stitch
         out = []
         for p in plans:
             toks = [st.EmittedToken(100 + p.index, 5, 1), st.EmittedToken(7, 150, 2), st.EmittedToken(8, 170, 1)]
             g = st.globalize_tdt_tokens(toks, p)
             out.append(st.DecodedTokenWindow(p.index, p.emission_start_sample, p.emission_end_sample, tuple(g)))
+            if on_window is not None:
+                on_window(out[-1])
         return out
 
 
@@ -77,7 +79,7 @@ def test_two_rank_merge_equals_single_rank(pk, tmp_path):
 class FailingEngine(FakeEngine):
     """decode_plans that fails the way a bounded device wait reports it."""
 
-    def decode_plans(self, pcm, plans, stream=None):
+    def decode_plans(self, pcm, plans, stream=None, on_window=None):
         raise self.pk.PkError(-7, "injected: a bounded device wait expired (status bits 0x1)")
 
 
