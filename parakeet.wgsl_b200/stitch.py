@@ -18,6 +18,7 @@ from __future__ import annotations
 import gc
 import unicodedata
 from contextlib import contextmanager
+from itertools import chain
 from dataclasses import dataclass
 from typing import Callable, NamedTuple, Optional, Sequence
 
@@ -242,9 +243,11 @@ class PartialStitch:
         return out
 
 
-def _token_rows(tokens) -> np.ndarray:
-    """int64 [n, 4] rows of TimedTokens (named tuples, so numpy reads them as rows)."""
-    return np.array(tokens, dtype=np.int64).reshape(-1, 4)
+def _token_rows(tokens, count: Optional[int] = None) -> np.ndarray:
+    """int64 [n, 4] rows of TimedTokens (4-field named tuples), read as one
+    flat run of ints."""
+    n = len(tokens) if count is None else count
+    return np.fromiter(chain.from_iterable(tokens), dtype=np.int64, count=4 * n).reshape(n, 4)
 
 
 class PartialStitchBuilder:
@@ -273,7 +276,7 @@ class PartialStitchBuilder:
         windows = self._windows
         meta = np.array([(w.index, w.start_sample, w.end_sample, len(w.tokens)) for w in windows],
                         dtype=np.int64).reshape(-1, 4)
-        raw = _token_rows([t for w in windows for t in w.tokens])
+        raw = _token_rows(chain.from_iterable(w.tokens for w in windows), int(meta[:, 3].sum()))
         ok = self._ok and len(windows) > 1
         if ok:
             lo, hi = (np.repeat(meta[:, c], meta[:, 3]) for c in (1, 2))
