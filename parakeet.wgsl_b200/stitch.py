@@ -307,7 +307,8 @@ def stitch_partial(windows: Sequence[DecodedTokenWindow],
     return builder.finish()
 
 
-def enforce_monotonic_token_times(tokens: Sequence[TimedToken], starts: Optional[np.ndarray] = None) -> list[TimedToken]:
+def enforce_monotonic_token_times(tokens: Sequence[TimedToken],
+                                  starts: Optional[np.ndarray] = None) -> list[TimedToken]:
     """Keep the merged text order; shift any token that starts before its
     predecessor forward by the difference (start and end together).  Each
     token's new start is the running maximum of the starts so far.
