@@ -12,6 +12,10 @@ common subsequence, or a timestamp midpoint (``merge_token_streams``,
 
 This is the host half of the multi-GPU design: windows are encoded and
 decoded on whichever GPU holds them, and only their token lists meet here.
+``PartialStitchBuilder`` and ``IncrementalStitchAccumulator.extend`` have no
+reference counterpart (the reference merges on one thread): each rank merges
+its own contiguous windows, and rank 0 splices the runs in at the rank seams,
+with the same tokens and trace as one merge of every window.
 """
 from __future__ import annotations
 
