@@ -14,9 +14,16 @@ reference's mixed policy).  One step = one encoder forward of the batch.
   host features copied in and the projected output copied out every step;
 * ``roofline``: the palette GEMMs (the dominant kernel, tcgen05 tensor
   cores) -- algorithmic FLOPs of one step's GEMM launches / their summed
-  CUDA-event time, against the measured bf16 peak;
+  CUDA-event time (each shape back to back over rotating operand sets larger
+  than twice the L2), against the measured bf16 peak;
 * ``cpu_baseline``: the CPU oracle (a port of the reference's shader math,
-  f16-accumulating GEMMs) on one window, scaled to audio-s/s.
+  f16-accumulating GEMMs) on one window, scaled to audio-s/s;
+* ``decoder`` / ``logmel`` / ``transcribe``: the TDT decoder on the step's
+  encoder output, the log-mel front end on 32 windows of PCM, and 60 s of PCM
+  through ``ParakeetEngine.transcribe`` (config 4);
+* ``longform``: config 5 -- an hour (FP16) or ten minutes (FP32) of PCM
+  through ``engine.transcribe_sharded`` on all ranks, host PCM in and merged
+  tokens out, for mixed and all-5-bit palettes (max over ranks).
 
 ``--impl reference`` times that CPU port on all host cores (rank 0 only):
 the reference's own WGSL path cannot run here (no browser / WebGPU stack).
