@@ -408,8 +408,11 @@ def _longest_contiguous(m: np.ndarray):
             below = here
         return [(bi + d, bj + d) for d in range(best)]
     runs = np.zeros((n + 1, k + 1), dtype=np.int32)
-    for i in range(n - 1, -1, -1):
-        runs[i, :k] = np.where(m[i], runs[i + 1, 1:] + 1, 0)
+    hits = m.astype(np.int32)
+    for i in range(n - 1, -1, -1):  # in place: run = (run below-right + 1) * match
+        row = runs[i, :k]
+        np.add(runs[i + 1, 1:], 1, out=row)
+        np.multiply(row, hits[i], out=row)
     best = int(runs[:n, :k].max(initial=0))
     if best == 0:
         return []
