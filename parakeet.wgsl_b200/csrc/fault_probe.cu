@@ -71,7 +71,10 @@ extern "C" int pk_debug_wait_probe(pk_device* device, int kind, uint32_t limit_m
   if (!coop) return set_error(PK_E_SHAPE, "device has no cooperative launch");
   unsigned int* sync = nullptr;  // barrier counter, abort flag
   if ((e = cudaMalloc(&sync, 2 * sizeof(unsigned int))) != cudaSuccess) return cuda_error(e, "probe counter");
-  cudaMemsetAsync(sync, 0, 2 * sizeof(unsigned int), s);
+  if ((e = cudaMemsetAsync(sync, 0, 2 * sizeof(unsigned int), s)) != cudaSuccess) {
+    cudaFree(sync);
+    return cuda_error(e, "probe counter reset");
+  }
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeCooperative;
