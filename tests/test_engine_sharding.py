@@ -154,3 +154,25 @@ def test_rank_that_exits_before_the_gather_is_detected(tmp_path):
 def test_shard_failure_message_orders_ranks_then_gather(pk):
     err = pk.engine.ShardFailure({3: "B", None: "C", 1: "A"})
     assert str(err) == "rank 1: A; rank 3: B; gather: C"
+
+
+def test_decode_into_streams_in_merge_order(pk):
+    """engine._decode_into hands windows to the merge as batches finish when
+    the plan is in (emission start, index) order, and sorts them first when
+    it is not; both give the one-shot merge."""
+    pcm = np.zeros(16_000 * 100, np.float32)
+    plans = pk.windows.plan_stateless_windows(len(pcm))
+    fake = FakeEngine(pk)
+    expect = pk.stitch.stitch_token_windows(fake.decode_plans(pcm, plans))
+    for order in (plans, list(reversed(plans))):
+        seen = []
+        acc = pk.stitch.IncrementalStitchAccumulator(collect_trace=True)
+
+        def sink(w, seen=seen, acc=acc):
+            seen.append(w.index)
+            acc.append(w)
+
+        pk.engine._decode_into(fake, pcm, order, sink)
+        assert seen == sorted(seen)
+        got = acc.snapshot()
+        assert got.tokens == expect.tokens and got.trace == expect.trace
