@@ -33,3 +33,8 @@ def test_longform_pcm_is_seeded_and_sized(pk):
     assert a.shape == (130 * 16_000,) and a.dtype == np.float32
     assert np.array_equal(a, b)
     assert not np.array_equal(a[: 60 * 16_000], a[60 * 16_000: 120 * 16_000])  # distinct blocks rotate
+
+
+def test_longform_prefix_equals_shorter_generation(pk):
+    hour = bench.longform_pcm(pk, 200.0)
+    assert np.array_equal(hour[: 70 * 16_000], bench.longform_pcm(pk, 70.0))
