@@ -132,10 +132,11 @@ class IncrementalStitchAccumulator:
         self._has_pieces = token_piece is not None
         self._trace: Optional[list] = [] if collect_trace else None
         self._merged: list = []
-        # start_sample of every merged token, in list order (the first
-        # len(self._merged) entries): the overlap scans of each merge read
-        # this array instead of the growing token list.
+        # start_sample and token_id of every merged token, in list order (the
+        # first len(self._merged) entries): the overlap scans of each merge
+        # read these arrays instead of the growing token list.
         self._starts = np.zeros(1024, dtype=np.int64)
+        self._ids = np.zeros(1024, dtype=np.int64)
         self._previous: Optional[DecodedTokenWindow] = None
 
     def append(self, window: DecodedTokenWindow) -> None:
@@ -155,7 +156,8 @@ class IncrementalStitchAccumulator:
         if (prev.start_sample, prev.index) > (window.start_sample, window.index):
             raise ValueError("incremental stitch windows must be appended in chronological order")
         n = len(self._merged)
-        method, keep = _merge_token_streams(self._merged, self._starts[:n], right, self._piece, self._has_pieces)
+        method, keep = _merge_token_streams(self._merged, self._starts[:n], self._ids[:n], right, self._piece,
+                                            self._has_pieces)
         self._set_starts(keep)
         if self._trace is not None:
             self._trace.append(StitchTrace(prev.index, window.index, method, window.start_sample,
@@ -196,10 +198,14 @@ class IncrementalStitchAccumulator:
         merged tokens in place."""
         n = len(self._merged)
         if n > self._starts.shape[0]:
-            grown = np.zeros(max(n, 2 * self._starts.shape[0]), dtype=np.int64)
-            grown[:keep] = self._starts[:keep]
-            self._starts = grown
-        self._starts[keep:n] = _start_array(self._merged[keep:])
+            size = max(n, 2 * self._starts.shape[0])
+            for name in ("_starts", "_ids"):
+                grown = np.zeros(size, dtype=np.int64)
+                grown[:keep] = getattr(self, name)[:keep]
+                setattr(self, name, grown)
+        tail = _token_rows(self._merged[keep:])
+        self._starts[keep:n] = tail[:, 1]
+        self._ids[keep:n] = tail[:, 0]
 
     def snapshot(self) -> StitchedTokens:
         tokens = enforce_monotonic_token_times(self._merged, self._starts[:len(self._merged)])
@@ -335,10 +341,11 @@ def _start_array(tokens) -> np.ndarray:
     return np.fromiter((t.start_sample for t in tokens), dtype=np.int64, count=len(tokens))
 
 
-def _merge_token_streams(left, left_starts, right, piece, has_pieces):
+def _merge_token_streams(left, left_starts, left_ids, right, piece, has_pieces):
     """Merges `right` (one window's tokens) into the merged stream `left` in
-    place; `left_starts` holds left's start samples.  Returns (method, keep):
-    the first `keep` tokens of the result are left's own first `keep`."""
+    place; `left_starts` / `left_ids` hold left's start samples and token
+    ids.  Returns (method, keep): the first `keep` tokens of the result are
+    left's own first `keep`."""
     if not left:
         left.extend(right)
         return "disjoint", 0
@@ -350,27 +357,30 @@ def _merge_token_streams(left, left_starts, right, piece, has_pieces):
         keep = len(left)
         left.extend(right)
         return "disjoint", keep
-    ov_left = [(int(i), left[i]) for i in
-               np.flatnonzero(left_starts + ENCODER_FRAME_SAMPLES > right_start - OVERLAP_SAMPLES)]
-    ov_right = [(i, t) for i, t in enumerate(right) if t.start_sample < left_end + OVERLAP_SAMPLES]
+    right_rows = _token_rows(right)
+    ov_left = np.flatnonzero(left_starts + ENCODER_FRAME_SAMPLES > right_start - OVERLAP_SAMPLES)
+    ov_right = np.flatnonzero(right_rows[:, 1] < left_end + OVERLAP_SAMPLES)
     if len(ov_left) < 2 or len(ov_right) < 2:
-        return "midpoint", _merge_by_midpoint(left, left_starts, right, left_end, right_start, piece, has_pieces)
+        return "midpoint", _merge_by_midpoint(left, left_starts, right, right_rows[:, 1], left_end, right_start,
+                                              piece, has_pieces)
 
-    m = _match_matrix(ov_left, ov_right, piece, has_pieces)
+    m = _match_matrix(left_ids[ov_left], left_starts[ov_left], right_rows[ov_right, 0], right_rows[ov_right, 1],
+                      piece, has_pieces)
+    ov_left, ov_right = ov_left.tolist(), ov_right.tolist()
     run = _longest_contiguous(m)
     if len(run) >= max(len(ov_left) // 2, 1):
         return "contiguous", _merge_using_matches(run, ov_left, ov_right, left, right, piece, has_pieces)
     lcs = _longest_common_subsequence(m)
     if not lcs:
-        return "midpoint", _merge_by_midpoint(left, left_starts, right, left_end, right_start, piece, has_pieces)
+        return "midpoint", _merge_by_midpoint(left, left_starts, right, right_rows[:, 1], left_end, right_start,
+                                              piece, has_pieces)
     return "lcs", _merge_using_matches(lcs, ov_left, ov_right, left, right, piece, has_pieces)
 
 
-def _match_matrix(ov_left, ov_right, piece, has_pieces) -> np.ndarray:
-    """m[i, j]: overlap tokens i (left) and j (right) match -- same id (or the
-    same piece ignoring case) and starts less than half the overlap apart."""
-    lid = np.array([t.token_id for _, t in ov_left], dtype=np.int64)
-    rid = np.array([t.token_id for _, t in ov_right], dtype=np.int64)
+def _match_matrix(lid, ls, rid, rs, piece, has_pieces) -> np.ndarray:
+    """m[i, j]: overlap tokens i (left: ids `lid`, starts `ls`) and j (right)
+    match -- same id (or the same piece ignoring case) and starts less than
+    half the overlap apart."""
     same = lid[:, None] == rid[None, :]
     if has_pieces:
         codes: dict = {}
@@ -379,11 +389,9 @@ def _match_matrix(ov_left, ov_right, piece, has_pieces) -> np.ndarray:
             p = piece(tid)
             return -1 if p is None else codes.setdefault(p.lower(), len(codes))
 
-        lc = np.array([code(t.token_id) for _, t in ov_left], dtype=np.int64)
-        rc = np.array([code(t.token_id) for _, t in ov_right], dtype=np.int64)
+        lc = np.array([code(t) for t in lid.tolist()], dtype=np.int64)
+        rc = np.array([code(t) for t in rid.tolist()], dtype=np.int64)
         same |= (lc[:, None] == rc[None, :]) & (lc[:, None] >= 0)
-    ls = np.array([t.start_sample for _, t in ov_left], dtype=np.int64)
-    rs = np.array([t.start_sample for _, t in ov_right], dtype=np.int64)
     return same & (np.abs(ls[:, None] - rs[None, :]) * 2 < OVERLAP_SAMPLES)
 
 
@@ -457,12 +465,13 @@ def _longest_common_subsequence(m: np.ndarray):
 
 def _merge_using_matches(pairs, ov_left, ov_right, out, right, piece, has_pieces):
     """Splices `right` into `out` (the merged stream, edited in place) at the
-    matched pairs; returns how many leading tokens of `out` are unchanged."""
-    base = ov_left[pairs[0][0]][0]
+    matched pairs (rows of ov_left / ov_right, the overlap tokens' indices);
+    returns how many leading tokens of `out` are unchanged."""
+    base = ov_left[pairs[0][0]]
     left = out[base:]  # left[x] below is the stream's token base + x
     del out[base:]
-    li = [ov_left[a][0] - base for a, _ in pairs]
-    ri = [ov_right[b][0] for _, b in pairs]
+    li = [ov_left[a] - base for a, _ in pairs]
+    ri = [ov_right[b] for _, b in pairs]
     keep = base + 1  # the first matched token follows the untouched prefix, unless the seam-word pop cuts into it
     for m in range(len(pairs)):
         out.append(left[li[m]])
@@ -507,13 +516,14 @@ def _pop_seam_word(out, piece) -> bool:
     return False
 
 
-def _merge_by_midpoint(left, left_starts, right, left_end, right_start, piece, has_pieces):
+def _merge_by_midpoint(left, left_starts, right, right_starts, left_end, right_start, piece, has_pieces):
     """Cuts `left` (edited in place) and `right` at the timestamp midpoint of
     their overlap; returns how many leading tokens of `left` are unchanged."""
     cutoff = (left_end + right_start) / 2
     at_or_after = np.flatnonzero(left_starts >= cutoff)
     le = int(at_or_after[0]) if at_or_after.size else len(left)
-    rs = next((i for i, t in enumerate(right) if t.start_sample >= cutoff), len(right))
+    at_or_after = np.flatnonzero(right_starts >= cutoff)
+    rs = int(at_or_after[0]) if at_or_after.size else len(right)
     if has_pieces and le > 0:
         while le < len(left) and not is_splice_safe_token(left[le].token_id, piece):
             le += 1
