@@ -193,7 +193,11 @@ int pk_logmel(pk_device* device, int batch, int sample_count, const float* sampl
  * pointers are device pointers; weights and the encoder input are f16
  * (PK_FP16) or f32 (PK_FP32), biases f32; weight, embedding and encoder
  * pointers 16-byte aligned.  The decoder state lives on chip, so the
- * reference's state / predictorScratch arena slices have no counterpart. */
+ * reference's state / predictorScratch arena slices have no counterpart.
+ * The resident FP16 kernel exchanges vectors through one area owned by the
+ * pk_device (its grid-barrier counter is reset by each launch): decoder calls
+ * on one pk_device must not overlap on the GPU -- issue them on one stream,
+ * or open one pk_device per stream. */
 typedef struct pk_tdt_desc {
   int precision;                      /* PK_FP16 or PK_FP32 */
   int batch;                          /* windows */
@@ -267,7 +271,10 @@ int pk_encoder_destroy(pk_encoder* encoder);
  * (tensor cores where the shape tiles, else CUDA cores), 1 = CUDA-core
  * kernel only, 2 = tensor-core kernel only (unsupported shapes fail),
  * 3 = as 2 but single-CTA tiles only, 4 = as 2 but CTA-pair tiles
- * (cta_group::2) wherever N is a multiple of 256. */
+ * (cta_group::2) wherever N is a multiple of 256, 5 = CUDA-core kernel with
+ * FP16 GEMMs accumulating in f16 in increasing K (each step an f32 fma
+ * rounded to f16): the reference's own accumulation
+ * (src/webgpu/kernels/gemm.ts:1445-1502), for parity runs only. */
 int pk_debug_set_gemm_route(int route);
 /* Test hook (no reference counterpart): forces the tensor-core GEMM token
  * tile for later launches in this process.  0 = automatic (cost model),

@@ -37,12 +37,22 @@ def build() -> Path:
     return _LIB_PATH
 
 
+def reference_root() -> Path | None:
+    """The reference checkout: $PARAKEET_REFERENCE, else a directory named
+    ``reference`` beside this repository; None when neither exists."""
+    env = os.environ.get("PARAKEET_REFERENCE")
+    for cand in ([Path(env)] if env else []) + [_HERE.parents[1] / "reference"]:
+        if (cand / "src" / "cpp" / "fbank" / "parakeet_fbank.cpp").exists():
+            return cand
+    return None
+
+
 def build_reference() -> bool:
     """Build oracle/_ref (the reference's own log-mel front end) when the
     reference checkout is present; a no-op otherwise.  Returns availability."""
-    src = Path(os.environ.get("PARAKEET_REFERENCE", "/root/reference")) / "src" / "cpp" / "fbank" / "parakeet_fbank.cpp"
-    if src.exists():
-        subprocess.run(["make", "-s", "-C", str(_HERE), "ref", f"REFERENCE={src.parents[3]}"], check=True)
+    root = reference_root()
+    if root is not None:
+        subprocess.run(["make", "-s", "-C", str(_HERE), "ref", f"REFERENCE={root}"], check=True)
     return (_HERE / "_ref" / "libparakeet_fbank.so").exists()
 
 

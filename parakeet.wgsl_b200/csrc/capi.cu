@@ -207,16 +207,17 @@ int pk_palette_gemm(pk_device* device, const pk_gemm_desc* d, pk_stream stream) 
   if (st != PK_OK) return st;
   cudaSetDevice(device->ctx.ordinal);
   const bool tc = gemm_tc_supported(g);
-  if (g_gemm_route >= 2 && !tc) return set_error(PK_E_SHAPE, "tensor-core GEMM forced but shape unsupported");
-  if (tc && g_gemm_route != 1) return launch_gemm_tc(device->ctx, g, as_stream(stream));
+  if (g_gemm_route >= 2 && g_gemm_route <= 4 && !tc) return set_error(PK_E_SHAPE, "tensor-core GEMM forced but shape unsupported");
+  if (tc && !gemm_route_simt()) return launch_gemm_tc(device->ctx, g, as_stream(stream));
   return launch_gemm_simt(device->ctx, g, as_stream(stream));
 }
 
 // Test hook: 0 automatic, 1 SIMT only, 2 tensor cores only, 3 tensor cores
 // with single-CTA tiles only, 4 tensor cores with CTA-pair tiles wherever N
-// is a multiple of 256.
+// is a multiple of 256, 5 SIMT with FP16 accumulating in f16 (the
+// reference's own algorithm; a parity route).
 int pk_debug_set_gemm_route(int route) {
-  if (route < 0 || route > 4) return set_error(PK_E_INVALID, "route must be 0..4");
+  if (route < 0 || route > 5) return set_error(PK_E_INVALID, "route must be 0..5");
   g_gemm_route = route;
   return PK_OK;
 }

@@ -189,7 +189,7 @@ int gemm(pk_encoder* e, const MatrixRef& m, int64_t rows, const void* a, void* c
   g.c = c;
   int st = validate_gemm(g);
   if (st) return st;
-  if (gemm_tc_supported(g) && g_gemm_route != 1) return launch_gemm_tc(e->device->ctx, g, s);
+  if (gemm_tc_supported(g) && !gemm_route_simt()) return launch_gemm_tc(e->device->ctx, g, s);
   return launch_gemm_simt(e->device->ctx, g, s);
 }
 

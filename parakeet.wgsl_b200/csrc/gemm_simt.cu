@@ -7,6 +7,12 @@
 // one fmaf chain in increasing k, so FP32 results are bit-identical to the
 // oracle's FP32 mode.  Weights are decoded from their packed codes straight
 // into shared memory per K-tile (never expanded to HBM).
+//
+// Reference-algorithm route (pk_debug_set_gemm_route(5), FP16 only): the
+// accumulator is rounded to f16 after every fma, in increasing k -- the
+// f16 vec4 accumulators of f16SubgroupGemmWgsl / f16PortableGemmWgsl
+// (gemm.ts:1445-1502), each step taken as an f32 fma then one rounding to
+// f16, as the CPU restatement states it.  A parity route, not a fast path.
 #include <algorithm>
 
 #include "pk_common.cuh"
@@ -32,7 +38,7 @@ __device__ __forceinline__ float from_f<float>(float v) { return v; }
 template <>
 __device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
 
-template <typename T, int BITS>
+template <typename T, int BITS, bool ACC16 = false>
 __global__ void __launch_bounds__(SG_THREADS) simt_palette_gemm_kernel(
     const T* __restrict__ a, const uint32_t* __restrict__ codes, const T* __restrict__ palette,
     const float* __restrict__ bias, const T* __restrict__ residual, T* __restrict__ out, int rows, int inner,
@@ -94,7 +100,10 @@ __global__ void __launch_bounds__(SG_THREADS) simt_palette_gemm_kernel(
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], wv[j], acc[i][j]);
+        for (int j = 0; j < 8; ++j) {
+          acc[i][j] = fmaf(av[i], wv[j], acc[i][j]);
+          if constexpr (ACC16) acc[i][j] = __half2float(__float2half_rn(acc[i][j]));
+        }
     }
     __syncthreads();
   }
@@ -140,14 +149,11 @@ int launch_gemm_simt(const DeviceCtx& dev, const GemmArgs& g, cudaStream_t strea
     auto* pal = static_cast<const __half*>(g.palette);
     auto* res = static_cast<const __half*>(g.residual);
     auto* c = static_cast<__half*>(g.c);
-    if (g.bits == 5)
-      launch_kernel(simt_palette_gemm_kernel<__half, 5>, grid, SG_THREADS, 0, stream, 
-          a, g.codes, pal, g.bias, res, c, rows, inner, columns, g.groups, gc, g.act, g.has_residual,
-          g.residual_scale);
-    else
-      launch_kernel(simt_palette_gemm_kernel<__half, 6>, grid, SG_THREADS, 0, stream, 
-          a, g.codes, pal, g.bias, res, c, rows, inner, columns, g.groups, gc, g.act, g.has_residual,
-          g.residual_scale);
+    const bool acc16 = g_gemm_route == 5;
+    auto kernel = g.bits == 5 ? (acc16 ? simt_palette_gemm_kernel<__half, 5, true> : simt_palette_gemm_kernel<__half, 5>)
+                              : (acc16 ? simt_palette_gemm_kernel<__half, 6, true> : simt_palette_gemm_kernel<__half, 6>);
+    launch_kernel(kernel, grid, SG_THREADS, 0, stream, a, g.codes, pal, g.bias, res, c, rows, inner, columns,
+                  g.groups, gc, g.act, g.has_residual, g.residual_scale);
   }
   return cuda_error(cudaGetLastError(), "simt_palette_gemm launch");
 }

@@ -121,8 +121,11 @@ int launch_logmel(int batch, int sample_count, const float* samples, const uint3
                   cudaStream_t stream);
 
 // Debug / test knob: 0 = automatic kernel choice, 1 = force the SIMT GEMM,
-// 2 = force the tensor-core GEMM (fails if the shape is unsupported).
+// 2 = force the tensor-core GEMM (fails if the shape is unsupported), 3/4 =
+// tensor cores with single-CTA / CTA-pair tiles, 5 = the SIMT GEMM with FP16
+// accumulating in f16 (the reference's algorithm, for parity runs).
 extern int g_gemm_route;
+inline bool gemm_route_simt() { return g_gemm_route == 1 || g_gemm_route == 5; }
 extern int g_gemm_tile;
 // Debug / test knob: 0 = automatic (FP16: the tcgen05 kernel when row-major
 // positions are at hand, else the mma.sync kernel), 1 = CUDA-core attention,

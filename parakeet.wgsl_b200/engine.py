@@ -93,7 +93,16 @@ class ParakeetEngine:
     def _run_batch(self, windows: Sequence[tuple], stream=None) -> list:
         """One batch through log-mel, encoder and decoder; per window its
         (token ids, frames, durations) arrays and overflow flag."""
-        return self._collect(self._submit(windows, stream, 0))
+        out = self._collect(self._submit(windows, stream, 0))
+        self._check_status()
+        return out
+
+    def _check_status(self) -> None:
+        """Raises PkError(PK_E_TIMEOUT) when a bounded device wait of this
+        device expired since the last check (the kernel that gave up returned
+        early, so its batch's tokens are not valid).  Called once no batch is
+        in flight: reading the status word clears it."""
+        self.device.status()
 
     def _submit(self, windows: Sequence[tuple], stream, slot: int):
         """Stages a batch in host slot `slot` and queues its copies and
@@ -181,6 +190,7 @@ class ParakeetEngine:
             pending = (chunk, ticket)
         if pending is not None:
             finish(*pending)
+        self._check_status()
         return decoded
 
     def transcribe(self, pcm: np.ndarray, token_piece=None, stream=None) -> st.StitchedTokens:

@@ -1,7 +1,7 @@
 """Generate the golden fixtures in this directory from the reference's own code.
 
 Run in a container that has the reference checkout (read-only) at
-``$PARAKEET_REFERENCE`` (default ``/root/reference``):
+``$PARAKEET_REFERENCE`` (default: a ``reference`` directory beside this repository):
 
     python tests/golden/make_golden.py
 
@@ -24,7 +24,7 @@ the reference's path that is executable without a browser -- and records:
   - ``pack_conformer_depthwise_kernel`` / ``pack_conv0_kernel`` layouts for a
     small seeded source (``model/convert.py:1839-1918``).
 
-The tests only read these files; nothing under ``/root/reference`` is touched
+The tests only read these files; nothing in the reference checkout is touched
 at test time.
 """
 from __future__ import annotations
@@ -39,7 +39,7 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 PROJECTION_SEED = 7  # weight = default_rng(7).standard_normal((1024, 1024)) * 0.02, f32
-REFERENCE = Path(os.environ.get("PARAKEET_REFERENCE", "/root/reference"))
+REFERENCE = Path(os.environ.get("PARAKEET_REFERENCE", str(HERE.parents[2] / "reference")))
 
 
 def main() -> None:

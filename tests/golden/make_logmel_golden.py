@@ -1,7 +1,7 @@
 """Generate ``logmel_ref.npz`` from the reference's own log-mel front end.
 
 Run in a container that has the reference checkout at ``$PARAKEET_REFERENCE``
-(default ``/root/reference``):
+(default: a ``reference`` directory beside this repository):
 
     python tests/golden/make_logmel_golden.py
 
@@ -37,7 +37,7 @@ def pcm16(seed: int, n: int) -> np.ndarray:
 
 def main() -> None:
     env = dict(os.environ)
-    env.setdefault("REFERENCE", os.environ.get("PARAKEET_REFERENCE", "/root/reference"))
+    env.setdefault("REFERENCE", os.environ.get("PARAKEET_REFERENCE", str(ROOT.parent / "reference")))
     subprocess.run(["make", "-s", "-C", str(ROOT / "oracle"), "ref", f"REFERENCE={env['REFERENCE']}"], check=True)
     sys.path.insert(0, str(ROOT))
     from oracle import oracle

@@ -80,3 +80,23 @@ def test_probe_rejects_bad_arguments(pk, own_device):
     for kind, limit in ((4, 10), (-1, 10), (1, 0), (1, 2001)):  # nothing launches
         with pytest.raises(pk.PkError, match="PK_E_INVALID"):
             pk._lib.call("pk_debug_wait_probe", own_device.handle, kind, limit, None)
+
+
+def test_engine_raises_on_expired_wait(pk, own_device):
+    """A bounded wait that ran out (here: the probe, before a transcription)
+    makes the engine raise PK_E_TIMEOUT instead of returning tokens; the read
+    clears the word, and the next transcription on the same engine is clean."""
+    package = pk.synthetic.make_package("fp16", bits_policy="all5", seed=0)
+    package.update(pk.synthetic.make_decoder("fp16", seed=0))
+    eng = pk.engine.ParakeetEngine(own_device, package, "fp16", capacity=2)
+    try:
+        pcm = pk.synthetic.make_pcm(20.0, seed=3)
+        clean = eng.transcribe(pcm)
+        pk._lib.call("pk_debug_wait_probe", own_device.handle, 1, LIMIT_MS, None)
+        with pytest.raises(pk.PkError, match="PK_E_TIMEOUT"):
+            eng.transcribe(pcm)
+        again = eng.transcribe(pcm)
+        assert again.tokens == clean.tokens
+        assert _status(pk, own_device) == (0, 0)
+    finally:
+        eng.destroy()

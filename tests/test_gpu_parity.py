@@ -1,0 +1,254 @@
+"""Parity against the reference's own algorithm, at the BASELINE shapes.
+
+* The reference's FP16 GEMMs accumulate in f16 in increasing K
+  (src/webgpu/kernels/gemm.ts:1445-1502).  GEMM route 5 runs that algorithm on
+  the CUDA cores (an f32 fma rounded to f16 after every step, as the oracle's
+  reference mode states it): single GEMMs match the oracle's reference mode
+  bit for bit where no transcendental is involved, and the full 24-layer
+  encoder -- production attention, LayerNorm, conv and subsampling kernels,
+  only the GEMM accumulation changed -- lands within the north-star FP16
+  tolerance (2e-2 relative Frobenius) of the oracle's reference mode.  The
+  production tensor-core path keeps fp32 accumulation (2.1e-3 from exact
+  arithmetic); its distance to the f16-accumulating reference is printed.
+* The CTA-pair tensor-core GEMM at the config-3 shapes (M = 32 x 188 = 6016)
+  against the oracle, not only against the single-CTA kernel.
+* one FastConformer block, B = 8 windows x 188 frames,
+  valid lengths 188 and 150, N(0, 1) inputs, mixed and all-6-bit palettes,
+  composed through the operator API (the reference's kernel classes) and
+  compared with the oracle's layer.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from gpu_util import gemm
+
+pytestmark = pytest.mark.gpu
+
+FP16_TOL = 2e-2  # north_star: FP16 package relative-Frobenius tolerance
+WIDE_TOL = 2e-3  # fp32 accumulation on both sides; f16 output rounding
+
+
+def rel(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+class _route:
+    """Context manager: a GEMM route for the duration of a block."""
+
+    def __init__(self, pk, route):
+        self.pk, self.route = pk, route
+
+    def __enter__(self):
+        self.pk._lib.call("pk_debug_set_gemm_route", self.route)
+
+    def __exit__(self, *exc):
+        self.pk._lib.call("pk_debug_set_gemm_route", 0)
+
+
+REFERENCE_ROUTE = 5
+
+# (rows, inner, columns, bits, groups, activation, bias, residual_scale)
+REF_GEMM_CASES = [
+    (1504, 1024, 4096, 5, 1, "silu", False, None),  # config-2 ff-expand
+    (1504, 4096, 1024, 5, 1, "none", False, 0.5),   # ff-contract + half residual
+    (1504, 1024, 3072, 5, 3, "none", False, None),  # qkv, 3 palette groups
+    (1504, 1024, 1024, 6, 1, "none", False, 1.0),   # o_proj 6-bit + residual
+    (300, 256, 256, 5, 1, "relu", True, None),      # subsampling pointwise
+    (188, 1024, 640, 5, 1, "none", True, None),     # projector + bias
+    (1, 4096, 1024, 5, 1, "none", True, None),      # one row of the flatten projection
+]
+
+
+@pytest.mark.parametrize("case", REF_GEMM_CASES)
+def test_reference_route_gemm_matches_reference_algorithm(pk, oracle, device, case):
+    rows, inner, columns, bits, groups, act, bias, rs = case
+    rng = np.random.default_rng(rows + inner + columns)
+    codes, lut = pk.synthetic.palette_matrix(rng, inner, columns, bits, groups, "fp16")
+    a = rng.standard_normal((rows, inner)).astype(np.float16)
+    b = (0.1 * rng.standard_normal(columns)).astype(np.float32) if bias else None
+    r = rng.standard_normal((rows, columns)).astype(np.float16) if rs is not None else None
+    kw = dict(bias=b, residual=r, residual_scale=rs or 1.0, activation=act)
+    with _route(pk, REFERENCE_ROUTE):
+        got = gemm(pk, device, a, codes["data"], lut["data"], bits, columns, **kw)
+    ref = oracle.palette_gemm(a, codes["data"], lut["data"], bits, columns, acc_mode=0, **kw)
+    assert device.status() == 0
+    if act == "silu":
+        # exp() of the SiLU epilogue: CUDA's expf and the host's differ by an
+        # ulp at most, which can move an f16 rounding by one step.
+        d = np.abs(got.astype(np.float64) - ref.astype(np.float64))
+        ulp = np.spacing(np.abs(ref).astype(np.float16)).astype(np.float64)
+        assert np.all(d <= ulp)
+        assert np.mean(d > 0) < 1e-3
+    else:
+        np.testing.assert_array_equal(got.view(np.uint16), ref.view(np.uint16))
+
+
+@pytest.fixture(scope="module")
+def package24(pk):
+    return pk.synthetic.make_package("fp16", layers=24, seed=0)
+
+
+def test_encoder_reference_route_within_fp16_tolerance(pk, oracle, device, package24):
+    """Config-3 encoder (24 layers) with the reference's f16 accumulation in
+    every GEMM and the production kernels everywhere else, against the
+    oracle's reference mode: within 2e-2 on the output and on every layer."""
+    fb = pk.synthetic.make_features(2, seed=2)
+    lengths = [1500, 1200]
+    with _route(pk, REFERENCE_ROUTE):
+        g = pk.encoder.ParakeetEncoderGraph.create(device, package24, "fp16", capacity=2)
+        try:
+            g.set_checkpoints(True)
+            out, enc = g.encode(fb, lengths)
+            got = out.cpu().numpy()
+            cps = {layer: g.checkpoint(layer).cpu().numpy()[: 2 * 188] for layer in range(-1, 24)}
+        finally:
+            g.destroy()
+    ref, ref_len, checkpoints = oracle.encoder(package24, fb, lengths, np.float16, acc_mode=0,
+                                               return_layers=True)
+    assert list(enc) == list(ref_len)
+    assert device.status() == 0
+    err = rel(got, ref)
+    layer_errs = [rel(cps[layer], checkpoints[layer + 1]) for layer in range(-1, 24)]
+    print(f"encoder (f16-accumulating GEMMs) vs oracle reference mode: output {err:.3e}, "
+          f"worst layer {max(layer_errs):.3e}")
+    assert np.isfinite(got).all()
+    assert err < FP16_TOL
+    assert max(layer_errs) < FP16_TOL
+
+
+C3_SHAPES = [
+    # rows, inner, columns, bits, groups, activation, residual_scale (the encoder's epilogues)
+    (6016, 1024, 4096, 5, 1, "silu", None),  # ff1 / ff2 linear1
+    (6016, 4096, 1024, 5, 1, "none", 0.5),   # ff1 / ff2 linear2 + half residual
+    (6016, 1024, 3072, 5, 3, "none", None),  # qkv, 3 palette groups
+    (6016, 1024, 1024, 6, 1, "none", 1.0),   # o_proj 6-bit + residual
+    (6016, 1024, 2048, 5, 1, "none", None),  # pointwise conv 1
+    (6016, 1024, 1024, 5, 1, "none", 1.0),   # pointwise conv 2 + residual
+]
+
+
+@pytest.mark.parametrize("case", C3_SHAPES)
+def test_pair_gemm_config3_shapes_vs_oracle(pk, oracle, device, case):
+    """The cta_group::2 kernel at every config-3 layer shape, with the tile the
+    encoder picks and with both large pair tiles, against the oracle's wide
+    mode (fp32 accumulation, as the tensor cores) and its reference mode."""
+    rows, inner, columns, bits, groups, act, rs = case
+    rng = np.random.default_rng(inner * 7 + columns + bits)
+    codes, lut = pk.synthetic.palette_matrix(rng, inner, columns, bits, groups, "fp16")
+    a = rng.standard_normal((rows, inner)).astype(np.float16)
+    r = rng.standard_normal((rows, columns)).astype(np.float16) if rs is not None else None
+    kw = dict(residual=r, residual_scale=rs or 1.0, activation=act)
+    outs = {}
+    try:
+        for tile in (0, -384, -512):
+            pk.kernels.set_gemm_tile(tile)
+            pk.kernels.set_gemm_route("tensor-pair")
+            outs[tile] = gemm(pk, device, a, codes["data"], lut["data"], bits, columns, **kw)
+    finally:
+        pk.kernels.set_gemm_tile(0)
+        pk.kernels.set_gemm_route("auto")
+    assert device.status() == 0
+    wide = oracle.palette_gemm(a, codes["data"], lut["data"], bits, columns, acc_mode=1, **kw)
+    for tile, out in outs.items():
+        assert np.isfinite(out).all(), tile
+        assert rel(out, wide) < WIDE_TOL, (tile, rel(out, wide))
+    ref = oracle.palette_gemm(a, codes["data"], lut["data"], bits, columns, acc_mode=0, **kw)
+    err = rel(outs[0], ref)
+    print(f"M={rows} K={inner} N={columns}: vs wide {rel(outs[0], wide):.2e}, vs reference algorithm {err:.2e}")
+    assert err < FP16_TOL
+
+
+# ------------------------------------------------------------------ config 2: one block
+
+def _block_operators(pk, device, weights, layer, x, lengths, batch, frames, attention_route):
+    """One Macaron Conformer layer (src/webgpu/encoder.ts:1869-2138) composed
+    from the operator API: the F16GemmKernel dispatches with the production
+    signatures (7520-row buffers, the active prefix selected per encode as
+    EncoderDispatchShape does), LayerNormKernel, RelativeAttentionKernel and
+    FusedConformerConvKernel."""
+    import torch
+
+    K = pk.kernels
+    cap = 7520  # the production signatures' row count (40 windows)
+    rows = batch * frames
+    p = f"encoder.layers.{layer}"
+    gt = {n: K.GpuTensor.from_record(n, r) for n, r in weights.items() if n.startswith(p)}
+    buf = lambda cols: torch.zeros((cap, cols), dtype=torch.float16, device="cuda")  # noqa: E731
+    xin = buf(1024)
+    xin[:rows] = torch.from_numpy(x).cuda()
+    lens = torch.from_numpy(np.asarray(lengths, np.uint32).view(np.int32)).cuda()
+    shape = {"rows": rows}
+    gk = K.F16GemmKernel.create(device)
+    ln = K.LayerNormKernel.create(device)
+
+    def norm(src, name):
+        out = buf(1024)
+        ln.create_dispatch(dict(label=name, input=src, output=out, gamma=gt[f"{p}.{name}.weight"],
+                                beta=gt[f"{p}.{name}.bias"], rows=cap, channels=1024)).encode(shape=shape)
+        return out
+
+    def linear(src, name, columns, activation="none", residual=None, scale=None):
+        out = buf(columns)
+        w, pal = gt[f"{p}.{name}.weight"], gt[f"{p}.{name}.weight.palette"]
+        gk.create_dispatch(K.GemmDescriptor(name, src, w, out, cap, src.shape[1], columns, b_palette=pal,
+                                            palette_group_columns=columns // pal.shape[0], residual=residual,
+                                            residual_scale=scale, activation=activation)).encode(shape=shape)
+        return out
+
+    a = norm(xin, "norm_feed_forward1")
+    x1 = linear(linear(a, "feed_forward1.linear1", 4096, "silu"), "feed_forward1.linear2", 1024,
+                residual=xin, scale=0.5)
+    qkv = linear(norm(x1, "norm_self_att"), "self_attn.qkv", 3072)
+    ctx = buf(1024)
+    pk.kernels.set_attention_route(attention_route)
+    try:
+        K.RelativeAttentionKernel.create(device).create_dispatch(dict(
+            label="attention", qkv=qkv, projected_positions=gt[f"{p}.self_attn.projected_positions"],
+            bias_u=gt[f"{p}.self_attn.bias_u"], bias_v=gt[f"{p}.self_attn.bias_v"], valid_lengths=lens,
+            output=ctx, batch_size=batch, frames=frames)).encode()
+    finally:
+        pk.kernels.set_attention_route("auto")
+    x2 = linear(ctx, "self_attn.o_proj", 1024, residual=x1, scale=1.0)
+    g = linear(norm(x2, "norm_conv"), "conv.pointwise_conv1", 2048)
+    c = buf(1024)
+    K.FusedConformerConvKernel.create(device).create_dispatch(dict(
+        label="conv", pointwise_input=g, depthwise_weights=gt[f"{p}.conv.depthwise_conv.weight"],
+        batch_norm_scale=gt[f"{p}.conv.norm.scale"], batch_norm_shift=gt[f"{p}.conv.norm.shift"],
+        valid_lengths=lens, output=c, batch_size=batch, frames=frames)).encode()
+    x3 = linear(c, "conv.pointwise_conv2", 1024, residual=x2, scale=1.0)
+    x4 = linear(linear(norm(x3, "norm_feed_forward2"), "feed_forward2.linear1", 4096, "silu"),
+                "feed_forward2.linear2", 1024, residual=x3, scale=0.5)
+    out = norm(x4, "norm_out")
+    torch.cuda.synchronize()
+    return out[:rows].cpu().numpy()
+
+
+@pytest.mark.parametrize("policy", ["mixed", "all6"])
+def test_config2_block(pk, oracle, device, policy):
+    """one FP16 block, batch 8 x 188 frames, valid lengths
+    188 (four windows) and 150 (four windows), inputs N(0, 1)."""
+    batch, frames = 8, 188
+    weights = pk.synthetic.make_package("fp16", layers=1, bits_policy=policy, seed=21)
+    rng = np.random.default_rng(22)
+    x = rng.standard_normal((batch * frames, 1024)).astype(np.float16)
+    lengths = [188, 150] * 4
+    lens = np.array(lengths, np.uint32)
+    wide = oracle.conformer_layer(weights, 0, x, lens, batch, frames, acc_mode=1)
+    ref = oracle.conformer_layer(weights, 0, x, lens, batch, frames, acc_mode=0)
+    for attention in ("auto", "simt"):
+        got = _block_operators(pk, device, weights, 0, x, lengths, batch, frames, attention)
+        assert np.isfinite(got).all()
+        e_wide, e_ref = rel(got, wide), rel(got, ref)
+        print(f"config 2 ({policy}, attention {attention}): vs wide {e_wide:.2e}, vs reference {e_ref:.2e}")
+        assert e_wide < 5e-3
+        assert e_ref < FP16_TOL
+    with _route(pk, REFERENCE_ROUTE):
+        got = _block_operators(pk, device, weights, 0, x, lengths, batch, frames, "simt")
+    e_ref = rel(got, ref)
+    print(f"config 2 ({policy}, reference route): vs reference {e_ref:.2e}")
+    assert e_ref < 5e-3
+    assert device.status() == 0
