@@ -293,7 +293,7 @@ def time_transcribe(pk, device, package, seconds=60.0, reps=2):
     windows = len(pk.windows.plan_stateless_windows(len(pcm)))
     eng.destroy()
     return {"workload": f"config4: {seconds:.0f} s synthetic PCM (pink noise + modulated tones), {windows} windows",
-            "s_per_run": round(dt, 4), "audio_s_per_s": round(seconds / dt, 1), "tokens": len(res.tokens),
+            "s_per_run": round(dt, 4), "audio_s_per_s": round(seconds / dt, 1), "tokens": len(res),
             "note": "random-init weights; the decoder's token count (not real speech) sets most of the time"}
 
 
@@ -301,6 +301,7 @@ def time_transcribe(pk, device, package, seconds=60.0, reps=2):
 # shorter stretch so the default benchmark stays within minutes.
 LONGFORM_VARIANTS = (("fp16", "mixed", 3600.0), ("fp16", "all5", 3600.0), ("fp32", "mixed", 600.0),
                      ("fp32", "all5", 600.0))
+LONGFORM_CAPACITY = 32  # windows per engine batch
 
 
 def longform_pcm(pk, seconds, seed=5, distinct=5):
@@ -313,28 +314,27 @@ def longform_pcm(pk, seconds, seed=5, distinct=5):
     return np.concatenate([blocks[i % distinct] for i in range(reps)])[:n]
 
 
-def time_longform(pk, device, rank, world, stream):
+def time_longform(pk, device, rank, world, stream, capacity=None):
     """engine.transcribe_sharded on synthetic audio, host PCM in and merged
     tokens out: each rank decodes its contiguous share of the window plan on
-    its own GPU; the token lists meet on rank 0 (a host gather, no collective
-    on the hot path), which merges them.  Time: CUDA events on each rank's
-    stream around its share, the gather and the merge; max over ranks."""
+    its own GPU and merges its own windows as they finish (native merge);
+    the runs meet on rank 0 as flat int64 arrays (a gather of plain tensors,
+    no collective on the hot path), which joins them at the rank seams.
+    Time: CUDA events on each rank's stream around its share, the gather and
+    the merge; max over ranks.  Per phase (host wall time, max over ranks):
+    decode (decode + the rank's own merge, overlapped), gather, rank-0 merge."""
     import torch
     import torch.distributed as dist
 
-    def gather(obj):
-        if world == 1:
-            return [obj]
-        parts = [None] * world if rank == 0 else None
-        dist.gather_object(obj, parts, dst=0)
-        return parts
+    capacity = capacity or LONGFORM_CAPACITY
+    gather = (lambda flat: [flat]) if world == 1 else pk.engine.array_gather(rank, world, torch.device("cuda"))
 
-    def max_over_ranks(x):
+    def max_over_ranks(values):
         if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+            return values
+        t = torch.tensor(values, dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return t.tolist()
 
     out = []
     # One generation serves every variant: the shorter runs take its prefix,
@@ -343,9 +343,10 @@ def time_longform(pk, device, rank, world, stream):
     for precision, policy, seconds in LONGFORM_VARIANTS:
         package = pk.synthetic.make_package(precision, bits_policy=policy, seed=0)
         package.update(pk.synthetic.make_decoder(precision, seed=0))
-        eng = pk.engine.ParakeetEngine(device, package, precision, capacity=BATCH)
+        eng = pk.engine.ParakeetEngine(device, package, precision, capacity=capacity)
         del package
         pcm = longest[: int(round(seconds * 16_000))]
+        timings = {}
         with torch.cuda.stream(stream):
             eng.transcribe(pcm[:30 * 16_000])  # warm-up
             if world > 1:
@@ -353,18 +354,23 @@ def time_longform(pk, device, rank, world, stream):
             torch.cuda.synchronize()
             start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             start.record(stream)
-            res = pk.engine.transcribe_sharded(eng, pcm, rank, world, gather)
+            res = pk.engine.transcribe_sharded(eng, pcm, rank, world, gather, timings=timings)
             end.record(stream)
             end.synchronize()
-        ms = max_over_ranks(start.elapsed_time(end))
+        ms, decode_s, gather_s, merge_s = max_over_ranks(
+            [start.elapsed_time(end), timings["decode_s"], timings["gather_s"], timings["merge_s"]])
         windows = len(pk.windows.plan_stateless_windows(len(pcm)))
+        batches = [len(r) for r in eng.batches(len(pk.windows.shard_windows(windows, world, rank)))]
         eng.destroy()
         out.append({"precision": precision, "palette_bits": policy, "audio_s": seconds, "windows": windows,
                     "s": round(ms / 1e3, 3), "audio_s_per_s": round(seconds / (ms / 1e3), 1),
-                    "tokens": None if res is None else len(res.tokens)})
+                    "tokens": None if res is None else len(res),
+                    "rank_batches": batches,
+                    "phases_s": {"decode": round(decode_s, 4), "gather": round(gather_s, 4),
+                                 "merge_rank0": round(merge_s, 4)}})
     return {"workload": "config5: synthetic PCM (five 60 s pink-noise + tone blocks in rotation), window plan "
                         "sharded over ranks, host PCM in, merged tokens out",
-            "n_gpus": world, "variants": out,
+            "n_gpus": world, "capacity": capacity, "variants": out,
             "note": "random-init weights; decoded token counts are not real speech and set most of the time"}
 
 
@@ -484,25 +490,31 @@ def run_ours(args):
     barrier()
     e2e_ms = max_over_ranks(t_start.elapsed_time(t_end) / args.steps)
 
+    legs = set(args.legs.split(","))
+
     # ---- log-mel front end for this batch (32 x 240 000 samples of PCM)
-    lm_info = time_logmel(pk, device, stream)
+    lm_info = time_logmel(pk, device, stream) if "logmel" in legs else None
     barrier()
 
     # ---- TDT greedy decoding of this batch's encoder output (synthetic decoder weights)
-    dec_info = time_decoder(pk, device, out.view(BATCH, FRAMES, 640), stream, reps=max(1, min(args.steps, 5)))
+    dec_info = None
+    if "decoder" in legs:
+        dec_info = time_decoder(pk, device, out.view(BATCH, FRAMES, 640), stream, reps=max(1, min(args.steps, 5)))
     barrier()
 
     # ---- end-to-end transcription (config 4): 60 s of PCM through the engine
-    tr_info = time_transcribe(pk, device, package) if rank == 0 else None
+    tr_info = time_transcribe(pk, device, package) if rank == 0 and "transcribe" in legs else None
     barrier()
 
     # ---- long-form (config 5): one hour's window plan sharded across all ranks
-    lf_info = None if args.skip_longform else time_longform(pk, device, rank, world, stream)
+    lf_info = None if args.skip_longform or "longform" not in legs else time_longform(pk, device, rank, world, stream)
     barrier()
 
     # ---- dominant kernel: palette GEMMs of one step, timed live
-    with torch.cuda.stream(stream):
-        gemm_flops, gemm_ms, gemm_detail = time_gemms(pk, device, BATCH, stream)
+    gemm_flops, gemm_ms, gemm_detail = 0.0, 1.0, []
+    if "gemm" in legs:
+        with torch.cuda.stream(stream):
+            gemm_flops, gemm_ms, gemm_detail = time_gemms(pk, device, BATCH, stream)
     barrier()
 
     if rank == 0:
@@ -669,6 +681,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
     ap.add_argument("--skip-longform", action="store_true")
+    ap.add_argument("--legs", default="logmel,decoder,transcribe,longform,gemm",
+                    help="comma-separated extra legs to run besides the encoder step (a subset for quick runs)")
     ap.add_argument("--kernel", choices=["gemm", "gemm-step", "attention", "attention-mma", "layernorm", "conv",
                                          "subsampling", "decoder", "logmel"],
                     help="profiling target: launch one operator only")

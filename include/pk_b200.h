@@ -266,6 +266,60 @@ int pk_encoder_set_checkpoints(pk_encoder* encoder, int enable);
 int pk_encoder_checkpoint(pk_encoder* encoder, int layer, void* out, pk_stream stream);
 int pk_encoder_destroy(pk_encoder* encoder);
 
+/* ---- Overlap merge of decoded windows (host code; no GPU) ----------------
+ * Replaces IncrementalStitchAccumulator (src/runtime/stitch.ts:135-213) for
+ * token streams without word pieces: append / snapshot with the same merge
+ * (mergeTokenStreams :247-359 -- disjoint, longest contiguous run, LCS,
+ * midpoint), the same trace and enforceMonotonicTokenTimes (:230-262).
+ * A token is int64[4] (token_id, start_sample, end_sample, duration_frames),
+ * a trace entry int64[5] (left window index, right window index, method 0
+ * disjoint / 1 contiguous / 2 lcs / 3 midpoint, overlap start and end
+ * sample).  Errors: PK_E_INVALID with the reference's RangeError messages
+ * (validateWindow, :715-775; out-of-order windows).  One accumulator must not
+ * be used from two threads at once. */
+typedef struct pk_stitch pk_stitch;
+enum { PK_STITCH_COLLECT_TRACE = 1, PK_STITCH_RECORD_RUN = 2 };
+int pk_stitch_create(int flags, pk_stitch** out);
+int pk_stitch_destroy(pk_stitch* stitch);
+/* window: int64[3] (index, start_sample, end_sample), the logical emission
+ * range; tokens: int64[count][4] sorted by start_sample (append, :146-179). */
+int pk_stitch_append(pk_stitch* stitch, const int64_t* window, const int64_t* tokens, int64_t count);
+/* globalizeTdtTokens (stitch.ts:69-99) + append: window int64[4] (index,
+ * emission start, emission end, timestamp offset sample); the decoder's
+ * per-emission token ids, window-local encoder frames and durations. */
+int pk_stitch_append_tdt(pk_stitch* stitch, const int64_t* window, const int32_t* token_ids,
+                         const int32_t* frames, const int32_t* durations, int64_t count);
+/* A contiguous run of windows merged on its own by an accumulator created with
+ * PK_STITCH_RECORD_RUN (no reference counterpart: the reference merges on one
+ * thread).  window_meta int64[windows][4] (index, start, end, token count),
+ * window_tokens the windows' own tokens, merged the run's merged stream,
+ * trace its internal trace; guard / local_ok from pk_stitch_read_run. */
+typedef struct pk_stitch_run {
+  const int64_t* window_meta;
+  int64_t windows;
+  const int64_t* window_tokens;
+  const int64_t* merged;
+  int64_t tokens;
+  const int64_t* trace;
+  int64_t trace_entries;
+  int64_t guard;
+  int local_ok;
+} pk_stitch_run;
+/* Appends a run: spliced in at its first seam when that is exact (an empty
+ * stream, a one-window run, or the run's locality conditions hold and the
+ * stream joined ends before the run's guard sample), otherwise window by
+ * window.  Either way the result equals appending the run's windows. */
+int pk_stitch_extend(pk_stitch* stitch, const pk_stitch_run* run);
+/* counts: int64[4] = merged tokens, trace entries, recorded windows,
+ * recorded window tokens. */
+int pk_stitch_counts(const pk_stitch* stitch, int64_t* counts);
+/* Copies the merged tokens (clamp != 0: snapshot's monotonic clamp) and the
+ * trace; either pointer may be null. */
+int pk_stitch_read(const pk_stitch* stitch, int clamp, int64_t* tokens, int64_t* trace);
+/* The recorded run: window_meta int64[windows][4], window_tokens, and
+ * conditions int64[2] = (guard sample, local_ok). */
+int pk_stitch_read_run(const pk_stitch* stitch, int64_t* window_meta, int64_t* window_tokens, int64_t* conditions);
+
 /* Test hook (no reference counterpart): selects the GEMM kernel for later
  * pk_palette_gemm / encoder launches in this process.  0 = automatic
  * (tensor cores where the shape tiles, else CUDA cores), 1 = CUDA-core

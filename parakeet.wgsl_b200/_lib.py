@@ -32,8 +32,19 @@ EXPORTED = (
     "pk_weights_upload", "pk_weights_release", "pk_encoder_create", "pk_encoder_forward",
     "pk_encoder_set_checkpoints", "pk_encoder_checkpoint", "pk_encoder_destroy", "pk_debug_set_gemm_route",
     "pk_debug_set_gemm_tile", "pk_debug_set_attention_route", "pk_debug_set_decoder_route",
-    "pk_debug_wait_probe",
+    "pk_debug_wait_probe", "pk_stitch_create", "pk_stitch_destroy", "pk_stitch_append", "pk_stitch_append_tdt",
+    "pk_stitch_extend", "pk_stitch_counts", "pk_stitch_read", "pk_stitch_read_run",
 )
+STITCH_COLLECT_TRACE, STITCH_RECORD_RUN = 1, 2
+
+
+class StitchRun(ctypes.Structure):
+    """pk_stitch_run: a run of windows merged on its own (another rank's)."""
+    _fields_ = [
+        ("window_meta", ctypes.c_void_p), ("windows", ctypes.c_int64), ("window_tokens", ctypes.c_void_p),
+        ("merged", ctypes.c_void_p), ("tokens", ctypes.c_int64), ("trace", ctypes.c_void_p),
+        ("trace_entries", ctypes.c_int64), ("guard", ctypes.c_int64), ("local_ok", ctypes.c_int),
+    ]
 
 
 class PkError(RuntimeError):
@@ -125,6 +136,14 @@ def load() -> ctypes.CDLL:
             "pk_debug_set_attention_route": [i32],
             "pk_debug_set_decoder_route": [i32],
             "pk_debug_wait_probe": [vp, i32, ctypes.c_uint32, vp],
+            "pk_stitch_create": [i32, ctypes.POINTER(vp)],
+            "pk_stitch_destroy": [vp],
+            "pk_stitch_append": [vp, vp, vp, i64],
+            "pk_stitch_append_tdt": [vp, vp, vp, vp, vp, i64],
+            "pk_stitch_extend": [vp, ctypes.POINTER(StitchRun)],
+            "pk_stitch_counts": [vp, vp],
+            "pk_stitch_read": [vp, i32, vp, vp],
+            "pk_stitch_read_run": [vp, vp, vp, vp],
         }
         for name, args in sig.items():
             fn = getattr(lib, name)

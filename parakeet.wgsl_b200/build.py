@@ -2,7 +2,8 @@
 
     python parakeet.wgsl_b200/build.py [--verbose]
 
-Each ``csrc/*.cu`` is compiled by nvcc (``-gencode arch=compute_100a,
+Each ``csrc/*.cu`` (device and host code) and ``csrc/*.cpp`` (host-only
+code, forwarded by nvcc to the host compiler) is compiled by nvcc (``-gencode arch=compute_100a,
 code=sm_100a -lineinfo -O3``) into ``_build/`` in parallel and linked into
 ``parakeet.wgsl_b200/libpk_b200.so`` with the CUDA runtime linked statically,
 so the library carries no dependency on the caller's CUDA runtime.  nvcc
@@ -61,7 +62,7 @@ def _compile(src: Path, verbose: bool) -> tuple[Path, str]:
 
 def build(verbose: bool = False, jobs: int | None = None) -> Path:
     BUILD.mkdir(parents=True, exist_ok=True)
-    sources = sorted(CSRC.glob("*.cu"))
+    sources = sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cpp"))
     jobs = jobs or min(len(sources), os.cpu_count() or 4)
     with cf.ThreadPoolExecutor(jobs) as ex:
         results = list(ex.map(lambda s: _compile(s, verbose), sources))

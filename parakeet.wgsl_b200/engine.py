@@ -163,16 +163,32 @@ class ParakeetEngine:
             out.append((tok[i, :n].copy(), fr[i, :n].copy(), du[i, :n].copy(), bool(flags[i] & 1)))
         return out
 
-    def decode_plans(self, pcm: np.ndarray, plans: Sequence[wp.WindowPlan], stream=None, on_window=None) -> list:
-        """Runs `plans` in capacity-sized batches; returns a DecodedTokenWindow
-        per plan.  Batches are pipelined: batch i+1 is staged on the host and
-        queued while the GPU runs batch i, and batch i's tokens are read,
-        globalized and handed to `on_window` (in plan order; a merge, for
-        instance) while batch i+1 runs."""
+    def batches(self, count: int) -> list[range]:
+        """Splits `count` windows into the fewest batches of at most
+        `capacity`, as equal in size as possible (35 windows at capacity 32
+        run as 18 + 17, not 32 + 3: a batch costs about as much as its
+        longest window, whatever its size)."""
+        n = -(-count // self.capacity) if count else 0
+        edges = [round(k * count / n) for k in range(n + 1)] if n else [0]
+        return [range(a, b) for a, b in zip(edges, edges[1:])]
+
+    def decode_plans(self, pcm: np.ndarray, plans: Sequence[wp.WindowPlan], stream=None, on_window=None,
+                     on_tdt=None) -> list:
+        """Runs `plans` in balanced batches of at most `capacity` windows;
+        returns a DecodedTokenWindow per plan.  Batches are pipelined: batch
+        i+1 is staged on the host and queued while the GPU runs batch i, and
+        batch i's tokens are read, globalized and handed to `on_window` (in
+        plan order; a merge, for instance) while batch i+1 runs.  With
+        `on_tdt`, each window's raw decoder output (plan, token ids, frames,
+        durations) goes to `on_tdt` instead and nothing is returned (no
+        per-token Python objects are built)."""
         decoded = []
 
         def finish(chunk, ticket):
             for plan, (tok, fr, du, _) in zip(chunk, self._collect(ticket)):
+                if on_tdt is not None:
+                    on_tdt(plan, tok, fr, du)
+                    continue
                 toks = st.globalize_tdt_arrays(tok, fr, du, plan)
                 window = st.DecodedTokenWindow(plan.index, plan.emission_start_sample, plan.emission_end_sample,
                                                tuple(toks))
@@ -181,8 +197,8 @@ class ParakeetEngine:
                     on_window(window)
 
         pending = None
-        for k, start in enumerate(range(0, len(plans), self.capacity)):
-            chunk = plans[start:start + self.capacity]
+        for k, rows in enumerate(self.batches(len(plans))):
+            chunk = plans[rows.start:rows.stop]
             batch = [(pcm[p.source_start_sample:p.source_end_sample], p) for p in chunk]
             ticket = self._submit(batch, stream, k % 2)
             if pending is not None:
@@ -193,12 +209,14 @@ class ParakeetEngine:
         self._check_status()
         return decoded
 
-    def transcribe(self, pcm: np.ndarray, token_piece=None, stream=None) -> st.StitchedTokens:
-        """Long-form transcription of 16 kHz mono f32 PCM on this GPU."""
+    def transcribe(self, pcm: np.ndarray, token_piece=None, stream=None):
+        """Long-form transcription of 16 kHz mono f32 PCM on this GPU; returns
+        StitchedTokens (StitchedTokenArrays from the native merge when no
+        token pieces are given)."""
         pcm = np.ascontiguousarray(pcm, dtype=np.float32)
         plans = wp.plan_stateless_windows(int(pcm.shape[0]))
-        acc = st.IncrementalStitchAccumulator(token_piece=token_piece, collect_trace=True)
-        _decode_into(self, pcm, plans, acc.append, stream)
+        acc = _accumulator(token_piece)
+        _decode_into(self, pcm, plans, acc, stream)
         return acc.snapshot()
 
     def destroy(self) -> None:
@@ -206,16 +224,36 @@ class ParakeetEngine:
         self.weights.release()
 
 
+def _accumulator(token_piece):
+    """The merge: native (no word pieces) or the Python restatement (pieces)."""
+    if token_piece is None:
+        return st.NativeStitchAccumulator(collect_trace=True)
+    return st.IncrementalStitchAccumulator(token_piece=token_piece, collect_trace=True)
+
+
 def _decode_into(engine, pcm, plans, sink, stream=None) -> None:
-    """Decodes `plans` and feeds each DecodedTokenWindow to `sink` in the
+    """Decodes `plans` and feeds each window to `sink` (an accumulator, a
+    partial-run builder, or a function of a DecodedTokenWindow) in the
     merge's (emission start, index) order -- as each batch finishes, while
-    the GPU runs the next one, when the plan is already in that order."""
+    the GPU runs the next one, when the plan is already in that order.
+    Sinks with ``append_tdt`` take the decoder's arrays directly."""
     keys = [(p.emission_start_sample, p.index) for p in plans]
-    if all(a <= b for a, b in zip(keys, keys[1:])):
-        engine.decode_plans(pcm, plans, stream, on_window=sink)
+    ordered = all(a <= b for a, b in zip(keys, keys[1:]))
+    if hasattr(sink, "append_tdt"):
+        if ordered:
+            engine.decode_plans(pcm, plans, stream, on_tdt=sink.append_tdt)
+            return
+        out = []
+        engine.decode_plans(pcm, plans, stream, on_tdt=lambda *w: out.append(w))
+        for w in sorted(out, key=lambda w: (w[0].emission_start_sample, w[0].index)):
+            sink.append_tdt(*w)
+        return
+    append = sink.append if hasattr(sink, "append") else sink
+    if ordered:
+        engine.decode_plans(pcm, plans, stream, on_window=append)
         return
     for w in sorted(engine.decode_plans(pcm, plans, stream), key=lambda w: (w.start_sample, w.index)):
-        sink(w)
+        append(w)
 
 
 class ShardFailure(RuntimeError):
@@ -230,16 +268,20 @@ class ShardFailure(RuntimeError):
                                    for r, m in sorted(self.failures.items(), key=lambda kv: (kv[0] is None, kv[0]))))
 
 
-def transcribe_sharded(engine, pcm: np.ndarray, rank: int, world_size: int, gather, token_piece=None):
+def transcribe_sharded(engine, pcm: np.ndarray, rank: int, world_size: int, gather, token_piece=None,
+                       timings: dict | None = None):
     """Multi-GPU long-form transcription: this rank decodes its contiguous
     share of the window plan with its own `engine` (its own GPU) and merges
-    its own windows (stitch.stitch_partial); `gather(obj)` brings every
-    rank's partial stream, packed as arrays, to rank 0 (for example
-    torch.distributed's gather_object), which joins them at the rank seams
-    (IncrementalStitchAccumulator.extend -- the same tokens and trace as
-    merging every window on one rank).  Returns the merged tokens on rank 0
-    and None elsewhere.  With world_size 1 it is ``engine.transcribe`` (no
-    gather; errors propagate as they are).
+    its own windows as they finish decoding (a partial run); `gather(array)`
+    brings every rank's run, packed as one flat int64 array
+    (stitch.pack_partial), to rank 0 (see ``array_gather``), which joins
+    them at the rank seams (extend -- the same tokens and trace as merging
+    every window on one rank).  Returns the merged tokens on rank 0 and None
+    elsewhere.  With world_size 1 it is ``engine.transcribe`` (no gather;
+    errors propagate as they are).  `timings`, when given, receives this
+    rank's host wall time per phase: decode_s (decode and the rank's own
+    merge, overlapped), gather_s, merge_s (rank 0: joining the runs and the
+    snapshot).
 
     Failures do not hang the other ranks: a rank whose decode raises (a
     PkError such as PK_E_TIMEOUT from a bounded device wait, a RangeError)
@@ -247,34 +289,76 @@ def transcribe_sharded(engine, pcm: np.ndarray, rank: int, world_size: int, gath
     and then re-raises; rank 0 raises ShardFailure naming every failed rank.
     A gather that itself fails (a rank that exited, a process-group timeout)
     raises ShardFailure on the ranks that see it."""
+    import time
+
+    clock = time.perf_counter
+    t0 = clock()
     pcm = np.ascontiguousarray(pcm, dtype=np.float32)
     plans = wp.plan_stateless_windows(int(pcm.shape[0]))
     if world_size == 1:
-        acc = st.IncrementalStitchAccumulator(token_piece=token_piece, collect_trace=True)
-        _decode_into(engine, pcm, plans, acc.append)
-        return acc.snapshot()
+        acc = _accumulator(token_piece)
+        _decode_into(engine, pcm, plans, acc)
+        t1 = clock()
+        out = acc.snapshot()
+        if timings is not None:
+            timings.update(decode_s=t1 - t0, gather_s=0.0, merge_s=clock() - t1)
+        return out
     mine = [plans[i] for i in wp.shard_windows(len(plans), world_size, rank)]
     error = None
     try:
-        builder = st.PartialStitchBuilder(token_piece)
+        builder = st.NativePartialStitchBuilder() if token_piece is None else st.PartialStitchBuilder(token_piece)
         if mine:
-            _decode_into(engine, pcm, mine, builder.append)
-        payload = ("ok", builder.finish())
+            _decode_into(engine, pcm, mine, builder)
+        payload = st.pack_partial(builder.finish())
     except Exception as exc:  # reported through the gather, re-raised below
         error = exc
-        payload = ("error", f"{type(exc).__name__}: {exc}")
+        payload = st.pack_error(f"{type(exc).__name__}: {exc}")
+    t1 = clock()
     try:
         gathered = gather(payload)
     except Exception as exc:
         raise ShardFailure({None: f"{type(exc).__name__}: {exc}"}) from exc
+    t2 = clock()
+    if timings is not None:
+        timings.update(decode_s=t1 - t0, gather_s=t2 - t1, merge_s=0.0)
     if rank != 0:
         if error is not None:
             raise error
         return None
-    failures = {r: part[1] for r, part in enumerate(gathered) if part[0] != "ok"}
+    parts = [st.unpack_partial(flat) for flat in gathered]
+    failures = {r: part[1] for r, part in enumerate(parts) if part[0] != "ok"}
     if failures:
         raise ShardFailure(failures) from error
-    acc = st.IncrementalStitchAccumulator(token_piece=token_piece, collect_trace=True)
-    for _, part in gathered:  # rank order is window order: the shards are contiguous
+    acc = _accumulator(token_piece)
+    for _, part in parts:  # rank order is window order: the shards are contiguous
         acc.extend(part)
-    return acc.snapshot()
+    out = acc.snapshot()
+    if timings is not None:
+        timings["merge_s"] = clock() - t2
+    return out
+
+
+def array_gather(rank: int, world_size: int, device=None):
+    """A `gather` for transcribe_sharded over torch.distributed: every rank's
+    flat int64 array reaches rank 0 as plain tensors (lengths first, then
+    one padded gather; NCCL tensors on `device`, CPU tensors for gloo).
+    Returns a list of arrays on rank 0 and None elsewhere."""
+    import torch.distributed as dist
+
+    def gather(flat: np.ndarray):
+        t = torch.from_numpy(np.ascontiguousarray(flat, dtype=np.int64))
+        if device is not None:
+            t = t.to(device)
+        n = torch.tensor([t.numel()], dtype=torch.int64, device=t.device)
+        sizes = [torch.zeros_like(n) for _ in range(world_size)]
+        dist.all_gather(sizes, n)
+        sizes = [int(v.item()) for v in sizes]
+        padded = torch.zeros(max(sizes), dtype=torch.int64, device=t.device)
+        padded[:t.numel()] = t
+        bufs = [torch.empty_like(padded) for _ in range(world_size)] if rank == 0 else None
+        dist.gather(padded, bufs, dst=0)
+        if rank != 0:
+            return None
+        return [b[:k].cpu().numpy() for b, k in zip(bufs, sizes)]
+
+    return gather

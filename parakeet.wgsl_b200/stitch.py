@@ -16,9 +16,15 @@ decoded on whichever GPU holds them, and only their token lists meet here.
 reference counterpart (the reference merges on one thread): each rank merges
 its own contiguous windows, and rank 0 splices the runs in at the rank seams,
 with the same tokens and trace as one merge of every window.
+
+``NativeStitchAccumulator`` / ``NativePartialStitchBuilder`` run the same
+merge (streams without word pieces, which is what the engine decodes) in
+libpk_b200.so's native implementation (``pk_stitch_*``) on int64 token rows:
+no per-token Python objects are built until a caller asks for them.
 """
 from __future__ import annotations
 
+import ctypes
 import gc
 import unicodedata
 from contextlib import contextmanager
@@ -28,6 +34,7 @@ from typing import Callable, NamedTuple, Optional, Sequence
 
 import numpy as np
 
+from . import _lib
 from .windows import ENCODER_FRAME_SAMPLES, OVERLAP_SAMPLES, WindowPlan
 
 TokenPieceResolver = Callable[[int], Optional[str]]
@@ -643,3 +650,190 @@ def _check_token(t: TimedToken, prev: int) -> None:
         raise ValueError("token endSample must not precede startSample")
     if t.start_sample < prev:
         raise ValueError("tokens must be sorted by startSample")
+
+
+# ------------------------------------------------------------------ native merge
+
+STITCH_METHODS = ("disjoint", "contiguous", "lcs", "midpoint")
+
+
+class StitchedTokenArrays:
+    """StitchedTokens held as arrays: ``token_rows`` int64 [n, 4] (token_id,
+    start_sample, end_sample, duration_frames; monotonic clamp applied) and
+    ``trace_rows`` int64 [m, 5].  ``tokens`` / ``trace`` build the record
+    tuples on first use; equality compares those with any StitchedTokens."""
+
+    def __init__(self, token_rows: np.ndarray, trace_rows: np.ndarray):
+        self.token_rows = token_rows
+        self.trace_rows = trace_rows
+        self._tokens = None
+        self._trace = None
+
+    @property
+    def tokens(self) -> tuple:
+        if self._tokens is None:
+            with _gc_paused():
+                self._tokens = tuple(map(TimedToken._make, self.token_rows.tolist()))
+        return self._tokens
+
+    @property
+    def trace(self) -> tuple:
+        if self._trace is None:
+            self._trace = _trace_records(self.trace_rows)
+        return self._trace
+
+    def __len__(self) -> int:
+        return int(self.token_rows.shape[0])
+
+    def __eq__(self, other) -> bool:
+        return self.tokens == other.tokens and self.trace == other.trace
+
+
+def _trace_records(rows: np.ndarray) -> tuple:
+    return tuple(StitchTrace(int(a), int(b), STITCH_METHODS[int(m)], int(s0), int(s1))
+                 for a, b, m, s0, s1 in rows.tolist())
+
+
+def _trace_rows(trace) -> np.ndarray:
+    if isinstance(trace, np.ndarray):
+        return np.ascontiguousarray(trace, dtype=np.int64).reshape(-1, 5)
+    return np.array([(t.left_window_index, t.right_window_index, STITCH_METHODS.index(t.method),
+                      t.overlap_start_sample, t.overlap_end_sample) for t in trace], dtype=np.int64).reshape(-1, 5)
+
+
+def _vp(a: np.ndarray):
+    return ctypes.c_void_p(a.ctypes.data) if a.size else None
+
+
+class NativeStitchAccumulator:
+    """IncrementalStitchAccumulator for streams without word pieces, on the
+    native merge (pk_stitch_*): the same tokens, trace and errors."""
+
+    def __init__(self, collect_trace: bool = False, record_run: bool = False):
+        flags = (_lib.STITCH_COLLECT_TRACE if collect_trace else 0) | (_lib.STITCH_RECORD_RUN if record_run else 0)
+        handle = ctypes.c_void_p()
+        self._call("pk_stitch_create", flags, ctypes.byref(handle))
+        self._h = handle
+
+    @staticmethod
+    def _call(name, *args) -> None:
+        try:
+            _lib.call(name, *args)
+        except _lib.PkError as exc:
+            if exc.status == -1:  # PK_E_INVALID: the reference's RangeError
+                raise ValueError(str(exc).split(": ", 1)[-1]) from None
+            raise
+
+    def append(self, window: DecodedTokenWindow) -> None:
+        rows = _token_rows(window.tokens) if window.tokens else np.zeros((0, 4), np.int64)
+        self.append_rows(window.index, window.start_sample, window.end_sample, rows)
+
+    def append_rows(self, index: int, start_sample: int, end_sample: int, rows: np.ndarray) -> None:
+        win = np.array([index, start_sample, end_sample], dtype=np.int64)
+        rows = np.ascontiguousarray(rows, dtype=np.int64).reshape(-1, 4)
+        self._call("pk_stitch_append", self._h, _vp(win), _vp(rows), rows.shape[0])
+
+    def append_tdt(self, plan: WindowPlan, token_ids, frames, durations) -> None:
+        """Globalizes one window's decoder output (token ids, window-local
+        encoder frames, durations) and appends it."""
+        win = np.array([plan.index, plan.emission_start_sample, plan.emission_end_sample,
+                        plan.timestamp_offset_sample], dtype=np.int64)
+        arrs = [np.ascontiguousarray(a, dtype=np.int32) for a in (token_ids, frames, durations)]
+        self._call("pk_stitch_append_tdt", self._h, _vp(win), *[_vp(a) for a in arrs], arrs[0].shape[0])
+
+    def extend(self, part: "PartialStitch") -> None:
+        """IncrementalStitchAccumulator.extend: splices a run merged on its
+        own (on another rank) in at its first seam where that is exact."""
+        meta = np.ascontiguousarray(part.window_meta, dtype=np.int64)
+        raw = np.ascontiguousarray(part.window_tokens, dtype=np.int64)
+        merged = np.ascontiguousarray(part.tokens, dtype=np.int64)
+        trace = _trace_rows(part.trace)
+        run = _lib.StitchRun(_vp(meta), meta.shape[0], _vp(raw), _vp(merged), merged.shape[0], _vp(trace),
+                             trace.shape[0], int(part.guard), int(bool(part.local_ok)))
+        self._call("pk_stitch_extend", self._h, ctypes.byref(run))
+
+    def counts(self) -> tuple:
+        c = np.zeros(4, np.int64)
+        self._call("pk_stitch_counts", self._h, _vp(c))
+        return tuple(int(v) for v in c)
+
+    def _read(self, clamp: bool):
+        n, t, _, _ = self.counts()
+        tokens = np.zeros((n, 4), np.int64)
+        trace = np.zeros((t, 5), np.int64)
+        self._call("pk_stitch_read", self._h, int(clamp), _vp(tokens), _vp(trace))
+        return tokens, trace
+
+    def snapshot(self) -> StitchedTokenArrays:
+        return StitchedTokenArrays(*self._read(True))
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            _lib.load().pk_stitch_destroy(self._h)
+            self._h = None
+
+    def __del__(self):  # pragma: no cover - best effort
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class NativePartialStitchBuilder:
+    """PartialStitchBuilder on the native merge (no word pieces): windows are
+    appended in order and ``finish`` packs the run with its splice
+    conditions."""
+
+    def __init__(self):
+        self._acc = NativeStitchAccumulator(collect_trace=True, record_run=True)
+
+    def append(self, window: DecodedTokenWindow) -> None:
+        self._acc.append(window)
+
+    def append_tdt(self, plan: WindowPlan, token_ids, frames, durations) -> None:
+        self._acc.append_tdt(plan, token_ids, frames, durations)
+
+    def finish(self) -> "PartialStitch":
+        merged, trace = self._acc._read(False)
+        _, _, windows, raw_count = self._acc.counts()
+        meta = np.zeros((windows, 4), np.int64)
+        raw = np.zeros((raw_count, 4), np.int64)
+        cond = np.zeros(2, np.int64)
+        self._acc._call("pk_stitch_read_run", self._acc._h, _vp(meta), _vp(raw), _vp(cond))
+        self._acc.close()
+        return PartialStitch(meta, raw, merged, _trace_records(trace), int(cond[0]), bool(cond[1]))
+
+
+# Flat int64 form of a rank's result, for a gather of plain arrays:
+# ok:    [0, windows, raw tokens, merged tokens, trace entries, guard, local_ok]
+#        + window_meta + window_tokens + tokens + trace (row-major);
+# error: [1, message bytes] + the UTF-8 message, zero-padded to 8 bytes.
+def pack_partial(part: "PartialStitch") -> np.ndarray:
+    trace = _trace_rows(part.trace)
+    head = np.array([0, part.window_meta.shape[0], part.window_tokens.shape[0], part.tokens.shape[0],
+                     trace.shape[0], part.guard, int(part.local_ok)], dtype=np.int64)
+    return np.concatenate([head, np.asarray(part.window_meta, np.int64).ravel(),
+                           np.asarray(part.window_tokens, np.int64).ravel(),
+                           np.asarray(part.tokens, np.int64).ravel(), trace.ravel()])
+
+
+def pack_error(message: str) -> np.ndarray:
+    raw = message.encode()
+    padded = raw + b"\0" * (-len(raw) % 8)
+    return np.concatenate([np.array([1, len(raw)], np.int64), np.frombuffer(padded, dtype=np.int64)])
+
+
+def unpack_partial(flat: np.ndarray):
+    """("ok", PartialStitch) or ("error", message) from pack_partial / pack_error."""
+    flat = np.asarray(flat, dtype=np.int64)
+    if int(flat[0]) == 1:
+        n = int(flat[1])
+        return "error", flat[2:].tobytes()[:n].decode(errors="replace")
+    w, nw, n, t, guard, ok = (int(v) for v in flat[1:7])
+    sizes = (4 * w, 4 * nw, 4 * n, 5 * t)
+    parts, off = [], 7
+    for size in sizes:
+        parts.append(flat[off:off + size])
+        off += size
+    meta, raw, merged, trace = (p.reshape(-1, c) for p, c in zip(parts, (4, 4, 4, 5)))
+    return "ok", PartialStitch(meta, raw, merged, _trace_records(trace), guard, bool(ok))

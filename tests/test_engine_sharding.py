@@ -19,11 +19,15 @@ class FakeEngine:
     def __init__(self, pk):
         self.pk = pk
 
-    def decode_plans(self, pcm, plans, stream=None, on_window=None):
+    def decode_plans(self, pcm, plans, stream=None, on_window=None, on_tdt=None):
         st = self.pk.stitch
         out = []
         for p in plans:
-            toks = [st.EmittedToken(100 + p.index, 5, 1), st.EmittedToken(7, 150, 2), st.EmittedToken(8, 170, 1)]
+            ids, frames, durs = np.array([100 + p.index, 7, 8]), np.array([5, 150, 170]), np.array([1, 2, 1])
+            if on_tdt is not None:
+                on_tdt(p, ids, frames, durs)
+                continue
+            toks = [st.EmittedToken(int(a), int(f), int(d)) for a, f, d in zip(ids, frames, durs)]
             g = st.globalize_tdt_tokens(toks, p)
             out.append(st.DecodedTokenWindow(p.index, p.emission_start_sample, p.emission_end_sample, tuple(g)))
             if on_window is not None:
@@ -43,13 +47,10 @@ def _rank(rank, world, port, result_path):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     pk = __graft_entry__.load()
     pcm = np.zeros(16_000 * 100, np.float32)
-
-    def gather(obj):
-        parts = [None] * world if rank == 0 else None
-        dist.gather_object(obj, parts, dst=0)
-        return parts
-
-    res = pk.engine.transcribe_sharded(FakeEngine(pk), pcm, rank, world, gather)
+    timings = {}
+    res = pk.engine.transcribe_sharded(FakeEngine(pk), pcm, rank, world, pk.engine.array_gather(rank, world),
+                                       timings=timings)
+    assert set(timings) == {"decode_s", "gather_s", "merge_s"}
     if rank == 0:
         with open(result_path, "w") as f:
             f.write(repr([(t.token_id, t.start_sample) for t in res.tokens]))
@@ -79,7 +80,7 @@ def test_two_rank_merge_equals_single_rank(pk, tmp_path):
 class FailingEngine(FakeEngine):
     """decode_plans that fails the way a bounded device wait reports it."""
 
-    def decode_plans(self, pcm, plans, stream=None, on_window=None):
+    def decode_plans(self, pcm, plans, stream=None, on_window=None, on_tdt=None):
         raise self.pk.PkError(-7, "injected: a bounded device wait expired (status bits 0x1)")
 
 
@@ -100,14 +101,9 @@ def _failing_rank(rank, world, port, out_dir, mode):
         outcome = "left"  # leaves between steps: nothing of this rank is in flight
     else:
         engine = FailingEngine(pk) if (mode == "raises" and rank == 1) else FakeEngine(pk)
-
-        def gather(obj):
-            parts = [None] * world if rank == 0 else None
-            dist.gather_object(obj, parts, dst=0)
-            return parts
-
         try:
-            pk.engine.transcribe_sharded(engine, np.zeros(16_000 * 100, np.float32), rank, world, gather)
+            pk.engine.transcribe_sharded(engine, np.zeros(16_000 * 100, np.float32), rank, world,
+                                         pk.engine.array_gather(rank, world))
         except Exception as exc:  # recorded for the test
             outcome = f"{type(exc).__name__}|{exc}"
     with open(os.path.join(out_dir, f"rank{rank}.txt"), "w") as f:
@@ -176,3 +172,28 @@ def test_decode_into_streams_in_merge_order(pk):
         assert seen == sorted(seen)
         got = acc.snapshot()
         assert got.tokens == expect.tokens and got.trace == expect.trace
+
+
+def test_decode_into_native_sink_equals_python_merge(pk):
+    """The native accumulator fed the decoder's arrays (on_tdt) merges as the
+    Python accumulator fed globalized windows, in and out of plan order."""
+    pcm = np.zeros(16_000 * 100, np.float32)
+    plans = pk.windows.plan_stateless_windows(len(pcm))
+    fake = FakeEngine(pk)
+    expect = pk.stitch.stitch_token_windows(fake.decode_plans(pcm, plans))
+    for order in (plans, list(reversed(plans))):
+        acc = pk.stitch.NativeStitchAccumulator(collect_trace=True)
+        pk.engine._decode_into(fake, pcm, order, acc)
+        assert acc.snapshot() == expect
+
+
+def test_batches_are_balanced(pk):
+    eng = object.__new__(pk.engine.ParakeetEngine)
+    eng.capacity = 32
+    assert [len(r) for r in eng.batches(35)] == [18, 17]
+    assert [len(r) for r in eng.batches(280)] == [31, 31, 31, 31, 32, 31, 31, 31, 31]
+    assert [len(r) for r in eng.batches(32)] == [32]
+    assert eng.batches(0) == []
+    eng.capacity = 40
+    assert [len(r) for r in eng.batches(35)] == [35]
+    assert [len(r) for r in eng.batches(280)] == [40] * 7
