@@ -330,6 +330,16 @@ int pk_stitch_read_run(const pk_stitch* stitch, int64_t* window_meta, int64_t* w
  * rounded to f16): the reference's own accumulation
  * (src/webgpu/kernels/gemm.ts:1445-1502), for parity runs only. */
 int pk_debug_set_gemm_route(int route);
+/* Test hook (no reference counterpart): while enabled, every FP16 operator --
+ * GEMM, LayerNorm, attention, conformer conv, subsampling -- and the encoder
+ * graphs recorded afterwards run CUDA-core kernels that replay the reference
+ * shaders' arithmetic step by step: f16 accumulation in increasing K in the
+ * GEMMs (gemm.ts:1445-1502), sequential f32 reductions (layernorm.ts:344-387,
+ * attention.ts:485-727), the conv and subsampling fma chains
+ * (conformer-conv.ts:505-574, subsampling.ts:1115-1372), every product and sum
+ * rounded as written and exp taken as the correctly rounded f32 value.  For
+ * parity runs against the CPU restatement; slow. */
+int pk_debug_set_reference_arithmetic(int enable);
 /* Test hook (no reference counterpart): forces the tensor-core GEMM token
  * tile for later launches in this process.  0 = automatic (cost model),
  * 128 / 192 / 256 = single-CTA tile, -256 / -384 / -512 = CTA-pair tile

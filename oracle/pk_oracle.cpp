@@ -144,11 +144,16 @@ void or_palette_expand(const uint32_t* codes, const void* palette, int prec, int
 // act: 0 none, 1 SiLU v/(1+exp(-clamp(v,-20,20))), 2 ReLU max(v,0).
 // Residual: value = residual + scale * value (bias and residual exclusive).
 // ---------------------------------------------------------------------------
+// The shaders' f32 exp is backend-defined to a few ulp; this restatement
+// uses the correctly rounded f32 value (the double-precision exp rounded
+// once), as the CUDA reference-arithmetic kernels do.
+static inline float exp_f32(float x) { return (float)std::exp((double)x); }
+
 static inline float epilogue(float v, const float* bias, int64_t n, int act) {
   if (bias) v += bias[n];
   if (act == 1) {
     const float b = std::min(std::max(v, -20.0f), 20.0f);
-    v = v / (1.0f + std::exp(-b));
+    v = v / (1.0f + exp_f32(-b));
   } else if (act == 2) {
     v = std::max(v, 0.0f);
   }
@@ -292,7 +297,7 @@ void or_rel_attention(int prec, int64_t batch, int64_t frames, const void* qkv,
         }
         float sum = 0.0f;
         for (int64_t j = 0; j < valid; ++j) {
-          sc[j] = std::exp(sc[j] - mx);
+          sc[j] = exp_f32(sc[j] - mx);
           sum += sc[j];
         }
         const float inv = 1.0f / sum;
@@ -317,7 +322,7 @@ void or_rel_attention(int prec, int64_t batch, int64_t frames, const void* qkv,
 // ---------------------------------------------------------------------------
 static inline float sigmoid_clamped(float v) {
   const float b = std::min(std::max(v, -20.0f), 20.0f);
-  return 1.0f / (1.0f + std::exp(-b));
+  return 1.0f / (1.0f + exp_f32(-b));
 }
 
 void or_conformer_conv(int prec, int64_t batch, int64_t frames, const void* pointwise,

@@ -34,6 +34,7 @@ EXPORTED = (
     "pk_debug_set_gemm_tile", "pk_debug_set_attention_route", "pk_debug_set_decoder_route",
     "pk_debug_wait_probe", "pk_stitch_create", "pk_stitch_destroy", "pk_stitch_append", "pk_stitch_append_tdt",
     "pk_stitch_extend", "pk_stitch_counts", "pk_stitch_read", "pk_stitch_read_run",
+    "pk_debug_set_reference_arithmetic",
 )
 STITCH_COLLECT_TRACE, STITCH_RECORD_RUN = 1, 2
 
@@ -133,6 +134,7 @@ def load() -> ctypes.CDLL:
             "pk_encoder_destroy": [vp],
             "pk_debug_set_gemm_route": [i32],
             "pk_debug_set_gemm_tile": [i32],
+            "pk_debug_set_reference_arithmetic": [i32],
             "pk_debug_set_attention_route": [i32],
             "pk_debug_set_decoder_route": [i32],
             "pk_debug_wait_probe": [vp, i32, ctypes.c_uint32, vp],

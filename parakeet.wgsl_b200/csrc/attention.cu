@@ -142,6 +142,8 @@ int launch_rel_attention(const DeviceCtx& dev, int precision, int batch, int fra
                          const void* positions, const float* bias_u, const float* bias_v,
                          const uint32_t* valid_lengths, void* context, cudaStream_t stream,
                          const void* positions_rowmajor) {
+  if (precision == PK_FP16 && g_reference_arith)
+    return launch_ref_attention(batch, frames, qkv, positions, bias_u, bias_v, valid_lengths, context, stream);
   if (precision == PK_FP16 && g_attention_route == 3)
     return launch_rel_attention_umma(dev, batch, frames, qkv, positions, bias_u, bias_v, valid_lengths, context,
                                      stream);

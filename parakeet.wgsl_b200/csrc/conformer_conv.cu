@@ -174,6 +174,8 @@ __global__ void __launch_bounds__(CONV_THREADS, 2) conformer_conv_kernel(
 int launch_conformer_conv(int precision, int batch, int frames, const void* pointwise, const void* dw,
                           const float* scale, const float* shift, const uint32_t* valid_lengths, void* out,
                           cudaStream_t stream) {
+  if (precision == PK_FP16 && g_reference_arith)
+    return launch_ref_conformer_conv(batch, frames, pointwise, dw, scale, shift, valid_lengths, out, stream);
   const dim3 grid(CONV_C / CONV_TC, (frames + CONV_TF - 1) / CONV_TF, batch);
   if (precision == PK_FP16)
     launch_kernel(conformer_conv_kernel<__half>, grid, CONV_THREADS, CONV_SMEM, stream, 

@@ -8,11 +8,14 @@
 // oracle's FP32 mode.  Weights are decoded from their packed codes straight
 // into shared memory per K-tile (never expanded to HBM).
 //
-// Reference-algorithm route (pk_debug_set_gemm_route(5), FP16 only): the
-// accumulator is rounded to f16 after every fma, in increasing k -- the
+// Reference-algorithm route (pk_debug_set_gemm_route(5) or
+// pk_debug_set_reference_arithmetic, FP16 only): the accumulator is rounded
+// to f16 after every fma, in increasing k -- the
 // f16 vec4 accumulators of f16SubgroupGemmWgsl / f16PortableGemmWgsl
 // (gemm.ts:1445-1502), each step taken as an f32 fma then one rounding to
-// f16, as the CPU restatement states it.  A parity route, not a fast path.
+// f16, as the CPU restatement states it; the epilogue rounds each step as
+// written, with the correctly rounded f32 exp.  A parity route, not a fast
+// path.
 #include <algorithm>
 
 #include "pk_common.cuh"
@@ -116,11 +119,22 @@ __global__ void __launch_bounds__(SG_THREADS) simt_palette_gemm_kernel(
       const int n = n0 + tx * 8 + j;
       if (n >= columns) continue;
       float v = acc[i][j];
-      if (bias) v += bias[n];
-      if (act == PK_ACT_SILU) v = silu_ref(v);
-      else if (act == PK_ACT_RELU) v = fmaxf(v, 0.0f);
       const size_t idx = (size_t)m * columns + n;
-      if (has_residual) v = to_f<T>(residual[idx]) + res_scale * v;
+      if constexpr (ACC16) {  // the reference epilogue, each step rounded as written
+        if (bias) v = __fadd_rn(v, bias[n]);
+        if (act == PK_ACT_SILU) {
+          const float b = fminf(fmaxf(v, -20.0f), 20.0f);
+          v = __fdiv_rn(v, __fadd_rn(1.0f, __double2float_rn(exp(-(double)b))));
+        } else if (act == PK_ACT_RELU) {
+          v = fmaxf(v, 0.0f);
+        }
+        if (has_residual) v = __fadd_rn(to_f<T>(residual[idx]), __fmul_rn(res_scale, v));
+      } else {
+        if (bias) v += bias[n];
+        if (act == PK_ACT_SILU) v = silu_ref(v);
+        else if (act == PK_ACT_RELU) v = fmaxf(v, 0.0f);
+        if (has_residual) v = to_f<T>(residual[idx]) + res_scale * v;
+      }
       out[idx] = from_f<T>(v);
     }
   }
@@ -149,7 +163,7 @@ int launch_gemm_simt(const DeviceCtx& dev, const GemmArgs& g, cudaStream_t strea
     auto* pal = static_cast<const __half*>(g.palette);
     auto* res = static_cast<const __half*>(g.residual);
     auto* c = static_cast<__half*>(g.c);
-    const bool acc16 = g_gemm_route == 5;
+    const bool acc16 = gemm_acc16();
     auto kernel = g.bits == 5 ? (acc16 ? simt_palette_gemm_kernel<__half, 5, true> : simt_palette_gemm_kernel<__half, 5>)
                               : (acc16 ? simt_palette_gemm_kernel<__half, 6, true> : simt_palette_gemm_kernel<__half, 6>);
     launch_kernel(kernel, grid, SG_THREADS, 0, stream, a, g.codes, pal, g.bias, res, c, rows, inner, columns,

@@ -251,6 +251,8 @@ __global__ void __launch_bounds__(256) layernorm_generic_kernel(const T* __restr
 
 int launch_layernorm(int precision, int64_t rows, int64_t channels, const void* x, const float* gamma,
                      const float* beta, float eps, void* y, cudaStream_t stream) {
+  if (precision == PK_FP16 && g_reference_arith)
+    return launch_ref_layernorm(rows, channels, x, gamma, beta, eps, y, stream);
   const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0;
   const bool params_aligned = ((reinterpret_cast<uintptr_t>(gamma) | reinterpret_cast<uintptr_t>(beta)) & 15) == 0;
   if (channels == 1024 && aligned && params_aligned) {
@@ -274,6 +276,10 @@ int launch_layernorm(int precision, int64_t rows, int64_t channels, const void* 
 
 int launch_layernorm_dual(int precision, int64_t rows, const void* x, const float* g1, const float* b1,
                           const float* g2, const float* b2, float eps, void* y1, void* y2, cudaStream_t stream) {
+  if (precision == PK_FP16 && g_reference_arith) {
+    const int st = launch_ref_layernorm(rows, 1024, x, g1, b1, eps, y1, stream);
+    return st != PK_OK ? st : launch_ref_layernorm(rows, 1024, y1, g2, b2, eps, y2, stream);
+  }
   const uintptr_t any = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y1) |
                         reinterpret_cast<uintptr_t>(y2) | reinterpret_cast<uintptr_t>(g1) |
                         reinterpret_cast<uintptr_t>(b1) | reinterpret_cast<uintptr_t>(g2) |

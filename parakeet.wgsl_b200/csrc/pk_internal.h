@@ -125,7 +125,22 @@ int launch_logmel(int batch, int sample_count, const float* samples, const uint3
 // tensor cores with single-CTA / CTA-pair tiles, 5 = the SIMT GEMM with FP16
 // accumulating in f16 (the reference's algorithm, for parity runs).
 extern int g_gemm_route;
-inline bool gemm_route_simt() { return g_gemm_route == 1 || g_gemm_route == 5; }
+// Parity knob (pk_debug_set_reference_arithmetic): FP16 operators replay the
+// reference shaders' arithmetic on the CUDA cores (reference_arith.cu).
+extern int g_reference_arith;
+inline bool gemm_route_simt() { return g_gemm_route == 1 || g_gemm_route == 5 || g_reference_arith; }
+inline bool gemm_acc16() { return g_gemm_route == 5 || g_reference_arith; }
+int launch_ref_layernorm(int64_t rows, int64_t channels, const void* x, const float* gamma, const float* beta,
+                         float eps, void* y, cudaStream_t stream);
+int launch_ref_attention(int batch, int frames, const void* qkv, const void* positions, const float* bias_u,
+                         const float* bias_v, const uint32_t* valid_lengths, void* context, cudaStream_t stream);
+int launch_ref_conformer_conv(int batch, int frames, const void* pointwise, const void* dw, const float* scale,
+                              const float* shift, const uint32_t* valid_lengths, void* out, cudaStream_t stream);
+int launch_ref_conv0_dw2(int batch, const float* features, const void* conv0_w, const float* conv0_b,
+                         const void* dw_w, const float* dw_b, const uint32_t* feature_lengths, void* out,
+                         cudaStream_t stream);
+int launch_ref_depthwise(int batch, int ih, int iw, int channels, const void* input, const void* w, const float* b,
+                         const uint32_t* feature_lengths, int steps, void* out, cudaStream_t stream);
 extern int g_gemm_tile;
 // Debug / test knob: 0 = automatic (FP16: the tcgen05 kernel when row-major
 // positions are at hand, else the mma.sync kernel), 1 = CUDA-core attention,

@@ -489,6 +489,8 @@ __global__ void time_mask_kernel(T* __restrict__ values, const uint32_t* __restr
 int launch_subsampling_conv0_dw2(int precision, int batch, const float* features, const void* conv0_w,
                                  const float* conv0_b, const void* dw_w, const float* dw_b,
                                  const uint32_t* feature_lengths, void* out, cudaStream_t stream) {
+  if (precision == PK_FP16 && g_reference_arith)
+    return launch_ref_conv0_dw2(batch, features, conv0_w, conv0_b, dw_w, dw_b, feature_lengths, out, stream);
   const dim3 grid(SUB_C / C0_CG, C0_STRIPS, batch);
   if (precision == PK_FP16) {
     int st = set_max_dynamic_smem(reinterpret_cast<const void*>(conv0_dw2_f16_kernel), C0H_SMEM);
@@ -507,6 +509,8 @@ int launch_subsampling_conv0_dw2(int precision, int batch, const float* features
 int launch_subsampling_depthwise(int precision, int batch, int ih, int iw, int channels, const void* input,
                                  const void* w, const float* b, const uint32_t* feature_lengths, int steps,
                                  void* out, cudaStream_t stream) {
+  if (precision == PK_FP16 && g_reference_arith)
+    return launch_ref_depthwise(batch, ih, iw, channels, input, w, b, feature_lengths, steps, out, stream);
   if (channels % 8 != 0) return set_error(PK_E_SHAPE, "depthwise subsampling needs channels %% 8 == 0");
   const int oh = (ih - 1) / 2 + 1, ow = (iw - 1) / 2 + 1;
   const int64_t total = (int64_t)batch * oh * ow * (channels / 8);

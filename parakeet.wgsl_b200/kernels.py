@@ -666,6 +666,14 @@ def set_gemm_route(route: str) -> None:
     _lib.call("pk_debug_set_gemm_route", routes[route])
 
 
+def set_reference_arithmetic(enable: bool) -> None:
+    """Test hook: FP16 operators (and encoder graphs recorded while it is on)
+    replay the reference shaders' arithmetic on the CUDA cores -- f16 GEMM
+    accumulation, sequential f32 reductions, correctly rounded exp -- for
+    value-by-value comparison with the CPU restatement's reference mode."""
+    _lib.call("pk_debug_set_reference_arithmetic", int(bool(enable)))
+
+
 def set_gemm_tile(tile: int) -> None:
     """Test hook: force the tensor-core GEMM token tile (0 = automatic;
     128/192/256 single-CTA; -256/-384/-512 CTA pair)."""
