@@ -354,7 +354,7 @@ int pk_debug_set_attention_route(int route);
 
 /* Test hook (no reference counterpart): selects the TDT decoder kernel for
  * later pk_tdt_decode calls in this process.  0 = automatic (the resident
- * kernel -- FP16, at most 32 windows, weights held across 128 co-resident
+ * kernel -- FP16, at most 40 windows, weights held across 128 co-resident
  * CTAs -- where it applies, else the cluster-per-window kernel), 1 = the
  * cluster kernel only, 2 = the resident kernel only (PK_E_SHAPE where it does
  * not apply). */

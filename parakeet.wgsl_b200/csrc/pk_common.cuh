@@ -109,15 +109,18 @@ __device__ __forceinline__ uint32_t ld_acquire_u32(const unsigned int* p) {
 // barrier's generation).  Bounded: after `limit_ns`, or once any CTA has
 // raised *abort_flag, it stops waiting; on expiry it raises *abort_flag (later
 // barriers then no longer wait) and ORs `bit` into the status word.  Returns
-// whether every CTA arrived.
+// whether every CTA arrived.  The arrival is a release reduction (the CTA's
+// writes, ordered before it by the caller's __syncthreads, become visible
+// with it); the wait polls the counter alone and reads the abort flag and
+// the clock only every 16th poll, so a poll costs one L2 round trip.
 __device__ __forceinline__ bool grid_arrive_wait(unsigned int* ctr, volatile unsigned int* abort_flag,
                                                  unsigned int target, unsigned int* status, unsigned int bit,
                                                  uint64_t limit_ns) {
-  __threadfence();
-  atomicAdd(ctr, 1u);
+  asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
   const uint64_t t0 = global_timer_ns();
   bool ok = true;
-  while (ld_acquire_u32(ctr) < target) {
+  for (uint32_t polls = 1; ld_acquire_u32(ctr) < target; ++polls) {
+    if ((polls & 15u) != 0u) continue;
     if (*abort_flag) {
       ok = false;
       break;
@@ -128,7 +131,6 @@ __device__ __forceinline__ bool grid_arrive_wait(unsigned int* ctr, volatile uns
       ok = false;
       break;
     }
-    __nanosleep(64);
   }
   __threadfence();
   return ok;

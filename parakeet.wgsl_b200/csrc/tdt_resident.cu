@@ -1,5 +1,6 @@
 // tdt_resident.cu -- the greedy TDT decoder with its FP16 weights resident on
-// chip, all windows in lockstep (up to 32 windows per launch).
+// chip, all windows in lockstep (up to 40 windows per launch, the reference's
+// batch capacity, src/webgpu/encoder.ts:68).
 //
 // The cluster-per-window decoder (tdt_decoder.cu) re-streams every LSTM
 // weight for every emitted token of every window, which bounds it by L2->SM
@@ -17,6 +18,13 @@
 // then the joint of the active windows (1 barrier); argmax partials of all
 // CTAs are reduced by every CTA, so all take the same decisions and run the
 // same number of barriers.
+//
+// Shared memory holds the weight slices (~131 KB) and one half of a phase's
+// inputs at a time: the 1280 LSTM inputs, the 640 projector inputs and the
+// 640 joint inputs are staged in two halves, and the chains -- whose order is
+// fixed -- carry their accumulators in registers across the halves.  Chain
+// threads prefetch the next chunk of operands while they compute the current
+// one.
 //
 // Two windows share each HFMA2 (one per half2 lane), so every lane computes
 // exactly the per-window chain the shader does: two f16 FMA chains per gate
@@ -44,34 +52,42 @@ constexpr int RCH = RH / RG;          // 5 LSTM channels per CTA
 constexpr int RGATES = 4 * RCH;       // 20 gate outputs per CTA
 constexpr int RTOK = 1024 / RG;       // 8 token columns per CTA
 constexpr int RHEADCOLS = 16;         // token columns + the tail slot
-constexpr int RMAXB = 32;             // windows per launch
+constexpr int RMAXB = 40;             // windows per launch
 constexpr int RPAIRS = RMAXB / 2;     // window pairs (half2 lanes)
-constexpr int RLSTM_GROUPS = 4;       // groups of 4 window pairs
-constexpr int RLSTM_THREADS = 2 * RGATES * RLSTM_GROUPS;  // (output, parity) x group
+constexpr int RHALF = RH / 2;         // joint / projector inputs per staged half
+constexpr int RLSTM_PAIRS = 2;        // window pairs per LSTM chain thread
+constexpr int RLSTM_GROUPS = RPAIRS / RLSTM_PAIRS;       // 10
+constexpr int RLSTM_THREADS = 2 * RGATES * RLSTM_GROUPS;  // (output, parity) x group: 400
 constexpr int RW_STRIDE = RKIN + 8;   // padded weight row (halfs): rows start 16 bytes apart in the banks
-constexpr int RHEAD_THREADS = RHEADCOLS * RPAIRS;        // column x window pair
-constexpr int RCHUNK = 8;             // chain steps whose operands a thread loads before chaining them
+constexpr int RHW_STRIDE = RH + 8;    // padded head row: the 16 columns' loads spread over the banks
+constexpr int RHEAD_THREADS = RHEADCOLS * RPAIRS;        // column x window pair: 320
+constexpr int RPROJ_THREADS = RCH * RMAXB;               // output x window: 200
+constexpr int RCHUNK = 8;             // chain steps per operand load
 constexpr int RTHREADS = 640;
+constexpr int RROW16 = RMAXB * 2 / 16;  // 16-byte chunks per exchanged f16 row (one value per window)
 constexpr float RNEG = -3.402823466e+38f;
 static_assert(RG * RCH == RH && RG * RTOK == 1024, "slices tile the matrices");
-static_assert(RTHREADS == RMAXB * 20 && RTHREADS == RH, "one thread per (window, partial slot) and per input");
-static_assert(RH % (2 * RCHUNK) == 0, "chunks never straddle the input halves");
+static_assert(RTHREADS == RH, "one thread per joint input");
+static_assert(RLSTM_THREADS <= RTHREADS && RHEAD_THREADS % 32 == 0 && RHEAD_THREADS <= RTHREADS, "thread roles fit");
+static_assert((RMAXB * 2) % 16 == 0, "exchanged f16 rows are whole 16-byte chunks");
+static_assert(RH % (2 * RCHUNK) == 0 && RHALF % RCHUNK == 0, "chunks never straddle a staged half");
 
 // Exchange area (bytes from DeviceCtx::tdt_exchange).  Hidden vectors are
-// input-major with the windows fastest ([640][32]), so a CTA stages a phase's
+// input-major with the windows fastest ([640][40]), so a CTA stages a phase's
 // inputs for all windows as plain row copies.  Each LSTM layer writes its new
 // hidden slice to the *N array (read by the next layer / the projector) and
 // commits it to the current array one barrier later, when every CTA has
 // finished reading the old values.
-constexpr size_t XH0 = 0;                                 // __half [640][32]: layer-0 hidden (current)
-constexpr size_t XH0N = XH0 + 1ull * RH * RMAXB * 2;      // __half [640][32]: layer-0 hidden (this update)
-constexpr size_t XH1 = XH0N + 1ull * RH * RMAXB * 2;      // __half [640][32]: layer-1 hidden (current)
-constexpr size_t XH1N = XH1 + 1ull * RH * RMAXB * 2;      // __half [640][32]: layer-1 hidden (this update)
-constexpr size_t XH1F = XH1N + 1ull * RH * RMAXB * 2;     // float [640][32]: layer-1 hidden for the projector
-constexpr size_t XPROJ = XH1F + 1ull * RH * RMAXB * 4;    // float [32][640]: predictor projection
-constexpr size_t XPART = XPROJ + 1ull * RMAXB * RH * 4;   // RPartial [2][32][128]: argmax partials
+constexpr size_t XH0 = 0;                                 // __half [640][40]: layer-0 hidden (current)
+constexpr size_t XH0N = XH0 + 1ull * RH * RMAXB * 2;      // __half [640][40]: layer-0 hidden (this update)
+constexpr size_t XH1 = XH0N + 1ull * RH * RMAXB * 2;      // __half [640][40]: layer-1 hidden (current)
+constexpr size_t XH1N = XH1 + 1ull * RH * RMAXB * 2;      // __half [640][40]: layer-1 hidden (this update)
+constexpr size_t XH1F = XH1N + 1ull * RH * RMAXB * 2;     // float [640][40]: layer-1 hidden for the projector
+constexpr size_t XPROJ = XH1F + 1ull * RH * RMAXB * 4;    // float [40][640]: predictor projection
+constexpr size_t XPART = XPROJ + 1ull * RMAXB * RH * 4;   // RPartial [2][40][128]: argmax partials
 constexpr size_t XSYNC = XPART + 2ull * RMAXB * RG * 16;  // barrier counter, abort flag
 static_assert(XSYNC + 256 <= kTdtExchangeBytes, "exchange area fits");
+static_assert(XSYNC % 16 == 0, "exchange arrays stay 16-byte aligned");
 
 struct __align__(16) RPartial {
   float tv;
@@ -92,14 +108,14 @@ struct RWin {
 struct RSmem {
   __half w0[RGATES][RW_STRIDE];      // [gate output][input] (inputs fastest)
   __half w1[RGATES][RW_STRIDE];
-  __half hw[RHEADCOLS][RH];          // [head column][input]
+  __half hw[RHEADCOLS][RHW_STRIDE];  // [head column][input]
   __half pw[RH][RCH + 1];
   union {
-    __half2 x2[RKIN][RPAIRS];        // LSTM inputs, [input][window pair]
-    float hf[RH][RMAXB];             // projector inputs, [input][window]
+    __half2 x2[RH][RPAIRS];          // one half of an LSTM layer's inputs, [input][window pair]
+    float hf[RHALF][RMAXB];          // one half of the projector inputs, [input][window]
     struct {
-      uint32_t j2[RPAIRS][RH];       // joint inputs, [window pair][input] (half2 bits)
-      uint32_t keep[RPAIRS][RH];     // per pair and input: the lanes whose head chain skips it
+      uint32_t j2[RPAIRS][RHALF];    // one half of the joint inputs, [window pair][input] (half2 bits)
+      uint32_t keep[RPAIRS][RHALF];  // per pair and input: the lanes whose head chain skips it
     } jt;
     RPartial red[RMAXB][20];         // argmax reduction
   } in;
@@ -110,7 +126,7 @@ struct RSmem {
   float b0[RGATES], b1[RGATES], pb[8], hb[RHEADCOLS];
   int first_exc[RMAXB];
   RWin win[RMAXB];
-  int any_pending, any_joint;
+  int any_pending, any_token, any_joint;
   unsigned int gen;
 };
 static_assert(sizeof(RSmem) + 128 <= 232448, "resident decoder shared memory");
@@ -178,27 +194,22 @@ __device__ __forceinline__ RPartial* part_at(const RParams& p, int slot, int w, 
   return reinterpret_cast<RPartial*>(p.xchg + XPART) + ((size_t)slot * RMAXB + w) * RG + cta;
 }
 
-// Copies `rows` rows of 64 bytes (32 f16, one per window) from the exchange
-// into x2 rows [row0, row0 + rows): 16-byte loads, all issued before any store.
-__device__ void copy_rows(RSmem& s, const __half* src, int row0, int rows) {
-  const int chunks = rows * 4;  // 16-byte chunks
-  constexpr int MAXPER = (RH * 4 + RTHREADS - 1) / RTHREADS;
-  uint4 v[MAXPER];
+// Copies the 640 exchanged f16 rows at `src` (one value per window) into x2:
+// every thread issues all of its 16-byte loads before any store.
+__device__ void stage_rows(RSmem& s, const __half* src) {
+  constexpr int CHUNKS = RH * RROW16;
+  constexpr int PER = CHUNKS / RTHREADS;
+  static_assert(CHUNKS % RTHREADS == 0, "whole chunks per thread");
+  uint4 v[PER];
 #pragma unroll
-  for (int j = 0; j < MAXPER; ++j) {
-    const int i = threadIdx.x + j * RTHREADS;
-    if (i < chunks) v[j] = __ldcg(reinterpret_cast<const uint4*>(src) + i);
-  }
+  for (int j = 0; j < PER; ++j) v[j] = __ldcg(reinterpret_cast<const uint4*>(src) + threadIdx.x + j * RTHREADS);
 #pragma unroll
-  for (int j = 0; j < MAXPER; ++j) {
-    const int i = threadIdx.x + j * RTHREADS;
-    if (i < chunks) reinterpret_cast<uint4*>(&s.in.x2[row0][0])[i] = v[j];
-  }
+  for (int j = 0; j < PER; ++j) reinterpret_cast<uint4*>(&s.in.x2[0][0])[threadIdx.x + j * RTHREADS] = v[j];
 }
 
-// The embedding rows of the windows updating with a token, into x2 rows
-// [0, 640); lane = window (8 halfs per 16-byte load), so a warp's half-word
-// stores land in adjacent words.
+// The embedding rows of the windows updating with a token, into x2; lane =
+// window (8 halfs per 16-byte load), so a warp's half-word stores land in
+// adjacent words.
 __device__ void stage_embeddings(RSmem& s, const RParams& p) {
   constexpr int PER = RMAXB * RH / 8 / RTHREADS;
   static_assert(RMAXB * RH / 8 % RTHREADS == 0, "whole chunks per thread");
@@ -219,68 +230,110 @@ __device__ void stage_embeddings(RSmem& s, const RParams& p) {
   }
 }
 
+// One staged half (640 inputs) of this thread's gate chains: gate output of
+// `wrow` (its 640 weights of this half, both parities interleaved), parity
+// `par`, window pairs 2 g and 2 g + 1.  Operands of the next 16 inputs load
+// while the current 16 are chained.  REC: lanes in `keep` leave their
+// accumulator as it was (start-of-sequence windows skip the recurrent half).
+template <bool REC>
+__device__ __forceinline__ void lstm_chain_half(const RSmem& s, const __half* wrow, int g, int par,
+                                                const uint32_t (&keep)[RLSTM_PAIRS], __half2 (&acc)[RLSTM_PAIRS]) {
+  uint4 wa = *reinterpret_cast<const uint4*>(wrow), wb = *reinterpret_cast<const uint4*>(wrow + 8);
+  uint2 xv[RCHUNK];
+#pragma unroll
+  for (int j = 0; j < RCHUNK; ++j) xv[j] = *reinterpret_cast<const uint2*>(&s.in.x2[2 * j + par][2 * g]);
+#pragma unroll 1
+  for (int k0 = 0; k0 < RH; k0 += 2 * RCHUNK) {
+    // Word j holds the weights of inputs k0 + 2j (low half) and k0 + 2j + 1 (high half).
+    const uint32_t ww[RCHUNK] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+    uint2 cx[RCHUNK];
+#pragma unroll
+    for (int j = 0; j < RCHUNK; ++j) cx[j] = xv[j];
+    if (k0 + 2 * RCHUNK < RH) {
+      const int k1 = k0 + 2 * RCHUNK;
+      wa = *reinterpret_cast<const uint4*>(wrow + k1);
+      wb = *reinterpret_cast<const uint4*>(wrow + k1 + 8);
+#pragma unroll
+      for (int j = 0; j < RCHUNK; ++j) xv[j] = *reinterpret_cast<const uint2*>(&s.in.x2[k1 + 2 * j + par][2 * g]);
+    }
+#pragma unroll
+    for (int j = 0; j < RCHUNK; ++j) {
+      const __half2 wv = __half2half2(__ushort_as_half((unsigned short)(par ? ww[j] >> 16 : ww[j] & 0xffffu)));
+      const uint32_t xs[RLSTM_PAIRS] = {cx[j].x, cx[j].y};
+#pragma unroll
+      for (int i = 0; i < RLSTM_PAIRS; ++i) {
+        if constexpr (REC)
+          acc[i] = keep_mask(acc[i], __hfma2(bits_h2(xs[i]), wv, acc[i]), keep[i]);
+        else
+          acc[i] = __hfma2(bits_h2(xs[i]), wv, acc[i]);
+      }
+    }
+  }
+}
+
 // Gate chains of one LSTM layer for the windows that need them; gates land in
 // s.gates[window][gate * 5 + channel].  Thread: (output o, parity) x group of
-// 2 window pairs.  layer1: start-of-sequence windows stop at input 640 (their
-// recurrent input is zero and the shader does not run those steps); lanes of
-// windows that do not update compute values nobody reads.
-__device__ void lstm_chains(RSmem& s, const __half (*w)[RW_STRIDE], const float* bias, bool layer1) {
+// 2 window pairs.  Inputs: layer 0 [embedding(token) | h0], layer 1 [new h0 |
+// h1], staged one half at a time.  Layer 1's start-of-sequence windows stop
+// at input 640 (their recurrent input is zero and the shader does not run
+// those steps); lanes of windows that do not update compute values nobody
+// reads.
+__device__ void lstm_layer(RSmem& s, const RParams& p, bool layer1) {
   const int tid = threadIdx.x;
-  if (tid < RLSTM_THREADS) {
-    const int grp = tid / (2 * RGATES), r = tid % (2 * RGATES);
-    const int o = r >> 1, par = r & 1;
-    bool any = false, any_full = false;
-    uint32_t keep_rec[4];  // recurrent half of layer 1: start-of-sequence lanes keep their sums
+  const bool chain = tid < RLSTM_THREADS;
+  const int grp = tid / (2 * RGATES), r = tid % (2 * RGATES);
+  const int o = r >> 1, par = r & 1;
+  const __half* wrow = layer1 ? &s.w1[o][0] : &s.w0[o][0];
+  bool any = false, any_full = false;
+  uint32_t keep_rec[RLSTM_PAIRS];
+  __half2 acc[RLSTM_PAIRS];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int p0 = s.win[grp * 8 + 2 * i].pending, p1 = s.win[grp * 8 + 2 * i + 1].pending;
+  for (int i = 0; i < RLSTM_PAIRS; ++i) {
+    keep_rec[i] = 0u;
+    acc[i] = __float2half2_rn(0.0f);
+  }
+  if (chain) {
+    const __half2 init = par == 0 ? __float2half2_rn((layer1 ? s.b1 : s.b0)[o]) : __float2half2_rn(0.0f);
+#pragma unroll
+    for (int i = 0; i < RLSTM_PAIRS; ++i) {
+      const int w0 = (grp * RLSTM_PAIRS + i) * 2;
+      const int p0 = s.win[w0].pending, p1 = s.win[w0 + 1].pending;
       keep_rec[i] = lane_mask(p0 == 1, p1 == 1);
       any |= layer1 ? (p0 | p1) != 0 : (p0 == 2 || p1 == 2);
       any_full |= p0 == 2 || p1 == 2;
+      acc[i] = init;
     }
-    const __half2 init = par == 0 ? __float2half2_rn(bias[o]) : __float2half2_rn(0.0f);
-    __half2 acc[4] = {init, init, init, init};
-    if (any) {
-      const int kend = (!layer1 || any_full) ? RKIN : RH;
-      const __half* wrow = &w[o][0];
-      for (int k0 = 0; k0 < kend; k0 += 2 * RCHUNK) {
-        const bool recurrent = layer1 && k0 >= RH;
-        // 16 consecutive weights (two 16-byte loads); this thread's parity takes every other one.
-        const uint4 wa = *reinterpret_cast<const uint4*>(wrow + k0);
-        const uint4 wb = *reinterpret_cast<const uint4*>(wrow + k0 + 8);
-        // Word j holds the weights of inputs k0 + 2j (low half) and k0 + 2j + 1 (high half).
-        const uint32_t ww[RCHUNK] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
-        uint4 xv[RCHUNK];
-#pragma unroll
-        for (int j = 0; j < RCHUNK; ++j) xv[j] = *reinterpret_cast<const uint4*>(&s.in.x2[k0 + 2 * j + par][grp * 4]);
-        if (!recurrent) {  // plain chains: nothing to keep
-#pragma unroll
-          for (int j = 0; j < RCHUNK; ++j) {
-            const __half2 wv = __half2half2(__ushort_as_half((unsigned short)(par ? ww[j] >> 16 : ww[j] & 0xffffu)));
-            acc[0] = __hfma2(bits_h2(xv[j].x), wv, acc[0]);
-            acc[1] = __hfma2(bits_h2(xv[j].y), wv, acc[1]);
-            acc[2] = __hfma2(bits_h2(xv[j].z), wv, acc[2]);
-            acc[3] = __hfma2(bits_h2(xv[j].w), wv, acc[3]);
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < RCHUNK; ++j) {
-            const __half2 wv = __half2half2(__ushort_as_half((unsigned short)(par ? ww[j] >> 16 : ww[j] & 0xffffu)));
-            const uint32_t xs[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
-#pragma unroll
-            for (int i = 0; i < 4; ++i) acc[i] = keep_mask(acc[i], __hfma2(bits_h2(xs[i]), wv, acc[i]), keep_rec[i]);
-          }
-        }
-      }
+  }
+  const bool tokens = s.any_token != 0;
+  if (layer1 || tokens) {
+    if (layer1)
+      stage_rows(s, xh(p, XH0N));
+    else
+      stage_embeddings(s, p);
+    __syncthreads();
+    if (chain && any) lstm_chain_half<false>(s, wrow, grp, par, keep_rec, acc);
+  }
+  if (tokens) {
+    __syncthreads();  // the first half is consumed
+    stage_rows(s, xh(p, layer1 ? XH1 : XH0));
+    __syncthreads();
+    if (chain && (layer1 ? any_full : any)) {
+      if (layer1)
+        lstm_chain_half<true>(s, wrow + RH, grp, par, keep_rec, acc);
+      else
+        lstm_chain_half<false>(s, wrow + RH, grp, par, keep_rec, acc);
     }
+  }
+  // The two parity chains of a gate sum in f16 (every thread takes part in
+  // the shuffle; only chain threads of parity 0 store).
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const __half2 other = bits_h2(__shfl_xor_sync(0xffffffffu, h2_bits(acc[i]), 1));
-      if (par == 0) {
-        const float2 g = __half22float2(__hadd2(acc[i], other));
-        s.gates[grp * 8 + 2 * i][o] = g.x;
-        s.gates[grp * 8 + 2 * i + 1][o] = g.y;
-      }
+  for (int i = 0; i < RLSTM_PAIRS; ++i) {
+    const __half2 other = bits_h2(__shfl_xor_sync(0xffffffffu, h2_bits(acc[i]), 1));
+    if (chain && par == 0) {
+      const float2 g = __half22float2(__hadd2(acc[i], other));
+      const int w0 = (grp * RLSTM_PAIRS + i) * 2;
+      s.gates[w0][o] = g.x;
+      s.gates[w0 + 1][o] = g.y;
     }
   }
 }
@@ -315,13 +368,61 @@ __device__ void commit_hidden(RSmem& s, const RParams& p, bool layer1) {
   }
 }
 
+// The f32 projection chains of this CTA's 5 projector outputs, in two staged
+// halves of the new layer-1 hidden state; thread: (output, window).
+__device__ void projector(RSmem& s, const RParams& p) {
+  const int tid = threadIdx.x;
+  const int o = tid / RMAXB, w = tid % RMAXB;
+  const bool live = tid < RPROJ_THREADS && w < p.batch && s.win[w].pending;
+  float acc = live ? s.pb[o] : 0.0f;
+  for (int h = 0; h < 2; ++h) {
+    if (h) __syncthreads();  // the first half is consumed
+    {
+      constexpr int PER = RHALF * RMAXB / 4 / RTHREADS;
+      static_assert(RHALF * RMAXB / 4 % RTHREADS == 0, "whole chunks per thread");
+      const uint4* src = reinterpret_cast<const uint4*>(h1f_at(p) + (size_t)h * RHALF * RMAXB);
+      uint4 v[PER];
+#pragma unroll
+      for (int j = 0; j < PER; ++j) v[j] = __ldcg(src + tid + j * RTHREADS);
+#pragma unroll
+      for (int j = 0; j < PER; ++j) reinterpret_cast<uint4*>(&s.in.hf[0][0])[tid + j * RTHREADS] = v[j];
+    }
+    __syncthreads();
+    if (live) {
+      const int kb = h * RHALF;
+      float hv[RCHUNK], wv[RCHUNK];
+#pragma unroll
+      for (int j = 0; j < RCHUNK; ++j) {
+        hv[j] = s.in.hf[j][w];
+        wv[j] = __half2float(s.pw[kb + j][o]);
+      }
+#pragma unroll 1
+      for (int k0 = 0; k0 < RHALF; k0 += RCHUNK) {
+        float ch[RCHUNK], cw[RCHUNK];
+#pragma unroll
+        for (int j = 0; j < RCHUNK; ++j) {
+          ch[j] = hv[j];
+          cw[j] = wv[j];
+        }
+        if (k0 + RCHUNK < RHALF) {
+#pragma unroll
+          for (int j = 0; j < RCHUNK; ++j) {
+            hv[j] = s.in.hf[k0 + RCHUNK + j][w];
+            wv[j] = __half2float(s.pw[kb + k0 + RCHUNK + j][o]);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < RCHUNK; ++j) acc = __fmaf_rn(ch[j], cw[j], acc);
+      }
+    }
+  }
+  if (live) proj_at(p, w)[blockIdx.x * RCH + o] = acc;
+}
+
 __device__ void lstm_update(RSmem& s, const RParams& p) {
   const int tid = threadIdx.x;
   // Layer 0: inputs [embedding(token) | h0]; start-of-sequence windows take the bias.
-  stage_embeddings(s, p);
-  copy_rows(s, xh(p, XH0), RH, RH);
-  __syncthreads();
-  lstm_chains(s, s.w0, s.b0, false);
+  lstm_layer(s, p, false);
   __syncthreads();
   for (int i = tid; i < p.batch * RGATES; i += RTHREADS) {
     const int w = i / RGATES, o = i % RGATES;
@@ -332,123 +433,122 @@ __device__ void lstm_update(RSmem& s, const RParams& p) {
   grid_sync(s, p);
   // Every CTA has read the old h0: commit the new slice.  Layer 1: inputs
   // [new h0 | h1] (the h1 lanes of start-of-sequence windows are not used).
-  __syncthreads();
   commit_hidden(s, p, false);
-  copy_rows(s, xh(p, XH0N), 0, RH);
-  copy_rows(s, xh(p, XH1), RH, RH);
-  __syncthreads();
-  lstm_chains(s, s.w1, s.b1, true);
+  lstm_layer(s, p, true);
   __syncthreads();
   cell_update(s, p, s.c1, true);
   grid_sync(s, p);
-  // Projector: f32 chains over the new f32 h1; then commit h1.
-  {
-    constexpr int PER = RH * RMAXB / 4 / RTHREADS;
-    uint4 v[PER];
-#pragma unroll
-    for (int j = 0; j < PER; ++j) v[j] = __ldcg(reinterpret_cast<const uint4*>(h1f_at(p)) + tid + j * RTHREADS);
-#pragma unroll
-    for (int j = 0; j < PER; ++j) reinterpret_cast<uint4*>(&s.in.hf[0][0])[tid + j * RTHREADS] = v[j];
-  }
+  // Projector over the new f32 h1; h1 itself is committed now (every CTA has
+  // read the old one).
   commit_hidden(s, p, true);
-  __syncthreads();
-  if (tid < RCH * RMAXB) {
-    const int o = tid / RMAXB, w = tid % RMAXB;
-    if (w < p.batch && s.win[w].pending) {
-      float acc = s.pb[o];
-      for (int k0 = 0; k0 < RH; k0 += RCHUNK) {
-        float hv[RCHUNK], wv[RCHUNK];
-#pragma unroll
-        for (int j = 0; j < RCHUNK; ++j) {
-          hv[j] = s.in.hf[k0 + j][w];
-          wv[j] = __half2float(s.pw[k0 + j][o]);
-        }
-#pragma unroll
-        for (int j = 0; j < RCHUNK; ++j) acc = __fmaf_rn(hv[j], wv[j], acc);
-      }
-      proj_at(p, w)[blockIdx.x * RCH + o] = acc;
-    }
-  }
+  projector(s, p);
   grid_sync(s, p);
   if (tid < p.batch) s.win[tid].pending = 0;
   __syncthreads();
 }
 
+// One staged half (320 inputs) of this thread's head chain: column `col`,
+// window pair `pair`, starting at input `kb`.  The next 8 inputs' operands
+// load while the current 8 are chained.
+__device__ __forceinline__ void head_chain_half(const RSmem& s, int col, int pair, int kb, __half2& acc) {
+  const __half* wrow = &s.hw[col][kb];
+  const uint32_t* xrow = &s.in.jt.j2[pair][0];
+  const uint32_t* mrow = &s.in.jt.keep[pair][0];
+  uint4 wq = *reinterpret_cast<const uint4*>(wrow);
+  uint4 xa = *reinterpret_cast<const uint4*>(xrow), xb = *reinterpret_cast<const uint4*>(xrow + 4);
+  uint4 ma = *reinterpret_cast<const uint4*>(mrow), mb = *reinterpret_cast<const uint4*>(mrow + 4);
+#pragma unroll 1
+  for (int k0 = 0; k0 < RHALF; k0 += RCHUNK) {
+    const uint4 cw = wq;
+    const uint32_t xs[RCHUNK] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+    const uint32_t ms[RCHUNK] = {ma.x, ma.y, ma.z, ma.w, mb.x, mb.y, mb.z, mb.w};
+    if (k0 + RCHUNK < RHALF) {
+      const int k1 = k0 + RCHUNK;
+      wq = *reinterpret_cast<const uint4*>(wrow + k1);
+      xa = *reinterpret_cast<const uint4*>(xrow + k1);
+      xb = *reinterpret_cast<const uint4*>(xrow + k1 + 4);
+      ma = *reinterpret_cast<const uint4*>(mrow + k1);
+      mb = *reinterpret_cast<const uint4*>(mrow + k1 + 4);
+    }
+    const __half* wh = reinterpret_cast<const __half*>(&cw);
+    if ((ms[0] | ms[1] | ms[2] | ms[3] | ms[4] | ms[5] | ms[6] | ms[7]) == 0u) {  // no skipped input here
+#pragma unroll
+      for (int j = 0; j < RCHUNK; ++j) acc = __hfma2(bits_h2(xs[j]), __half2half2(wh[j]), acc);
+    } else {
+#pragma unroll
+      for (int j = 0; j < RCHUNK; ++j) acc = keep_mask(acc, __hfma2(bits_h2(xs[j]), __half2half2(wh[j]), acc), ms[j]);
+    }
+  }
+}
+
 // Joint of the active windows: inputs, head columns, this CTA's partials.
-// Thread k builds input k for every window (coalesced loads along k).
+// Thread k builds input k for every window (coalesced loads along k) and
+// keeps them in registers; the inputs are staged for the head chains in two
+// halves.
 __device__ void joint_partials(RSmem& s, const RParams& p, int slot) {
   const int tid = threadIdx.x;
   if (tid < RMAXB) s.first_exc[tid] = RH;
   __syncthreads();
-  {
-    const int k = tid;
-    // All of this input's loads first (32 windows), then the arithmetic.
-    __half ev[RMAXB];
-    float pv[RMAXB];
+  const int k = tid;
+  uint32_t packed[RPAIRS];  // half2 bits of input k, per window pair
+  uint64_t zero_bits = 0ull;
+  constexpr int WG = 8;  // windows whose loads are in flight together
 #pragma unroll
-    for (int w = 0; w < RMAXB; ++w) {
-      ev[w] = __float2half_rn(0.0f);
-      pv[w] = 0.0f;
+  for (int w0 = 0; w0 < RMAXB; w0 += WG) {
+    __half ev[WG];
+    float pv[WG];
+#pragma unroll
+    for (int i = 0; i < WG; ++i) {
+      const int w = w0 + i;
+      ev[i] = __float2half_rn(0.0f);
+      pv[i] = 0.0f;
       if (w < p.batch && s.win[w].joint) {
-        ev[w] = p.enc[((size_t)w * p.frames + s.win[w].joint_t) * RH + k];
-        pv[w] = __ldcg(proj_at(p, w) + k);
+        ev[i] = p.enc[((size_t)w * p.frames + s.win[w].joint_t) * RH + k];
+        pv[i] = __ldcg(proj_at(p, w) + k);
       }
     }
-    uint32_t zero_bits = 0u;
 #pragma unroll
-    for (int pr = 0; pr < RPAIRS; ++pr) {
+    for (int i = 0; i < WG; i += 2) {
       __half hv[2];
 #pragma unroll
       for (int l = 0; l < 2; ++l) {
-        const int w = 2 * pr + l;
+        const int w = w0 + i + l;
         hv[l] = __float2half_rn(0.0f);
         if (w < p.batch && s.win[w].joint) {
-          const float x = __fadd_rn(__half2float(ev[w]), pv[w]);
+          const float x = __fadd_rn(__half2float(ev[i + l]), pv[i + l]);
           const float jv = x < 0.0f ? 0.0f : x;  // max(x, 0) keeping -0 and NaN, as the oracle's std::max
           const uint32_t bits = __float_as_uint(jv);
           hv[l] = __float2half_rn(jv);
-          if (bits == 0u) zero_bits |= 1u << w;
+          if (bits == 0u) zero_bits |= 1ull << w;
           if (bits == 0x80000000u || (bits & 0x7fffffffu) > 0x7f800000u) atomicMin(&s.first_exc[w], k);
         }
       }
-      s.in.jt.j2[pr][k] = h2_bits(__halves2half2(hv[0], hv[1]));
-    }
-    __syncthreads();
-    // The shader skips input k while no -0 / NaN input has been seen and k is +0.
-#pragma unroll
-    for (int pr = 0; pr < RPAIRS; ++pr) {
-      const bool lo = ((zero_bits >> (2 * pr)) & 1u) && k < s.first_exc[2 * pr];
-      const bool hi = ((zero_bits >> (2 * pr + 1)) & 1u) && k < s.first_exc[2 * pr + 1];
-      s.in.jt.keep[pr][k] = lane_mask(lo, hi);
+      packed[(w0 + i) / 2] = h2_bits(__halves2half2(hv[0], hv[1]));
     }
   }
-  __syncthreads();
-  if (tid < RHEAD_THREADS) {
-    const int col = tid % RHEADCOLS, pair = tid / RHEADCOLS;  // windows 2 pair, 2 pair + 1
-    const bool tail = col >= RTOK;
-    const bool live = !tail || blockIdx.x == RG - 1;
-    __half2 acc = __float2half2_rn(s.hb[col]);
-    if (live && (s.win[2 * pair].joint || s.win[2 * pair + 1].joint)) {
-      for (int k0 = 0; k0 < RH; k0 += RCHUNK) {
-        // 8 steps per 16-byte load of each operand.
-        const uint4 wq = *reinterpret_cast<const uint4*>(&s.hw[col][k0]);
-        const uint4 xa = *reinterpret_cast<const uint4*>(&s.in.jt.j2[pair][k0]);
-        const uint4 xb = *reinterpret_cast<const uint4*>(&s.in.jt.j2[pair][k0 + 4]);
-        const uint4 ma = *reinterpret_cast<const uint4*>(&s.in.jt.keep[pair][k0]);
-        const uint4 mb = *reinterpret_cast<const uint4*>(&s.in.jt.keep[pair][k0 + 4]);
-        const __half* wh = reinterpret_cast<const __half*>(&wq);
-        const uint32_t xs[RCHUNK] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-        const uint32_t ms[RCHUNK] = {ma.x, ma.y, ma.z, ma.w, mb.x, mb.y, mb.z, mb.w};
-        if ((ma.x | ma.y | ma.z | ma.w | mb.x | mb.y | mb.z | mb.w) == 0u) {  // no skipped input here
+  __syncthreads();  // first_exc is final
+  const int col = tid % RHEADCOLS, pair = tid / RHEADCOLS;  // windows 2 pair, 2 pair + 1
+  const bool head = tid < RHEAD_THREADS;
+  const bool tail = col >= RTOK;
+  const bool live = head && (!tail || blockIdx.x == RG - 1);
+  __half2 acc = __float2half2_rn(head ? s.hb[col] : 0.0f);
+  const bool run = live && (s.win[2 * pair].joint || s.win[2 * pair + 1].joint);
+  for (int h = 0; h < 2; ++h) {
+    if (h) __syncthreads();  // the first half is consumed
+    if (k / RHALF == h) {
+      // The shader skips input k while no -0 / NaN input has been seen and k is +0.
 #pragma unroll
-          for (int j = 0; j < RCHUNK; ++j) acc = __hfma2(bits_h2(xs[j]), __half2half2(wh[j]), acc);
-        } else {
-#pragma unroll
-          for (int j = 0; j < RCHUNK; ++j)
-            acc = keep_mask(acc, __hfma2(bits_h2(xs[j]), __half2half2(wh[j]), acc), ms[j]);
-        }
+      for (int pr = 0; pr < RPAIRS; ++pr) {
+        const bool lo = ((zero_bits >> (2 * pr)) & 1ull) && k < s.first_exc[2 * pr];
+        const bool hi = ((zero_bits >> (2 * pr + 1)) & 1ull) && k < s.first_exc[2 * pr + 1];
+        s.in.jt.j2[pr][k - h * RHALF] = packed[pr];
+        s.in.jt.keep[pr][k - h * RHALF] = lane_mask(lo, hi);
       }
     }
+    __syncthreads();
+    if (run) head_chain_half(s, col, pair, h * RHALF, acc);
+  }
+  if (head) {
     const float2 v01 = __half22float2(acc);
     const float vals[2] = {sanitize(v01.x), sanitize(v01.y)};
 #pragma unroll
@@ -499,15 +599,22 @@ __device__ void emit(RSmem& s, const RParams& p, int w, uint32_t tok, uint32_t f
 
 // Reduce every CTA's partials (each CTA does it, so all agree) and advance the
 // control of every active window (the shader's main loop and flush, :1702-1990).
+// Thread (window, q) loads its 6 or 7 partials at once, then reduces them.
 __device__ void joint_decide(RSmem& s, const RParams& p, int slot) {
   const int tid = threadIdx.x;
-  {
-    const int w = tid / 20, q = tid % 20;
+  constexpr int PER = (RG + 19) / 20;
+  for (int i = tid; i < RMAXB * 20; i += RTHREADS) {
+    const int w = i / 20, q = i % 20;
     RPartial b{RNEG, 0xffffffffu, RNEG, 0xffffffffu};
     if (w < p.batch && s.win[w].joint) {
-      for (int r = q; r < RG; r += 20) {
-        const uint4 raw = __ldcg(reinterpret_cast<const uint4*>(part_at(p, slot, w, r)));
-        const RPartial v{__uint_as_float(raw.x), raw.y, __uint_as_float(raw.z), raw.w};
+      uint4 raw[PER];
+#pragma unroll
+      for (int j = 0; j < PER; ++j)
+        if (q + 20 * j < RG) raw[j] = __ldcg(reinterpret_cast<const uint4*>(part_at(p, slot, w, q + 20 * j)));
+#pragma unroll
+      for (int j = 0; j < PER; ++j) {
+        if (q + 20 * j >= RG) continue;
+        const RPartial v{__uint_as_float(raw[j].x), raw[j].y, __uint_as_float(raw[j].z), raw[j].w};
         if (better(b.tv, b.ti, v.tv, v.ti)) b.tv = v.tv, b.ti = v.ti;
         if (better(b.dv, b.di, v.dv, v.di)) b.dv = v.dv, b.di = v.di;
       }
@@ -631,12 +738,14 @@ __global__ void __launch_bounds__(RTHREADS, 1) tdt_resident_kernel(const RParams
   int slot = 0;
   while (true) {
     if (tid == 0) {
-      int ap = 0, aj = 0;
+      int ap = 0, at = 0, aj = 0;
       for (int w = 0; w < p.batch; ++w) {
         ap |= s.win[w].pending != 0;
+        at |= s.win[w].pending == 2;
         aj |= s.win[w].joint != 0;
       }
       s.any_pending = ap;
+      s.any_token = at;
       s.any_joint = aj;
     }
     __syncthreads();

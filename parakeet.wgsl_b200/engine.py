@@ -33,6 +33,7 @@ except ImportError:  # pragma: no cover
 
 WINDOW_SAMPLES = wp.WINDOW_SAMPLES
 MAX_TOKENS_PER_WINDOW = 2048  # src/runtime/webgpu-engine.ts:84
+BATCH_CAPACITY = 40  # windows per batch, the reference's encoder capacity (src/webgpu/encoder.ts:68)
 
 
 @dataclass(frozen=True)
@@ -43,7 +44,7 @@ class WindowResult:
 
 
 class ParakeetEngine:
-    def __init__(self, device: Device, package: dict, precision: str = "fp16", capacity: int = 32,
+    def __init__(self, device: Device, package: dict, precision: str = "fp16", capacity: int = BATCH_CAPACITY,
                  max_tokens: int = MAX_TOKENS_PER_WINDOW, keep_intermediates: bool = False):
         """package: encoder + decoder tensors (name -> record), as produced by
         the reference converter or ``synthetic.make_package`` + ``make_decoder``."""

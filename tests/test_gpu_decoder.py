@@ -102,12 +102,13 @@ def test_tdt_decoder_rejects_bad_descriptors(pk, device):
         pk._lib.call("pk_tdt_decode", device.handle, ctypes.byref(desc), None)
 
 
-def test_resident_and_cluster_decoders_agree_on_32_windows(pk, device):
-    """32 windows (the resident kernel's capacity) with ragged lengths, start /
-    end ranges and flushes: both kernels return identical tokens, frames,
-    durations, counts and flags."""
-    rng = np.random.default_rng(21)
-    b = 32
+@pytest.mark.parametrize("b", [40, 32, 7])
+def test_resident_and_cluster_decoders_agree(pk, device, b):
+    """40 windows (the resident kernel's capacity, the reference's batch
+    capacity), 32 and an odd count, with ragged lengths, start / end ranges
+    and flushes: both kernels return identical tokens, frames, durations,
+    counts and flags."""
+    rng = np.random.default_rng(21 + b)
     enc = rng.normal(0, 1, (b, 188, 640)).astype(np.float16)
     dec = {k: v["data"] for k, v in pk.synthetic.make_decoder("fp16", seed=5).items()}
     lengths = rng.integers(1, 189, size=b).tolist()
@@ -128,4 +129,4 @@ def test_resident_and_cluster_decoders_agree_on_32_windows(pk, device):
         n = int(c0[w])
         assert np.array_equal(t0[w, :n], t1[w, :n]) and np.array_equal(f0[w, :n], f1[w, :n])
         assert np.array_equal(d0[w, :n], d1[w, :n])
-    print(f"decoder: 32-window agreement, {int(np.sum(c0))} tokens")
+    print(f"decoder: {b}-window agreement, {int(np.sum(c0))} tokens")
