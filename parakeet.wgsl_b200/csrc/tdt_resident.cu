@@ -55,9 +55,10 @@ constexpr int RHEADCOLS = 16;         // token columns + the tail slot
 constexpr int RMAXB = 40;             // windows per launch
 constexpr int RPAIRS = RMAXB / 2;     // window pairs (half2 lanes)
 constexpr int RHALF = RH / 2;         // joint / projector inputs per staged half
-constexpr int RLSTM_PAIRS = 2;        // window pairs per LSTM chain thread
-constexpr int RLSTM_GROUPS = RPAIRS / RLSTM_PAIRS;       // 10
-constexpr int RLSTM_THREADS = 2 * RGATES * RLSTM_GROUPS;  // (output, parity) x group: 400
+constexpr int RLSTM_PAIRS = 4;        // window pairs per LSTM chain thread
+constexpr int RLSTM_GROUPS = RPAIRS / RLSTM_PAIRS;       // 5
+constexpr int RLSTM_PER_PAR = RGATES * RLSTM_GROUPS;     // chain threads per parity: (output, group), 100
+constexpr int RLSTM_THREADS = 2 * RLSTM_PER_PAR;         // 200
 constexpr int RW_STRIDE = RKIN + 8;   // padded weight row (halfs): rows start 16 bytes apart in the banks
 constexpr int RHW_STRIDE = RH + 8;    // padded head row: the 16 columns' loads spread over the banks
 constexpr int RHEAD_THREADS = RHEADCOLS * RPAIRS;        // column x window pair: 320
@@ -109,10 +110,10 @@ struct RSmem {
   __half w0[RGATES][RW_STRIDE];      // [gate output][input] (inputs fastest)
   __half w1[RGATES][RW_STRIDE];
   __half hw[RHEADCOLS][RHW_STRIDE];  // [head column][input]
-  __half pw[RH][RCH + 1];
+  float pwf[RCH][RH];                // projector weights as f32, [output][input]
   union {
     __half2 x2[RH][RPAIRS];          // one half of an LSTM layer's inputs, [input][window pair]
-    float hf[RHALF][RMAXB];          // one half of the projector inputs, [input][window]
+    float hf[RMAXB][RHALF + 4];      // one half of the projector inputs, [window][input] (rows padded)
     struct {
       uint32_t j2[RPAIRS][RHALF];    // one half of the joint inputs, [window pair][input] (half2 bits)
       uint32_t keep[RPAIRS][RHALF];  // per pair and input: the lanes whose head chain skips it
@@ -123,6 +124,7 @@ struct RSmem {
   float c0[RMAXB][RCH];
   float c1[RMAXB][RCH];
   __half hnew[RMAXB][RCH];           // this CTA's new hidden slice, committed one barrier later
+  uint32_t psum[2][RPAIRS][RGATES];  // the parity chains' sums (half2 bits), [parity][window pair][gate]
   float b0[RGATES], b1[RGATES], pb[8], hb[RHEADCOLS];
   int first_exc[RMAXB];
   RWin win[RMAXB];
@@ -232,66 +234,79 @@ __device__ void stage_embeddings(RSmem& s, const RParams& p) {
 
 // One staged half (640 inputs) of this thread's gate chains: gate output of
 // `wrow` (its 640 weights of this half, both parities interleaved), parity
-// `par`, window pairs 2 g and 2 g + 1.  Operands of the next 16 inputs load
-// while the current 16 are chained.  REC: lanes in `keep` leave their
+// `par`, window pairs 4 g .. 4 g + 3.  REC: lanes in `keep` leave their
 // accumulator as it was (start-of-sequence windows skip the recurrent half).
+// The chain threads of one warp share their parity, so every x2 load of a
+// warp reads one 80-byte row (one wavefront) and its weight loads a few rows.
+// Operands of 4 chain steps (8 inputs from k): this parity's 4 weights and
+// the 4 window pairs' inputs.
+struct LstmChunk {
+  uint4 w;     // 8 weights, inputs k .. k + 7
+  uint4 x[4];  // inputs k + par, k + 2 + par, ... for the thread's 4 pairs
+};
+
+__device__ __forceinline__ void lstm_load(const RSmem& s, const __half* wrow, int k, int g, int par, LstmChunk& c) {
+  c.w = *reinterpret_cast<const uint4*>(wrow + k);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) c.x[j] = *reinterpret_cast<const uint4*>(&s.in.x2[k + 2 * j + par][4 * g]);
+}
+
 template <bool REC>
-__device__ __forceinline__ void lstm_chain_half(const RSmem& s, const __half* wrow, int g, int par,
-                                                const uint32_t (&keep)[RLSTM_PAIRS], __half2 (&acc)[RLSTM_PAIRS]) {
-  uint4 wa = *reinterpret_cast<const uint4*>(wrow), wb = *reinterpret_cast<const uint4*>(wrow + 8);
-  uint2 xv[RCHUNK];
+__device__ __forceinline__ void lstm_math(const LstmChunk& c, int par, const uint32_t (&keep)[RLSTM_PAIRS],
+                                          __half2 (&acc)[RLSTM_PAIRS]) {
+  const uint32_t ww[4] = {c.w.x, c.w.y, c.w.z, c.w.w};
 #pragma unroll
-  for (int j = 0; j < RCHUNK; ++j) xv[j] = *reinterpret_cast<const uint2*>(&s.in.x2[2 * j + par][2 * g]);
-#pragma unroll 1
-  for (int k0 = 0; k0 < RH; k0 += 2 * RCHUNK) {
-    // Word j holds the weights of inputs k0 + 2j (low half) and k0 + 2j + 1 (high half).
-    const uint32_t ww[RCHUNK] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
-    uint2 cx[RCHUNK];
+  for (int j = 0; j < 4; ++j) {
+    const __half2 wv = __half2half2(__ushort_as_half((unsigned short)(par ? ww[j] >> 16 : ww[j] & 0xffffu)));
+    const uint32_t xs[RLSTM_PAIRS] = {c.x[j].x, c.x[j].y, c.x[j].z, c.x[j].w};
 #pragma unroll
-    for (int j = 0; j < RCHUNK; ++j) cx[j] = xv[j];
-    if (k0 + 2 * RCHUNK < RH) {
-      const int k1 = k0 + 2 * RCHUNK;
-      wa = *reinterpret_cast<const uint4*>(wrow + k1);
-      wb = *reinterpret_cast<const uint4*>(wrow + k1 + 8);
-#pragma unroll
-      for (int j = 0; j < RCHUNK; ++j) xv[j] = *reinterpret_cast<const uint2*>(&s.in.x2[k1 + 2 * j + par][2 * g]);
-    }
-#pragma unroll
-    for (int j = 0; j < RCHUNK; ++j) {
-      const __half2 wv = __half2half2(__ushort_as_half((unsigned short)(par ? ww[j] >> 16 : ww[j] & 0xffffu)));
-      const uint32_t xs[RLSTM_PAIRS] = {cx[j].x, cx[j].y};
-#pragma unroll
-      for (int i = 0; i < RLSTM_PAIRS; ++i) {
-        if constexpr (REC)
-          acc[i] = keep_mask(acc[i], __hfma2(bits_h2(xs[i]), wv, acc[i]), keep[i]);
-        else
-          acc[i] = __hfma2(bits_h2(xs[i]), wv, acc[i]);
-      }
+    for (int i = 0; i < RLSTM_PAIRS; ++i) {
+      if constexpr (REC)
+        acc[i] = keep_mask(acc[i], __hfma2(bits_h2(xs[i]), wv, acc[i]), keep[i]);
+      else
+        acc[i] = __hfma2(bits_h2(xs[i]), wv, acc[i]);
     }
   }
 }
 
+// One staged half (640 inputs) of this thread's gate chains: gate output of
+// `wrow` (its 640 weights of this half, both parities interleaved), parity
+// `par`, window pairs 4 g .. 4 g + 3.  REC: lanes in `keep` leave their
+// accumulator as it was (start-of-sequence windows skip the recurrent half).
+// The chain threads of one warp share their parity, so every x2 load of a
+// warp reads one 80-byte row (one wavefront) and its weight loads a few rows.
+// Two operand buffers alternate: the loads of the next 8 inputs are issued
+// before the chain steps of the current 8.
+template <bool REC>
+__device__ __forceinline__ void lstm_chain_half(const RSmem& s, const __half* wrow, int g, int par,
+                                                const uint32_t (&keep)[RLSTM_PAIRS], __half2 (&acc)[RLSTM_PAIRS]) {
+  LstmChunk a, b;
+  lstm_load(s, wrow, 0, g, par, a);
+#pragma unroll 1
+  for (int k = 0; k < RH; k += 16) {
+    lstm_load(s, wrow, k + 8, g, par, b);
+    lstm_math<REC>(a, par, keep, acc);
+    if (k + 16 < RH) lstm_load(s, wrow, k + 16, g, par, a);
+    lstm_math<REC>(b, par, keep, acc);
+  }
+}
+
 // Gate chains of one LSTM layer for the windows that need them; gates land in
-// s.gates[window][gate * 5 + channel].  Thread: (output o, parity) x group of
-// 2 window pairs.  Inputs: layer 0 [embedding(token) | h0], layer 1 [new h0 |
-// h1], staged one half at a time.  Layer 1's start-of-sequence windows stop
-// at input 640 (their recurrent input is zero and the shader does not run
-// those steps); lanes of windows that do not update compute values nobody
-// reads.
+// s.gates[window][gate * 5 + channel].  Chain thread t < 200: parity t / 100,
+// output (t % 100) / 5, group of 4 window pairs t % 5.  Inputs: layer 0
+// [embedding(token) | h0], layer 1 [new h0 | h1], staged one half at a time.
+// Layer 1's start-of-sequence windows stop at input 640 (their recurrent
+// input is zero and the shader does not run those steps); lanes of windows
+// that do not update compute values nobody reads.
 __device__ void lstm_layer(RSmem& s, const RParams& p, bool layer1) {
   const int tid = threadIdx.x;
   const bool chain = tid < RLSTM_THREADS;
-  const int grp = tid / (2 * RGATES), r = tid % (2 * RGATES);
-  const int o = r >> 1, par = r & 1;
+  const int par = tid / RLSTM_PER_PAR, idx = tid % RLSTM_PER_PAR;
+  const int o = idx / RLSTM_GROUPS, grp = idx % RLSTM_GROUPS;
   const __half* wrow = layer1 ? &s.w1[o][0] : &s.w0[o][0];
   bool any = false, any_full = false;
   uint32_t keep_rec[RLSTM_PAIRS];
   __half2 acc[RLSTM_PAIRS];
-#pragma unroll
-  for (int i = 0; i < RLSTM_PAIRS; ++i) {
-    keep_rec[i] = 0u;
-    acc[i] = __float2half2_rn(0.0f);
-  }
   if (chain) {
     const __half2 init = par == 0 ? __float2half2_rn((layer1 ? s.b1 : s.b0)[o]) : __float2half2_rn(0.0f);
 #pragma unroll
@@ -324,16 +339,20 @@ __device__ void lstm_layer(RSmem& s, const RParams& p, bool layer1) {
         lstm_chain_half<false>(s, wrow + RH, grp, par, keep_rec, acc);
     }
   }
-  // The two parity chains of a gate sum in f16 (every thread takes part in
-  // the shuffle; only chain threads of parity 0 store).
+  // The two parity chains of a gate sum in f16.
+  if (chain && any) {
 #pragma unroll
-  for (int i = 0; i < RLSTM_PAIRS; ++i) {
-    const __half2 other = bits_h2(__shfl_xor_sync(0xffffffffu, h2_bits(acc[i]), 1));
-    if (chain && par == 0) {
-      const float2 g = __half22float2(__hadd2(acc[i], other));
-      const int w0 = (grp * RLSTM_PAIRS + i) * 2;
-      s.gates[w0][o] = g.x;
-      s.gates[w0 + 1][o] = g.y;
+    for (int i = 0; i < RLSTM_PAIRS; ++i) s.psum[par][grp * RLSTM_PAIRS + i][o] = h2_bits(acc[i]);
+  }
+  __syncthreads();
+  for (int i = tid; i < RPAIRS * RGATES; i += RTHREADS) {
+    const int pr = i / RGATES, g = i % RGATES;
+    const bool upd = layer1 ? (s.win[2 * pr].pending | s.win[2 * pr + 1].pending) != 0
+                            : (s.win[2 * pr].pending == 2 || s.win[2 * pr + 1].pending == 2);
+    if (upd) {
+      const float2 v = __half22float2(__hadd2(bits_h2(s.psum[0][pr][g]), bits_h2(s.psum[1][pr][g])));
+      s.gates[2 * pr][g] = v.x;
+      s.gates[2 * pr + 1][g] = v.y;
     }
   }
 }
@@ -369,7 +388,9 @@ __device__ void commit_hidden(RSmem& s, const RParams& p, bool layer1) {
 }
 
 // The f32 projection chains of this CTA's 5 projector outputs, in two staged
-// halves of the new layer-1 hidden state; thread: (output, window).
+// halves of the new layer-1 hidden state (transposed to [window][input] while
+// staging, so a thread's inputs and weights are 16-byte loads along k);
+// thread: (output, window).
 __device__ void projector(RSmem& s, const RParams& p) {
   const int tid = threadIdx.x;
   const int o = tid / RMAXB, w = tid % RMAXB;
@@ -378,41 +399,43 @@ __device__ void projector(RSmem& s, const RParams& p) {
   for (int h = 0; h < 2; ++h) {
     if (h) __syncthreads();  // the first half is consumed
     {
-      constexpr int PER = RHALF * RMAXB / 4 / RTHREADS;
-      static_assert(RHALF * RMAXB / 4 % RTHREADS == 0, "whole chunks per thread");
+      constexpr int Q = RMAXB / 4;  // 16-byte chunks per exchanged row
+      constexpr int PER = RHALF * Q / RTHREADS;
+      static_assert(RHALF * Q % RTHREADS == 0, "whole chunks per thread");
       const uint4* src = reinterpret_cast<const uint4*>(h1f_at(p) + (size_t)h * RHALF * RMAXB);
       uint4 v[PER];
 #pragma unroll
       for (int j = 0; j < PER; ++j) v[j] = __ldcg(src + tid + j * RTHREADS);
 #pragma unroll
-      for (int j = 0; j < PER; ++j) reinterpret_cast<uint4*>(&s.in.hf[0][0])[tid + j * RTHREADS] = v[j];
+      for (int j = 0; j < PER; ++j) {
+        const int i = tid + j * RTHREADS, k = i / Q, w4 = 4 * (i % Q);
+        s.in.hf[w4][k] = __uint_as_float(v[j].x);
+        s.in.hf[w4 + 1][k] = __uint_as_float(v[j].y);
+        s.in.hf[w4 + 2][k] = __uint_as_float(v[j].z);
+        s.in.hf[w4 + 3][k] = __uint_as_float(v[j].w);
+      }
     }
     __syncthreads();
     if (live) {
-      const int kb = h * RHALF;
-      float hv[RCHUNK], wv[RCHUNK];
-#pragma unroll
-      for (int j = 0; j < RCHUNK; ++j) {
-        hv[j] = s.in.hf[j][w];
-        wv[j] = __half2float(s.pw[kb + j][o]);
-      }
+      const float* hrow = &s.in.hf[w][0];
+      const float* wrow = &s.pwf[o][h * RHALF];
+      float4 ha = *reinterpret_cast<const float4*>(hrow), wa = *reinterpret_cast<const float4*>(wrow);
 #pragma unroll 1
-      for (int k0 = 0; k0 < RHALF; k0 += RCHUNK) {
-        float ch[RCHUNK], cw[RCHUNK];
-#pragma unroll
-        for (int j = 0; j < RCHUNK; ++j) {
-          ch[j] = hv[j];
-          cw[j] = wv[j];
+      for (int k = 0; k < RHALF; k += 8) {
+        const float4 hb = *reinterpret_cast<const float4*>(hrow + k + 4);
+        const float4 wb = *reinterpret_cast<const float4*>(wrow + k + 4);
+        acc = __fmaf_rn(ha.x, wa.x, acc);
+        acc = __fmaf_rn(ha.y, wa.y, acc);
+        acc = __fmaf_rn(ha.z, wa.z, acc);
+        acc = __fmaf_rn(ha.w, wa.w, acc);
+        if (k + 8 < RHALF) {
+          ha = *reinterpret_cast<const float4*>(hrow + k + 8);
+          wa = *reinterpret_cast<const float4*>(wrow + k + 8);
         }
-        if (k0 + RCHUNK < RHALF) {
-#pragma unroll
-          for (int j = 0; j < RCHUNK; ++j) {
-            hv[j] = s.in.hf[k0 + RCHUNK + j][w];
-            wv[j] = __half2float(s.pw[kb + k0 + RCHUNK + j][o]);
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < RCHUNK; ++j) acc = __fmaf_rn(ch[j], cw[j], acc);
+        acc = __fmaf_rn(hb.x, wb.x, acc);
+        acc = __fmaf_rn(hb.y, wb.y, acc);
+        acc = __fmaf_rn(hb.z, wb.z, acc);
+        acc = __fmaf_rn(hb.w, wb.w, acc);
       }
     }
   }
@@ -448,35 +471,32 @@ __device__ void lstm_update(RSmem& s, const RParams& p) {
 }
 
 // One staged half (320 inputs) of this thread's head chain: column `col`,
-// window pair `pair`, starting at input `kb`.  The next 8 inputs' operands
-// load while the current 8 are chained.
+// window pair `pair`, starting at input `kb`.
 __device__ __forceinline__ void head_chain_half(const RSmem& s, int col, int pair, int kb, __half2& acc) {
   const __half* wrow = &s.hw[col][kb];
   const uint32_t* xrow = &s.in.jt.j2[pair][0];
   const uint32_t* mrow = &s.in.jt.keep[pair][0];
-  uint4 wq = *reinterpret_cast<const uint4*>(wrow);
-  uint4 xa = *reinterpret_cast<const uint4*>(xrow), xb = *reinterpret_cast<const uint4*>(xrow + 4);
-  uint4 ma = *reinterpret_cast<const uint4*>(mrow), mb = *reinterpret_cast<const uint4*>(mrow + 4);
-#pragma unroll 1
+#pragma unroll 2
   for (int k0 = 0; k0 < RHALF; k0 += RCHUNK) {
-    const uint4 cw = wq;
+    // 8 steps per 16-byte load of each operand.
+    const uint4 wq = *reinterpret_cast<const uint4*>(wrow + k0);
+    const uint4 xa = *reinterpret_cast<const uint4*>(xrow + k0), xb = *reinterpret_cast<const uint4*>(xrow + k0 + 4);
+    const uint4 ma = *reinterpret_cast<const uint4*>(mrow + k0), mb = *reinterpret_cast<const uint4*>(mrow + k0 + 4);
+    const uint32_t wpair[4] = {wq.x, wq.y, wq.z, wq.w};
     const uint32_t xs[RCHUNK] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
     const uint32_t ms[RCHUNK] = {ma.x, ma.y, ma.z, ma.w, mb.x, mb.y, mb.z, mb.w};
-    if (k0 + RCHUNK < RHALF) {
-      const int k1 = k0 + RCHUNK;
-      wq = *reinterpret_cast<const uint4*>(wrow + k1);
-      xa = *reinterpret_cast<const uint4*>(xrow + k1);
-      xb = *reinterpret_cast<const uint4*>(xrow + k1 + 4);
-      ma = *reinterpret_cast<const uint4*>(mrow + k1);
-      mb = *reinterpret_cast<const uint4*>(mrow + k1 + 4);
-    }
-    const __half* wh = reinterpret_cast<const __half*>(&cw);
-    if ((ms[0] | ms[1] | ms[2] | ms[3] | ms[4] | ms[5] | ms[6] | ms[7]) == 0u) {  // no skipped input here
+    if ((ma.x | ma.y | ma.z | ma.w | mb.x | mb.y | mb.z | mb.w) == 0u) {  // no skipped input here
 #pragma unroll
-      for (int j = 0; j < RCHUNK; ++j) acc = __hfma2(bits_h2(xs[j]), __half2half2(wh[j]), acc);
+      for (int j = 0; j < RCHUNK; ++j) {
+        const uint32_t wb = (j & 1) ? (wpair[j >> 1] >> 16) : (wpair[j >> 1] & 0xffffu);
+        acc = __hfma2(bits_h2(xs[j]), __half2half2(__ushort_as_half((unsigned short)wb)), acc);
+      }
     } else {
 #pragma unroll
-      for (int j = 0; j < RCHUNK; ++j) acc = keep_mask(acc, __hfma2(bits_h2(xs[j]), __half2half2(wh[j]), acc), ms[j]);
+      for (int j = 0; j < RCHUNK; ++j) {
+        const uint32_t wb = (j & 1) ? (wpair[j >> 1] >> 16) : (wpair[j >> 1] & 0xffffu);
+        acc = keep_mask(acc, __hfma2(bits_h2(xs[j]), __half2half2(__ushort_as_half((unsigned short)wb)), acc), ms[j]);
+      }
     }
   }
 }
@@ -492,7 +512,7 @@ __device__ void joint_partials(RSmem& s, const RParams& p, int slot) {
   const int k = tid;
   uint32_t packed[RPAIRS];  // half2 bits of input k, per window pair
   uint64_t zero_bits = 0ull;
-  constexpr int WG = 8;  // windows whose loads are in flight together
+  constexpr int WG = 20;  // windows whose loads are in flight together
 #pragma unroll
   for (int w0 = 0; w0 < RMAXB; w0 += WG) {
     __half ev[WG];
@@ -694,9 +714,9 @@ __global__ void __launch_bounds__(RTHREADS, 1) tdt_resident_kernel(const RParams
     s.w0[o][k] = p.w0[(size_t)k * 4 * RH + col];
     s.w1[o][k] = p.w1[(size_t)k * 4 * RH + col];
   }
-  for (int i = tid; i < RH * (RCH + 1); i += RTHREADS) {
-    const int k = i / (RCH + 1), o = i % (RCH + 1);
-    s.pw[k][o] = o < RCH ? p.pw[(size_t)k * RH + cta * RCH + o] : __float2half_rn(0.0f);
+  for (int i = tid; i < RH * RCH; i += RTHREADS) {
+    const int k = i / RCH, o = i % RCH;
+    s.pwf[o][k] = __half2float(p.pw[(size_t)k * RH + cta * RCH + o]);
   }
   for (int i = tid; i < RH * RHEADCOLS; i += RTHREADS) {
     const int k = i / RHEADCOLS, c = i % RHEADCOLS;
