@@ -347,8 +347,12 @@ def time_longform(pk, device, rank, world, stream, capacity=None):
         del package
         pcm = longest[: int(round(seconds * 16_000))]
         timings = {}
+        plans = pk.windows.plan_stateless_windows(len(pcm))
+        mine = [plans[i] for i in pk.windows.shard_windows(len(plans), world, rank)]
         with torch.cuda.stream(stream):
             eng.transcribe(pcm[:30 * 16_000])  # warm-up
+            for size in sorted({len(r) for r in eng.batches(len(mine))}):  # record every graph size used
+                eng.encode_plans(pcm, mine[:size])
             if world > 1:
                 dist.barrier()
             torch.cuda.synchronize()
@@ -372,6 +376,48 @@ def time_longform(pk, device, rank, world, stream, capacity=None):
                         "sharded over ranks, host PCM in, merged tokens out",
             "n_gpus": world, "capacity": capacity, "variants": out,
             "note": "random-init weights; decoded token counts are not real speech and set most of the time"}
+
+
+def time_longform_encoder(pk, device, rank, world, stream, capacity=None, seconds=3600.0):
+    """The encoder alone on an hour of synthetic audio (BASELINE config 5's
+    workload, FP16, mixed palettes): each rank takes its contiguous share of
+    the window plan and runs log-mel + the 24-layer encoder on it in balanced
+    batches, host PCM in, projected encoder output left on the device.  CUDA
+    events around each rank's share, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    capacity = capacity or LONGFORM_CAPACITY
+    package = pk.synthetic.make_package("fp16", seed=0)
+    package.update(pk.synthetic.make_decoder("fp16", seed=0))
+    eng = pk.engine.ParakeetEngine(device, package, "fp16", capacity=capacity)
+    del package
+    pcm = longform_pcm(pk, seconds)
+    plans = pk.windows.plan_stateless_windows(len(pcm))
+    mine = [plans[i] for i in pk.windows.shard_windows(len(plans), world, rank)]
+    with torch.cuda.stream(stream):
+        eng.encode_plans(pcm, mine[:capacity])  # warm-up: every graph size this rank uses is recorded
+        for rows in eng.batches(len(mine)):
+            eng.encode_plans(pcm, mine[rows.start:rows.stop])
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        eng.encode_plans(pcm, mine)
+        end.record(stream)
+        end.synchronize()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    eng.destroy()
+    return {"workload": "config5 encoder only: one hour of synthetic PCM, window plan sharded over ranks, "
+                        "log-mel + 24-layer FP16 encoder (mixed palettes), host PCM in, encoder output on device",
+            "n_gpus": world, "audio_s": seconds, "windows": len(plans),
+            "rank_batches": [len(r) for r in eng.batches(len(mine))],
+            "s": round(ms / 1e3, 4), "audio_s_per_s": round(seconds / (ms / 1e3), 1)}
 
 
 def cpu_baseline(pk, package, window_count=1):
@@ -510,6 +556,10 @@ def run_ours(args):
     lf_info = None if args.skip_longform or "longform" not in legs else time_longform(pk, device, rank, world, stream)
     barrier()
 
+    # ---- the encoder alone on config 5's hour, sharded across all ranks
+    lfe_info = None if "longform" not in legs else time_longform_encoder(pk, device, rank, world, stream)
+    barrier()
+
     # ---- dominant kernel: palette GEMMs of one step, timed live
     gemm_flops, gemm_ms, gemm_detail = 0.0, 1.0, []
     if "gemm" in legs:
@@ -549,6 +599,7 @@ def run_ours(args):
             "logmel": lm_info,
             "transcribe": tr_info,
             "longform": lf_info,
+            "longform_encoder": lfe_info,
             "cpu_baseline": None if cpu_value is None else {
                 "value": round(cpu_value, 3), "unit": UNIT, "cores": int(os.environ.get("OMP_NUM_THREADS", cores)),
                 "kind": "port", "sample": f"1 window x 24 layers, oracle reference mode, {cpu_dt:.1f} s"},

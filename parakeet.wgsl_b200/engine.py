@@ -105,9 +105,10 @@ class ParakeetEngine:
         in flight: reading the status word clears it."""
         self.device.status()
 
-    def _submit(self, windows: Sequence[tuple], stream, slot: int):
+    def _submit(self, windows: Sequence[tuple], stream, slot: int, decode: bool = True):
         """Stages a batch in host slot `slot` and queues its copies and
-        kernels on `stream` without waiting for them."""
+        kernels on `stream` without waiting for them (without the decoder
+        and the token read-back when `decode` is False)."""
         b = len(windows)
         if not 0 < b <= self.capacity:
             raise RangeError(f"Engine batch must contain 1-{self.capacity} windows")
@@ -139,9 +140,10 @@ class ParakeetEngine:
             self._control.copy_(ctrl, non_blocking=True)
             self.fbank.compute_batch(self._pcm[:b], self._control[0, :b], out=self._features[:b], stream=stream)
             projected, _ = self.graph.encode(self._features[:b], lengths, stream=stream)
-            self._dispatch.encode(stream, active_batch_size=b)
-            host["tokens"][:, :b].copy_(self._tokens[:, :b], non_blocking=True)
-            host["meta"].copy_(self._meta, non_blocking=True)
+            if decode:
+                self._dispatch.encode(stream, active_batch_size=b)
+                host["tokens"][:, :b].copy_(self._tokens[:, :b], non_blocking=True)
+                host["meta"].copy_(self._meta, non_blocking=True)
             host["done"].record(stream)
         if self.keep_intermediates:
             stream.synchronize()
@@ -209,6 +211,24 @@ class ParakeetEngine:
             finish(*pending)
         self._check_status()
         return decoded
+
+    def encode_plans(self, pcm: np.ndarray, plans: Sequence[wp.WindowPlan], stream=None) -> int:
+        """Log-mel front end and encoder only, for `plans` in balanced
+        batches with the same two-slot pipelining as decode_plans; each
+        batch's projected encoder output is left on the device (where the
+        decoder would read it).  Returns the number of windows encoded."""
+        pending = None
+        for k, rows in enumerate(self.batches(len(plans))):
+            chunk = plans[rows.start:rows.stop]
+            ticket = self._submit([(pcm[p.source_start_sample:p.source_end_sample], p) for p in chunk], stream,
+                                  k % 2, decode=False)
+            if pending is not None:
+                self._slots[pending[0]]["done"].synchronize()
+            pending = ticket
+        if pending is not None:
+            self._slots[pending[0]]["done"].synchronize()
+        self._check_status()
+        return len(plans)
 
     def transcribe(self, pcm: np.ndarray, token_piece=None, stream=None):
         """Long-form transcription of 16 kHz mono f32 PCM on this GPU; returns
