@@ -10,20 +10,27 @@ reference's mixed policy).  One step = one encoder forward of the batch.
 
 * ``value``: audio seconds encoded per second over all ranks, inputs resident
   in HBM, timed with CUDA events on the launching stream (max over ranks);
-* ``e2e``: the same metric through the public API with host buffers: pinned
-  host features copied in and the projected output copied out every step;
+* ``e2e``: the same metric through the public API with host buffers: every
+  step's features copied in from pinned host memory and its projected
+  output copied out, the copies on a second stream overlapping the
+  neighbouring steps' encoder work;
 * ``roofline``: the palette GEMMs (the dominant kernel, tcgen05 tensor
   cores) -- algorithmic FLOPs of one step's GEMM launches / their summed
   CUDA-event time (each shape back to back over rotating operand sets larger
   than twice the L2), against the measured bf16 peak;
 * ``cpu_baseline``: the CPU oracle (a port of the reference's shader math,
   f16-accumulating GEMMs) on one window, scaled to audio-s/s;
+* ``config1_config2``: BASELINE configs 1 (the FP32 6-bit GEMM) and 2 (one
+  FP16 block, 8 windows) on the GPU, GFLOP/s, beside the oracle on the host;
+* ``fp32_encoder``: the FP32 package's encoder against the FFMA peak;
 * ``decoder`` / ``logmel`` / ``transcribe``: the TDT decoder on the step's
   encoder output, the log-mel front end on 32 windows of PCM, and 60 s of PCM
   through ``ParakeetEngine.transcribe`` (config 4);
 * ``longform``: config 5 -- an hour (FP16) or ten minutes (FP32) of PCM
   through ``engine.transcribe_sharded`` on all ranks, host PCM in and merged
-  tokens out, for mixed and all-5-bit palettes (max over ranks).
+  tokens out, for mixed and all-5-bit palettes (max over ranks), with the
+  phases (decode, gather, rank-0 merge); ``longform_encoder``: the same hour
+  through log-mel and the encoder only, sharded the same way.
 
 ``--impl reference`` times that CPU port on all host cores (rank 0 only):
 the reference's own WGSL path cannot run here (no browser / WebGPU stack).
@@ -302,6 +309,7 @@ def time_transcribe(pk, device, package, seconds=60.0, reps=2):
 LONGFORM_VARIANTS = (("fp16", "mixed", 3600.0), ("fp16", "all5", 3600.0), ("fp32", "mixed", 600.0),
                      ("fp32", "all5", 600.0))
 LONGFORM_CAPACITY = 40  # windows per engine batch (the reference's encoder capacity)
+LONGFORM_ENCODER_BATCH = 20  # encoder-only leg: windows per pipelined batch (staging overlaps the GPU)
 
 
 def longform_pcm(pk, seconds, seed=5, distinct=5):
@@ -354,6 +362,8 @@ def time_longform(pk, device, rank, world, stream, capacity=None):
             for size in sorted({len(r) for r in eng.batches(len(mine))}):  # record every graph size used
                 eng.encode_plans(pcm, mine[:size])
             if world > 1:
+                gather(np.zeros(8, np.int64))  # the gather's buffers and channels exist before timing
+            if world > 1:
                 dist.barrier()
             torch.cuda.synchronize()
             start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -396,15 +406,14 @@ def time_longform_encoder(pk, device, rank, world, stream, capacity=None, second
     plans = pk.windows.plan_stateless_windows(len(pcm))
     mine = [plans[i] for i in pk.windows.shard_windows(len(plans), world, rank)]
     with torch.cuda.stream(stream):
-        eng.encode_plans(pcm, mine[:capacity])  # warm-up: every graph size this rank uses is recorded
-        for rows in eng.batches(len(mine)):
+        for rows in eng.batches(len(mine), LONGFORM_ENCODER_BATCH):  # warm-up: every graph size is recorded
             eng.encode_plans(pcm, mine[rows.start:rows.stop])
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record(stream)
-        eng.encode_plans(pcm, mine)
+        eng.encode_plans(pcm, mine, batch=LONGFORM_ENCODER_BATCH)
         end.record(stream)
         end.synchronize()
     ms = start.elapsed_time(end)
@@ -416,8 +425,258 @@ def time_longform_encoder(pk, device, rank, world, stream, capacity=None, second
     return {"workload": "config5 encoder only: one hour of synthetic PCM, window plan sharded over ranks, "
                         "log-mel + 24-layer FP16 encoder (mixed palettes), host PCM in, encoder output on device",
             "n_gpus": world, "audio_s": seconds, "windows": len(plans),
-            "rank_batches": [len(r) for r in eng.batches(len(mine))],
+            "rank_batches": [len(r) for r in eng.batches(len(mine), LONGFORM_ENCODER_BATCH)],
             "s": round(ms / 1e3, 4), "audio_s_per_s": round(seconds / (ms / 1e3), 1)}
+
+
+def time_e2e_pipelined(pk, graph, features, lengths, stream, steps):
+    """``value``'s metric through the public API with host buffers, every
+    step copying its features in from pinned host memory and its projected
+    output back out, with the copies of one step overlapping the encoder
+    work of its neighbours: two device input / output buffers, the copies on
+    a second stream (ParakeetEncoderGraph.encode reads the device buffer).
+    CUDA events bracket the whole run on the launching stream, which joins
+    the copy stream at the end.  Returns ms per step."""
+    import torch
+
+    copy = torch.cuda.Stream()
+    pinned_in = torch.from_numpy(features).pin_memory()
+    rows = features.shape[0] * FRAMES
+    dev_in = [torch.empty(features.shape, dtype=torch.float32, device="cuda") for _ in range(2)]
+    dev_out = [torch.empty((rows, 640), dtype=torch.float16, device="cuda") for _ in range(2)]
+    host_out = [torch.empty((rows, 640), dtype=torch.float16).pin_memory() for _ in range(2)]
+    landed = [torch.cuda.Event() for _ in range(2)]   # features of a buffer on the device
+    computed = [torch.cuda.Event() for _ in range(2)]  # outputs of a buffer written
+    drained = [torch.cuda.Event() for _ in range(2)]   # outputs of a buffer read back
+
+    def run(n):
+        for i in range(n):
+            b = i % 2
+            with torch.cuda.stream(copy):
+                if i >= 2:
+                    copy.wait_event(computed[b])  # the encoder of step i-2 has read dev_in[b]
+                dev_in[b].copy_(pinned_in, non_blocking=True)
+                landed[b].record(copy)
+            stream.wait_event(landed[b])
+            if i >= 2:
+                stream.wait_event(drained[b])  # step i-2's output left dev_out[b]
+            with torch.cuda.stream(stream):
+                graph.encode(dev_in[b], lengths, stream=stream, out=dev_out[b])
+                computed[b].record(stream)
+            with torch.cuda.stream(copy):
+                copy.wait_event(computed[b])
+                host_out[b].copy_(dev_out[b], non_blocking=True)
+                drained[b].record(copy)
+        stream.wait_stream(copy)
+
+    run(3)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    copy.wait_event(start)
+    run(steps)
+    end.record(stream)
+    end.synchronize()
+    return start.elapsed_time(end) / steps, int(pinned_in.numel() * 4), int(host_out[0].numel() * 2)
+
+
+# FFMA peak of the FP32 package's GEMMs: SMs x 128 FP32 lanes x 2 FLOP per FMA x clock.
+FFMA_LANES_PER_SM = 128
+
+
+def time_config1(pk, device, stream, reps=50):
+    """the FP32 palette GEMM [188 x 1024] . [1024 x 4096]
+    (6-bit, 64-entry f32 LUT ~ N(0, 0.02) sorted, seed 0), raw product and
+    the SiLU epilogue; CUDA events, inputs resident (operands total 20 MB,
+    timed back to back: this single GEMM's figure includes L2 reuse)."""
+    import ctypes
+
+    import torch
+
+    L = pk._lib
+    rng = np.random.default_rng(0)
+    a = torch.from_numpy(rng.standard_normal((188, 1024)).astype(np.float32)).cuda()
+    codes, lut = pk.synthetic.palette_matrix(rng, 1024, 4096, 6, 1, "fp32")
+    tc = torch.from_numpy(codes["data"].view(np.int32)).cuda()
+    tl = torch.from_numpy(lut["data"]).cuda()
+    out = torch.empty((188, 4096), dtype=torch.float32, device="cuda")
+    res = {}
+    h = ctypes.c_void_p(stream.cuda_stream)
+    for act in ("none", "silu"):
+        desc = L.GemmDesc(L.FP32, 188, 1024, 4096, 6, 1, 4096, L.ACT[act], 0, 1.0, None, None, a.data_ptr(),
+                          tc.data_ptr(), tl.data_ptr(), out.data_ptr())
+        for _ in range(5):
+            L.call("pk_palette_gemm", device.handle, ctypes.byref(desc), h)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(reps):
+            L.call("pk_palette_gemm", device.handle, ctypes.byref(desc), h)
+        end.record(stream)
+        end.synchronize()
+        us = start.elapsed_time(end) / reps * 1e3
+        res[act] = {"us": round(us, 2), "gflops": round(2 * 188 * 1024 * 4096 / (us * 1e-6) / 1e9, 1)}
+    return {"workload": "config1: FP32 palette GEMM 188x1024x4096, 6-bit, CUDA-core fp32 fma chain "
+                        "(bit-exact with the reference's order)", **res}
+
+
+def block_launcher(pk, device, weights, batch, stream):
+    """The 15 launches of one Macaron Conformer block (src/webgpu/encoder.ts:
+    1869-2138) on the production kernels, through the C ABI, for `batch`
+    188-frame windows: returns (launch function, device buffers).  The
+    attention takes the positions re-laid out row-major, as the encoder does."""
+    import ctypes
+
+    import torch
+
+    L = pk._lib
+    rows = batch * FRAMES
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    w = {n: (dev(r["data"].view(np.int32)) if r["data"].dtype == np.dtype("<u4") else dev(r["data"]))
+         for n, r in weights.items() if n.startswith("encoder.layers.0.")}
+    p = "encoder.layers.0."
+    f16 = lambda cols: torch.randn((rows, cols), dtype=torch.float16, device="cuda")  # noqa: E731
+    buf = {"x": f16(1024), "a": f16(1024), "h": f16(4096), "x1": f16(1024), "qkv": f16(3072), "ctx": f16(1024),
+           "x2": f16(1024), "g": f16(2048), "c": f16(1024), "x3": f16(1024), "x4": f16(1024), "y": f16(1024)}
+    pos = weights[p + "self_attn.projected_positions"]["data"].reshape(8, 32, 375, 4)
+    w["pos_rm"] = dev(np.ascontiguousarray(pos.transpose(0, 2, 1, 3).reshape(8, 375, 128)))
+    lens = dev(np.full(batch, FRAMES, np.uint32).view(np.int32))
+    vp = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    h = ctypes.c_void_p(stream.cuda_stream)
+    descs = []
+
+    def gemm(name, src, dst, cols, act="none", res=None, scale=1.0):
+        rec = weights[p + name + ".weight"]
+        groups = weights[p + name + ".weight.palette"]["data"].shape[0]
+        d = L.GemmDesc(L.FP16, rows, src.shape[1], cols, rec["bits"], groups, cols // groups, L.ACT[act],
+                       int(res is not None), scale, None, None if res is None else res.data_ptr(), src.data_ptr(),
+                       w[p + name + ".weight"].data_ptr(), w[p + name + ".weight.palette"].data_ptr(), dst.data_ptr())
+        descs.append(d)
+        return lambda: L.call("pk_palette_gemm", device.handle, ctypes.byref(d), h)
+
+    def norm(name, src, dst):
+        return lambda: L.call("pk_layernorm", device.handle, L.FP16, rows, 1024, vp(src), vp(w[p + name + ".weight"]),
+                              vp(w[p + name + ".bias"]), 1e-5, vp(dst), h)
+
+    b = buf
+    ops = [norm("norm_feed_forward1", b["x"], b["a"]), gemm("feed_forward1.linear1", b["a"], b["h"], 4096, "silu"),
+           gemm("feed_forward1.linear2", b["h"], b["x1"], 1024, res=b["x"], scale=0.5),
+           norm("norm_self_att", b["x1"], b["a"]), gemm("self_attn.qkv", b["a"], b["qkv"], 3072),
+           lambda: L.call("pk_rel_attention", device.handle, L.FP16, batch, FRAMES, vp(b["qkv"]), vp(w["pos_rm"]),
+                          vp(w[p + "self_attn.bias_u"]), vp(w[p + "self_attn.bias_v"]), vp(lens), vp(b["ctx"]), h),
+           gemm("self_attn.o_proj", b["ctx"], b["x2"], 1024, res=b["x1"]), norm("norm_conv", b["x2"], b["a"]),
+           gemm("conv.pointwise_conv1", b["a"], b["g"], 2048),
+           lambda: L.call("pk_conformer_conv", device.handle, L.FP16, batch, FRAMES, vp(b["g"]),
+                          vp(w[p + "conv.depthwise_conv.weight"]), vp(w[p + "conv.norm.scale"]),
+                          vp(w[p + "conv.norm.shift"]), vp(lens), vp(b["c"]), h),
+           gemm("conv.pointwise_conv2", b["c"], b["x3"], 1024, res=b["x2"]),
+           norm("norm_feed_forward2", b["x3"], b["a"]), gemm("feed_forward2.linear1", b["a"], b["h"], 4096, "silu"),
+           gemm("feed_forward2.linear2", b["h"], b["x4"], 1024, res=b["x3"], scale=0.5),
+           norm("norm_out", b["x4"], b["y"])]
+
+    def launch():
+        for op in ops:
+            op()
+
+    return launch, (w, buf, lens, descs)
+
+
+def time_config2(pk, device, stream, batch=8, reps=50):
+    """one FP16 FastConformer block, batch 8 x 188 frames,
+    mixed 5/6-bit palettes, inputs N(0, 1); its 15 launches captured in a
+    CUDA graph (the attention on the tcgen05 route with row-major positions,
+    as in the encoder), CUDA events over `reps` replays."""
+    import torch
+
+    weights = pk.synthetic.make_package("fp16", layers=1, seed=21)
+    pk.kernels.set_attention_route("tcgen05-rowmajor")
+    try:
+        launch, keep = block_launcher(pk, device, weights, batch, stream)
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                launch()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream, capture_error_mode="thread_local"):
+            launch()
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(reps):
+                g.replay()
+        end.record(stream)
+        end.synchronize()
+    finally:
+        pk.kernels.set_attention_route("auto")
+    us = start.elapsed_time(end) / reps * 1e3
+    flops = 2.0 * batch * FRAMES * 24117248 + 3 * 2 * batch * FRAMES ** 2 * 1024
+    del keep, g
+    return {"workload": "config2: one FP16 block, 8 x 188 frames, mixed palettes (15 launches in one CUDA graph)",
+            "us_per_block": round(us, 1), "gflops": round(flops / (us * 1e-6) / 1e9, 1),
+            "flop_per_block": flops}
+
+
+def cpu_config12(pk):
+    """CPU baselines of configs 1 and 2: the oracle's reference mode (FP32
+    fma chain for config 1; f16-accumulating GEMMs for config 2) on the
+    host's cores; config 2 on one window (of the 8), scaled per block."""
+    from oracle import oracle
+
+    rng = np.random.default_rng(0)
+    a = rng.standard_normal((188, 1024)).astype(np.float32)
+    codes, lut = pk.synthetic.palette_matrix(rng, 1024, 4096, 6, 1, "fp32")
+    oracle.palette_gemm(a, codes["data"], lut["data"], 6, 4096, acc_mode=0)
+    t0 = time.perf_counter()
+    reps = 5
+    for _ in range(reps):
+        oracle.palette_gemm(a, codes["data"], lut["data"], 6, 4096, acc_mode=0)
+    c1 = (time.perf_counter() - t0) / reps
+    weights = pk.synthetic.make_package("fp16", layers=1, seed=21)
+    x = rng.standard_normal((FRAMES, 1024)).astype(np.float16)
+    t0 = time.perf_counter()
+    oracle.conformer_layer(weights, 0, x, np.array([FRAMES], np.uint32), 1, FRAMES, acc_mode=0)
+    c2 = time.perf_counter() - t0
+    c2_flops = 2.0 * FRAMES * 24117248 + 3 * 2 * FRAMES ** 2 * 1024
+    return {"config1": {"s": round(c1, 4), "gflops": round(2 * 188 * 1024 * 4096 / c1 / 1e9, 2)},
+            "config2": {"s_per_window": round(c2, 3), "gflops": round(c2_flops / c2 / 1e9, 2),
+                        "sample": "1 window of the 8 (windows are independent)"}}
+
+
+def time_fp32_encoder(pk, device, stream, batch=8, reps=5):
+    """The FP32 package's 24-layer encoder (f32 activations and LUTs, CUDA-core
+    fp32 fma-chain GEMMs in the reference's order) on `batch` 15 s windows:
+    audio-s/s and the GEMMs' FLOP rate against the FFMA peak."""
+    import torch
+
+    package = pk.synthetic.make_package("fp32", seed=7)
+    g = pk.encoder.ParakeetEncoderGraph.create(device, package, "fp32", capacity=batch)
+    feats = torch.from_numpy(pk.synthetic.make_features(batch, seed=8)).cuda()
+    lengths = [FEATURE_LENGTH] * batch
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            g.encode(feats, lengths, stream=stream)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(reps):
+            g.encode(feats, lengths, stream=stream)
+        end.record(stream)
+    end.synchronize()
+    ms = start.elapsed_time(end) / reps
+    g.destroy()
+    g.weights.release()
+    props = torch.cuda.get_device_properties(device.ordinal)
+    gemm_flops = sum(2.0 * (m // BATCH) * batch * k * n * launches
+                     for m, k, n, _, _, _, _, launches in gemm_shapes(BATCH))
+    return {"workload": f"FP32 package encoder, {batch} x 15 s windows", "ms_per_step": round(ms, 2),
+            "audio_s_per_s": round(batch * WINDOW_SECONDS / (ms * 1e-3), 1),
+            "gemm_tflop_per_step": round(gemm_flops / 1e12, 3),
+            "gemm_tflops_if_all_time": round(gemm_flops / (ms * 1e-3) / 1e12, 2),
+            "ffma_peak_tflops_at_max_clock": round(props.multi_processor_count * FFMA_LANES_PER_SM * 2 * 1.965e9
+                                                   / 1e12, 1),
+            "peak_note": "SMs x 128 FP32 lanes x 2 FLOP x 1965 MHz (clocks.max.sm); the GEMM rate counts the whole "
+                         "step's time, so it is a lower bound"}
 
 
 def cpu_baseline(pk, package, window_count=1):
@@ -519,24 +778,21 @@ def run_ours(args):
     ms = max_over_ranks(start.elapsed_time(end) / args.steps)
     status = device.status()
 
-    # ---- end to end through the public API with host buffers
-    pinned = torch.from_numpy(features).pin_memory()
-    host_out = torch.empty((BATCH * FRAMES, 640), dtype=torch.float16).pin_memory()
-    with torch.cuda.stream(stream):
-        for _ in range(2):
-            graph.encode(pinned.numpy(), lengths, stream=stream, out=host_out)
+    # ---- end to end through the public API with host buffers (copies overlapped with compute)
     barrier()
-    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t_start.record(stream)
-    with torch.cuda.stream(stream):
-        for _ in range(args.steps):
-            graph.encode(pinned.numpy(), lengths, stream=stream, out=host_out)
-    t_end.record(stream)
-    t_end.synchronize()
+    e2e_ms, h2d_bytes, d2h_bytes = time_e2e_pipelined(pk, graph, features, lengths, stream, args.steps)
     barrier()
-    e2e_ms = max_over_ranks(t_start.elapsed_time(t_end) / args.steps)
+    e2e_ms = max_over_ranks(e2e_ms)
 
     legs = set(args.legs.split(","))
+
+    # ---- BASELINE configs 1 and 2 on the GPU, and the FP32 package's encoder
+    c12_info = None
+    if "config12" in legs:
+        c12_info = {"config1": time_config1(pk, device, stream), "config2": time_config2(pk, device, stream)}
+    barrier()
+    fp32_info = time_fp32_encoder(pk, device, stream) if "fp32" in legs else None
+    barrier()
 
     # ---- log-mel front end for this batch (32 x 240 000 samples of PCM)
     lm_info = time_logmel(pk, device, stream) if "logmel" in legs else None
@@ -576,6 +832,9 @@ def run_ours(args):
         if world == 1 and not args.skip_cpu_baseline:
             os.environ.setdefault("OMP_NUM_THREADS", str(cores))
             cpu_value, cpu_dt = cpu_baseline(pk, package, 1)
+            if c12_info is not None:
+                c12_info["cpu"] = cpu_config12(pk)
+                c12_info["cpu"]["cores"] = int(os.environ.get("OMP_NUM_THREADS", cores))
         traffic = GEMM_DRAM_BYTES_PER_STEP
         line = {
             "metric": METRIC, "value": round(audio / (ms * 1e-3), 1), "unit": UNIT, "n_gpus": world,
@@ -584,10 +843,14 @@ def run_ours(args):
             "config": {"workload": "config3: full 24-layer FP16 encoder, batch 32 x 15 s windows per GPU",
                        "global_batch": world * BATCH, "seq_len": FRAMES, "parallelism": f"window-shard x{world}",
                        "palette_bits": "mixed (o_proj 6-bit, rest 5-bit)",
+                       "audio_seconds": "each of the 32 independent 15 s windows counts 15 s (window-seconds); "
+                                        "the longform legs count source audio",
                        "l2": "working set per step > 126 MB L2 (weights 365 MB packed + activations); "
                              "roofline GEMMs timed back to back over rotating operand sets > 256 MB"},
             "e2e": {"value": round(audio / (e2e_ms * 1e-3), 1), "unit": UNIT,
-                    "h2d_bytes_per_step": int(features.nbytes), "d2h_bytes_per_step": int(host_out.numel() * 2)},
+                    "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h_bytes,
+                    "note": "ParakeetEncoderGraph.encode per step; each step's pinned H2D features and D2H "
+                            "projected output on a copy stream, overlapping the neighbouring steps' encoder work"},
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": round(achieved / peak_tf, 4), "traffic": traffic,
                          "kernel": "palette GEMMs (tc2_/tc_palette_gemm, all launches of one step)",
@@ -595,6 +858,8 @@ def run_ours(args):
                          "peak_kind": f"bf16 dense burst, {peak_kind}",
                          "gemm_ms_per_step": round(gemm_ms, 3), "gemm_tflop_per_step": round(gemm_flops / 1e12, 3)},
             "gemm_shapes": gemm_detail,
+            "config1_config2": c12_info,
+            "fp32_encoder": fp32_info,
             "decoder": dec_info,
             "logmel": lm_info,
             "transcribe": tr_info,
@@ -727,12 +992,12 @@ def run_kernel(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=250)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
     ap.add_argument("--skip-longform", action="store_true")
-    ap.add_argument("--legs", default="logmel,decoder,transcribe,longform,gemm",
+    ap.add_argument("--legs", default="logmel,decoder,transcribe,longform,gemm,config12,fp32",
                     help="comma-separated extra legs to run besides the encoder step (a subset for quick runs)")
     ap.add_argument("--kernel", choices=["gemm", "gemm-step", "attention", "attention-mma", "layernorm", "conv",
                                          "subsampling", "decoder", "logmel"],

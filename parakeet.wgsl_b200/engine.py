@@ -15,6 +15,7 @@ window plan across ranks (one GPU each); only the token lists travel to rank
 """
 from __future__ import annotations
 
+from concurrent.futures import ThreadPoolExecutor
 from dataclasses import dataclass
 from typing import Sequence
 
@@ -75,6 +76,9 @@ class ParakeetEngine:
             tokens=torch.zeros((3, capacity, max_tokens), dtype=torch.int32).pin_memory(),
             meta=torch.zeros(2 * capacity, dtype=torch.int32).pin_memory(),
             done=torch.cuda.Event()) for _ in range(2)]
+        for slot in self._slots:
+            slot["pcm_np"] = slot["pcm"].numpy()
+        self._copy_pool = ThreadPoolExecutor(max_workers=_staging_threads())
         self._dispatch = self.decoder.create_dispatch(dict(
             encoder_projected=self.graph.decoder_input(), encoded_lengths=self._control[1],
             decode_starts=self._control[2], decode_ends=self._control[3], flush_finals=self._control[4],
@@ -115,16 +119,15 @@ class ParakeetEngine:
         stream = torch.cuda.current_stream() if stream is None else stream
         host = self._slots[slot]
         pcm, ctrl = host["pcm"], host["control"]
+        arena = host["pcm_np"]
         lengths = []
+        copies = []
         for i, (samples, plan) in enumerate(windows):
             samples = np.asarray(samples, dtype=np.float32)
             if samples.ndim != 1 or samples.shape[0] > WINDOW_SAMPLES or plan.valid_sample_count > samples.shape[0]:
                 raise RangeError(f"Window {i} must hold its {plan.valid_sample_count} valid samples in at most "
                                  f"{WINDOW_SAMPLES}")
-            n = samples.shape[0]
-            pcm[i, :n] = torch.from_numpy(samples)
-            if n < WINDOW_SAMPLES:
-                pcm[i, n:].zero_()
+            copies.append((i, samples))
             feature_frames = max(1, plan.valid_sample_count // wp.HOP_SAMPLES)
             enc_len = derive_encoder_valid_length(feature_frames)
             if plan.decode_start_frame > enc_len:
@@ -135,6 +138,10 @@ class ParakeetEngine:
             ctrl[2, i] = plan.decode_start_frame
             ctrl[3, i] = plan.decode_end_frame
             ctrl[4, i] = int(plan.flush_final)
+        # The PCM copies into the pinned slot run on a few host threads (numpy
+        # releases the GIL while copying): at one batch per rank they are not
+        # hidden behind a previous batch's GPU work.
+        list(self._copy_pool.map(lambda job: _stage_window(arena, *job), copies))
         with torch.cuda.stream(stream):
             self._pcm[:b].copy_(pcm[:b], non_blocking=True)
             self._control.copy_(ctrl, non_blocking=True)
@@ -166,12 +173,13 @@ class ParakeetEngine:
             out.append((tok[i, :n].copy(), fr[i, :n].copy(), du[i, :n].copy(), bool(flags[i] & 1)))
         return out
 
-    def batches(self, count: int) -> list[range]:
+    def batches(self, count: int, limit: int | None = None) -> list[range]:
         """Splits `count` windows into the fewest batches of at most
-        `capacity`, as equal in size as possible (35 windows at capacity 32
-        run as 18 + 17, not 32 + 3: a batch costs about as much as its
-        longest window, whatever its size)."""
-        n = -(-count // self.capacity) if count else 0
+        `limit` (default: capacity) windows, as equal in size as possible (35
+        windows at capacity 32 run as 18 + 17, not 32 + 3: a decoder batch
+        costs about as much as its longest window, whatever its size)."""
+        cap = min(self.capacity, limit or self.capacity)
+        n = -(-count // cap) if count else 0
         edges = [round(k * count / n) for k in range(n + 1)] if n else [0]
         return [range(a, b) for a, b in zip(edges, edges[1:])]
 
@@ -212,13 +220,15 @@ class ParakeetEngine:
         self._check_status()
         return decoded
 
-    def encode_plans(self, pcm: np.ndarray, plans: Sequence[wp.WindowPlan], stream=None) -> int:
+    def encode_plans(self, pcm: np.ndarray, plans: Sequence[wp.WindowPlan], stream=None,
+                     batch: int | None = None) -> int:
         """Log-mel front end and encoder only, for `plans` in balanced
-        batches with the same two-slot pipelining as decode_plans; each
-        batch's projected encoder output is left on the device (where the
-        decoder would read it).  Returns the number of windows encoded."""
+        batches of at most `batch` (default: capacity) windows with the same
+        two-slot pipelining as decode_plans; each batch's projected encoder
+        output is left on the device (where the decoder would read it).
+        Returns the number of windows encoded."""
         pending = None
-        for k, rows in enumerate(self.batches(len(plans))):
+        for k, rows in enumerate(self.batches(len(plans), batch)):
             chunk = plans[rows.start:rows.stop]
             ticket = self._submit([(pcm[p.source_start_sample:p.source_end_sample], p) for p in chunk], stream,
                                   k % 2, decode=False)
@@ -241,8 +251,29 @@ class ParakeetEngine:
         return acc.snapshot()
 
     def destroy(self) -> None:
+        self._copy_pool.shutdown(wait=True)
         self.graph.destroy()
         self.weights.release()
+
+
+def _staging_threads() -> int:
+    """Host threads for staging PCM: the cores this process may use, shared
+    among the ranks of this node (LOCAL_WORLD_SIZE), at most 8."""
+    import os
+
+    try:
+        cores = len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover - non-Linux
+        cores = os.cpu_count() or 1
+    ranks = int(os.environ.get("LOCAL_WORLD_SIZE", "1") or 1)
+    return max(1, min(8, cores // max(1, ranks)))
+
+
+def _stage_window(arena: np.ndarray, i: int, samples: np.ndarray) -> None:
+    n = samples.shape[0]
+    np.copyto(arena[i, :n], samples)
+    if n < WINDOW_SAMPLES:
+        arena[i, n:] = 0.0
 
 
 def _accumulator(token_piece):
@@ -361,25 +392,29 @@ def transcribe_sharded(engine, pcm: np.ndarray, rank: int, world_size: int, gath
 
 def array_gather(rank: int, world_size: int, device=None):
     """A `gather` for transcribe_sharded over torch.distributed: every rank's
-    flat int64 array reaches rank 0 as plain tensors (lengths first, then
-    one padded gather; NCCL tensors on `device`, CPU tensors for gloo).
-    Returns a list of arrays on rank 0 and None elsewhere."""
+    flat int64 array reaches rank 0 as plain tensors -- the lengths first,
+    then one padded all-gather (the communicator's collective channels; a
+    point-to-point gather would set up peer connections on first use).  NCCL
+    tensors on `device`, CPU tensors for gloo.  Returns a list of arrays on
+    rank 0 and None elsewhere."""
     import torch.distributed as dist
 
     def gather(flat: np.ndarray):
         t = torch.from_numpy(np.ascontiguousarray(flat, dtype=np.int64))
         if device is not None:
-            t = t.to(device)
+            t = t.to(device, non_blocking=False)
         n = torch.tensor([t.numel()], dtype=torch.int64, device=t.device)
-        sizes = [torch.zeros_like(n) for _ in range(world_size)]
-        dist.all_gather(sizes, n)
-        sizes = [int(v.item()) for v in sizes]
-        padded = torch.zeros(max(sizes), dtype=torch.int64, device=t.device)
+        sizes = torch.zeros(world_size, dtype=torch.int64, device=t.device)
+        dist.all_gather_into_tensor(sizes, n)
+        sizes = sizes.tolist()
+        width = max(sizes)
+        padded = torch.zeros(width, dtype=torch.int64, device=t.device)
         padded[:t.numel()] = t
-        bufs = [torch.empty_like(padded) for _ in range(world_size)] if rank == 0 else None
-        dist.gather(padded, bufs, dst=0)
+        everything = torch.empty(world_size * width, dtype=torch.int64, device=t.device)
+        dist.all_gather_into_tensor(everything, padded)
         if rank != 0:
             return None
-        return [b[:k].cpu().numpy() for b, k in zip(bufs, sizes)]
+        host = everything.cpu().numpy()
+        return [host[r * width:r * width + k] for r, k in enumerate(sizes)]
 
     return gather
