@@ -309,7 +309,13 @@ def time_transcribe(pk, device, package, seconds=60.0, reps=2):
 LONGFORM_VARIANTS = (("fp16", "mixed", 3600.0), ("fp16", "all5", 3600.0), ("fp32", "mixed", 600.0),
                      ("fp32", "all5", 600.0))
 LONGFORM_CAPACITY = 40  # windows per engine batch (the reference's encoder capacity)
-LONGFORM_ENCODER_BATCH = 20  # encoder-only leg: windows per pipelined batch (staging overlaps the GPU)
+
+
+def encoder_batch(windows: int, capacity: int) -> int:
+    """Encoder-only leg: batches of up to `capacity` windows, but at least two
+    batches per rank, so one batch's host staging overlaps the other's GPU
+    work (one hour on one GPU: 7 x 40; on eight: 18 + 17)."""
+    return max(1, min(capacity, -(-windows // 2)))
 
 
 def longform_pcm(pk, seconds, seed=5, distinct=5):
@@ -405,15 +411,16 @@ def time_longform_encoder(pk, device, rank, world, stream, capacity=None, second
     pcm = longform_pcm(pk, seconds)
     plans = pk.windows.plan_stateless_windows(len(pcm))
     mine = [plans[i] for i in pk.windows.shard_windows(len(plans), world, rank)]
+    batch = encoder_batch(len(mine), capacity)
     with torch.cuda.stream(stream):
-        for rows in eng.batches(len(mine), LONGFORM_ENCODER_BATCH):  # warm-up: every graph size is recorded
+        for rows in eng.batches(len(mine), batch):  # warm-up: every graph size is recorded
             eng.encode_plans(pcm, mine[rows.start:rows.stop])
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record(stream)
-        eng.encode_plans(pcm, mine, batch=LONGFORM_ENCODER_BATCH)
+        eng.encode_plans(pcm, mine, batch=batch)
         end.record(stream)
         end.synchronize()
     ms = start.elapsed_time(end)
@@ -425,7 +432,7 @@ def time_longform_encoder(pk, device, rank, world, stream, capacity=None, second
     return {"workload": "config5 encoder only: one hour of synthetic PCM, window plan sharded over ranks, "
                         "log-mel + 24-layer FP16 encoder (mixed palettes), host PCM in, encoder output on device",
             "n_gpus": world, "audio_s": seconds, "windows": len(plans),
-            "rank_batches": [len(r) for r in eng.batches(len(mine), LONGFORM_ENCODER_BATCH)],
+            "rank_batches": [len(r) for r in eng.batches(len(mine), batch)],
             "s": round(ms / 1e3, 4), "audio_s_per_s": round(seconds / (ms / 1e3), 1)}
 
 
