@@ -168,8 +168,13 @@ int require_matrix(pk_weights* w, const std::string& name, int64_t inner, int64_
   return PK_OK;
 }
 
+// `mask`: the subsampling time mask (rows of mask_group outputs per frame,
+// 188 frames per window, encoder lengths on the device), fused into the
+// single-CTA tensor-core epilogue when that kernel runs; *masked says whether
+// it was, else the caller masks.
 int gemm(pk_encoder* e, const MatrixRef& m, int64_t rows, const void* a, void* c, int act, const float* bias,
-         const void* residual, float res_scale, cudaStream_t s) {
+         const void* residual, float res_scale, cudaStream_t s, const uint32_t* mask = nullptr, int mask_group = 1,
+         bool* masked = nullptr) {
   GemmArgs g;
   g.precision = e->precision;
   g.rows = rows;
@@ -189,7 +194,14 @@ int gemm(pk_encoder* e, const MatrixRef& m, int64_t rows, const void* a, void* c
   g.c = c;
   int st = validate_gemm(g);
   if (st) return st;
-  if (gemm_tc_supported(g) && !gemm_route_simt()) return launch_gemm_tc(e->device->ctx, g, s);
+  if (masked) *masked = false;
+  if (gemm_tc_supported(g) && !gemm_route_simt()) {
+    g.mask_lengths = mask;
+    g.mask_group = mask_group;
+    g.mask_frames = kFrames;
+    g.mask_applied = masked;
+    return launch_gemm_tc(e->device->ctx, g, s);
+  }
   return launch_gemm_simt(e->device->ctx, g, s);
 }
 
@@ -211,8 +223,12 @@ int record_forward(pk_encoder* e, int batch, cudaStream_t s) {
   PK_TRY(gemm(e, e->pw3, (int64_t)batch * 376 * 32, e->s376, e->p376, PK_ACT_RELU, e->pw3_b, nullptr, 1.0f, s));
   PK_TRY(launch_subsampling_depthwise(prec, batch, 376, 32, 256, e->p376, e->dw5_w, e->dw5_b, e->feature_lengths, 3,
                                       e->s188, s));
-  PK_TRY(gemm(e, e->pw6, (int64_t)batch * 188 * 16, e->s188, e->p188, PK_ACT_RELU, e->pw6_b, nullptr, 1.0f, s));
-  PK_TRY(launch_subsampling_time_mask(prec, batch, 188, 16, 256, e->p188, e->feature_lengths, 3, s));
+  // Frames past each window's encoder length are zeroed in the pointwise-6
+  // epilogue (the tensor-core path), else by the separate mask kernel.
+  bool masked = false;
+  PK_TRY(gemm(e, e->pw6, (int64_t)batch * 188 * 16, e->s188, e->p188, PK_ACT_RELU, e->pw6_b, nullptr, 1.0f, s,
+              e->encoder_lengths, 16, &masked));
+  if (!masked) PK_TRY(launch_subsampling_time_mask(prec, batch, 188, 16, 256, e->p188, e->feature_lengths, 3, s));
   PK_TRY(gemm(e, e->flat, rows, e->p188, e->slots[0], PK_ACT_NONE, e->flat_b, nullptr, 1.0f, s));
   if (e->keep_checkpoints)
     PK_TRY(cuda_error(cudaMemcpyAsync(e->checkpoints[0], e->slots[0], rows * kHidden * e->scalar,

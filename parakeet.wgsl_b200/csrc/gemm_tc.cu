@@ -73,7 +73,23 @@ struct TcGemmParams {
   int m_tiles, n_tiles;
   CUtensorMap tmap_res;     // CTA-pair kernel: residual [M, N] f16, box {64, T/2}, 128B swizzle
   uint32_t res_inv_h;       // CTA-pair kernel: f16 bits of 1 / res_scale (a power of two)
+  const uint32_t* mask_lengths;  // time mask (GemmArgs), or null
+  int mask_group, mask_frames;
 };
+
+// Whether output row `row` passes the time mask (rows past the end read no
+// length; they are not stored).
+__device__ __forceinline__ bool mask_keeps(const TcGemmParams& p, int row) {
+  if (row >= p.rows) return false;
+  const int fr = row / p.mask_group;
+  const int w = fr / p.mask_frames;
+  return (uint32_t)(fr - w * p.mask_frames) < __ldg(p.mask_lengths + w);
+}
+// Bit e set: output row row0 + e is kept by the time mask.  Lane e evaluates
+// row row0 + e; the warp must be converged.
+__device__ __forceinline__ uint32_t mask_keep_bits(const TcGemmParams& p, int row0) {
+  return __ballot_sync(0xffffffffu, mask_keeps(p, row0 + (int)(threadIdx.x & 31)));
+}
 
 template <int BN, int BITS>
 struct TcLayout {
@@ -201,7 +217,8 @@ __device__ __forceinline__ float activate(float v) {
 // between two slots).
 template <int EPI, int ACT, int COUNT>
 __device__ __forceinline__ void epilogue_run(const uint32_t (&r)[32], float bias_v, const __half* __restrict__ res,
-                                             __half* __restrict__ out, int ld, float res_scale, int count) {
+                                             __half* __restrict__ out, int ld, float res_scale, int count,
+                                             uint32_t keep) {
   __half rv[EPI == EPI_RESIDUAL ? 32 : 1];
   if constexpr (EPI == EPI_RESIDUAL) {
 #pragma unroll
@@ -216,7 +233,7 @@ __device__ __forceinline__ void epilogue_run(const uint32_t (&r)[32], float bias
       v = activate<ACT>(v);
       if constexpr (EPI == EPI_RESIDUAL) v = __half2float(rv[j]) + res_scale * v;
       if constexpr (EPI == EPI_RESADD) v *= res_scale;
-      out[(size_t)j * ld] = __float2half_rn(v);
+      out[(size_t)j * ld] = (keep >> j) & 1u ? __float2half_rn(v) : __float2half_rn(0.0f);
     }
   }
 }
@@ -254,7 +271,7 @@ __device__ __forceinline__ void pair_epilogue_chunk(const uint32_t (&r)[32], flo
   }
 }
 
-template <int BN, int BITS, int EPI, int ACT>
+template <int BN, int BITS, int EPI, int ACT, bool MASK = false>
 __global__ void __launch_bounds__(TC_THREADS, 1) tc_palette_gemm_kernel(const __grid_constant__ TcGemmParams p) {
   using L = TcLayout<BN, BITS>;
   __shared__ __align__(16) uint16_t s_lut[3 * 64];
@@ -466,10 +483,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_palette_gemm_kernel(const __
         tc_wait_ld();
         const size_t base = (size_t)(m0 + c) * ld + n;
         const __half* res = EPI == EPI_RESIDUAL ? p.residual + base : nullptr;
+        const uint32_t keep = MASK ? mask_keep_bits(p, m0 + c) : 0xffffffffu;
         if (left >= 32)
-          epilogue_run<EPI, ACT, 32>(r, bias_v, res, p.out + base, ld, p.res_scale, 32);
+          epilogue_run<EPI, ACT, 32>(r, bias_v, res, p.out + base, ld, p.res_scale, 32, keep);
         else
-          epilogue_run<EPI, ACT, 31>(r, bias_v, res, p.out + base, ld, p.res_scale, left);
+          epilogue_run<EPI, ACT, 31>(r, bias_v, res, p.out + base, ld, p.res_scale, left, keep);
       }
       tc_fence_before();
       __syncwarp();
@@ -966,10 +984,10 @@ bool gemm_tc_supported(const GemmArgs& g) {
          (reinterpret_cast<uintptr_t>(g.a) & 15) == 0 && (reinterpret_cast<uintptr_t>(g.codes) & 15) == 0;
 }
 
-template <int BN, int BITS, int EPI, int ACT>
-static int launch_tc_spec(const DeviceCtx& dev, const TcGemmParams& p, cudaStream_t stream) {
+template <int BN, int BITS, int EPI, int ACT, bool MASK>
+static int launch_tc_kernel(const DeviceCtx& dev, const TcGemmParams& p, cudaStream_t stream) {
   using L = TcLayout<BN, BITS>;
-  auto kernel = tc_palette_gemm_kernel<BN, BITS, EPI, ACT>;
+  auto kernel = tc_palette_gemm_kernel<BN, BITS, EPI, ACT, MASK>;
   // Opt-in shared memory is a per-device function attribute; set it once per
   // device (a racing duplicate set is harmless).
   static bool configured[32] = {};
@@ -981,6 +999,15 @@ static int launch_tc_spec(const DeviceCtx& dev, const TcGemmParams& p, cudaStrea
   const int tiles = p.m_tiles * p.n_tiles;
   return cuda_error(launch_kernel(kernel, dim3(std::min(tiles, dev.sm_count)), dim3(TC_THREADS), L::SMEM_BYTES, stream, p),
                     "tc_palette_gemm launch");
+}
+
+// The time mask has its own instantiation of the bias + ReLU epilogue (the
+// subsampling pointwise GEMMs); every other launch compiles without it.
+template <int BN, int BITS, int EPI, int ACT>
+static int launch_tc_spec(const DeviceCtx& dev, const TcGemmParams& p, cudaStream_t stream) {
+  if constexpr (EPI == EPI_BIAS && ACT == PK_ACT_RELU)
+    if (p.mask_lengths) return launch_tc_kernel<BN, BITS, EPI, ACT, true>(dev, p, stream);
+  return launch_tc_kernel<BN, BITS, EPI, ACT, false>(dev, p, stream);
 }
 
 // Whether the residual is folded into the accumulator as residual / scale
@@ -1023,6 +1050,9 @@ static int launch_tc(const DeviceCtx& dev, const GemmArgs& g, cudaStream_t strea
   p.groups = g.groups;
   p.group_cols = (int)g.group_cols;
   p.res_scale = g.residual_scale;
+  p.mask_lengths = g.mask_lengths;
+  p.mask_group = g.mask_group > 0 ? g.mask_group : 1;
+  p.mask_frames = g.mask_frames > 0 ? g.mask_frames : 1;
   p.m_tiles = (int)((g.rows + BN - 1) / BN);
   p.n_tiles = (int)(g.columns / TC_BM);
   const bool fold = residual_folds(g);
@@ -1105,6 +1135,9 @@ static int launch_tc2(const DeviceCtx& dev, const GemmArgs& g, cudaStream_t stre
   p.groups = g.groups;
   p.group_cols = (int)g.group_cols;
   p.res_scale = g.residual_scale;
+  p.mask_lengths = g.mask_lengths;
+  p.mask_group = g.mask_group > 0 ? g.mask_group : 1;
+  p.mask_frames = g.mask_frames > 0 ? g.mask_frames : 1;
   p.m_tiles = (int)((g.rows + L::T - 1) / L::T);
   p.n_tiles = (int)(g.columns / TC_BM);
   if (g.has_residual && !residual_folds(g)) return set_error(PK_E_INVALID, "CTA-pair GEMM: residual must fold");
@@ -1173,6 +1206,17 @@ int launch_gemm_tc(const DeviceCtx& dev, const GemmArgs& g, cudaStream_t stream,
   const bool allow_single = g_gemm_route != 4 || !allow_pair;
   int bn = forced_bn ? forced_bn : g_gemm_tile ? g_gemm_tile : choose_tile(dev, g, allow_single, allow_pair);
   if (bn < 0 && !allow_pair) bn = 256;
+  if (g.mask_lengths) {
+    // The time mask rides on the single-CTA bias + ReLU epilogue only; the
+    // caller masks separately otherwise.
+    const bool fused = bn > 0 && g.bias && g.act == PK_ACT_RELU && !g.has_residual;
+    if (g.mask_applied) *g.mask_applied = fused;
+    if (!fused) {
+      GemmArgs plain = g;
+      plain.mask_lengths = nullptr;
+      return launch_gemm_tc(dev, plain, stream, bn);
+    }
+  }
   const bool b5 = g.bits == 5;
   switch (bn) {
     case -512: return b5 ? launch_tc2<256, 2, 5>(dev, g, stream) : launch_tc2<256, 2, 6>(dev, g, stream);

@@ -64,6 +64,12 @@ struct GemmArgs {
   const uint32_t* codes = nullptr;
   const void* palette = nullptr;
   void* c = nullptr;
+  // Optional time mask fused into the tensor-core epilogues: output row r
+  // (frame f = (r / mask_group) % mask_frames of window (r / mask_group) /
+  // mask_frames) is stored as zero when f >= mask_lengths[window].
+  const uint32_t* mask_lengths = nullptr;
+  int mask_group = 1, mask_frames = 1;
+  bool* mask_applied = nullptr;  // set by the tensor-core launcher: whether the mask was fused
 };
 
 // Raises a kernel's dynamic shared-memory limit on the current device, once
