@@ -22,7 +22,7 @@ struct DeviceCtx {
 // Bytes of the resident TDT decoder's exchange area (hidden / projection
 // vectors, argmax partials and the grid-barrier counter for up to 40 windows),
 // allocated with the device handle.
-constexpr size_t kTdtExchangeBytes = 1024 * 1024;
+constexpr size_t kTdtExchangeBytes = 12ull * 1024 * 1024;
 
 // Thread-local error reporting.
 int set_error(int code, const char* fmt, ...);

@@ -8,8 +8,8 @@
 // each hold a fixed 1/128 of every decoder weight in shared memory for the
 // whole launch: LSTM channels [5 c, 5 c + 5) of both layers (all four gates
 // of each, so the cell update is local), the projector outputs of those
-// channels and head columns [8 c, 8 c + 8) (the last CTA also the 8-column
-// blank/duration tail).  Each step every CTA computes its slice for every
+// channels and head columns [8 c, 8 c + 8) (CTA 0 also the blank's column,
+// CTAs 1..5 one duration column each).  Each step every CTA computes its slice for every
 // window that needs it, writes the slice to an exchange area in global memory
 // and meets the others at a grid barrier (thread 0 arrives on a counter and
 // waits with an acquire load, bounded by %globaltimer); readers fetch the
@@ -51,17 +51,21 @@ constexpr int RG = 128;               // CTAs, all resident at once
 constexpr int RCH = RH / RG;          // 5 LSTM channels per CTA
 constexpr int RGATES = 4 * RCH;       // 20 gate outputs per CTA
 constexpr int RTOK = 1024 / RG;       // 8 token columns per CTA
-constexpr int RHEADCOLS = 16;         // token columns + the tail slot
+constexpr int RHEADCOLS = 9;          // head columns per CTA: 8 tokens, + one tail column in CTAs 0..5
+constexpr int RTAIL_CTAS = 6;         // CTA 0: the blank (head column 1024); CTA c in 1..5: duration c - 1
+constexpr int RHG = 3;                // head columns per chain thread
 constexpr int RMAXB = 40;             // windows per launch
 constexpr int RPAIRS = RMAXB / 2;     // window pairs (half2 lanes)
 constexpr int RHALF = RH / 2;         // joint / projector inputs per staged half
-constexpr int RLSTM_PAIRS = 4;        // window pairs per LSTM chain thread
-constexpr int RLSTM_GROUPS = RPAIRS / RLSTM_PAIRS;       // 5
-constexpr int RLSTM_PER_PAR = RGATES * RLSTM_GROUPS;     // chain threads per parity: (output, group), 100
+constexpr int RLSTM_RP = RGATES / 2;  // gate-output pairs (an LSTM chain thread owns two outputs)
+constexpr int RLSTM_PP = RPAIRS / 2;  // window-pair pairs (... and two window pairs)
+constexpr int RLSTM_PER_PAR = RLSTM_RP * RLSTM_PP;       // chain threads per parity: 100
 constexpr int RLSTM_THREADS = 2 * RLSTM_PER_PAR;         // 200
-constexpr int RW_STRIDE = RKIN + 8;   // padded weight row (halfs): rows start 16 bytes apart in the banks
-constexpr int RHW_STRIDE = RH + 8;    // padded head row: the 16 columns' loads spread over the banks
-constexpr int RHEAD_THREADS = RHEADCOLS * RPAIRS;        // column x window pair: 320
+constexpr int RPW = RH / 2;           // same-parity inputs of a staged half
+constexpr int RW1P = RH + 8;          // layer-1 weight row of one parity (640 inputs), padded
+constexpr int RW0P = RPW + 8;         // layer-0 recurrent weight row of one parity (320 inputs), padded
+constexpr int RHW_STRIDE = RH + 8;    // padded head / layer-0 row: consecutive rows' loads hit different banks
+constexpr int RHEAD_THREADS = RHEADCOLS / RHG * RPAIRS;  // column group x window pair: 60
 constexpr int RPROJ_THREADS = RCH * RMAXB;               // output x window: 200
 constexpr int RCHUNK = 8;             // chain steps per operand load
 constexpr int RTHREADS = 640;
@@ -69,7 +73,7 @@ constexpr int RROW16 = RMAXB * 2 / 16;  // 16-byte chunks per exchanged f16 row 
 constexpr float RNEG = -3.402823466e+38f;
 static_assert(RG * RCH == RH && RG * RTOK == 1024, "slices tile the matrices");
 static_assert(RTHREADS == RH, "one thread per joint input");
-static_assert(RLSTM_THREADS <= RTHREADS && RHEAD_THREADS % 32 == 0 && RHEAD_THREADS <= RTHREADS, "thread roles fit");
+static_assert(RLSTM_THREADS <= RTHREADS && RHEAD_THREADS <= RTHREADS && RHEADCOLS % RHG == 0, "thread roles fit");
 static_assert((RMAXB * 2) % 16 == 0, "exchanged f16 rows are whole 16-byte chunks");
 static_assert(RH % (2 * RCHUNK) == 0 && RHALF % RCHUNK == 0, "chunks never straddle a staged half");
 
@@ -87,7 +91,20 @@ constexpr size_t XH1F = XH1N + 1ull * RH * RMAXB * 2;     // float [640][40]: la
 constexpr size_t XPROJ = XH1F + 1ull * RH * RMAXB * 4;    // float [40][640]: predictor projection
 constexpr size_t XPART = XPROJ + 1ull * RMAXB * RH * 4;   // RPartial [2][40][128]: argmax partials
 constexpr size_t XSYNC = XPART + 2ull * RMAXB * RG * 16;  // barrier counter, abort flag
-static_assert(XSYNC + 256 <= kTdtExchangeBytes, "exchange area fits");
+// __half [128 CTAs][1024 tokens][20 gates][2 parities]: the state of each of a
+// CTA's layer-0 gate chains after the 640 embedding inputs of a token (even
+// chain from f16(bias), odd chain from zero), written by tdt_token_table_kernel
+// before the decode; a token's 80 bytes per CTA are contiguous.
+constexpr size_t XTT = XSYNC + 256;
+constexpr int RTOKENS = 1024;         // tokens that feed the LSTM (the blank never does)
+constexpr size_t XTT_BYTES = 1ull * RG * RTOKENS * RGATES * 2 * 2;
+// float [640][40]: the joint inputs max(enc + proj, 0) of the step, row k
+// written by the CTA that owns projector output k (steps with an LSTM update).
+constexpr size_t XJIN = XTT + XTT_BYTES;
+// uint32 [20][640]: the same inputs rounded to f16, as the half2 of windows
+// 2 p, 2 p + 1 (the head chains' operand layout, staged by plain copies).
+constexpr size_t XJ2 = XJIN + 1ull * RH * RMAXB * 4;
+static_assert(XJ2 + 1ull * RPAIRS * RH * 4 <= kTdtExchangeBytes, "exchange area fits");
 static_assert(XSYNC % 16 == 0, "exchange arrays stay 16-byte aligned");
 
 struct __align__(16) RPartial {
@@ -107,28 +124,32 @@ struct RWin {
 };
 
 struct RSmem {
-  __half w0[RGATES][RW_STRIDE];      // [gate output][input] (inputs fastest)
-  __half w1[RGATES][RW_STRIDE];
+  __half w0[2][RGATES][RW0P];        // layer 0, recurrent input 640 + 2 m + parity: [parity][gate output][m]
+  __half w1[2][RGATES][RW1P];        // layer 1, input 2 m + parity: [parity][gate output][m]
   __half hw[RHEADCOLS][RHW_STRIDE];  // [head column][input]
   float pwf[RCH][RH];                // projector weights as f32, [output][input]
   union {
     __half2 x2[RH][RPAIRS];          // one half of an LSTM layer's inputs, [input][window pair]
     float hf[RMAXB][RHALF + 4];      // one half of the projector inputs, [window][input] (rows padded)
     struct {
-      uint32_t j2[RPAIRS][RHALF];    // one half of the joint inputs, [window pair][input] (half2 bits)
-      uint32_t keep[RPAIRS][RHALF];  // per pair and input: the lanes whose head chain skips it
-    } jt;
+      uint32_t j2[RPAIRS][RHALF + 4];    // one half of the joint inputs, [window pair][input] (half2 bits)
+      uint32_t keep[RPAIRS][RHALF + 4];  // per pair and input: the lanes whose head chain skips it
+    } jt;                                // (rows padded: the pairs of a warp read different banks)
     RPartial red[RMAXB][20];         // argmax reduction
   } in;
   float gates[RMAXB][RGATES];
+  float projv[RMAXB][RCH];           // this CTA's projector outputs of every window (last update)
   float c0[RMAXB][RCH];
   float c1[RMAXB][RCH];
   __half hnew[RMAXB][RCH];           // this CTA's new hidden slice, committed one barrier later
   uint32_t psum[2][RPAIRS][RGATES];  // the parity chains' sums (half2 bits), [parity][window pair][gate]
+  uint32_t l0init[2][RPAIRS][RGATES];  // layer-0 chains after the token's embedding inputs (half2 bits)
   float b0[RGATES], b1[RGATES], pb[8], hb[RHEADCOLS];
   int first_exc[RMAXB];
+  RPartial hred[RMAXB][RHEADCOLS / RHG];  // per window: the column groups' partials
   RWin win[RMAXB];
   int any_pending, any_token, any_joint;
+  int head_finite;                   // every head weight of this CTA is finite (the head chains skip no input)
   unsigned int gen;
 };
 static_assert(sizeof(RSmem) + 128 <= 232448, "resident decoder shared memory");
@@ -189,6 +210,8 @@ __device__ __forceinline__ float sanitize(float v) { return v != v ? RNEG : v; }
 
 __device__ __forceinline__ __half* xh(const RParams& p, size_t off) { return reinterpret_cast<__half*>(p.xchg + off); }
 __device__ __forceinline__ float* h1f_at(const RParams& p) { return reinterpret_cast<float*>(p.xchg + XH1F); }
+__device__ __forceinline__ float* jin_at(const RParams& p) { return reinterpret_cast<float*>(p.xchg + XJIN); }
+__device__ __forceinline__ __half* j2_at(const RParams& p) { return reinterpret_cast<__half*>(p.xchg + XJ2); }
 __device__ __forceinline__ float* proj_at(const RParams& p, int w) {
   return reinterpret_cast<float*>(p.xchg + XPROJ) + (size_t)w * RH;
 }
@@ -209,140 +232,153 @@ __device__ void stage_rows(RSmem& s, const __half* src) {
   for (int j = 0; j < PER; ++j) reinterpret_cast<uint4*>(&s.in.x2[0][0])[threadIdx.x + j * RTHREADS] = v[j];
 }
 
-// The embedding rows of the windows updating with a token, into x2; lane =
-// window (8 halfs per 16-byte load), so a warp's half-word stores land in
-// adjacent words.
-__device__ void stage_embeddings(RSmem& s, const RParams& p) {
-  constexpr int PER = RMAXB * RH / 8 / RTHREADS;
-  static_assert(RMAXB * RH / 8 % RTHREADS == 0, "whole chunks per thread");
-  uint4 v[PER];
-#pragma unroll
-  for (int j = 0; j < PER; ++j) {
-    const int i = threadIdx.x + j * RTHREADS, w = i % RMAXB, k = 8 * (i / RMAXB);
-    v[j] = make_uint4(0u, 0u, 0u, 0u);
-    if (w < p.batch && s.win[w].pending == 2)
-      v[j] = *reinterpret_cast<const uint4*>(p.emb + (size_t)s.win[w].token * RH + k);
+// The layer-0 chain states after the embedding inputs of each updating
+// window's token (the token table), into l0init: thread (window, q) loads
+// gates 4 q .. 4 q + 3 of both parities (16 bytes).
+__device__ void stage_token_init(RSmem& s, const RParams& p) {
+  const int tid = threadIdx.x;
+  if (tid >= RMAXB * 5) return;
+  const int w = tid / 5, q = tid % 5;
+  uint4 v = make_uint4(0u, 0u, 0u, 0u);
+  if (w < p.batch && s.win[w].pending == 2) {
+    const size_t at = ((size_t)blockIdx.x * RTOKENS + s.win[w].token) * RGATES * 2 + 8 * q;
+    v = __ldcg(reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(p.xchg + XTT) + at));
   }
+  const __half* h = reinterpret_cast<const __half*>(&v);
 #pragma unroll
-  for (int j = 0; j < PER; ++j) {
-    const int i = threadIdx.x + j * RTHREADS, w = i % RMAXB, k = 8 * (i / RMAXB);
-    const __half* h = reinterpret_cast<const __half*>(&v[j]);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) set_lane(&s.in.x2[k + e][w >> 1], w & 1, h[e]);
+  for (int e = 0; e < 4; ++e) {
+    set_lane(reinterpret_cast<__half2*>(&s.l0init[0][w >> 1][4 * q + e]), w & 1, h[2 * e]);
+    set_lane(reinterpret_cast<__half2*>(&s.l0init[1][w >> 1][4 * q + e]), w & 1, h[2 * e + 1]);
   }
 }
 
-// One staged half (640 inputs) of this thread's gate chains: gate output of
-// `wrow` (its 640 weights of this half, both parities interleaved), parity
-// `par`, window pairs 4 g .. 4 g + 3.  REC: lanes in `keep` leave their
-// accumulator as it was (start-of-sequence windows skip the recurrent half).
-// The chain threads of one warp share their parity, so every x2 load of a
-// warp reads one 80-byte row (one wavefront) and its weight loads a few rows.
-// Operands of 4 chain steps (8 inputs from k): this parity's 4 weights and
-// the 4 window pairs' inputs.
-struct LstmChunk {
-  uint4 w;     // 8 weights, inputs k .. k + 7
-  uint4 x[4];  // inputs k + par, k + 2 + par, ... for the thread's 4 pairs
+// Operands of 8 same-parity chain steps from m: 8 weights of each of the
+// thread's two gate outputs and the two window pairs' inputs of each step.
+struct LstmOps {
+  uint4 wa, wb;
+  uint2 x[8];
 };
 
-__device__ __forceinline__ void lstm_load(const RSmem& s, const __half* wrow, int k, int g, int par, LstmChunk& c) {
-  c.w = *reinterpret_cast<const uint4*>(wrow + k);
+__device__ __forceinline__ void lstm_load(const RSmem& s, const __half* wa, const __half* wb, int m, int pp, int par,
+                                          LstmOps& c) {
+  c.wa = *reinterpret_cast<const uint4*>(wa + m);
+  c.wb = *reinterpret_cast<const uint4*>(wb + m);
 #pragma unroll
-  for (int j = 0; j < 4; ++j) c.x[j] = *reinterpret_cast<const uint4*>(&s.in.x2[k + 2 * j + par][4 * g]);
+  for (int j = 0; j < 8; ++j) c.x[j] = *reinterpret_cast<const uint2*>(&s.in.x2[2 * (m + j) + par][2 * pp]);
 }
 
-template <bool REC>
-__device__ __forceinline__ void lstm_math(const LstmChunk& c, int par, const uint32_t (&keep)[RLSTM_PAIRS],
-                                          __half2 (&acc)[RLSTM_PAIRS]) {
-  const uint32_t ww[4] = {c.w.x, c.w.y, c.w.z, c.w.w};
+__device__ __forceinline__ void lstm_math(const LstmOps& c, __half2 (&acc)[2][2]) {
+  const uint32_t a[4] = {c.wa.x, c.wa.y, c.wa.z, c.wa.w};
+  const uint32_t b[4] = {c.wb.x, c.wb.y, c.wb.z, c.wb.w};
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const __half2 wv = __half2half2(__ushort_as_half((unsigned short)(par ? ww[j] >> 16 : ww[j] & 0xffffu)));
-    const uint32_t xs[RLSTM_PAIRS] = {c.x[j].x, c.x[j].y, c.x[j].z, c.x[j].w};
-#pragma unroll
-    for (int i = 0; i < RLSTM_PAIRS; ++i) {
-      if constexpr (REC)
-        acc[i] = keep_mask(acc[i], __hfma2(bits_h2(xs[i]), wv, acc[i]), keep[i]);
-      else
-        acc[i] = __hfma2(bits_h2(xs[i]), wv, acc[i]);
-    }
+  for (int j = 0; j < 8; ++j) {
+    // Broadcasts of one half of a weight pair (an operand selector of the
+    // f16x2 FMA, not a separate instruction).
+    const __half2 va = (j & 1) ? __high2half2(bits_h2(a[j >> 1])) : __low2half2(bits_h2(a[j >> 1]));
+    const __half2 vb = (j & 1) ? __high2half2(bits_h2(b[j >> 1])) : __low2half2(bits_h2(b[j >> 1]));
+    acc[0][0] = __hfma2(bits_h2(c.x[j].x), va, acc[0][0]);
+    acc[0][1] = __hfma2(bits_h2(c.x[j].y), va, acc[0][1]);
+    acc[1][0] = __hfma2(bits_h2(c.x[j].x), vb, acc[1][0]);
+    acc[1][1] = __hfma2(bits_h2(c.x[j].y), vb, acc[1][1]);
   }
 }
 
-// One staged half (640 inputs) of this thread's gate chains: gate output of
-// `wrow` (its 640 weights of this half, both parities interleaved), parity
-// `par`, window pairs 4 g .. 4 g + 3.  REC: lanes in `keep` leave their
-// accumulator as it was (start-of-sequence windows skip the recurrent half).
-// The chain threads of one warp share their parity, so every x2 load of a
-// warp reads one 80-byte row (one wavefront) and its weight loads a few rows.
-// Two operand buffers alternate: the loads of the next 8 inputs are issued
-// before the chain steps of the current 8.
-template <bool REC>
-__device__ __forceinline__ void lstm_chain_half(const RSmem& s, const __half* wrow, int g, int par,
-                                                const uint32_t (&keep)[RLSTM_PAIRS], __half2 (&acc)[RLSTM_PAIRS]) {
-  LstmChunk a, b;
-  lstm_load(s, wrow, 0, g, par, a);
+// One staged half (640 inputs) of this thread's gate chains: gate outputs
+// whose same-parity weights of this half start at `wa` and `wb`, parity
+// `par`, window pairs 2 pp and 2 pp + 1 (four chains per thread, each in
+// increasing input order).  Each 16-byte weight load serves 8 steps of two
+// window pairs, each 8-byte input load 2 steps of two gate outputs.  Two
+// operand buffers alternate: the next 8 steps' loads are issued before the
+// current 8 steps.
+__device__ __forceinline__ void lstm_chain_half(const RSmem& s, const __half* wa, const __half* wb, int pp, int par,
+                                                __half2 (&acc)[2][2]) {
+  LstmOps a, b;
+  lstm_load(s, wa, wb, 0, pp, par, a);
 #pragma unroll 1
-  for (int k = 0; k < RH; k += 16) {
-    lstm_load(s, wrow, k + 8, g, par, b);
-    lstm_math<REC>(a, par, keep, acc);
-    if (k + 16 < RH) lstm_load(s, wrow, k + 16, g, par, a);
-    lstm_math<REC>(b, par, keep, acc);
+  for (int m = 0; m < RPW; m += 16) {
+    lstm_load(s, wa, wb, m + 8, pp, par, b);
+    lstm_math(a, acc);
+    if (m + 16 < RPW) lstm_load(s, wa, wb, m + 16, pp, par, a);
+    lstm_math(b, acc);
   }
 }
 
 // Gate chains of one LSTM layer for the windows that need them; gates land in
 // s.gates[window][gate * 5 + channel].  Chain thread t < 200: parity t / 100,
-// output (t % 100) / 5, group of 4 window pairs t % 5.  Inputs: layer 0
-// [embedding(token) | h0], layer 1 [new h0 | h1], staged one half at a time.
-// Layer 1's start-of-sequence windows stop at input 640 (their recurrent
-// input is zero and the shader does not run those steps); lanes of windows
-// that do not update compute values nobody reads.
+// gate outputs 2 q and 2 q + 1 with q = (t % 100) / 10, window pairs 2 v and
+// 2 v + 1 with v = t % 10.  Inputs: layer 0 [embedding(token) | h0] (the
+// chains' states after the embedding half come from the token table), layer 1
+// [new h0 | h1], staged one half at a time.  Layer 1's start-of-sequence
+// windows stop at input 640 (their recurrent input is zero and the shader
+// does not run those steps): their lanes take back the accumulator they had
+// before the recurrent half.  Lanes of windows that do not update compute
+// values nobody reads.
 __device__ void lstm_layer(RSmem& s, const RParams& p, bool layer1) {
   const int tid = threadIdx.x;
   const bool chain = tid < RLSTM_THREADS;
-  const int par = tid / RLSTM_PER_PAR, idx = tid % RLSTM_PER_PAR;
-  const int o = idx / RLSTM_GROUPS, grp = idx % RLSTM_GROUPS;
-  const __half* wrow = layer1 ? &s.w1[o][0] : &s.w0[o][0];
+  const int par = (tid / RLSTM_PER_PAR) & 1, r = tid % RLSTM_PER_PAR;
+  const int oa = 2 * (r / RLSTM_PP), pp = r % RLSTM_PP;
+  const __half* wa = layer1 ? &s.w1[par][oa][0] : &s.w0[par][oa][0];
+  const __half* wb = layer1 ? &s.w1[par][oa + 1][0] : &s.w0[par][oa + 1][0];
   bool any = false, any_full = false;
-  uint32_t keep_rec[RLSTM_PAIRS];
-  __half2 acc[RLSTM_PAIRS];
+  uint32_t keep_rec[2];
+  __half2 acc[2][2];
   if (chain) {
-    const __half2 init = par == 0 ? __float2half2_rn((layer1 ? s.b1 : s.b0)[o]) : __float2half2_rn(0.0f);
 #pragma unroll
-    for (int i = 0; i < RLSTM_PAIRS; ++i) {
-      const int w0 = (grp * RLSTM_PAIRS + i) * 2;
+    for (int rr = 0; rr < 2; ++rr) {
+      const __half2 init = par == 0 ? __float2half2_rn((layer1 ? s.b1 : s.b0)[oa + rr]) : __float2half2_rn(0.0f);
+      acc[rr][0] = init;
+      acc[rr][1] = init;
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int w0 = (2 * pp + i) * 2;
       const int p0 = s.win[w0].pending, p1 = s.win[w0 + 1].pending;
       keep_rec[i] = lane_mask(p0 == 1, p1 == 1);
       any |= layer1 ? (p0 | p1) != 0 : (p0 == 2 || p1 == 2);
       any_full |= p0 == 2 || p1 == 2;
-      acc[i] = init;
     }
   }
   const bool tokens = s.any_token != 0;
-  if (layer1 || tokens) {
-    if (layer1)
-      stage_rows(s, xh(p, XH0N));
-    else
-      stage_embeddings(s, p);
+  if (layer1) {
+    stage_rows(s, xh(p, XH0N));
     __syncthreads();
-    if (chain && any) lstm_chain_half<false>(s, wrow, grp, par, keep_rec, acc);
-  }
-  if (tokens) {
-    __syncthreads();  // the first half is consumed
-    stage_rows(s, xh(p, layer1 ? XH1 : XH0));
+    if (chain && any) lstm_chain_half(s, wa, wb, pp, par, acc);
+    if (tokens) {
+      __syncthreads();  // the first half is consumed
+      stage_rows(s, xh(p, XH1));
+      __syncthreads();
+      if (chain && any_full) {
+        __half2 before[2][2];
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) before[rr][0] = acc[rr][0], before[rr][1] = acc[rr][1];
+        lstm_chain_half(s, wa + RPW, wb + RPW, pp, par, acc);
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr)
+#pragma unroll
+          for (int i = 0; i < 2; ++i) acc[rr][i] = keep_mask(before[rr][i], acc[rr][i], keep_rec[i]);
+      }
+    }
+  } else if (tokens) {
+    // Layer 0: the chains over the token's embedding inputs are read from the
+    // token table; the recurrent inputs (h0) continue them here.
+    stage_token_init(s, p);
+    stage_rows(s, xh(p, XH0));
     __syncthreads();
-    if (chain && (layer1 ? any_full : any)) {
-      if (layer1)
-        lstm_chain_half<true>(s, wrow + RH, grp, par, keep_rec, acc);
-      else
-        lstm_chain_half<false>(s, wrow + RH, grp, par, keep_rec, acc);
+    if (chain && any) {
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr)
+#pragma unroll
+        for (int i = 0; i < 2; ++i) acc[rr][i] = bits_h2(s.l0init[par][2 * pp + i][oa + rr]);
+      lstm_chain_half(s, wa, wb, pp, par, acc);
     }
   }
   // The two parity chains of a gate sum in f16.
   if (chain && any) {
 #pragma unroll
-    for (int i = 0; i < RLSTM_PAIRS; ++i) s.psum[par][grp * RLSTM_PAIRS + i][o] = h2_bits(acc[i]);
+    for (int rr = 0; rr < 2; ++rr)
+#pragma unroll
+      for (int i = 0; i < 2; ++i) s.psum[par][2 * pp + i][oa + rr] = h2_bits(acc[rr][i]);
   }
   __syncthreads();
   for (int i = tid; i < RPAIRS * RGATES; i += RTHREADS) {
@@ -390,11 +426,16 @@ __device__ void commit_hidden(RSmem& s, const RParams& p, bool layer1) {
 // The f32 projection chains of this CTA's 5 projector outputs, in two staged
 // halves of the new layer-1 hidden state (transposed to [window][input] while
 // staging, so a thread's inputs and weights are 16-byte loads along k);
-// thread: (output, window).
+// thread: (output, window).  The same threads then build this CTA's rows of
+// the step's joint inputs.
 __device__ void projector(RSmem& s, const RParams& p) {
   const int tid = threadIdx.x;
   const int o = tid / RMAXB, w = tid % RMAXB;
   const bool live = tid < RPROJ_THREADS && w < p.batch && s.win[w].pending;
+  const bool joint = tid < RPROJ_THREADS && w < p.batch && s.win[w].joint;
+  // The encoder value of this thread's joint input (read now, used at the end).
+  const __half ev = joint ? p.enc[((size_t)w * p.frames + s.win[w].joint_t) * RH + blockIdx.x * RCH + o]
+                          : __float2half_rn(0.0f);
   float acc = live ? s.pb[o] : 0.0f;
   for (int h = 0; h < 2; ++h) {
     if (h) __syncthreads();  // the first half is consumed
@@ -439,7 +480,18 @@ __device__ void projector(RSmem& s, const RParams& p) {
       }
     }
   }
-  if (live) proj_at(p, w)[blockIdx.x * RCH + o] = acc;
+  if (live) {
+    proj_at(p, w)[blockIdx.x * RCH + o] = acc;
+    s.projv[w][o] = acc;
+  }
+  // Joint input k = 5 cta + o of every window that takes a joint next (the
+  // windows that did not update keep their last projector output).
+  if (joint) {
+    const float x = __fadd_rn(__half2float(ev), s.projv[w][o]);
+    const float jv = x < 0.0f ? 0.0f : x;  // as in joint_partials
+    jin_at(p)[(size_t)(blockIdx.x * RCH + o) * RMAXB + w] = jv;
+    j2_at(p)[((size_t)(w >> 1) * RH + blockIdx.x * RCH + o) * 2 + (w & 1)] = __float2half_rn(jv);
+  }
 }
 
 __device__ void lstm_update(RSmem& s, const RParams& p) {
@@ -470,42 +522,53 @@ __device__ void lstm_update(RSmem& s, const RParams& p) {
   __syncthreads();
 }
 
-// One staged half (320 inputs) of this thread's head chain: column `col`,
-// window pair `pair`, starting at input `kb`.
-__device__ __forceinline__ void head_chain_half(const RSmem& s, int col, int pair, int kb, __half2& acc) {
-  const __half* wrow = &s.hw[col][kb];
+// One staged half (320 inputs) of this thread's head chains: columns
+// 3 g .. 3 g + 2, window pair `pair`, starting at input `kb`.  Per 8 inputs
+// the three columns share the pair's input (and mask) loads.  MASKED: lanes
+// set in the staged masks skip the input (the shader's +0 rule); unmasked,
+// every input is applied -- used when the CTA's head weights are all finite,
+// where applying a skipped input (+0 x w) changes an accumulator at most in
+// the sign of a zero, which no argmax comparison sees.
+template <bool MASKED>
+__device__ __forceinline__ void head_chain_half(const RSmem& s, int g, int pair, int kb, __half2 (&acc)[RHG]) {
+  const __half* wrow = &s.hw[RHG * g][kb];
   const uint32_t* xrow = &s.in.jt.j2[pair][0];
   const uint32_t* mrow = &s.in.jt.keep[pair][0];
-#pragma unroll 2
+#pragma unroll 1
   for (int k0 = 0; k0 < RHALF; k0 += RCHUNK) {
-    // 8 steps per 16-byte load of each operand.
-    const uint4 wq = *reinterpret_cast<const uint4*>(wrow + k0);
+    uint4 wq[RHG];
+#pragma unroll
+    for (int c = 0; c < RHG; ++c) wq[c] = *reinterpret_cast<const uint4*>(wrow + c * RHW_STRIDE + k0);
     const uint4 xa = *reinterpret_cast<const uint4*>(xrow + k0), xb = *reinterpret_cast<const uint4*>(xrow + k0 + 4);
-    const uint4 ma = *reinterpret_cast<const uint4*>(mrow + k0), mb = *reinterpret_cast<const uint4*>(mrow + k0 + 4);
-    const uint32_t wpair[4] = {wq.x, wq.y, wq.z, wq.w};
     const uint32_t xs[RCHUNK] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-    const uint32_t ms[RCHUNK] = {ma.x, ma.y, ma.z, ma.w, mb.x, mb.y, mb.z, mb.w};
-    if ((ma.x | ma.y | ma.z | ma.w | mb.x | mb.y | mb.z | mb.w) == 0u) {  // no skipped input here
+    uint32_t ms[RCHUNK] = {};
+    bool masked = false;
+    if constexpr (MASKED) {
+      const uint4 ma = *reinterpret_cast<const uint4*>(mrow + k0), mb = *reinterpret_cast<const uint4*>(mrow + k0 + 4);
+      const uint32_t m8[RCHUNK] = {ma.x, ma.y, ma.z, ma.w, mb.x, mb.y, mb.z, mb.w};
 #pragma unroll
-      for (int j = 0; j < RCHUNK; ++j) {
-        const uint32_t wb = (j & 1) ? (wpair[j >> 1] >> 16) : (wpair[j >> 1] & 0xffffu);
-        acc = __hfma2(bits_h2(xs[j]), __half2half2(__ushort_as_half((unsigned short)wb)), acc);
-      }
-    } else {
+      for (int j = 0; j < RCHUNK; ++j) ms[j] = m8[j];
+      masked = (ma.x | ma.y | ma.z | ma.w | mb.x | mb.y | mb.z | mb.w) != 0u;
+    }
 #pragma unroll
-      for (int j = 0; j < RCHUNK; ++j) {
-        const uint32_t wb = (j & 1) ? (wpair[j >> 1] >> 16) : (wpair[j >> 1] & 0xffffu);
-        acc = keep_mask(acc, __hfma2(bits_h2(xs[j]), __half2half2(__ushort_as_half((unsigned short)wb)), acc), ms[j]);
+    for (int j = 0; j < RCHUNK; ++j) {
+#pragma unroll
+      for (int c = 0; c < RHG; ++c) {
+        const uint32_t wp = (&wq[c].x)[j >> 1];
+        const __half2 wv = (j & 1) ? __high2half2(bits_h2(wp)) : __low2half2(bits_h2(wp));
+        const __half2 v = __hfma2(bits_h2(xs[j]), wv, acc[c]);
+        acc[c] = MASKED && masked ? keep_mask(acc[c], v, ms[j]) : v;
       }
     }
   }
 }
 
-// Joint of the active windows: inputs, head columns, this CTA's partials.
-// Thread k builds input k for every window (coalesced loads along k) and
-// keeps them in registers; the inputs are staged for the head chains in two
-// halves.
-__device__ void joint_partials(RSmem& s, const RParams& p, int slot) {
+// The general path of the joint inputs (a step without an LSTM update, or a
+// CTA whose head weights are not all finite): thread k builds input k of
+// every window, applies the shader's skip rule when `fast` is false, and
+// stages the inputs (and skip masks) for the head chains in two halves.
+__device__ void joint_inputs_staged(RSmem& s, const RParams& p, bool built, bool fast, int g, int pair, bool run,
+                                    __half2 (&acc)[RHG]) {
   const int tid = threadIdx.x;
   if (tid < RMAXB) s.first_exc[tid] = RH;
   __syncthreads();
@@ -515,16 +578,35 @@ __device__ void joint_partials(RSmem& s, const RParams& p, int slot) {
   constexpr int WG = 20;  // windows whose loads are in flight together
 #pragma unroll
   for (int w0 = 0; w0 < RMAXB; w0 += WG) {
-    __half ev[WG];
-    float pv[WG];
+    float jvs[WG];
+    if (built) {
+      // Row k of the inputs the projector phase built (windows w0 .. w0 + 19).
+      const uint4* src = reinterpret_cast<const uint4*>(jin_at(p) + (size_t)k * RMAXB + w0);
 #pragma unroll
-    for (int i = 0; i < WG; ++i) {
-      const int w = w0 + i;
-      ev[i] = __float2half_rn(0.0f);
-      pv[i] = 0.0f;
-      if (w < p.batch && s.win[w].joint) {
-        ev[i] = p.enc[((size_t)w * p.frames + s.win[w].joint_t) * RH + k];
-        pv[i] = __ldcg(proj_at(p, w) + k);
+      for (int q = 0; q < WG / 4; ++q) {
+        const uint4 v = __ldcg(src + q);
+        jvs[4 * q] = __uint_as_float(v.x);
+        jvs[4 * q + 1] = __uint_as_float(v.y);
+        jvs[4 * q + 2] = __uint_as_float(v.z);
+        jvs[4 * q + 3] = __uint_as_float(v.w);
+      }
+    } else {
+      __half ev[WG];
+      float pv[WG];
+#pragma unroll
+      for (int i = 0; i < WG; ++i) {
+        const int w = w0 + i;
+        ev[i] = __float2half_rn(0.0f);
+        pv[i] = 0.0f;
+        if (w < p.batch && s.win[w].joint) {
+          ev[i] = p.enc[((size_t)w * p.frames + s.win[w].joint_t) * RH + k];
+          pv[i] = __ldcg(proj_at(p, w) + k);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < WG; ++i) {
+        const float x = __fadd_rn(__half2float(ev[i]), pv[i]);
+        jvs[i] = x < 0.0f ? 0.0f : x;  // max(x, 0) keeping -0 and NaN, as the oracle's std::max
       }
     }
 #pragma unroll
@@ -535,8 +617,7 @@ __device__ void joint_partials(RSmem& s, const RParams& p, int slot) {
         const int w = w0 + i + l;
         hv[l] = __float2half_rn(0.0f);
         if (w < p.batch && s.win[w].joint) {
-          const float x = __fadd_rn(__half2float(ev[i + l]), pv[i + l]);
-          const float jv = x < 0.0f ? 0.0f : x;  // max(x, 0) keeping -0 and NaN, as the oracle's std::max
+          const float jv = jvs[i + l];
           const uint32_t bits = __float_as_uint(jv);
           hv[l] = __float2half_rn(jv);
           if (bits == 0u) zero_bits |= 1ull << w;
@@ -547,12 +628,6 @@ __device__ void joint_partials(RSmem& s, const RParams& p, int slot) {
     }
   }
   __syncthreads();  // first_exc is final
-  const int col = tid % RHEADCOLS, pair = tid / RHEADCOLS;  // windows 2 pair, 2 pair + 1
-  const bool head = tid < RHEAD_THREADS;
-  const bool tail = col >= RTOK;
-  const bool live = head && (!tail || blockIdx.x == RG - 1);
-  __half2 acc = __float2half2_rn(head ? s.hb[col] : 0.0f);
-  const bool run = live && (s.win[2 * pair].joint || s.win[2 * pair + 1].joint);
   for (int h = 0; h < 2; ++h) {
     if (h) __syncthreads();  // the first half is consumed
     if (k / RHALF == h) {
@@ -566,40 +641,89 @@ __device__ void joint_partials(RSmem& s, const RParams& p, int slot) {
       }
     }
     __syncthreads();
-    if (run) head_chain_half(s, col, pair, h * RHALF, acc);
-  }
-  if (head) {
-    const float2 v01 = __half22float2(acc);
-    const float vals[2] = {sanitize(v01.x), sanitize(v01.y)};
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      float tv = RNEG, dv = RNEG;
-      uint32_t ti = 0xffffffffu, di = 0xffffffffu;
-      if (live) {
-        if (!tail) {
-          tv = vals[i];
-          ti = blockIdx.x * RTOK + col;
-        } else if (col == RTOK) {
-          tv = vals[i];
-          ti = RBLANK;
-        } else if (col <= RTOK + 5) {
-          dv = vals[i];
-          di = col - RTOK - 1;
-        }
-      }
-#pragma unroll
-      for (int off = RHEADCOLS / 2; off > 0; off >>= 1) {
-        const float otv = __shfl_xor_sync(0xffffffffu, tv, off);
-        const uint32_t oti = __shfl_xor_sync(0xffffffffu, ti, off);
-        const float odv = __shfl_xor_sync(0xffffffffu, dv, off);
-        const uint32_t odi = __shfl_xor_sync(0xffffffffu, di, off);
-        if (better(tv, ti, otv, oti)) tv = otv, ti = oti;
-        if (better(dv, di, odv, odi)) dv = odv, di = odi;
-      }
-      const int w = pair * 2 + i;
-      if (col == 0 && w < p.batch && s.win[w].joint) *part_at(p, slot, w, blockIdx.x) = RPartial{tv, ti, dv, di};
+    if (run) {
+      if (fast)
+        head_chain_half<false>(s, g, pair, h * RHALF, acc);
+      else
+        head_chain_half<true>(s, g, pair, h * RHALF, acc);
     }
   }
+}
+
+// Each thread's best token and duration of its two windows over its three
+// columns, then per window over the column groups: this CTA's partials.
+__device__ void joint_reduce(RSmem& s, const RParams& p, int slot, int g, int pair, bool head,
+                             const __half2 (&acc)[RHG]) {
+  const int tid = threadIdx.x;
+  // This thread's best token and duration of each of its two windows; column
+  // 8 is the tail column of CTAs 0..5 (the blank, or duration cta - 1).
+  if (head) {
+    const int ncols = blockIdx.x < RTAIL_CTAS ? RHEADCOLS : RTOK;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      RPartial b{RNEG, 0xffffffffu, RNEG, 0xffffffffu};
+#pragma unroll
+      for (int c = 0; c < RHG; ++c) {
+        const int col = RHG * g + c;
+        if (col >= ncols) continue;
+        const float v = sanitize(i ? __high2float(acc[c]) : __low2float(acc[c]));
+        if (col < RTOK) {
+          if (better(b.tv, b.ti, v, blockIdx.x * RTOK + col)) b.tv = v, b.ti = blockIdx.x * RTOK + col;
+        } else if (blockIdx.x == 0) {
+          if (better(b.tv, b.ti, v, RBLANK)) b.tv = v, b.ti = RBLANK;
+        } else {
+          b.dv = v;
+          b.di = blockIdx.x - 1;
+        }
+      }
+      s.hred[2 * pair + i][g] = b;
+    }
+  }
+  __syncthreads();
+  if (tid < p.batch && s.win[tid].joint) {
+    RPartial b = s.hred[tid][0];
+#pragma unroll
+    for (int q = 1; q < RHEADCOLS / RHG; ++q) {
+      const RPartial v = s.hred[tid][q];
+      if (better(b.tv, b.ti, v.tv, v.ti)) b.tv = v.tv, b.ti = v.ti;
+      if (better(b.dv, b.di, v.dv, v.di)) b.dv = v.dv, b.di = v.di;
+    }
+    *part_at(p, slot, tid, blockIdx.x) = b;
+  }
+}
+
+// Joint of the active windows: inputs, head columns, this CTA's partials.
+// In a step that updated the LSTM (`built`) the projector phase has left the
+// inputs in the exchange area: a CTA whose head weights are all finite copies
+// their f16 form straight into the chains' layout; otherwise the general path
+// below builds them (and the shader's skip masks) input by input.
+__device__ void joint_partials(RSmem& s, const RParams& p, int slot, bool built) {
+  const int tid = threadIdx.x;
+  const bool fast = s.head_finite != 0;  // no skip rule to apply (head_chain_half)
+  const int g = tid % (RHEADCOLS / RHG), pair = tid / (RHEADCOLS / RHG);  // windows 2 pair, 2 pair + 1
+  const bool head = tid < RHEAD_THREADS;
+  __half2 acc[RHG];
+#pragma unroll
+  for (int c = 0; c < RHG; ++c) acc[c] = __float2half2_rn(head ? s.hb[RHG * g + c] : 0.0f);
+  const bool run = head && (s.win[2 * pair].joint || s.win[2 * pair + 1].joint);
+  if (built && fast) {
+    // The projector phase left the f16 inputs in the chains' layout: each
+    // half is a plain copy of 20 rows of 320 words.
+    constexpr int CH = RPAIRS * RHALF / 4;  // 16-byte chunks per half
+    for (int h = 0; h < 2; ++h) {
+      if (h) __syncthreads();  // the first half is consumed
+      for (int i = tid; i < CH; i += RTHREADS) {
+        const int pr = i / (RHALF / 4), c4 = 4 * (i % (RHALF / 4));
+        *reinterpret_cast<uint4*>(&s.in.jt.j2[pr][c4]) =
+            __ldcg(reinterpret_cast<const uint4*>(j2_at(p) + ((size_t)pr * RH + h * RHALF + c4) * 2));
+      }
+      __syncthreads();
+      if (run) head_chain_half<false>(s, g, pair, h * RHALF, acc);
+    }
+  } else {
+    joint_inputs_staged(s, p, built, fast, g, pair, run, acc);
+  }
+  joint_reduce(s, p, slot, g, pair, head, acc);
 }
 
 __device__ void emit(RSmem& s, const RParams& p, int w, uint32_t tok, uint32_t frame, uint32_t dur) {
@@ -703,6 +827,61 @@ __device__ void joint_decide(RSmem& s, const RParams& p, int slot) {
   __syncthreads();
 }
 
+// The token table: for every token that feeds the LSTM and every layer-0 gate
+// column, the two parity chains' states after the 640 embedding inputs --
+// exactly the first half of the chains the shader runs for that token (even
+// chain from f16(bias), odd chain from zero, inputs in increasing order).
+// Block (CTA slice c of the resident kernel, 64 tokens); thread (gate o,
+// parity, 4 token pairs, one per half2 lane pair).
+constexpr int TT_TOKENS = 64;
+constexpr int TT_THREADS = RGATES * 2 * 8;
+struct TtSmem {
+  __half w[RGATES][RHW_STRIDE];   // the slice's embedding-input weights, [gate][input]
+  __half2 x[RH][TT_TOKENS / 2];   // embedding rows, [input][token pair]
+};
+static_assert(RTOKENS % TT_TOKENS == 0 && TT_TOKENS / 2 == 4 * 8, "token blocks tile the table");
+
+__global__ void __launch_bounds__(TT_THREADS) tdt_token_table_kernel(const __half* __restrict__ emb,
+                                                                     const __half* __restrict__ w0,
+                                                                     const float* __restrict__ b0,
+                                                                     unsigned char* xchg) {
+  extern __shared__ __align__(16) unsigned char tt_raw[];
+  TtSmem& s = *reinterpret_cast<TtSmem*>(tt_raw);
+  const int c = blockIdx.x, t0 = blockIdx.y * TT_TOKENS, tid = threadIdx.x;
+  pdl_entry();
+  for (int i = tid; i < RH * RGATES; i += TT_THREADS) {
+    const int k = i / RGATES, o = i % RGATES;
+    s.w[o][k] = w0[(size_t)k * 4 * RH + (o / RCH) * RH + c * RCH + o % RCH];
+  }
+  for (int i = tid; i < TT_TOKENS * (RH / 8); i += TT_THREADS) {
+    const int tok = i / (RH / 8), k8 = 8 * (i % (RH / 8));
+    const uint4 v = *reinterpret_cast<const uint4*>(emb + (size_t)(t0 + tok) * RH + k8);
+    const __half* h = reinterpret_cast<const __half*>(&v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) set_lane(&s.x[k8 + e][tok >> 1], tok & 1, h[e]);
+  }
+  __syncthreads();
+  const int o = tid % RGATES, par = (tid / RGATES) & 1, tg = tid / (2 * RGATES);
+  const __half2 init = par == 0 ? __float2half2_rn(b0[(o / RCH) * RH + c * RCH + o % RCH]) : __float2half2_rn(0.0f);
+  __half2 acc[4] = {init, init, init, init};
+#pragma unroll 4
+  for (int k = par; k < RH; k += 2) {
+    const __half2 wv = __half2half2(s.w[o][k]);
+    const uint4 xv = *reinterpret_cast<const uint4*>(&s.x[k][4 * tg]);
+    acc[0] = __hfma2(bits_h2(xv.x), wv, acc[0]);
+    acc[1] = __hfma2(bits_h2(xv.y), wv, acc[1]);
+    acc[2] = __hfma2(bits_h2(xv.z), wv, acc[2]);
+    acc[3] = __hfma2(bits_h2(xv.w), wv, acc[3]);
+  }
+  __half* out = reinterpret_cast<__half*>(xchg + XTT) + (size_t)c * RTOKENS * RGATES * 2;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int tok = t0 + 2 * (4 * tg + i);
+    out[((size_t)tok * RGATES + o) * 2 + par] = __low2half(acc[i]);
+    out[((size_t)(tok + 1) * RGATES + o) * 2 + par] = __high2half(acc[i]);
+  }
+}
+
 __global__ void __launch_bounds__(RTHREADS, 1) tdt_resident_kernel(const RParams p) {
   extern __shared__ __align__(128) unsigned char rsmem_raw[];
   RSmem& s = *reinterpret_cast<RSmem*>((reinterpret_cast<uintptr_t>(rsmem_raw) + 127) & ~static_cast<uintptr_t>(127));
@@ -711,18 +890,23 @@ __global__ void __launch_bounds__(RTHREADS, 1) tdt_resident_kernel(const RParams
   for (int i = tid; i < RKIN * RGATES; i += RTHREADS) {
     const int k = i / RGATES, o = i % RGATES;
     const size_t col = (size_t)(o / RCH) * RH + cta * RCH + o % RCH;
-    s.w0[o][k] = p.w0[(size_t)k * 4 * RH + col];
-    s.w1[o][k] = p.w1[(size_t)k * 4 * RH + col];
+    if (k >= RH) s.w0[k & 1][o][(k - RH) >> 1] = p.w0[(size_t)k * 4 * RH + col];
+    s.w1[k & 1][o][k >> 1] = p.w1[(size_t)k * 4 * RH + col];
   }
   for (int i = tid; i < RH * RCH; i += RTHREADS) {
     const int k = i / RCH, o = i % RCH;
     s.pwf[o][k] = __half2float(p.pw[(size_t)k * RH + cta * RCH + o]);
   }
+  bool finite = true;
   for (int i = tid; i < RH * RHEADCOLS; i += RTHREADS) {
     const int k = i / RHEADCOLS, c = i % RHEADCOLS;
-    const int col = c < RTOK ? cta * RTOK + c : (cta == RG - 1 ? RBLANK + (c - RTOK) : -1);
-    s.hw[c][k] = col >= 0 ? p.hw[(size_t)k * ROUT + col] : __float2half_rn(0.0f);
+    const int col = c < RTOK ? cta * RTOK + c : (cta < RTAIL_CTAS ? RBLANK + cta : -1);
+    const __half v = col >= 0 ? p.hw[(size_t)k * ROUT + col] : __float2half_rn(0.0f);
+    s.hw[c][k] = v;
+    finite = finite && !__hisinf(v) && !__hisnan(v);
   }
+  finite = __syncthreads_and(finite) != 0;
+  if (tid == 0) s.head_finite = finite;
   if (tid < RGATES) {
     const size_t col = (size_t)(tid / RCH) * RH + cta * RCH + tid % RCH;
     s.b0[tid] = p.b0[col];
@@ -730,7 +914,7 @@ __global__ void __launch_bounds__(RTHREADS, 1) tdt_resident_kernel(const RParams
   }
   if (tid < 8) s.pb[tid] = tid < RCH ? p.pb[cta * RCH + tid] : 0.0f;
   if (tid < RHEADCOLS) {
-    const int col = tid < RTOK ? cta * RTOK + tid : (cta == RG - 1 ? RBLANK + (tid - RTOK) : -1);
+    const int col = tid < RTOK ? cta * RTOK + tid : (cta < RTAIL_CTAS ? RBLANK + cta : -1);
     s.hb[tid] = col >= 0 ? p.hb[col] : 0.0f;
   }
   for (int i = tid; i < RMAXB * RCH; i += RTHREADS) {
@@ -773,7 +957,7 @@ __global__ void __launch_bounds__(RTHREADS, 1) tdt_resident_kernel(const RParams
     if (!ap && !aj) break;
     if (ap) lstm_update(s, p);
     if (aj) {
-      joint_partials(s, p, slot);
+      joint_partials(s, p, slot, ap);
       grid_sync(s, p);
       joint_decide(s, p, slot);
       slot ^= 1;
@@ -822,6 +1006,12 @@ int launch_tdt_resident(const DeviceCtx& dev, const pk_tdt_desc& d, cudaStream_t
   p.batch = d.batch;
   p.frames = d.frames;
   p.max_tokens = d.max_tokens;
+  // The token table for these weights (read by every decode step's layer 0).
+  st = set_max_dynamic_smem(reinterpret_cast<const void*>(tdt_token_table_kernel), (int)sizeof(TtSmem));
+  if (st != PK_OK) return st;
+  if ((e = launch_kernel(tdt_token_table_kernel, dim3(RG, RTOKENS / TT_TOKENS), dim3(TT_THREADS), sizeof(TtSmem),
+                         stream, p.emb, p.w0, p.b0, p.xchg)) != cudaSuccess)
+    return cuda_error(e, "tdt_token_table launch");
   // The barrier counter and abort flag start at zero every launch.
   if ((e = cudaMemsetAsync(p.xchg + XSYNC, 0, 256, stream)) != cudaSuccess)
     return cuda_error(e, "clearing the decoder barrier");
