@@ -87,10 +87,14 @@ constexpr size_t XH0 = 0;                                 // __half [640][40]: l
 constexpr size_t XH0N = XH0 + 1ull * RH * RMAXB * 2;      // __half [640][40]: layer-0 hidden (this update)
 constexpr size_t XH1 = XH0N + 1ull * RH * RMAXB * 2;      // __half [640][40]: layer-1 hidden (current)
 constexpr size_t XH1N = XH1 + 1ull * RH * RMAXB * 2;      // __half [640][40]: layer-1 hidden (this update)
-constexpr size_t XH1F = XH1N + 1ull * RH * RMAXB * 2;     // float [640][40]: layer-1 hidden for the projector
+constexpr size_t XH1F = XH1N + 1ull * RH * RMAXB * 2;     // float [40][640]: layer-1 hidden for the projector
 constexpr size_t XPROJ = XH1F + 1ull * RH * RMAXB * 4;    // float [40][640]: predictor projection
-constexpr size_t XPART = XPROJ + 1ull * RMAXB * RH * 4;   // RPartial [2][40][128]: argmax partials
-constexpr size_t XSYNC = XPART + 2ull * RMAXB * RG * 16;  // barrier counter, abort flag
+// Argmax partials of every CTA, double-buffered by step parity: the token
+// part {value, id} of all 128 CTAs ([2][40][128] x 8 bytes), the duration
+// part of CTAs 1..5 ([2][40][5] x 8 bytes).
+constexpr size_t XPART = XPROJ + 1ull * RMAXB * RH * 4;
+constexpr size_t XDPART = XPART + 2ull * RMAXB * RG * 8;
+constexpr size_t XSYNC = XDPART + 2ull * RMAXB * 8 * 8;  // barrier counter, abort flag
 // __half [128 CTAs][1024 tokens][20 gates][2 parities]: the state of each of a
 // CTA's layer-0 gate chains after the 640 embedding inputs of a token (even
 // chain from f16(bias), odd chain from zero), written by tdt_token_table_kernel
@@ -191,6 +195,16 @@ __device__ void grid_sync(RSmem& s, const RParams& p) {
 }
 
 __device__ __forceinline__ uint32_t h2_bits(__half2 v) { return *reinterpret_cast<uint32_t*>(&v); }
+// The 200 LSTM chain threads are lanes 0..24 of warps 0..7, so each SM
+// sub-partition issues for two warps of 25 (not two full warps on two
+// sub-partitions and one on the others).
+constexpr int RSPREAD_LANES = 25;
+static_assert(8 * RSPREAD_LANES == RLSTM_THREADS, "spread roles");
+__device__ __forceinline__ int spread_index(int tid, bool& on) {
+  const int lane = tid & 31, wid = tid >> 5;
+  on = wid < 8 && lane < RSPREAD_LANES;
+  return wid * RSPREAD_LANES + lane;
+}
 __device__ __forceinline__ __half2 bits_h2(uint32_t v) { return *reinterpret_cast<__half2*>(&v); }
 // Lane masks: keep `old` in the lanes of `m` (a skipped input leaves the
 // accumulator exactly as it was), take `fresh` elsewhere -- one LOP3.
@@ -215,8 +229,11 @@ __device__ __forceinline__ __half* j2_at(const RParams& p) { return reinterpret_
 __device__ __forceinline__ float* proj_at(const RParams& p, int w) {
   return reinterpret_cast<float*>(p.xchg + XPROJ) + (size_t)w * RH;
 }
-__device__ __forceinline__ RPartial* part_at(const RParams& p, int slot, int w, int cta) {
-  return reinterpret_cast<RPartial*>(p.xchg + XPART) + ((size_t)slot * RMAXB + w) * RG + cta;
+__device__ __forceinline__ uint2* part_at(const RParams& p, int slot, int w, int cta) {
+  return reinterpret_cast<uint2*>(p.xchg + XPART) + ((size_t)slot * RMAXB + w) * RG + cta;
+}
+__device__ __forceinline__ uint2* dpart_at(const RParams& p, int slot, int w, int d) {
+  return reinterpret_cast<uint2*>(p.xchg + XDPART) + ((size_t)slot * RMAXB + w) * 8 + d;
 }
 
 // Copies the 640 exchanged f16 rows at `src` (one value per window) into x2:
@@ -304,9 +321,9 @@ __device__ __forceinline__ void lstm_chain_half(const RSmem& s, const __half* wa
 }
 
 // Gate chains of one LSTM layer for the windows that need them; gates land in
-// s.gates[window][gate * 5 + channel].  Chain thread t < 200: parity t / 100,
-// gate outputs 2 q and 2 q + 1 with q = (t % 100) / 10, window pairs 2 v and
-// 2 v + 1 with v = t % 10.  Inputs: layer 0 [embedding(token) | h0] (the
+// s.gates[window][gate * 5 + channel].  Chain thread t (spread_index) < 200:
+// parity t / 100, gate outputs 2 q and 2 q + 1 with q = (t % 100) / 10,
+// window pairs 2 v and 2 v + 1 with v = t % 10.  Inputs: layer 0 [embedding(token) | h0] (the
 // chains' states after the embedding half come from the token table), layer 1
 // [new h0 | h1], staged one half at a time.  Layer 1's start-of-sequence
 // windows stop at input 640 (their recurrent input is zero and the shader
@@ -315,8 +332,9 @@ __device__ __forceinline__ void lstm_chain_half(const RSmem& s, const __half* wa
 // values nobody reads.
 __device__ void lstm_layer(RSmem& s, const RParams& p, bool layer1) {
   const int tid = threadIdx.x;
-  const bool chain = tid < RLSTM_THREADS;
-  const int par = (tid / RLSTM_PER_PAR) & 1, r = tid % RLSTM_PER_PAR;
+  bool chain;
+  const int ci = spread_index(tid, chain);
+  const int par = (ci / RLSTM_PER_PAR) & 1, r = ci % RLSTM_PER_PAR;
   const int oa = 2 * (r / RLSTM_PP), pp = r % RLSTM_PP;
   const __half* wa = layer1 ? &s.w1[par][oa][0] : &s.w0[par][oa][0];
   const __half* wb = layer1 ? &s.w1[par][oa + 1][0] : &s.w0[par][oa + 1][0];
@@ -383,12 +401,13 @@ __device__ void lstm_layer(RSmem& s, const RParams& p, bool layer1) {
   __syncthreads();
   for (int i = tid; i < RPAIRS * RGATES; i += RTHREADS) {
     const int pr = i / RGATES, g = i % RGATES;
-    const bool upd = layer1 ? (s.win[2 * pr].pending | s.win[2 * pr + 1].pending) != 0
-                            : (s.win[2 * pr].pending == 2 || s.win[2 * pr + 1].pending == 2);
+    const bool upd = (s.win[2 * pr].pending | s.win[2 * pr + 1].pending) != 0;
     if (upd) {
       const float2 v = __half22float2(__hadd2(bits_h2(s.psum[0][pr][g]), bits_h2(s.psum[1][pr][g])));
-      s.gates[2 * pr][g] = v.x;
-      s.gates[2 * pr + 1][g] = v.y;
+      // Layer 0's start-of-sequence windows take the bias as their gates.
+      const float bias = layer1 ? 0.0f : __half2float(__float2half_rn(s.b0[g]));
+      s.gates[2 * pr][g] = !layer1 && s.win[2 * pr].pending == 1 ? bias : v.x;
+      s.gates[2 * pr + 1][g] = !layer1 && s.win[2 * pr + 1].pending == 1 ? bias : v.y;
     }
   }
 }
@@ -410,7 +429,7 @@ __device__ void cell_update(RSmem& s, const RParams& p, float (*cst)[RCH], bool 
     const __half hh = __float2half_rn(h);
     s.hnew[w][c] = hh;
     xh(p, layer1 ? XH1N : XH0N)[at] = hh;
-    if (layer1) h1f_at(p)[at] = h;
+    if (layer1) h1f_at(p)[(size_t)w * RH + blockIdx.x * RCH + c] = h;
   }
 }
 
@@ -424,8 +443,9 @@ __device__ void commit_hidden(RSmem& s, const RParams& p, bool layer1) {
 }
 
 // The f32 projection chains of this CTA's 5 projector outputs, in two staged
-// halves of the new layer-1 hidden state (transposed to [window][input] while
-// staging, so a thread's inputs and weights are 16-byte loads along k);
+// halves of the new layer-1 hidden state (exchanged as [window][input], so
+// the staging is a plain copy and a thread's inputs and weights are 16-byte
+// loads along k);
 // thread: (output, window).  The same threads then build this CTA's rows of
 // the step's joint inputs.
 __device__ void projector(RSmem& s, const RParams& p) {
@@ -440,20 +460,21 @@ __device__ void projector(RSmem& s, const RParams& p) {
   for (int h = 0; h < 2; ++h) {
     if (h) __syncthreads();  // the first half is consumed
     {
-      constexpr int Q = RMAXB / 4;  // 16-byte chunks per exchanged row
-      constexpr int PER = RHALF * Q / RTHREADS;
-      static_assert(RHALF * Q % RTHREADS == 0, "whole chunks per thread");
-      const uint4* src = reinterpret_cast<const uint4*>(h1f_at(p) + (size_t)h * RHALF * RMAXB);
+      // Row w of the exchanged state holds window w's 640 values: a half is
+      // 80 chunks of 16 bytes per window, copied as they lie.
+      constexpr int Q = RHALF / 4;
+      constexpr int PER = RMAXB * Q / RTHREADS;
+      static_assert(RMAXB * Q % RTHREADS == 0, "whole chunks per thread");
       uint4 v[PER];
 #pragma unroll
-      for (int j = 0; j < PER; ++j) v[j] = __ldcg(src + tid + j * RTHREADS);
+      for (int j = 0; j < PER; ++j) {
+        const int i = tid + j * RTHREADS, r = i / Q, c4 = 4 * (i % Q);
+        v[j] = __ldcg(reinterpret_cast<const uint4*>(h1f_at(p) + (size_t)r * RH + h * RHALF + c4));
+      }
 #pragma unroll
       for (int j = 0; j < PER; ++j) {
-        const int i = tid + j * RTHREADS, k = i / Q, w4 = 4 * (i % Q);
-        s.in.hf[w4][k] = __uint_as_float(v[j].x);
-        s.in.hf[w4 + 1][k] = __uint_as_float(v[j].y);
-        s.in.hf[w4 + 2][k] = __uint_as_float(v[j].z);
-        s.in.hf[w4 + 3][k] = __uint_as_float(v[j].w);
+        const int i = tid + j * RTHREADS, r = i / Q, c4 = 4 * (i % Q);
+        *reinterpret_cast<uint4*>(&s.in.hf[r][c4]) = v[j];
       }
     }
     __syncthreads();
@@ -499,11 +520,6 @@ __device__ void lstm_update(RSmem& s, const RParams& p) {
   // Layer 0: inputs [embedding(token) | h0]; start-of-sequence windows take the bias.
   lstm_layer(s, p, false);
   __syncthreads();
-  for (int i = tid; i < p.batch * RGATES; i += RTHREADS) {
-    const int w = i / RGATES, o = i % RGATES;
-    if (s.win[w].pending == 1) s.gates[w][o] = __half2float(__float2half_rn(s.b0[o]));
-  }
-  __syncthreads();
   cell_update(s, p, s.c0, false);
   grid_sync(s, p);
   // Every CTA has read the old h0: commit the new slice.  Layer 1: inputs
@@ -522,9 +538,55 @@ __device__ void lstm_update(RSmem& s, const RParams& p) {
   __syncthreads();
 }
 
+// Operands of 8 head-chain steps from input k0: 8 weights of each of the
+// thread's columns, the pair's 8 inputs and (MASKED) their skip masks.
+template <bool MASKED>
+struct HeadOps {
+  uint4 w[RHG];
+  uint4 xa, xb;
+  uint4 ma, mb;
+};
+
+template <bool MASKED>
+__device__ __forceinline__ void head_load(const __half* wrow, const uint32_t* xrow, const uint32_t* mrow, int k0,
+                                          HeadOps<MASKED>& c) {
+#pragma unroll
+  for (int j = 0; j < RHG; ++j) c.w[j] = *reinterpret_cast<const uint4*>(wrow + j * RHW_STRIDE + k0);
+  c.xa = *reinterpret_cast<const uint4*>(xrow + k0);
+  c.xb = *reinterpret_cast<const uint4*>(xrow + k0 + 4);
+  if constexpr (MASKED) {
+    c.ma = *reinterpret_cast<const uint4*>(mrow + k0);
+    c.mb = *reinterpret_cast<const uint4*>(mrow + k0 + 4);
+  }
+}
+
+template <bool MASKED>
+__device__ __forceinline__ void head_math(const HeadOps<MASKED>& c, __half2 (&acc)[RHG]) {
+  const uint32_t xs[RCHUNK] = {c.xa.x, c.xa.y, c.xa.z, c.xa.w, c.xb.x, c.xb.y, c.xb.z, c.xb.w};
+  uint32_t ms[RCHUNK] = {};
+  bool masked = false;
+  if constexpr (MASKED) {
+    const uint32_t m8[RCHUNK] = {c.ma.x, c.ma.y, c.ma.z, c.ma.w, c.mb.x, c.mb.y, c.mb.z, c.mb.w};
+#pragma unroll
+    for (int j = 0; j < RCHUNK; ++j) ms[j] = m8[j];
+    masked = (c.ma.x | c.ma.y | c.ma.z | c.ma.w | c.mb.x | c.mb.y | c.mb.z | c.mb.w) != 0u;
+  }
+#pragma unroll
+  for (int j = 0; j < RCHUNK; ++j) {
+#pragma unroll
+    for (int q = 0; q < RHG; ++q) {
+      const uint32_t wp = (&c.w[q].x)[j >> 1];
+      const __half2 wv = (j & 1) ? __high2half2(bits_h2(wp)) : __low2half2(bits_h2(wp));
+      const __half2 v = __hfma2(bits_h2(xs[j]), wv, acc[q]);
+      acc[q] = MASKED && masked ? keep_mask(acc[q], v, ms[j]) : v;
+    }
+  }
+}
+
 // One staged half (320 inputs) of this thread's head chains: columns
 // 3 g .. 3 g + 2, window pair `pair`, starting at input `kb`.  Per 8 inputs
-// the three columns share the pair's input (and mask) loads.  MASKED: lanes
+// the three columns share the pair's input (and mask) loads; unmasked, the
+// next 8 inputs' operands are loaded while the current 8 steps run.  MASKED: lanes
 // set in the staged masks skip the input (the shader's +0 rule); unmasked,
 // every input is applied -- used when the CTA's head weights are all finite,
 // where applying a skipped input (+0 x w) changes an accumulator at most in
@@ -534,31 +596,23 @@ __device__ __forceinline__ void head_chain_half(const RSmem& s, int g, int pair,
   const __half* wrow = &s.hw[RHG * g][kb];
   const uint32_t* xrow = &s.in.jt.j2[pair][0];
   const uint32_t* mrow = &s.in.jt.keep[pair][0];
+  if constexpr (MASKED) {
+    // The masked form (head weights that are not all finite) loads as it goes.
 #pragma unroll 1
-  for (int k0 = 0; k0 < RHALF; k0 += RCHUNK) {
-    uint4 wq[RHG];
-#pragma unroll
-    for (int c = 0; c < RHG; ++c) wq[c] = *reinterpret_cast<const uint4*>(wrow + c * RHW_STRIDE + k0);
-    const uint4 xa = *reinterpret_cast<const uint4*>(xrow + k0), xb = *reinterpret_cast<const uint4*>(xrow + k0 + 4);
-    const uint32_t xs[RCHUNK] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-    uint32_t ms[RCHUNK] = {};
-    bool masked = false;
-    if constexpr (MASKED) {
-      const uint4 ma = *reinterpret_cast<const uint4*>(mrow + k0), mb = *reinterpret_cast<const uint4*>(mrow + k0 + 4);
-      const uint32_t m8[RCHUNK] = {ma.x, ma.y, ma.z, ma.w, mb.x, mb.y, mb.z, mb.w};
-#pragma unroll
-      for (int j = 0; j < RCHUNK; ++j) ms[j] = m8[j];
-      masked = (ma.x | ma.y | ma.z | ma.w | mb.x | mb.y | mb.z | mb.w) != 0u;
+    for (int k0 = 0; k0 < RHALF; k0 += RCHUNK) {
+      HeadOps<MASKED> a;
+      head_load<MASKED>(wrow, xrow, mrow, k0, a);
+      head_math<MASKED>(a, acc);
     }
-#pragma unroll
-    for (int j = 0; j < RCHUNK; ++j) {
-#pragma unroll
-      for (int c = 0; c < RHG; ++c) {
-        const uint32_t wp = (&wq[c].x)[j >> 1];
-        const __half2 wv = (j & 1) ? __high2half2(bits_h2(wp)) : __low2half2(bits_h2(wp));
-        const __half2 v = __hfma2(bits_h2(xs[j]), wv, acc[c]);
-        acc[c] = MASKED && masked ? keep_mask(acc[c], v, ms[j]) : v;
-      }
+  } else {
+    HeadOps<MASKED> a, b;
+    head_load<MASKED>(wrow, xrow, mrow, 0, a);
+#pragma unroll 1
+    for (int k0 = 0; k0 < RHALF; k0 += 2 * RCHUNK) {
+      head_load<MASKED>(wrow, xrow, mrow, k0 + RCHUNK, b);
+      head_math<MASKED>(a, acc);
+      if (k0 + 2 * RCHUNK < RHALF) head_load<MASKED>(wrow, xrow, mrow, k0 + 2 * RCHUNK, a);
+      head_math<MASKED>(b, acc);
     }
   }
 }
@@ -688,7 +742,9 @@ __device__ void joint_reduce(RSmem& s, const RParams& p, int slot, int g, int pa
       if (better(b.tv, b.ti, v.tv, v.ti)) b.tv = v.tv, b.ti = v.ti;
       if (better(b.dv, b.di, v.dv, v.di)) b.dv = v.dv, b.di = v.di;
     }
-    *part_at(p, slot, tid, blockIdx.x) = b;
+    *part_at(p, slot, tid, blockIdx.x) = make_uint2(__float_as_uint(b.tv), b.ti);
+    if (blockIdx.x >= 1 && blockIdx.x < RTAIL_CTAS)
+      *dpart_at(p, slot, tid, blockIdx.x - 1) = make_uint2(__float_as_uint(b.dv), b.di);
   }
 }
 
@@ -743,25 +799,30 @@ __device__ void emit(RSmem& s, const RParams& p, int w, uint32_t tok, uint32_t f
 
 // Reduce every CTA's partials (each CTA does it, so all agree) and advance the
 // control of every active window (the shader's main loop and flush, :1702-1990).
-// Thread (window, q) loads its 6 or 7 partials at once, then reduces them.
 __device__ void joint_decide(RSmem& s, const RParams& p, int slot) {
   const int tid = threadIdx.x;
-  constexpr int PER = (RG + 19) / 20;
-  for (int i = tid; i < RMAXB * 20; i += RTHREADS) {
-    const int w = i / 20, q = i % 20;
+  // Thread (window, q): the token partials of CTAs 8 q .. 8 q + 7 (four
+  // 16-byte loads).
+  constexpr int QN = RG / 8;
+  static_assert(RMAXB * QN == RTHREADS && QN <= 20, "one thread per (window, group of 8 CTAs)");
+  {
+    const int w = tid / QN, q = tid % QN;
     RPartial b{RNEG, 0xffffffffu, RNEG, 0xffffffffu};
     if (w < p.batch && s.win[w].joint) {
-      uint4 raw[PER];
+      uint4 raw[4];
+      const uint4* src = reinterpret_cast<const uint4*>(part_at(p, slot, w, 8 * q));
 #pragma unroll
-      for (int j = 0; j < PER; ++j)
-        if (q + 20 * j < RG) raw[j] = __ldcg(reinterpret_cast<const uint4*>(part_at(p, slot, w, q + 20 * j)));
+      for (int j = 0; j < 4; ++j) raw[j] = __ldcg(src + j);
+      // Thread q < 5 also takes duration q's partial (from CTA q + 1).
+      const uint2 dr = q < RTAIL_CTAS - 1 ? __ldcg(dpart_at(p, slot, w, q)) : make_uint2(__float_as_uint(RNEG), ~0u);
 #pragma unroll
-      for (int j = 0; j < PER; ++j) {
-        if (q + 20 * j >= RG) continue;
-        const RPartial v{__uint_as_float(raw[j].x), raw[j].y, __uint_as_float(raw[j].z), raw[j].w};
-        if (better(b.tv, b.ti, v.tv, v.ti)) b.tv = v.tv, b.ti = v.ti;
-        if (better(b.dv, b.di, v.dv, v.di)) b.dv = v.dv, b.di = v.di;
+      for (int j = 0; j < 4; ++j) {
+        const float v0 = __uint_as_float(raw[j].x), v1 = __uint_as_float(raw[j].z);
+        if (better(b.tv, b.ti, v0, raw[j].y)) b.tv = v0, b.ti = raw[j].y;
+        if (better(b.tv, b.ti, v1, raw[j].w)) b.tv = v1, b.ti = raw[j].w;
       }
+      b.dv = __uint_as_float(dr.x);
+      b.di = dr.y;
     }
     s.in.red[w][q] = b;
   }
@@ -769,7 +830,7 @@ __device__ void joint_decide(RSmem& s, const RParams& p, int slot) {
   if (tid < p.batch && s.win[tid].joint) {
     const int w = tid;
     RPartial b = s.in.red[w][0];
-    for (int q = 1; q < 20; ++q) {
+    for (int q = 1; q < RG / 8; ++q) {
       const RPartial v = s.in.red[w][q];
       if (better(b.tv, b.ti, v.tv, v.ti)) b.tv = v.tv, b.ti = v.ti;
       if (better(b.dv, b.di, v.dv, v.di)) b.dv = v.dv, b.di = v.di;

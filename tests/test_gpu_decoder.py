@@ -77,6 +77,30 @@ def test_tdt_decoder_matches_oracle(pk, oracle, device, precision, route):
     assert agree >= FRAME_BAR
 
 
+def test_tdt_decoder_skip_rule_with_nonfinite_head_weights(pk, oracle, device, route):
+    """Head weights that are not all finite: the shader's +0 skip rule decides
+    whether an infinite weight meets a zero input, so the kernels must apply it
+    (the resident kernel takes its masked path in the CTAs that hold such a
+    column).  Tokens, frames, durations and counts equal the oracle's."""
+    rng = np.random.default_rng(17)
+    enc = rng.normal(0, 1, (4, 40, 640)).astype(np.float16)
+    dec = {k: v["data"].copy() for k, v in pk.synthetic.make_decoder("fp16", seed=3).items()}
+    hw = dec["joint.head.weight"].reshape(640, -1)
+    hw[5, 100] = np.inf     # a token column (CTA 12)
+    hw[7, 1024] = -np.inf   # the blank (CTA 0)
+    hw[9, 1026] = np.inf    # duration 1 (CTA 2)
+    lengths = [40, 33, 40, 7]
+    got = _run_gpu(pk, device, enc, lengths, dec, "fp16", 200, flush=[1, 0, 1, 0])
+    ref = oracle.tdt_decode(enc, lengths, dec, max_tokens=200, flush=[1, 0, 1, 0])
+    assert device.status() == 0
+    assert list(got[3]) == list(ref[3]) and list(got[4]) == list(ref[4])
+    for b in range(4):
+        n = int(ref[3][b])
+        assert np.array_equal(got[0][b, :n], ref[0][b, :n]) and np.array_equal(got[1][b, :n], ref[1][b, :n])
+        assert np.array_equal(got[2][b, :n], ref[2][b, :n])
+    print(f"decoder (non-finite head weights, {route}): counts {list(got[3])}")
+
+
 @pytest.mark.parametrize("token,duration,max_tokens,flush", [(1024, 3, 8, 0), (7, 0, 64, 0), (7, 0, 15, 0),
                                                              (9, 2, 32, 1)])
 def test_tdt_decoder_control_paths(pk, oracle, device, token, duration, max_tokens, flush, route):
