@@ -195,7 +195,8 @@ int pk_logmel(pk_device* device, int batch, int sample_count, const float* sampl
  * pointers 16-byte aligned.  The decoder state lives on chip, so the
  * reference's state / predictorScratch arena slices have no counterpart.
  * The resident FP16 kernel exchanges vectors through one area owned by the
- * pk_device (its grid-barrier counter is reset by each launch): decoder calls
+ * pk_device (each launch first rebuilds the layer-0 token table there from
+ * the call's weights and resets the grid-barrier counter): decoder calls
  * on one pk_device must not overlap on the GPU -- issue them on one stream,
  * or open one pk_device per stream. */
 typedef struct pk_tdt_desc {
