@@ -57,10 +57,11 @@ constexpr int RHG = 3;                // head columns per chain thread
 constexpr int RMAXB = 40;             // windows per launch
 constexpr int RPAIRS = RMAXB / 2;     // window pairs (half2 lanes)
 constexpr int RHALF = RH / 2;         // joint / projector inputs per staged half
-constexpr int RLSTM_RP = RGATES / 2;  // gate-output pairs (an LSTM chain thread owns two outputs)
-constexpr int RLSTM_PP = RPAIRS / 2;  // window-pair pairs (... and two window pairs)
-constexpr int RLSTM_PER_PAR = RLSTM_RP * RLSTM_PP;       // chain threads per parity: 100
-constexpr int RLSTM_THREADS = 2 * RLSTM_PER_PAR;         // 200
+constexpr int RLSTM_R = 4;            // gate outputs per LSTM chain thread
+constexpr int RLSTM_RQ = RGATES / RLSTM_R;  // their groups: 5
+constexpr int RLSTM_PP = RPAIRS / 2;  // window-pair pairs (a chain thread also owns two window pairs)
+constexpr int RLSTM_PER_PAR = RLSTM_RQ * RLSTM_PP;       // chain threads per parity: 50
+constexpr int RLSTM_THREADS = 2 * RLSTM_PER_PAR;         // 100
 constexpr int RPW = RH / 2;           // same-parity inputs of a staged half
 constexpr int RW1P = RH + 8;          // layer-1 weight row of one parity (640 inputs), padded
 constexpr int RW0P = RPW + 8;         // layer-0 recurrent weight row of one parity (320 inputs), padded
@@ -195,14 +196,15 @@ __device__ void grid_sync(RSmem& s, const RParams& p) {
 }
 
 __device__ __forceinline__ uint32_t h2_bits(__half2 v) { return *reinterpret_cast<uint32_t*>(&v); }
-// The 200 LSTM chain threads are lanes 0..24 of warps 0..7, so each SM
-// sub-partition issues for two warps of 25 (not two full warps on two
-// sub-partitions and one on the others).
+// The 100 LSTM chain threads are lanes 0..24 of warps 0..3, one warp per SM
+// sub-partition (not three full warps on three sub-partitions and one lane
+// group on the fourth).
 constexpr int RSPREAD_LANES = 25;
-static_assert(8 * RSPREAD_LANES == RLSTM_THREADS, "spread roles");
+constexpr int RSPREAD_WARPS = RLSTM_THREADS / RSPREAD_LANES;
+static_assert(RSPREAD_WARPS * RSPREAD_LANES == RLSTM_THREADS && RSPREAD_WARPS == 4, "spread roles");
 __device__ __forceinline__ int spread_index(int tid, bool& on) {
   const int lane = tid & 31, wid = tid >> 5;
-  on = wid < 8 && lane < RSPREAD_LANES;
+  on = wid < RSPREAD_WARPS && lane < RSPREAD_LANES;
   return wid * RSPREAD_LANES + lane;
 }
 __device__ __forceinline__ __half2 bits_h2(uint32_t v) { return *reinterpret_cast<__half2*>(&v); }
@@ -270,60 +272,55 @@ __device__ void stage_token_init(RSmem& s, const RParams& p) {
 }
 
 // Operands of 8 same-parity chain steps from m: 8 weights of each of the
-// thread's two gate outputs and the two window pairs' inputs of each step.
+// thread's RLSTM_R gate outputs and the two window pairs' inputs of each step.
 struct LstmOps {
-  uint4 wa, wb;
+  uint4 w[RLSTM_R];
   uint2 x[8];
 };
 
-__device__ __forceinline__ void lstm_load(const RSmem& s, const __half* wa, const __half* wb, int m, int pp, int par,
+__device__ __forceinline__ void lstm_load(const RSmem& s, const __half* w0, int wstride, int m, int pp, int par,
                                           LstmOps& c) {
-  c.wa = *reinterpret_cast<const uint4*>(wa + m);
-  c.wb = *reinterpret_cast<const uint4*>(wb + m);
+#pragma unroll
+  for (int r = 0; r < RLSTM_R; ++r) c.w[r] = *reinterpret_cast<const uint4*>(w0 + r * wstride + m);
 #pragma unroll
   for (int j = 0; j < 8; ++j) c.x[j] = *reinterpret_cast<const uint2*>(&s.in.x2[2 * (m + j) + par][2 * pp]);
 }
 
-__device__ __forceinline__ void lstm_math(const LstmOps& c, __half2 (&acc)[2][2]) {
-  const uint32_t a[4] = {c.wa.x, c.wa.y, c.wa.z, c.wa.w};
-  const uint32_t b[4] = {c.wb.x, c.wb.y, c.wb.z, c.wb.w};
+__device__ __forceinline__ void lstm_math(const LstmOps& c, __half2 (&acc)[RLSTM_R][2]) {
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    // Broadcasts of one half of a weight pair (an operand selector of the
-    // f16x2 FMA, not a separate instruction).
-    const __half2 va = (j & 1) ? __high2half2(bits_h2(a[j >> 1])) : __low2half2(bits_h2(a[j >> 1]));
-    const __half2 vb = (j & 1) ? __high2half2(bits_h2(b[j >> 1])) : __low2half2(bits_h2(b[j >> 1]));
-    acc[0][0] = __hfma2(bits_h2(c.x[j].x), va, acc[0][0]);
-    acc[0][1] = __hfma2(bits_h2(c.x[j].y), va, acc[0][1]);
-    acc[1][0] = __hfma2(bits_h2(c.x[j].x), vb, acc[1][0]);
-    acc[1][1] = __hfma2(bits_h2(c.x[j].y), vb, acc[1][1]);
+#pragma unroll
+    for (int r = 0; r < RLSTM_R; ++r) {
+      // Broadcast of one half of a weight pair (an operand selector of the
+      // f16x2 FMA, not a separate instruction).
+      const uint32_t wp = (&c.w[r].x)[j >> 1];
+      const __half2 wv = (j & 1) ? __high2half2(bits_h2(wp)) : __low2half2(bits_h2(wp));
+      acc[r][0] = __hfma2(bits_h2(c.x[j].x), wv, acc[r][0]);
+      acc[r][1] = __hfma2(bits_h2(c.x[j].y), wv, acc[r][1]);
+    }
   }
 }
 
-// One staged half (640 inputs) of this thread's gate chains: gate outputs
-// whose same-parity weights of this half start at `wa` and `wb`, parity
-// `par`, window pairs 2 pp and 2 pp + 1 (four chains per thread, each in
-// increasing input order).  Each 16-byte weight load serves 8 steps of two
-// window pairs, each 8-byte input load 2 steps of two gate outputs.  Two
-// operand buffers alternate: the next 8 steps' loads are issued before the
-// current 8 steps.
-__device__ __forceinline__ void lstm_chain_half(const RSmem& s, const __half* wa, const __half* wb, int pp, int par,
-                                                __half2 (&acc)[2][2]) {
-  LstmOps a, b;
-  lstm_load(s, wa, wb, 0, pp, par, a);
-#pragma unroll 1
-  for (int m = 0; m < RPW; m += 16) {
-    lstm_load(s, wa, wb, m + 8, pp, par, b);
+// One staged half (640 inputs) of this thread's gate chains: RLSTM_R gate
+// outputs whose same-parity weights of this half start at `w0` (rows
+// `wstride` apart), parity `par`, window pairs 2 pp and 2 pp + 1 (2 RLSTM_R
+// chains per thread, each in increasing input order).  Each 16-byte weight
+// load serves 8 steps of two window pairs, each 8-byte input load 2 steps of
+// RLSTM_R gate outputs.
+__device__ __forceinline__ void lstm_chain_half(const RSmem& s, const __half* w0, int wstride, int pp, int par,
+                                                __half2 (&acc)[RLSTM_R][2]) {
+#pragma unroll 2
+  for (int m = 0; m < RPW; m += 8) {
+    LstmOps a;
+    lstm_load(s, w0, wstride, m, pp, par, a);
     lstm_math(a, acc);
-    if (m + 16 < RPW) lstm_load(s, wa, wb, m + 16, pp, par, a);
-    lstm_math(b, acc);
   }
 }
 
 // Gate chains of one LSTM layer for the windows that need them; gates land in
-// s.gates[window][gate * 5 + channel].  Chain thread t (spread_index) < 200:
-// parity t / 100, gate outputs 2 q and 2 q + 1 with q = (t % 100) / 10,
-// window pairs 2 v and 2 v + 1 with v = t % 10.  Inputs: layer 0 [embedding(token) | h0] (the
+// s.gates[window][gate * 5 + channel].  Chain thread t (spread_index) < 100:
+// parity t / 50, gate outputs 4 q .. 4 q + 3 with q = (t % 50) / 10, window
+// pairs 2 v and 2 v + 1 with v = t % 10.  Inputs: layer 0 [embedding(token) | h0] (the
 // chains' states after the embedding half come from the token table), layer 1
 // [new h0 | h1], staged one half at a time.  Layer 1's start-of-sequence
 // windows stop at input 640 (their recurrent input is zero and the shader
@@ -335,23 +332,23 @@ __device__ void lstm_layer(RSmem& s, const RParams& p, bool layer1) {
   bool chain;
   const int ci = spread_index(tid, chain);
   const int par = (ci / RLSTM_PER_PAR) & 1, r = ci % RLSTM_PER_PAR;
-  const int oa = 2 * (r / RLSTM_PP), pp = r % RLSTM_PP;
-  const __half* wa = layer1 ? &s.w1[par][oa][0] : &s.w0[par][oa][0];
-  const __half* wb = layer1 ? &s.w1[par][oa + 1][0] : &s.w0[par][oa + 1][0];
+  const int oa = RLSTM_R * (r / RLSTM_PP), pp = r % RLSTM_PP;
+  const __half* w0 = layer1 ? &s.w1[par][oa][0] : &s.w0[par][oa][0];
+  const int wstride = layer1 ? RW1P : RW0P;
   bool any = false, any_full = false;
   uint32_t keep_rec[2];
-  __half2 acc[2][2];
+  __half2 acc[RLSTM_R][2];
   if (chain) {
 #pragma unroll
-    for (int rr = 0; rr < 2; ++rr) {
+    for (int rr = 0; rr < RLSTM_R; ++rr) {
       const __half2 init = par == 0 ? __float2half2_rn((layer1 ? s.b1 : s.b0)[oa + rr]) : __float2half2_rn(0.0f);
       acc[rr][0] = init;
       acc[rr][1] = init;
     }
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
-      const int w0 = (2 * pp + i) * 2;
-      const int p0 = s.win[w0].pending, p1 = s.win[w0 + 1].pending;
+      const int w0i = (2 * pp + i) * 2;
+      const int p0 = s.win[w0i].pending, p1 = s.win[w0i + 1].pending;
       keep_rec[i] = lane_mask(p0 == 1, p1 == 1);
       any |= layer1 ? (p0 | p1) != 0 : (p0 == 2 || p1 == 2);
       any_full |= p0 == 2 || p1 == 2;
@@ -361,18 +358,18 @@ __device__ void lstm_layer(RSmem& s, const RParams& p, bool layer1) {
   if (layer1) {
     stage_rows(s, xh(p, XH0N));
     __syncthreads();
-    if (chain && any) lstm_chain_half(s, wa, wb, pp, par, acc);
+    if (chain && any) lstm_chain_half(s, w0, wstride, pp, par, acc);
     if (tokens) {
       __syncthreads();  // the first half is consumed
       stage_rows(s, xh(p, XH1));
       __syncthreads();
       if (chain && any_full) {
-        __half2 before[2][2];
+        __half2 before[RLSTM_R][2];
 #pragma unroll
-        for (int rr = 0; rr < 2; ++rr) before[rr][0] = acc[rr][0], before[rr][1] = acc[rr][1];
-        lstm_chain_half(s, wa + RPW, wb + RPW, pp, par, acc);
+        for (int rr = 0; rr < RLSTM_R; ++rr) before[rr][0] = acc[rr][0], before[rr][1] = acc[rr][1];
+        lstm_chain_half(s, w0 + RPW, wstride, pp, par, acc);
 #pragma unroll
-        for (int rr = 0; rr < 2; ++rr)
+        for (int rr = 0; rr < RLSTM_R; ++rr)
 #pragma unroll
           for (int i = 0; i < 2; ++i) acc[rr][i] = keep_mask(before[rr][i], acc[rr][i], keep_rec[i]);
       }
@@ -385,16 +382,16 @@ __device__ void lstm_layer(RSmem& s, const RParams& p, bool layer1) {
     __syncthreads();
     if (chain && any) {
 #pragma unroll
-      for (int rr = 0; rr < 2; ++rr)
+      for (int rr = 0; rr < RLSTM_R; ++rr)
 #pragma unroll
         for (int i = 0; i < 2; ++i) acc[rr][i] = bits_h2(s.l0init[par][2 * pp + i][oa + rr]);
-      lstm_chain_half(s, wa, wb, pp, par, acc);
+      lstm_chain_half(s, w0, wstride, pp, par, acc);
     }
   }
   // The two parity chains of a gate sum in f16.
   if (chain && any) {
 #pragma unroll
-    for (int rr = 0; rr < 2; ++rr)
+    for (int rr = 0; rr < RLSTM_R; ++rr)
 #pragma unroll
       for (int i = 0; i < 2; ++i) s.psum[par][2 * pp + i][oa + rr] = h2_bits(acc[rr][i]);
   }
