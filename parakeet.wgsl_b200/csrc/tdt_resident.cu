@@ -142,6 +142,13 @@ struct RSmem {
     } jt;                                // (rows padded: the pairs of a warp read different banks)
     RPartial red[RMAXB][20];         // argmax reduction
   } in;
+  // The second half of a phase's inputs, staged by the threads that run no
+  // chains while the chain threads work through the first half in `in`.
+  union {
+    __half2 x2[RH][RPAIRS];
+    float hf[RMAXB][RHALF + 4];
+    uint32_t j2[RPAIRS][RHALF + 4];
+  } in2;
   float gates[RMAXB][RGATES];
   float projv[RMAXB][RCH];           // this CTA's projector outputs of every window (last update)
   float c0[RMAXB][RCH];
@@ -251,6 +258,23 @@ __device__ void stage_rows(RSmem& s, const __half* src) {
   for (int j = 0; j < PER; ++j) reinterpret_cast<uint4*>(&s.in.x2[0][0])[threadIdx.x + j * RTHREADS] = v[j];
 }
 
+// Background staging by the threads of warps `first_warp` .. 19 (the others
+// run chains meanwhile): `chunks` 16-byte chunks, chunk i read from
+// src_chunk(i) and written to dst_chunk(i).
+constexpr int RWARPS = RTHREADS / 32;
+template <typename Src, typename Dst>
+__device__ __forceinline__ void stage_background(int first_warp, int chunks, Src src_chunk, Dst dst_chunk) {
+  const int idx = (int)threadIdx.x - first_warp * 32, n = (RWARPS - first_warp) * 32;
+  if (idx < 0) return;
+  for (int i = idx; i < chunks; i += 2 * n) {
+    const uint4 a = __ldcg(src_chunk(i));
+    uint4 b = make_uint4(0u, 0u, 0u, 0u);
+    if (i + n < chunks) b = __ldcg(src_chunk(i + n));
+    *dst_chunk(i) = a;
+    if (i + n < chunks) *dst_chunk(i + n) = b;
+  }
+}
+
 // The layer-0 chain states after the embedding inputs of each updating
 // window's token (the token table), into l0init: thread (window, q) loads
 // gates 4 q .. 4 q + 3 of both parities (16 bytes).
@@ -278,12 +302,12 @@ struct LstmOps {
   uint2 x[8];
 };
 
-__device__ __forceinline__ void lstm_load(const RSmem& s, const __half* w0, int wstride, int m, int pp, int par,
-                                          LstmOps& c) {
+__device__ __forceinline__ void lstm_load(const __half2 (*x2)[RPAIRS], const __half* w0, int wstride, int m, int pp,
+                                          int par, LstmOps& c) {
 #pragma unroll
   for (int r = 0; r < RLSTM_R; ++r) c.w[r] = *reinterpret_cast<const uint4*>(w0 + r * wstride + m);
 #pragma unroll
-  for (int j = 0; j < 8; ++j) c.x[j] = *reinterpret_cast<const uint2*>(&s.in.x2[2 * (m + j) + par][2 * pp]);
+  for (int j = 0; j < 8; ++j) c.x[j] = *reinterpret_cast<const uint2*>(&x2[2 * (m + j) + par][2 * pp]);
 }
 
 __device__ __forceinline__ void lstm_math(const LstmOps& c, __half2 (&acc)[RLSTM_R][2]) {
@@ -301,18 +325,18 @@ __device__ __forceinline__ void lstm_math(const LstmOps& c, __half2 (&acc)[RLSTM
   }
 }
 
-// One staged half (640 inputs) of this thread's gate chains: RLSTM_R gate
+// One staged half (640 inputs, in `x2`) of this thread's gate chains: RLSTM_R gate
 // outputs whose same-parity weights of this half start at `w0` (rows
 // `wstride` apart), parity `par`, window pairs 2 pp and 2 pp + 1 (2 RLSTM_R
 // chains per thread, each in increasing input order).  Each 16-byte weight
 // load serves 8 steps of two window pairs, each 8-byte input load 2 steps of
 // RLSTM_R gate outputs.
-__device__ __forceinline__ void lstm_chain_half(const RSmem& s, const __half* w0, int wstride, int pp, int par,
-                                                __half2 (&acc)[RLSTM_R][2]) {
-#pragma unroll 2
+__device__ __forceinline__ void lstm_chain_half(const __half2 (*x2)[RPAIRS], const __half* w0, int wstride, int pp,
+                                                int par, __half2 (&acc)[RLSTM_R][2]) {
+#pragma unroll 4
   for (int m = 0; m < RPW; m += 8) {
     LstmOps a;
-    lstm_load(s, w0, wstride, m, pp, par, a);
+    lstm_load(x2, w0, wstride, m, pp, par, a);
     lstm_math(a, acc);
   }
 }
@@ -358,16 +382,19 @@ __device__ void lstm_layer(RSmem& s, const RParams& p, bool layer1) {
   if (layer1) {
     stage_rows(s, xh(p, XH0N));
     __syncthreads();
-    if (chain && any) lstm_chain_half(s, w0, wstride, pp, par, acc);
+    if (chain && any) lstm_chain_half(s.in.x2, w0, wstride, pp, par, acc);
     if (tokens) {
-      __syncthreads();  // the first half is consumed
-      stage_rows(s, xh(p, XH1));
+      // The recurrent half (h1) is staged into in2 by warps 4.. while the
+      // chain warps run the first half.
+      const uint4* src = reinterpret_cast<const uint4*>(xh(p, XH1));
+      uint4* dst = reinterpret_cast<uint4*>(&s.in2.x2[0][0]);
+      stage_background(RSPREAD_WARPS, RH * RROW16, [&](int i) { return src + i; }, [&](int i) { return dst + i; });
       __syncthreads();
       if (chain && any_full) {
         __half2 before[RLSTM_R][2];
 #pragma unroll
         for (int rr = 0; rr < RLSTM_R; ++rr) before[rr][0] = acc[rr][0], before[rr][1] = acc[rr][1];
-        lstm_chain_half(s, w0 + RPW, wstride, pp, par, acc);
+        lstm_chain_half(s.in2.x2, w0 + RPW, wstride, pp, par, acc);
 #pragma unroll
         for (int rr = 0; rr < RLSTM_R; ++rr)
 #pragma unroll
@@ -385,7 +412,7 @@ __device__ void lstm_layer(RSmem& s, const RParams& p, bool layer1) {
       for (int rr = 0; rr < RLSTM_R; ++rr)
 #pragma unroll
         for (int i = 0; i < 2; ++i) acc[rr][i] = bits_h2(s.l0init[par][2 * pp + i][oa + rr]);
-      lstm_chain_half(s, w0, wstride, pp, par, acc);
+      lstm_chain_half(s.in.x2, w0, wstride, pp, par, acc);
     }
   }
   // The two parity chains of a gate sum in f16.
@@ -454,50 +481,56 @@ __device__ void projector(RSmem& s, const RParams& p) {
   const __half ev = joint ? p.enc[((size_t)w * p.frames + s.win[w].joint_t) * RH + blockIdx.x * RCH + o]
                           : __float2half_rn(0.0f);
   float acc = live ? s.pb[o] : 0.0f;
-  for (int h = 0; h < 2; ++h) {
-    if (h) __syncthreads();  // the first half is consumed
-    {
-      // Row w of the exchanged state holds window w's 640 values: a half is
-      // 80 chunks of 16 bytes per window, copied as they lie.
-      constexpr int Q = RHALF / 4;
-      constexpr int PER = RMAXB * Q / RTHREADS;
-      static_assert(RMAXB * Q % RTHREADS == 0, "whole chunks per thread");
-      uint4 v[PER];
+  // Row w of the exchanged state holds window w's 640 values: a half is 80
+  // chunks of 16 bytes per window, copied as they lie.  All threads stage the
+  // first half; the second is staged into in2 by warps 7.. (no chain thread
+  // among them) while the chains run through the first.
+  constexpr int Q = RHALF / 4;
+  constexpr int PER = RMAXB * Q / RTHREADS;
+  static_assert(RMAXB * Q % RTHREADS == 0 && RPROJ_THREADS <= 7 * 32, "whole chunks per thread; chain warps 0..6");
+  {
+    uint4 v[PER];
 #pragma unroll
-      for (int j = 0; j < PER; ++j) {
-        const int i = tid + j * RTHREADS, r = i / Q, c4 = 4 * (i % Q);
-        v[j] = __ldcg(reinterpret_cast<const uint4*>(h1f_at(p) + (size_t)r * RH + h * RHALF + c4));
-      }
-#pragma unroll
-      for (int j = 0; j < PER; ++j) {
-        const int i = tid + j * RTHREADS, r = i / Q, c4 = 4 * (i % Q);
-        *reinterpret_cast<uint4*>(&s.in.hf[r][c4]) = v[j];
-      }
+    for (int j = 0; j < PER; ++j) {
+      const int i = tid + j * RTHREADS, r = i / Q, c4 = 4 * (i % Q);
+      v[j] = __ldcg(reinterpret_cast<const uint4*>(h1f_at(p) + (size_t)r * RH + c4));
     }
-    __syncthreads();
-    if (live) {
-      const float* hrow = &s.in.hf[w][0];
-      const float* wrow = &s.pwf[o][h * RHALF];
-      float4 ha = *reinterpret_cast<const float4*>(hrow), wa = *reinterpret_cast<const float4*>(wrow);
-#pragma unroll 1
-      for (int k = 0; k < RHALF; k += 8) {
-        const float4 hb = *reinterpret_cast<const float4*>(hrow + k + 4);
-        const float4 wb = *reinterpret_cast<const float4*>(wrow + k + 4);
-        acc = __fmaf_rn(ha.x, wa.x, acc);
-        acc = __fmaf_rn(ha.y, wa.y, acc);
-        acc = __fmaf_rn(ha.z, wa.z, acc);
-        acc = __fmaf_rn(ha.w, wa.w, acc);
-        if (k + 8 < RHALF) {
-          ha = *reinterpret_cast<const float4*>(hrow + k + 8);
-          wa = *reinterpret_cast<const float4*>(wrow + k + 8);
-        }
-        acc = __fmaf_rn(hb.x, wb.x, acc);
-        acc = __fmaf_rn(hb.y, wb.y, acc);
-        acc = __fmaf_rn(hb.z, wb.z, acc);
-        acc = __fmaf_rn(hb.w, wb.w, acc);
-      }
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const int i = tid + j * RTHREADS, r = i / Q, c4 = 4 * (i % Q);
+      *reinterpret_cast<uint4*>(&s.in.hf[r][c4]) = v[j];
     }
   }
+  __syncthreads();
+  auto chain_half = [&](const float (*hf)[RHALF + 4], int h) {
+    const float* hrow = &hf[w][0];
+    const float* wrow = &s.pwf[o][h * RHALF];
+    float4 ha = *reinterpret_cast<const float4*>(hrow), wa = *reinterpret_cast<const float4*>(wrow);
+#pragma unroll 1
+    for (int k = 0; k < RHALF; k += 8) {
+      const float4 hb = *reinterpret_cast<const float4*>(hrow + k + 4);
+      const float4 wb = *reinterpret_cast<const float4*>(wrow + k + 4);
+      acc = __fmaf_rn(ha.x, wa.x, acc);
+      acc = __fmaf_rn(ha.y, wa.y, acc);
+      acc = __fmaf_rn(ha.z, wa.z, acc);
+      acc = __fmaf_rn(ha.w, wa.w, acc);
+      if (k + 8 < RHALF) {
+        ha = *reinterpret_cast<const float4*>(hrow + k + 8);
+        wa = *reinterpret_cast<const float4*>(wrow + k + 8);
+      }
+      acc = __fmaf_rn(hb.x, wb.x, acc);
+      acc = __fmaf_rn(hb.y, wb.y, acc);
+      acc = __fmaf_rn(hb.z, wb.z, acc);
+      acc = __fmaf_rn(hb.w, wb.w, acc);
+    }
+  };
+  if (live) chain_half(s.in.hf, 0);
+  stage_background(
+      7, RMAXB * Q,
+      [&](int i) { return reinterpret_cast<const uint4*>(h1f_at(p) + (size_t)(i / Q) * RH + RHALF + 4 * (i % Q)); },
+      [&](int i) { return reinterpret_cast<uint4*>(&s.in2.hf[i / Q][4 * (i % Q)]); });
+  __syncthreads();
+  if (live) chain_half(s.in2.hf, 1);
   if (live) {
     proj_at(p, w)[blockIdx.x * RCH + o] = acc;
     s.projv[w][o] = acc;
@@ -589,9 +622,10 @@ __device__ __forceinline__ void head_math(const HeadOps<MASKED>& c, __half2 (&ac
 // where applying a skipped input (+0 x w) changes an accumulator at most in
 // the sign of a zero, which no argmax comparison sees.
 template <bool MASKED>
-__device__ __forceinline__ void head_chain_half(const RSmem& s, int g, int pair, int kb, __half2 (&acc)[RHG]) {
+__device__ __forceinline__ void head_chain_half(const RSmem& s, const uint32_t (*j2)[RHALF + 4], int g, int pair, int kb,
+                                                __half2 (&acc)[RHG]) {
   const __half* wrow = &s.hw[RHG * g][kb];
-  const uint32_t* xrow = &s.in.jt.j2[pair][0];
+  const uint32_t* xrow = &j2[pair][0];
   const uint32_t* mrow = &s.in.jt.keep[pair][0];
   if constexpr (MASKED) {
     // The masked form (head weights that are not all finite) loads as it goes.
@@ -694,9 +728,9 @@ __device__ void joint_inputs_staged(RSmem& s, const RParams& p, bool built, bool
     __syncthreads();
     if (run) {
       if (fast)
-        head_chain_half<false>(s, g, pair, h * RHALF, acc);
+        head_chain_half<false>(s, s.in.jt.j2, g, pair, h * RHALF, acc);
       else
-        head_chain_half<true>(s, g, pair, h * RHALF, acc);
+        head_chain_half<true>(s, s.in.jt.j2, g, pair, h * RHALF, acc);
     }
   }
 }
@@ -761,18 +795,23 @@ __device__ void joint_partials(RSmem& s, const RParams& p, int slot, bool built)
   const bool run = head && (s.win[2 * pair].joint || s.win[2 * pair + 1].joint);
   if (built && fast) {
     // The projector phase left the f16 inputs in the chains' layout: each
-    // half is a plain copy of 20 rows of 320 words.
+    // half is a plain copy of 20 rows of 320 words.  The second half goes to
+    // in2 (warps 2..) while the head chains (warps 0..1) run the first.
     constexpr int CH = RPAIRS * RHALF / 4;  // 16-byte chunks per half
-    for (int h = 0; h < 2; ++h) {
-      if (h) __syncthreads();  // the first half is consumed
-      for (int i = tid; i < CH; i += RTHREADS) {
-        const int pr = i / (RHALF / 4), c4 = 4 * (i % (RHALF / 4));
-        *reinterpret_cast<uint4*>(&s.in.jt.j2[pr][c4]) =
-            __ldcg(reinterpret_cast<const uint4*>(j2_at(p) + ((size_t)pr * RH + h * RHALF + c4) * 2));
-      }
-      __syncthreads();
-      if (run) head_chain_half<false>(s, g, pair, h * RHALF, acc);
-    }
+    constexpr int QH = RHALF / 4;
+    static_assert(RHEAD_THREADS <= 64, "head chain warps 0..1");
+    auto src = [&](int i, int h) {
+      return reinterpret_cast<const uint4*>(j2_at(p) + ((size_t)(i / QH) * RH + h * RHALF + 4 * (i % QH)) * 2);
+    };
+    for (int i = tid; i < CH; i += RTHREADS)
+      *reinterpret_cast<uint4*>(&s.in.jt.j2[i / QH][4 * (i % QH)]) = __ldcg(src(i, 0));
+    __syncthreads();
+    if (run) head_chain_half<false>(s, s.in.jt.j2, g, pair, 0, acc);
+    stage_background(
+        2, CH, [&](int i) { return src(i, 1); },
+        [&](int i) { return reinterpret_cast<uint4*>(&s.in2.j2[i / QH][4 * (i % QH)]); });
+    __syncthreads();
+    if (run) head_chain_half<false>(s, s.in2.j2, g, pair, RHALF, acc);
   } else {
     joint_inputs_staged(s, p, built, fast, g, pair, run, acc);
   }
