@@ -140,7 +140,6 @@ struct RSmem {
       uint32_t j2[RPAIRS][RHALF + 4];    // one half of the joint inputs, [window pair][input] (half2 bits)
       uint32_t keep[RPAIRS][RHALF + 4];  // per pair and input: the lanes whose head chain skips it
     } jt;                                // (rows padded: the pairs of a warp read different banks)
-    RPartial red[RMAXB][20];         // argmax reduction
   } in;
   // The second half of a phase's inputs, staged by the threads that run no
   // chains while the chain threads work through the first half in `in`.
@@ -148,6 +147,7 @@ struct RSmem {
     __half2 x2[RH][RPAIRS];
     float hf[RMAXB][RHALF + 4];
     uint32_t j2[RPAIRS][RHALF + 4];
+    RPartial red[RMAXB][20];  // argmax reduction
   } in2;
   float gates[RMAXB][RGATES];
   float projv[RMAXB][RCH];           // this CTA's projector outputs of every window (last update)
@@ -162,6 +162,7 @@ struct RSmem {
   RWin win[RMAXB];
   int any_pending, any_token, any_joint;
   int head_finite;                   // every head weight of this CTA is finite (the head chains skip no input)
+  int h0_staged;                     // in.x2 already holds the committed h0 (prefetched by the joint phase)
   unsigned int gen;
 };
 static_assert(sizeof(RSmem) + 128 <= 232448, "resident decoder shared memory");
@@ -405,7 +406,7 @@ __device__ void lstm_layer(RSmem& s, const RParams& p, bool layer1) {
     // Layer 0: the chains over the token's embedding inputs are read from the
     // token table; the recurrent inputs (h0) continue them here.
     stage_token_init(s, p);
-    stage_rows(s, xh(p, XH0));
+    if (!s.h0_staged) stage_rows(s, xh(p, XH0));
     __syncthreads();
     if (chain && any) {
 #pragma unroll
@@ -786,6 +787,7 @@ __device__ void joint_reduce(RSmem& s, const RParams& p, int slot, int g, int pa
 // below builds them (and the shader's skip masks) input by input.
 __device__ void joint_partials(RSmem& s, const RParams& p, int slot, bool built) {
   const int tid = threadIdx.x;
+  if (tid == 0) s.h0_staged = 0;  // the joint inputs reuse in
   const bool fast = s.head_finite != 0;  // no skip rule to apply (head_chain_half)
   const int g = tid % (RHEADCOLS / RHG), pair = tid / (RHEADCOLS / RHG);  // windows 2 pair, 2 pair + 1
   const bool head = tid < RHEAD_THREADS;
@@ -812,6 +814,15 @@ __device__ void joint_partials(RSmem& s, const RParams& p, int slot, bool built)
         [&](int i) { return reinterpret_cast<uint4*>(&s.in2.j2[i / QH][4 * (i % QH)]); });
     __syncthreads();
     if (run) head_chain_half<false>(s, s.in2.j2, g, pair, RHALF, acc);
+    // Meanwhile warps 2.. stage the committed h0 -- the recurrent inputs of
+    // the next step's layer 0, unchanged until that step commits -- into
+    // in.x2, which the head chains no longer read.
+    {
+      const uint4* h0 = reinterpret_cast<const uint4*>(xh(p, XH0));
+      uint4* dst = reinterpret_cast<uint4*>(&s.in.x2[0][0]);
+      stage_background(2, RH * RROW16, [&](int i) { return h0 + i; }, [&](int i) { return dst + i; });
+    }
+    if (tid == 0) s.h0_staged = 1;
   } else {
     joint_inputs_staged(s, p, built, fast, g, pair, run, acc);
   }
@@ -860,14 +871,14 @@ __device__ void joint_decide(RSmem& s, const RParams& p, int slot) {
       b.dv = __uint_as_float(dr.x);
       b.di = dr.y;
     }
-    s.in.red[w][q] = b;
+    s.in2.red[w][q] = b;
   }
   __syncthreads();
   if (tid < p.batch && s.win[tid].joint) {
     const int w = tid;
-    RPartial b = s.in.red[w][0];
+    RPartial b = s.in2.red[w][0];
     for (int q = 1; q < RG / 8; ++q) {
-      const RPartial v = s.in.red[w][q];
+      const RPartial v = s.in2.red[w][q];
       if (better(b.tv, b.ti, v.tv, v.ti)) b.tv = v.tv, b.ti = v.ti;
       if (better(b.dv, b.di, v.dv, v.di)) b.dv = v.dv, b.di = v.di;
     }
@@ -1034,7 +1045,10 @@ __global__ void __launch_bounds__(RTHREADS, 1) tdt_resident_kernel(const RParams
     }
     s.win[tid] = c;
   }
-  if (tid == 0) s.gen = 0;
+  if (tid == 0) {
+    s.gen = 0;
+    s.h0_staged = 0;
+  }
   __syncthreads();
   int slot = 0;
   while (true) {
