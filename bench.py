@@ -59,10 +59,11 @@ FRAMES = 188
 METRIC = "encoder audio-sec/sec (RTFx)"
 UNIT = "audio-s/s"
 # Kernel launches of one encoder step: subsampling (conv0+dw2, pw3 GEMM, dw5,
-# pw6 GEMM, mask, flatten GEMM), 14 per layer (the out-LN of one layer and the
-# FF1 LN of the next share one dual-LayerNorm launch), the last layer's own
-# out-LN and the projector: 344, as counted by ncu's launch list of a step.
-LAUNCHES_PER_STEP = 6 + 24 * 14 + 1 + 1
+# pw6 GEMM with the time mask in its epilogue, flatten GEMM), 14 per layer (the
+# out-LN of one layer and the FF1 LN of the next share one dual-LayerNorm
+# launch), the last layer's own out-LN and the projector: 343, as counted by
+# ncu's launch list of a step.
+LAUNCHES_PER_STEP = 5 + 24 * 14 + 1 + 1
 # DRAM bytes (read + write) of one step's palette-GEMM launches: per-launch bytes from one ncu
 # capture of each bench.gemm_shapes(32) shape run alone, times its launches per step (the
 # per-shape table and the command are kept with the other ncu summaries under profiles/).

@@ -20,8 +20,9 @@ constexpr int CONV_K = 9;
 constexpr int CONV_TF = 64;                  // frames per CTA
 constexpr int CONV_TC = 128;                 // channels per CTA
 constexpr int CONV_ROWS = CONV_TF + CONV_K - 1;
-constexpr int CONV_THREADS = 256;
-constexpr int CONV_FPT = CONV_TF / (CONV_THREADS / (CONV_TC / 4));  // 8 consecutive frames per thread
+constexpr int CONV_THREADS = 512;
+constexpr int CONV_CPT = 2;                  // channels per thread in the depthwise phase
+constexpr int CONV_FPT = CONV_TF / (CONV_THREADS / (CONV_TC / CONV_CPT));  // 8 consecutive frames per thread
 constexpr int CONV_SMEM = CONV_ROWS * CONV_TC * 4;                  // 36 KB GLU tile
 
 __device__ __forceinline__ float fast_sigmoid(float v) {
@@ -63,6 +64,29 @@ template <>
 __device__ __forceinline__ void store4<float>(float* p, const float* v) {
   *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
 }
+// Two consecutive channels.
+template <typename T>
+__device__ __forceinline__ void load2(const T* p, float* v);
+template <>
+__device__ __forceinline__ void load2<__half>(const __half* p, float* v) {
+  const float2 a = __half22float2(__ldg(reinterpret_cast<const __half2*>(p)));
+  v[0] = a.x, v[1] = a.y;
+}
+template <>
+__device__ __forceinline__ void load2<float>(const float* p, float* v) {
+  const float2 f = __ldg(reinterpret_cast<const float2*>(p));
+  v[0] = f.x, v[1] = f.y;
+}
+template <typename T>
+__device__ __forceinline__ void store2(T* p, const float* v);
+template <>
+__device__ __forceinline__ void store2<__half>(__half* p, const float* v) {
+  *reinterpret_cast<__half2*>(p) = __floats2half2_rn(v[0], v[1]);
+}
+template <>
+__device__ __forceinline__ void store2<float>(float* p, const float* v) {
+  *reinterpret_cast<float2*>(p) = make_float2(v[0], v[1]);
+}
 template <typename T>
 __device__ __forceinline__ void load4(const T* p, float* v);
 template <>
@@ -81,10 +105,12 @@ __device__ __forceinline__ void load4<float>(const float* p, float* v) {
 // One CTA = (window, CONV_TF frames, CONV_TC channels).  Phase 1: the GLU of
 // the (CONV_TF + 8)-frame halo tile goes to shared memory (f32), every
 // 128-bit load issued before any GLU math.  Phase 2: thread (u, sg) owns
-// channels 4u .. 4u+3 and frames sg*CONV_FPT ..: it slides the 9-tap window
+// channels 2u, 2u+1 and frames sg*CONV_FPT ..: it slides the 9-tap window
 // down its frames, so each of its CONV_FPT + 8 rows is read from shared
-// memory once (a warp reads one 512-byte row: conflict-free) and reused by
-// up to 9 outputs.
+// memory once (a warp reads 256 contiguous bytes of one row: conflict-free)
+// and reused by up to 9 outputs.  512 threads with two channels each (not
+// 256 with four) keep the register count low enough for two CTAs -- 32
+// warps -- per SM.
 template <typename T>
 __global__ void __launch_bounds__(CONV_THREADS, 2) conformer_conv_kernel(
     const T* __restrict__ g, const T* __restrict__ dw, const float* __restrict__ scale,
@@ -125,35 +151,35 @@ __global__ void __launch_bounds__(CONV_THREADS, 2) conformer_conv_kernel(
       *reinterpret_cast<float4*>(&glu[r * CONV_TC + v * VEC + j]) =
           make_float4(val[j], val[j + 1], val[j + 2], val[j + 3]);
   }
-  const int u = tid % (CONV_TC / 4), sg = tid / (CONV_TC / 4);
-  const int c = c0 + 4 * u;
-  float w[CONV_K][4], sc[4], sh[4];
+  const int u = tid % (CONV_TC / CONV_CPT), sg = tid / (CONV_TC / CONV_CPT);
+  const int c = c0 + CONV_CPT * u;
+  float w[CONV_K][CONV_CPT], sc[CONV_CPT], sh[CONV_CPT];
 #pragma unroll
-  for (int k = 0; k < CONV_K; ++k) load4<T>(dw + k * CONV_C + c, w[k]);
+  for (int k = 0; k < CONV_K; ++k) load2<T>(dw + k * CONV_C + c, w[k]);
   {
-    const float4 a = __ldg(reinterpret_cast<const float4*>(scale + c));
-    const float4 s = __ldg(reinterpret_cast<const float4*>(shift + c));
-    sc[0] = a.x, sc[1] = a.y, sc[2] = a.z, sc[3] = a.w;
-    sh[0] = s.x, sh[1] = s.y, sh[2] = s.z, sh[3] = s.w;
+    const float2 a = __ldg(reinterpret_cast<const float2*>(scale + c));
+    const float2 s = __ldg(reinterpret_cast<const float2*>(shift + c));
+    sc[0] = a.x, sc[1] = a.y;
+    sh[0] = s.x, sh[1] = s.y;
   }
   __syncthreads();
   const int f0 = sg * CONV_FPT;  // first frame of this thread within the tile
-  float acc[CONV_FPT][4];
+  float acc[CONV_FPT][CONV_CPT];
 #pragma unroll
   for (int f = 0; f < CONV_FPT; ++f)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[f][j] = 0.0f;
+    for (int j = 0; j < CONV_CPT; ++j) acc[f][j] = 0.0f;
   // Row f0 + r feeds output frames f0 + r - k for taps k (fma in tap order).
 #pragma unroll
   for (int r = 0; r < CONV_FPT + CONV_K - 1; ++r) {
-    const float4 q = *reinterpret_cast<const float4*>(&glu[(f0 + r) * CONV_TC + 4 * u]);
-    const float x[4] = {q.x, q.y, q.z, q.w};
+    const float2 q = *reinterpret_cast<const float2*>(&glu[(f0 + r) * CONV_TC + CONV_CPT * u]);
+    const float x[CONV_CPT] = {q.x, q.y};
 #pragma unroll
     for (int k = 0; k < CONV_K; ++k) {
       const int f = r - k;
       if (f >= 0 && f < CONV_FPT) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[f][j] = fmaf(x[j], w[k][j], acc[f][j]);
+        for (int j = 0; j < CONV_CPT; ++j) acc[f][j] = fmaf(x[j], w[k][j], acc[f][j]);
       }
     }
   }
@@ -161,13 +187,13 @@ __global__ void __launch_bounds__(CONV_THREADS, 2) conformer_conv_kernel(
   for (int f = 0; f < CONV_FPT; ++f) {
     const int t = t0 + f0 + f;
     if (t >= frames) break;
-    float y[4];
+    float y[CONV_CPT];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < CONV_CPT; ++j) {
       const float a = fmaf(acc[f][j], sc[j], sh[j]);
       y[j] = a * fast_sigmoid(a);
     }
-    store4<T>(out + ((size_t)b * frames + t) * CONV_C + c, y);
+    store2<T>(out + ((size_t)b * frames + t) * CONV_C + c, y);
   }
 }
 
