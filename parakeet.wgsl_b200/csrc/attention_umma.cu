@@ -31,10 +31,12 @@
 // every thread parks its row's 64 values in shared memory and reads back the
 // 32 it needs at its own offset (both directions conflict-free).
 //
-// Persistent CTAs, one per SM (shared memory ~195 KB, TMEM all 512 columns),
+// Persistent CTAs, one per SM (shared memory ~225 KB, TMEM all 512 columns),
 // walk the tiles; the next tile's operands load while this one finishes: the
-// band once the scores are formed, Q once PV has consumed the probabilities,
-// K once the context tile staged over V has been stored.
+// band once the scores are formed, Q and K once PV has consumed the
+// probabilities and V.  The context is staged in a buffer of its own, so its
+// TMA store overlaps the next tile (the store of tile i must have read the
+// staging before tile i+1 writes it, a whole tile later).
 // Threads: 8 warps; warp w reads TMEM lanes 32 (w % 4) .. +31 (query rows) and
 // handles keys [96 (w / 4), +96) of them in the softmax and dims
 // [64 (w / 4), +64) in the epilogue.  Thread 0 issues the TMA loads and MMAs.
@@ -59,12 +61,18 @@ constexpr int U_QV = 32768;                    // (Q+v)
 constexpr int U_P = 0;                         // probabilities: 3 key blocks x 128 rows x 128 B (after the MMAs)
 constexpr int U_KV = 65536;                    // K (then V): 2 dim blocks x 192 rows x 128 B
 constexpr int U_PB = U_KV + 2 * UKEYS * 128;   // positional band: 2 dim blocks x 320 rows x 128 B
-constexpr int U_RED = U_PB + 2 * UBAND * 128;  // row max [2][128], row sum [2][128]
-constexpr int U_BAR = U_RED + 4 * UQ * 4;      // 6 mbarriers
+constexpr int U_CTX = U_PB + 2 * UBAND * 128;  // context staging: 2 dim blocks x 128 rows x 128 B
+// Row max [2][128] and row sum [2][128] live in the second half of the (Q+v)
+// block: written after the S and BD MMAs have read (Q+v), past the end of the
+// probabilities, and read before the next tile rebuilds (Q+v).
+constexpr int U_RED = U_P + 3 * UQ * 128;
+constexpr int U_BAR = U_CTX + 2 * UQ * 128;    // 6 mbarriers
 constexpr int U_MISC = U_BAR + 64;             // TMEM slot, abort flag, barrier arm counts
 constexpr int U_SMEM = U_MISC + 64 + 1024;     // + alignment slack
-static_assert(U_PB % 1024 == 0 && (UKEYS * 128) % 1024 == 0 && (UBAND / 2 * 128) % 1024 == 0,
+static_assert(U_PB % 1024 == 0 && U_CTX % 1024 == 0 && (UKEYS * 128) % 1024 == 0 && (UBAND / 2 * 128) % 1024 == 0,
               "swizzled operands must start on 1024-byte boundaries");
+static_assert(U_RED >= U_QV && U_RED + 4 * UQ * 4 <= U_KV, "row statistics inside the (Q+v) block, after P");
+static_assert(U_SMEM <= 232448, "shared memory budget");
 static_assert(8 * 32 * 68 * 4 <= 2 * UBAND * 128, "per-thread shift scratch rows fit in the band region");
 
 constexpr uint32_t IDESC_S = umma_idesc_f16(UQ, UKEYS, 0, 0);
@@ -369,6 +377,7 @@ __global__ void __launch_bounds__(UTHREADS, 1) rel_attention_umma_kernel(const _
     __syncthreads();
     // ---- O = P . V
     if (tid == 0) {
+      bulk_wait_group_read_all();  // the previous tile's context store has read the staging
       if (mbar_wait(bar_v, ph, abort_flag, p.status, PK_STATUS_TIMEOUT_TMA)) {
         tc_fence_after();
         const uint32_t pbuf = smem_addr(sm + U_P), vbase = smem_addr(sm + U_KV);
@@ -387,11 +396,14 @@ __global__ void __launch_bounds__(UTHREADS, 1) rel_attention_umma_kernel(const _
     ok = __syncthreads_and(ok) != 0;
     if (!ok) break;
     tc_fence_after();
-    if (tid == 0 && has_next) load_q(tn);  // the probabilities are consumed
+    if (tid == 0 && has_next) {  // the probabilities and V are consumed
+      load_q(tn);
+      load_kv(tn, bar_k, 1024, 1);
+    }
     {
       // ---- epilogue: warp w stages dims [64 (w / 4), +64) of its 32 rows
-      // (f16, swizzled) over the consumed V; one TMA store per dim block (rows
-      // past the window are clipped by the tensor bounds).
+      // (f16, swizzled) in the context buffer; one TMA store per dim block
+      // (rows past the window are clipped by the tensor bounds).
       const int dh = warp >> 2;
       uint32_t o0[32], o1[32];
       tc_ld_32x32b_x32(t_row + (uint32_t)(dh * 64), o0);
@@ -399,7 +411,7 @@ __global__ void __launch_bounds__(UTHREADS, 1) rel_attention_umma_kernel(const _
       tc_wait_ld();
       const bool live = q0 + r < valid;
       const float inv = live ? 1.0f / (red_sum[r] + red_sum[UQ + r]) : 0.0f;  // rows past valid: zero
-      const uint32_t obuf = smem_addr(sm + U_KV + dh * (UQ * 128));
+      const uint32_t obuf = smem_addr(sm + U_CTX + dh * (UQ * 128));
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         const uint32_t(&o)[32] = q < 4 ? o0 : o1;
@@ -415,10 +427,8 @@ __global__ void __launch_bounds__(UTHREADS, 1) rel_attention_umma_kernel(const _
     __syncthreads();  // O read out of TMEM (the next tile's MMAs may overwrite it) and staged
     if (tid == 0) {
       for (int kb = 0; kb < 2; ++kb)
-        tma_store_3d(&p.tmap_ctx, sm + U_KV + kb * (UQ * 128), h * 128 + kb * 64, q0, b);
+        tma_store_3d(&p.tmap_ctx, sm + U_CTX + kb * (UQ * 128), h * 128 + kb * 64, q0, b);
       bulk_commit_group();
-      bulk_wait_group_read_all();  // the staging has been read: K of the next tile may land there
-      if (has_next) load_kv(tn, bar_k, 1024, 1);
     }
   }
   // Unwind: every load and MMA commit this CTA armed has completed, and its
