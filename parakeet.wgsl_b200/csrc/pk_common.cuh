@@ -357,6 +357,19 @@ __device__ __forceinline__ void pdl_entry() {
   pdl_wait();
 }
 
+// ------------------------------------------------------- paired f32 FMA
+// Two independent f32 fused multiply-adds in one instruction (sm_100
+// fma.rn.f32x2): each lane of the pair is exactly fmaf(a, b, c), so chains
+// written with it round as the scalar chains do.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(d)
+      : "l"(*reinterpret_cast<const uint64_t*>(&a)), "l"(*reinterpret_cast<const uint64_t*>(&b)),
+        "l"(*reinterpret_cast<const uint64_t*>(&c)));
+  return *reinterpret_cast<const float2*>(&d);
+}
+
 // -------------------------------------------------------------- math bits
 // SiLU exactly as the reference epilogue writes it:
 // v / (1 + exp(-clamp(v, -20, 20)))  (src/webgpu/kernels/gemm.ts:2018-2032).

@@ -309,11 +309,13 @@ __global__ void __launch_bounds__(256, 3) conv0_dw2_f16_kernel(const float* __re
   }
   // Depthwise: thread = (output x, channels 4 dq .. 4 dq + 3).
   const int ox = warp * 4 + (lane >> 3), dq = lane & 7;
-  float wdr[9][4];
+  float2 wdr[9][2];  // channel pairs (4 dq, 4 dq + 1), (4 dq + 2, 4 dq + 3)
 #pragma unroll
   for (int k = 0; k < 9; ++k)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) wdr[k][j] = __half2float(wd[k * SUB_C + cbase + 4 * dq + j]);
+    for (int j = 0; j < 2; ++j)
+      wdr[k][j] = make_float2(__half2float(wd[k * SUB_C + cbase + 4 * dq + 2 * j]),
+                              __half2float(wd[k * SUB_C + cbase + 4 * dq + 2 * j + 1]));
   asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
   // In place: f32 pairs -> {hi pair, lo pair}; consecutive threads walk rows.
@@ -392,13 +394,15 @@ __global__ void __launch_bounds__(256, 3) conv0_dw2_f16_kernel(const float* __re
     const int y = 2 * oy + (warp >> 2);
     if (y <= y_last) conv0_mma(y, (warp & 3) * 16);
     __syncthreads();
-    float acc[4];
+    // Per channel an fma chain from the bias in tap order (ky outer, kx
+    // inner), two channels per paired FMA.
+    float2 acc01, acc23;
     if (oy >= vout) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) acc[j] = 0.0f;
+      acc01 = acc23 = make_float2(0.0f, 0.0f);
     } else {
       const float4 bq = *reinterpret_cast<const float4*>(biasd_s + 4 * dq);
-      acc[0] = bq.x, acc[1] = bq.y, acc[2] = bq.z, acc[3] = bq.w;
+      acc01 = make_float2(bq.x, bq.y);
+      acc23 = make_float2(bq.z, bq.w);
 #pragma unroll
       for (int ky = 0; ky < 3; ++ky) {
         const int iy = oy * 2 + ky - 1;
@@ -409,17 +413,12 @@ __global__ void __launch_bounds__(256, 3) conv0_dw2_f16_kernel(const float* __re
           const int ix = ox * 2 + kx - 1;  // <= 63
           if (ix < 0) continue;
           const uint2 raw2 = *reinterpret_cast<const uint2*>(rowp + ix * C0H_POS);
-          const float2 v01 = __half22float2(*reinterpret_cast<const __half2*>(&raw2.x));
-          const float2 v23 = __half22float2(*reinterpret_cast<const __half2*>(&raw2.y));
-          const float* wk = wdr[ky * 3 + kx];
-          acc[0] = fmaf(v01.x, wk[0], acc[0]);
-          acc[1] = fmaf(v01.y, wk[1], acc[1]);
-          acc[2] = fmaf(v23.x, wk[2], acc[2]);
-          acc[3] = fmaf(v23.y, wk[3], acc[3]);
+          acc01 = ffma2(__half22float2(*reinterpret_cast<const __half2*>(&raw2.x)), wdr[ky * 3 + kx][0], acc01);
+          acc23 = ffma2(__half22float2(*reinterpret_cast<const __half2*>(&raw2.y)), wdr[ky * 3 + kx][1], acc23);
         }
       }
     }
-    const __half2 o01 = __floats2half2_rn(acc[0], acc[1]), o23 = __floats2half2_rn(acc[2], acc[3]);
+    const __half2 o01 = __floats2half2_rn(acc01.x, acc01.y), o23 = __floats2half2_rn(acc23.x, acc23.y);
     uint2 packed;
     packed.x = *reinterpret_cast<const uint32_t*>(&o01);
     packed.y = *reinterpret_cast<const uint32_t*>(&o23);
