@@ -153,46 +153,38 @@ __global__ void __launch_bounds__(CONV_THREADS, 2) conformer_conv_kernel(
   }
   const int u = tid % (CONV_TC / CONV_CPT), sg = tid / (CONV_TC / CONV_CPT);
   const int c = c0 + CONV_CPT * u;
-  float w[CONV_K][CONV_CPT], sc[CONV_CPT], sh[CONV_CPT];
+  static_assert(CONV_CPT == 2, "a thread's channel pair shares each paired FMA");
+  float2 w[CONV_K];
 #pragma unroll
-  for (int k = 0; k < CONV_K; ++k) load2<T>(dw + k * CONV_C + c, w[k]);
-  {
-    const float2 a = __ldg(reinterpret_cast<const float2*>(scale + c));
-    const float2 s = __ldg(reinterpret_cast<const float2*>(shift + c));
-    sc[0] = a.x, sc[1] = a.y;
-    sh[0] = s.x, sh[1] = s.y;
+  for (int k = 0; k < CONV_K; ++k) {
+    float wk[2];
+    load2<T>(dw + k * CONV_C + c, wk);
+    w[k] = make_float2(wk[0], wk[1]);
   }
+  const float2 sc = __ldg(reinterpret_cast<const float2*>(scale + c));
+  const float2 sh = __ldg(reinterpret_cast<const float2*>(shift + c));
   __syncthreads();
   const int f0 = sg * CONV_FPT;  // first frame of this thread within the tile
-  float acc[CONV_FPT][CONV_CPT];
+  float2 acc[CONV_FPT];
 #pragma unroll
-  for (int f = 0; f < CONV_FPT; ++f)
-#pragma unroll
-    for (int j = 0; j < CONV_CPT; ++j) acc[f][j] = 0.0f;
-  // Row f0 + r feeds output frames f0 + r - k for taps k (fma in tap order).
+  for (int f = 0; f < CONV_FPT; ++f) acc[f] = make_float2(0.0f, 0.0f);
+  // Row f0 + r feeds output frames f0 + r - k for taps k (fma in tap order),
+  // both channels in one paired FMA (each lane exactly fmaf).
 #pragma unroll
   for (int r = 0; r < CONV_FPT + CONV_K - 1; ++r) {
     const float2 q = *reinterpret_cast<const float2*>(&glu[(f0 + r) * CONV_TC + CONV_CPT * u]);
-    const float x[CONV_CPT] = {q.x, q.y};
 #pragma unroll
     for (int k = 0; k < CONV_K; ++k) {
       const int f = r - k;
-      if (f >= 0 && f < CONV_FPT) {
-#pragma unroll
-        for (int j = 0; j < CONV_CPT; ++j) acc[f][j] = fmaf(x[j], w[k][j], acc[f][j]);
-      }
+      if (f >= 0 && f < CONV_FPT) acc[f] = ffma2(q, w[k], acc[f]);
     }
   }
 #pragma unroll
   for (int f = 0; f < CONV_FPT; ++f) {
     const int t = t0 + f0 + f;
     if (t >= frames) break;
-    float y[CONV_CPT];
-#pragma unroll
-    for (int j = 0; j < CONV_CPT; ++j) {
-      const float a = fmaf(acc[f][j], sc[j], sh[j]);
-      y[j] = a * fast_sigmoid(a);
-    }
+    const float2 a = ffma2(acc[f], sc, sh);
+    const float y[CONV_CPT] = {a.x * fast_sigmoid(a.x), a.y * fast_sigmoid(a.y)};
     store2<T>(out + ((size_t)b * frames + t) * CONV_C + c, y);
   }
 }

@@ -169,11 +169,13 @@ __global__ void __launch_bounds__(SG_THREADS) simt_palette_gemm_kernel(
   // This thread's outputs: rows ty*4 + {0..3} (and 64 + ty*4 + {0..3} when
   // BM = 128), columns tx*4 + {0..3} and 64 + tx*4 + {0..3}.
   const int ty = tid / 16, tx = tid % 16;
-  float acc[TM][TN];
+  // Accumulator pairs (features j, j+1): the FP32 chains run two outputs per
+  // paired FMA (fma.rn.f32x2, each lane exactly fmaf, still in increasing k).
+  float2 acc[TM][TN / 2];
 #pragma unroll
   for (int i = 0; i < TM; ++i)
 #pragma unroll
-    for (int j = 0; j < TN; ++j) acc[i][j] = 0.0f;
+    for (int j = 0; j < TN / 2; ++j) acc[i][j] = make_float2(0.0f, 0.0f);
   cp_async_wait_all();
   __syncthreads();  // tile 0 and the LUT
   simt_decode<T, BITS, BM>(t, 0, lut, columns, n0, groups, group_cols);
@@ -195,13 +197,18 @@ __global__ void __launch_bounds__(SG_THREADS) simt_palette_gemm_kernel(
       for (int q = 0; q < 4; ++q) {
         const float4 w0 = *reinterpret_cast<const float4*>(&t.w[cur][k4 + q][tx * 4]);
         const float4 w1 = *reinterpret_cast<const float4*>(&t.w[cur][k4 + q][64 + tx * 4]);
-        const float wv[TN] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        const float2 wv[TN / 2] = {make_float2(w0.x, w0.y), make_float2(w0.z, w0.w), make_float2(w1.x, w1.y),
+                                   make_float2(w1.z, w1.w)};
 #pragma unroll
         for (int i = 0; i < TM; ++i)
 #pragma unroll
-          for (int j = 0; j < TN; ++j) {
-            acc[i][j] = fmaf(av[i][q], wv[j], acc[i][j]);
-            if constexpr (ACC16) acc[i][j] = __half2float(__float2half_rn(acc[i][j]));
+          for (int j = 0; j < TN / 2; ++j) {
+            if constexpr (ACC16) {
+              acc[i][j].x = __half2float(__float2half_rn(fmaf(av[i][q], wv[j].x, acc[i][j].x)));
+              acc[i][j].y = __half2float(__float2half_rn(fmaf(av[i][q], wv[j].y, acc[i][j].y)));
+            } else {
+              acc[i][j] = ffma2(make_float2(av[i][q], av[i][q]), wv[j], acc[i][j]);
+            }
           }
       }
     }
@@ -220,7 +227,7 @@ __global__ void __launch_bounds__(SG_THREADS) simt_palette_gemm_kernel(
     for (int j = 0; j < TN; ++j) {
       const int n = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + j - 4);
       if (n >= columns) continue;
-      float v = acc[i][j];
+      float v = (j & 1) ? acc[i][j / 2].y : acc[i][j / 2].x;
       const size_t idx = (size_t)m * columns + n;
       if constexpr (ACC16) {  // the reference epilogue, each step rounded as written
         if (bias) v = __fadd_rn(v, bias[n]);

@@ -457,6 +457,8 @@ __global__ void __launch_bounds__(256) depthwise_kernel(const T* __restrict__ in
   }
 #pragma unroll
   for (int j = 0; j < 8; ++j) acc[j] = __ldg(bias + c + j);
+  // Channel pairs share one paired FMA (each lane exactly fmaf).
+  float2* acc2 = reinterpret_cast<float2*>(acc);
 #pragma unroll
   for (int ky = 0; ky < 3; ++ky) {
     const int iy = oy * 2 + ky - 1;
@@ -469,7 +471,8 @@ __global__ void __launch_bounds__(256) depthwise_kernel(const T* __restrict__ in
       load8<T>(in + (((int64_t)b * ih + iy) * iw + ix) * channels + c, v);
       load8<T>(w + (ky * 3 + kx) * channels + c, wk);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j] = fmaf(v[j], wk[j], acc[j]);
+      for (int j = 0; j < 4; ++j)
+        acc2[j] = ffma2(make_float2(v[2 * j], v[2 * j + 1]), make_float2(wk[2 * j], wk[2 * j + 1]), acc2[j]);
     }
   }
   store8<T>(dst, acc);
