@@ -153,7 +153,7 @@ __device__ __forceinline__ float4 load4(const __half* p) {
 }
 
 template <typename T, int BITS, bool ACC16, int BM, bool VEC>
-__global__ void __launch_bounds__(SG_THREADS) simt_palette_gemm_kernel(
+__global__ void __launch_bounds__(SG_THREADS, 2) simt_palette_gemm_kernel(
     const T* __restrict__ a, const uint32_t* __restrict__ codes, const T* __restrict__ palette,
     const float* __restrict__ bias, const T* __restrict__ residual, T* __restrict__ out, int rows, int inner,
     int columns, int groups, int group_cols, int act, int has_residual, float res_scale) {
