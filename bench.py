@@ -495,6 +495,10 @@ def time_e2e_pipelined(pk, graph, features, lengths, stream, steps):
 
 # FFMA peak of the FP32 package's GEMMs: SMs x 128 FP32 lanes x 2 FLOP per FMA x clock.
 FFMA_LANES_PER_SM = 128
+# Dense TF32 tensor-core rate of one B200 (NVIDIA's 2:4-sparse figure halved);
+# nominal, not measured -- the FP32 package's GEMMs do not use it (each output
+# must be the reference's fp32 fma chain), it is reported for scale.
+TF32_DENSE_TFLOPS_NOMINAL = 1100.0
 
 
 def time_config1(pk, device, stream, reps=50):
@@ -682,14 +686,19 @@ def time_fp32_encoder(pk, device, stream, batch=8, reps=5):
     props = torch.cuda.get_device_properties(device.ordinal)
     gemm_flops = sum(2.0 * (m // BATCH) * batch * k * n * launches
                      for m, k, n, _, _, _, _, launches in gemm_shapes(BATCH))
+    rate = gemm_flops / (ms * 1e-3) / 1e12
+    ffma_peak = props.multi_processor_count * FFMA_LANES_PER_SM * 2 * 1.965e9 / 1e12
     return {"workload": f"FP32 package encoder, {batch} x 15 s windows", "ms_per_step": round(ms, 2),
             "audio_s_per_s": round(batch * WINDOW_SECONDS / (ms * 1e-3), 1),
             "gemm_tflop_per_step": round(gemm_flops / 1e12, 3),
-            "gemm_tflops_if_all_time": round(gemm_flops / (ms * 1e-3) / 1e12, 2),
-            "ffma_peak_tflops_at_max_clock": round(props.multi_processor_count * FFMA_LANES_PER_SM * 2 * 1.965e9
-                                                   / 1e12, 1),
-            "peak_note": "SMs x 128 FP32 lanes x 2 FLOP x 1965 MHz (clocks.max.sm); the GEMM rate counts the whole "
-                         "step's time, so it is a lower bound"}
+            "gemm_tflops_if_all_time": round(rate, 2),
+            "ffma_peak_tflops_at_max_clock": round(ffma_peak, 1),
+            "frac_of_ffma_peak": round(rate / ffma_peak, 3),
+            "tf32_dense_tflops_nominal": TF32_DENSE_TFLOPS_NOMINAL,
+            "frac_of_tf32_nominal": round(rate / TF32_DENSE_TFLOPS_NOMINAL, 4),
+            "peak_note": "FFMA: SMs x 128 FP32 lanes x 2 FLOP x 1965 MHz (clocks.max.sm); TF32: nominal dense tensor "
+                         "rate, unused by these bit-exact fp32 chains; the GEMM rate counts the whole step's time, so "
+                         "both fractions are lower bounds"}
 
 
 def cpu_baseline(pk, package, window_count=1):
