@@ -152,23 +152,26 @@ def measured_peaks():
     return 1590.0, 6650.0, "fallback"
 
 
-def gemm_operands(pk, rng, rows, inner, columns, bits, groups, act, epi):
+def gemm_operands(pk, rng, rows, inner, columns, bits, groups, act, epi, precision="fp16"):
     """Device operands and the pk_gemm_desc of one palette GEMM of the step
-    (random activations, codes and palettes; the encoder's epilogue)."""
+    (random activations, codes and palettes; the encoder's epilogue), FP16 or
+    FP32 package."""
     import torch
 
     L = pk._lib
-    codes, lut = pk.synthetic.palette_matrix(rng, inner, columns, bits, groups, "fp16")
+    dt = torch.float16 if precision == "fp16" else torch.float32
+    codes, lut = pk.synthetic.palette_matrix(rng, inner, columns, bits, groups, precision)
     keep = {
-        "a": torch.randn((rows, inner), dtype=torch.float16, device="cuda"),
-        "c": torch.empty((rows, columns), dtype=torch.float16, device="cuda"),
-        "res": torch.randn((rows, columns), dtype=torch.float16, device="cuda") if epi == "residual" else None,
+        "a": torch.randn((rows, inner), dtype=dt, device="cuda"),
+        "c": torch.empty((rows, columns), dtype=dt, device="cuda"),
+        "res": torch.randn((rows, columns), dtype=dt, device="cuda") if epi == "residual" else None,
         "bias": torch.randn(columns, dtype=torch.float32, device="cuda") if epi == "bias" else None,
         "codes": torch.from_numpy(codes["data"].view(np.int32)).cuda(),
         "lut": torch.from_numpy(lut["data"]).cuda(),
     }
     ptr = lambda name: None if keep[name] is None else keep[name].data_ptr()  # noqa: E731
-    desc = L.GemmDesc(L.FP16, rows, inner, columns, bits, groups, columns // groups, L.ACT[act],
+    desc = L.GemmDesc(L.FP16 if precision == "fp16" else L.FP32, rows, inner, columns, bits, groups,
+                      columns // groups, L.ACT[act],
                       int(epi == "residual"), 0.5, ptr("bias"), ptr("res"), ptr("a"), ptr("codes"), ptr("lut"),
                       ptr("c"))
     return desc, keep
@@ -924,9 +927,10 @@ def run_kernel(args):
         keep.append(t)
         return ctypes.c_void_p(t.data_ptr())
 
-    if args.kernel == "gemm":
+    if args.kernel in ("gemm", "gemm-fp32"):
         m, k, n, bits = (int(x) for x in args.shape.split(","))
-        desc, keep_gemm = gemm_operands(pk, rng, m, k, n, bits, 1, args.act, args.epi)
+        desc, keep_gemm = gemm_operands(pk, rng, m, k, n, bits, 1, args.act, args.epi,
+                                        "fp32" if args.kernel == "gemm-fp32" else "fp16")
         launch = lambda: L.call("pk_palette_gemm", device.handle, ctypes.byref(desc), None)  # noqa: E731
     elif args.kernel == "gemm-step":
         # Each distinct palette GEMM of a config-3 step once per launch() call.
@@ -1022,7 +1026,7 @@ def main():
     ap.add_argument("--skip-longform", action="store_true")
     ap.add_argument("--legs", default="logmel,decoder,transcribe,longform,gemm,config12,fp32",
                     help="comma-separated extra legs to run besides the encoder step (a subset for quick runs)")
-    ap.add_argument("--kernel", choices=["gemm", "gemm-step", "attention", "attention-mma", "layernorm", "conv",
+    ap.add_argument("--kernel", choices=["gemm", "gemm-fp32", "gemm-step", "attention", "attention-mma", "layernorm", "conv",
                                          "subsampling", "decoder", "logmel"],
                     help="profiling target: launch one operator only")
     ap.add_argument("--shape", default="", help="gemm: M,K,N,BITS; attention/conv/decoder: batch; layernorm: rows")
