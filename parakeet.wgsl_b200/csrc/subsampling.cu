@@ -273,14 +273,22 @@ __global__ void __launch_bounds__(256, 3) conv0_dw2_f16_kernel(const float* __re
   const int iy_first = 2 * y_first - 1;  // first input time sample
   // Stage the strip: 4-byte asynchronous copies, all in flight at once,
   // consecutive threads walking time (contiguous in the feature-major log-mel).
-  for (int i = tid; i < C0_IN_ROWS * SUB_IW; i += 256) {
-    const int r = i % C0_IN_ROWS, x = i / C0_IN_ROWS;
+  // Item i = x * C0_IN_ROWS + r; (r, x) advance by the stride's quotient and
+  // remainder instead of a division per item.
+  constexpr int STEP_R = 256 % C0_IN_ROWS, STEP_X = 256 / C0_IN_ROWS;
+  for (int i = tid, r = tid % C0_IN_ROWS, x = tid / C0_IN_ROWS; i < C0_IN_ROWS * SUB_IW; i += 256) {
     const int iy = iy_first + r;
     const bool in_range = iy >= 0 && iy < SUB_IH;
     const float* src = fbank + ((size_t)b * SUB_IW + x) * SUB_IH + (in_range ? iy : 0);
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_addr(plane + r * C0H_ROW_WORDS + x + 1)),
                  "l"(src), "r"(in_range ? 4 : 0)
                  : "memory");
+    r += STEP_R;
+    x += STEP_X;
+    if (r >= C0_IN_ROWS) {
+      r -= C0_IN_ROWS;
+      ++x;
+    }
   }
   asm volatile("cp.async.commit_group;" ::: "memory");
   for (int r = tid; r < C0_IN_ROWS; r += 256) {  // mel bins -1 and 128
@@ -319,8 +327,7 @@ __global__ void __launch_bounds__(256, 3) conv0_dw2_f16_kernel(const float* __re
   asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
   // In place: f32 pairs -> {hi pair, lo pair}; consecutive threads walk rows.
-  for (int i = tid; i < C0_IN_ROWS * (SUB_IW / 2 + 1); i += 256) {
-    const int r = i % C0_IN_ROWS, sl = i / C0_IN_ROWS;
+  for (int i = tid, r = tid % C0_IN_ROWS, sl = tid / C0_IN_ROWS; i < C0_IN_ROWS * (SUB_IW / 2 + 1); i += 256) {
     float2* slot = reinterpret_cast<float2*>(plane + r * C0H_ROW_WORDS) + sl;
     const float2 v = *slot;
     const __half2 hi = __floats2half2_rn(v.x, v.y);
@@ -330,6 +337,12 @@ __global__ void __launch_bounds__(256, 3) conv0_dw2_f16_kernel(const float* __re
     packed.x = *reinterpret_cast<const uint32_t*>(&hi);
     packed.y = *reinterpret_cast<const uint32_t*>(&lo);
     *reinterpret_cast<uint2*>(slot) = packed;
+    r += STEP_R;
+    sl += STEP_X;
+    if (r >= C0_IN_ROWS) {
+      r -= C0_IN_ROWS;
+      ++sl;
+    }
   }
   __syncthreads();
 
