@@ -976,6 +976,17 @@ def run_kernel(args):
         launch = lambda: L.call("pk_subsampling_conv0_dw2", device.handle, L.FP16, b,  # noqa: E731
                                 ctypes.c_void_p(fb.data_ptr()), w0, b0, wd, bd, lens,
                                 ctypes.c_void_p(out.data_ptr()), None)
+    elif args.kernel == "depthwise":
+        # The subsampling's second depthwise 3x3 / 2 (channel-last FP16, 376 x 32 -> 188 x 16 x 256).
+        b = int(args.shape or BATCH)
+        x = torch.randn((b, 376, 32, 256), dtype=torch.float16, device="cuda")
+        out = torch.empty((b, 188, 16, 256), dtype=torch.float16, device="cuda")
+        wd = dev((0.1 * rng.standard_normal((3, 3, 256))).astype(np.float16))
+        bd = dev((0.02 * rng.standard_normal(256)).astype(np.float32))
+        lens = dev(np.full(b, 1501, np.uint32))
+        launch = lambda: L.call("pk_subsampling_depthwise", device.handle, L.FP16, b, 376, 32, 256,  # noqa: E731
+                                ctypes.c_void_p(x.data_ptr()), wd, bd, lens, 3, ctypes.c_void_p(out.data_ptr()),
+                                None)
     elif args.kernel == "conv":
         b = int(args.shape or BATCH)
         gin = torch.randn((b * FRAMES, 2048), dtype=torch.float16, device="cuda")
@@ -1027,7 +1038,7 @@ def main():
     ap.add_argument("--legs", default="logmel,decoder,transcribe,longform,gemm,config12,fp32",
                     help="comma-separated extra legs to run besides the encoder step (a subset for quick runs)")
     ap.add_argument("--kernel", choices=["gemm", "gemm-fp32", "gemm-step", "attention", "attention-mma", "layernorm", "conv",
-                                         "subsampling", "decoder", "logmel"],
+                                         "subsampling", "depthwise", "decoder", "logmel"],
                     help="profiling target: launch one operator only")
     ap.add_argument("--shape", default="", help="gemm: M,K,N,BITS; attention/conv/decoder: batch; layernorm: rows")
     ap.add_argument("--act", default="none", choices=["none", "silu", "relu"])
